@@ -1,0 +1,91 @@
+/*
+ * uttt_b200.h -- C ABI of the B200-native uTTT serving hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*), launches asynchronously on that stream and returns an
+ * int status (UTTT_OK or one of the error codes below).  Invalid arguments
+ * are rejected on the host before any launch.  Bounded device-side waits
+ * that expire record UTTT_ERR_TIMEOUT in the first int of the workspace;
+ * read it with uttt_read_status() after the stream is synchronised.
+ *
+ * Tensor layouts are the reference's (Phova/uTTTCompanion,
+ * model/uttt_layer.py): activations (B, T, d) row-major, fast weights
+ * w_up / w_gate (B, d, h) and w_down (B, h, d) row-major FP32 masters,
+ * LayerNorm weight / bias (d,).  BF16 buffers hold IEEE bfloat16 bits.
+ */
+#ifndef UTTT_B200_H
+#define UTTT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define UTTT_OK 0
+#define UTTT_ERR_INVALID 1     /* bad argument or shape   -> Python ValueError   */
+#define UTTT_ERR_UNSUPPORTED 2 /* unsupported size/option  -> Python ValueError   */
+#define UTTT_ERR_CUDA 3        /* CUDA launch/runtime error -> Python RuntimeError */
+#define UTTT_ERR_TIMEOUT 4     /* bounded device wait expired -> RuntimeError    */
+#define UTTT_ERR_WORKSPACE 5   /* workspace too small       -> ValueError        */
+
+/* dtype tags for outputs */
+#define UTTT_DTYPE_F32 0
+#define UTTT_DTYPE_BF16 1
+
+/* ---- library ----------------------------------------------------------- */
+int uttt_version(void);
+const char* uttt_status_string(int status);
+/* Last CUDA runtime error code seen by the library on this thread (0 if none). */
+int uttt_last_cuda_error(void);
+/* Reads (and, if reset != 0, clears) the device status word at the start of a
+ * workspace.  Synchronises `stream`. */
+int uttt_read_status(void* workspace, int reset, void* stream);
+
+/* ---- diagnostics -------------------------------------------------------- */
+/* D(MxN, fp32) = A * B^T on the tensor cores, used by the self-tests that pin
+ * the descriptor / swizzle / TMEM conventions.  mode bit0: A is given
+ * MN-major (K x M row-major) instead of K-major (M x K); bit1: same for B;
+ * bit2: A is FP32 (converted to BF16 by software producers).  M % 128 == 0,
+ * N in {64,128,256}, K % 64 == 0.  No counterpart in the reference. */
+int uttt_selftest_gemm(int mode, int M, int N, int K, const void* a, const void* b, float* d, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---- chunk-wise TTT write ---------------------------------------------- */
+/*
+ * Replaces fused_chunk_ttt_step (model/uttt_layer.py:414-534) and its
+ * analytical gradient analytical_swiglu_chunk_grad (:279-411), for B
+ * independent states, over n_chunks consecutive chunks of C tokens starting
+ * at token chunk_begin*C of every state's T-token sequence.  Chunks are
+ * applied sequentially (each reads the state the previous one wrote), as
+ * SharedFastWeightPool.chunk_step (:697-771) chains them.
+ *
+ *   q, k, v        BF16 (B, T, d); q may equal k.
+ *   eta, alpha     FP32 (B, T) per-token inner lr and decay gate.
+ *   mask           FP32 (B, T) right-padding mask or NULL.
+ *   w_*, s_*       FP32 masters, updated IN PLACE.
+ *   ln_weight/bias FP32 (d,).
+ *   out            readout (B, T, d) of f_W(q) with each chunk's pre-update
+ *                  weights, written only when q == k (it is then v_hat);
+ *                  otherwise pass NULL and call uttt_fast_readout first.
+ *   token_loss     FP32 (B, T): 0.5*||f_W(k_t) - v_t||^2 (/d if normalize)
+ *                  per token (the unweighted surprise terms), or NULL.
+ *   clip_scale     FP32 (B, n_chunks): applied clip factor per chunk, or NULL.
+ *
+ * Requires d % 128 == 0, 1 <= C <= 64.
+ */
+size_t uttt_chunk_write_workspace(int B, int C, int d, int h);
+int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q, const void* k,
+                     const void* v, const float* eta, const float* alpha, const float* mask, float* w_up,
+                     float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
+                     const float* ln_weight, const float* ln_bias, float momentum_beta, float max_grad_norm,
+                     int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss,
+                     float* clip_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UTTT_B200_H */

@@ -256,9 +256,9 @@ def main():
     chunk_case(ul, "f64_full", f64, f64, 4, 8, 16, 24, "ragged", 0.9, 0.05, False, True, 2)
     chunk_case(ul, "f32_plain", f32, f32, 2, 16, 32, 48, None, 0.0, 0.0, True, False, 3)
     chunk_case(ul, "f32_full", f32, f32, 4, 16, 32, 48, "ragged", 0.9, 0.5, False, True, 4)
-    chunk_case(ul, "bf16_plain", f32, bf, 2, 64, 64, 96, None, 0.0, 0.0, True, False, 5)
-    chunk_case(ul, "bf16_full", f32, bf, 4, 64, 64, 96, "ragged", 0.9, 1.0, False, True, 6)
-    chunk_case(ul, "bf16_clipbite", f32, bf, 2, 64, 64, 96, None, 0.5, 0.02, False, False, 7)
+    chunk_case(ul, "bf16_plain", f32, bf, 2, 64, 128, 160, None, 0.0, 0.0, True, False, 5)
+    chunk_case(ul, "bf16_full", f32, bf, 3, 64, 128, 160, "ragged", 0.9, 1.0, False, True, 6)
+    chunk_case(ul, "bf16_clipbite", f32, bf, 2, 64, 128, 160, None, 0.5, 0.02, False, False, 7)
     swiglu_case(ul, "f32", f32, 21)
     swiglu_case(ul, "bf16", bf, 22)
     elastic_case(ul)

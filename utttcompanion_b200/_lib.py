@@ -1,0 +1,91 @@
+"""ctypes binding of ``libuttt_b200.so`` (the C ABI declared in include/uttt_b200.h).
+
+The library is loaded from the package directory (built in-tree by
+``python -m utttcompanion_b200.build``).  There is no fallback: if it is
+missing, every op raises.  Status codes map to the reference's error
+classes: invalid arguments / unsupported shapes -> ``ValueError`` (the
+server maps those to HTTP 422, ``server/app.py:271-272``), runtime and
+device-wait failures -> ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+from typing import Dict, Optional
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libuttt_b200.so")
+HEADER = os.path.join(os.path.dirname(PKG), "include", "uttt_b200.h")
+
+UTTT_OK = 0
+UTTT_ERR_INVALID = 1
+UTTT_ERR_UNSUPPORTED = 2
+UTTT_ERR_CUDA = 3
+UTTT_ERR_TIMEOUT = 4
+UTTT_ERR_WORKSPACE = 5
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+vp = C.c_void_p
+i32 = C.c_int
+f32 = C.c_float
+sz = C.c_size_t
+
+# argtypes per exported symbol; kept in the same order as include/uttt_b200.h
+SIGNATURES: Dict[str, tuple] = {
+    "uttt_version": (i32, []),
+    "uttt_status_string": (C.c_char_p, [i32]),
+    "uttt_last_cuda_error": (i32, []),
+    "uttt_read_status": (i32, [vp, i32, vp]),
+    "uttt_selftest_gemm": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
+    "uttt_chunk_write_workspace": (sz, [i32, i32, i32, i32]),
+    "uttt_chunk_write": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                               vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp, sz, vp]),
+}
+
+_lib: Optional[C.CDLL] = None
+
+
+class UtttError(RuntimeError):
+    pass
+
+
+def load() -> C.CDLL:
+    """Load the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m utttcompanion_b200.build` "
+            "(there is no CPU fallback for the uTTT B200 ops)")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        try:
+            fn = getattr(lib, name)
+        except AttributeError:      # reported by tests/test_capi.py
+            continue
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def header_symbols() -> list:
+    """Function names declared in include/uttt_b200.h."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(uttt_[a-z0-9_]+)\s*\(", text)))
+
+
+def check(status: int, what: str = "uttt op") -> None:
+    if status == UTTT_OK:
+        return
+    lib = load()
+    msg = lib.uttt_status_string(status).decode()
+    if status in (UTTT_ERR_INVALID, UTTT_ERR_UNSUPPORTED, UTTT_ERR_WORKSPACE):
+        raise ValueError(f"{what}: {msg}")
+    cuda = lib.uttt_last_cuda_error()
+    raise UtttError(f"{what}: {msg}" + (f" (cudaError {cuda})" if cuda else ""))

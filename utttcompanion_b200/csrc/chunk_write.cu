@@ -1,0 +1,842 @@
+// Chunk-wise TTT write for B independent FP32 fast-weight states on the
+// tcgen05 tensor cores.  Replaces fused_chunk_ttt_step and
+// analytical_swiglu_chunk_grad (model/uttt_layer.py:279-534).
+//
+// One chunk is three (four with gradient clipping) launches over a grid of
+// (h / 128 hidden tiles) x (B states):
+//
+//   fwd   U,G = K W_up, K W_gate        (tile: 128 hidden x 64 tokens, K = d)
+//         H   = silu(G) * U              (FP32 in registers -> BF16 operand)
+//         Z  += H W_down                 (partial over this hidden tile; FP32
+//                                         red.add into an L2-resident buffer)
+//   ln    per token: LayerNorm stats of Z, v_hat = k + LN(Z), err = v_hat - v,
+//         token loss, dZ (analytical LayerNorm backward, BF16)
+//   bwd   dH  = dZ W_down^T              (K = d)
+//         dU  = dH * silu(G),  dG = dH * U * silu'(G)
+//         gradW_up^T = dU^T K,  gradW_gate^T = dG^T K,  gradW_down^T = dZ^T H
+//         (K = 64 tokens, per 128-wide slice of d)  then, in the epilogue,
+//         S' = beta S - clip * grad,  W' = (1 - alpha_bar) W + S'  in FP32,
+//         in place.  With clipping, a first bwd pass only accumulates the
+//         squared gradient norm of each state.
+//
+// W masters are FP32 in HBM; software producer warps convert them to BF16
+// straight into 128B-swizzled UMMA operand tiles.  Activation tiles (K, dZ)
+// arrive by TMA.  All accumulators live in tensor memory.
+#include <string.h>
+
+#include "common.cuh"
+#include "host_util.cuh"
+
+namespace uttt {
+namespace {
+
+constexpr int HT = 128;            // hidden rows per CTA
+constexpr int CT = 64;             // token columns (chunk padded to 64)
+constexpr int NPROD = 256;         // producer / epilogue threads (8 warps)
+constexpr int NTHREADS = NPROD + 64;  // + TMA warp + MMA warp
+constexpr int NSLOT = 4;
+constexpr int SLOT_BYTES = 40 * 1024;
+constexpr int TMA_WARP = 8, MMA_WARP = 9;
+constexpr int BWD_SLOT = 24 * 1024;
+
+struct ChunkParams {
+  int B, T, C, Cc, d, h, tok0;
+  const float* w_up;   // (B, d, h)
+  const float* w_gate;
+  const float* w_down;  // (B, h, d)
+  float* w_up_out;
+  float* w_gate_out;
+  float* w_down_out;
+  const float* s_up;
+  const float* s_gate;
+  const float* s_down;
+  float* s_up_out;
+  float* s_gate_out;
+  float* s_down_out;
+  const float* eta;    // (B, T)
+  const float* alpha;  // (B, T)
+  const float* mask;   // (B, T) or null
+  const float* ln_w;
+  const float* ln_b;
+  const __nv_bfloat16* k;  // (B, T, d)
+  const __nv_bfloat16* v;
+  float* zacc;     // (B, 64, d)
+  float* u_save;   // (B, 64, hp)
+  float* g_save;   // (B, 64, hp)
+  __nv_bfloat16* dz;  // (B, 64, d)
+  float* norm2;    // (B)
+  float* token_loss;  // (B, T) or null
+  void* out;          // (B, T, d) or null
+  int out_bf16;
+  float* clip_out;    // (B, n_chunks) or null
+  int chunk_index;
+  int n_chunks;
+  int hp;             // hidden padded to 128
+  float beta, clip, eps, inv_scale;
+  int* status;
+};
+
+// Per-state chunk statistics: number of valid tokens, masked mean of alpha,
+// whether any token is valid (model/uttt_layer.py:371-378,501-520).
+struct ChunkStats {
+  float count;   // valid tokens (Cc without a mask)
+  float alpha_bar;
+  bool active;
+};
+
+__device__ ChunkStats chunk_stats(const ChunkParams& p, int b) {
+  // executed by one warp
+  const int lane = threadIdx.x & 31;
+  float cnt = 0.f, asum = 0.f;
+  for (int c = lane; c < p.Cc; c += 32) {
+    const size_t idx = (size_t)b * p.T + p.tok0 + c;
+    const float m = p.mask ? p.mask[idx] : 1.f;
+    cnt += m;
+    asum += p.alpha[idx] * m;
+  }
+  cnt = warp_sum(cnt);
+  asum = warp_sum(asum);
+  ChunkStats s;
+  s.count = cnt;
+  s.alpha_bar = p.mask ? asum / fmaxf(cnt, 1.f) : asum / (float)p.Cc;
+  s.active = p.mask ? (cnt != 0.f) : true;
+  return s;
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* raw) {
+  const uint32_t pad = (1024u - (smem_u32(raw) & 1023u)) & 1023u;
+  return raw + pad;
+}
+
+// ============================================================================
+// fwd: U, G, H and the partial Z of one 128-row hidden tile
+// ============================================================================
+__global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                const ChunkParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], ug_done, h_ready, zfull[2], zfree[2];
+  __shared__ uint32_t tmem_slot;
+  uint8_t* slots = align1024(smem_raw);
+  uint8_t* sH = slots + NSLOT * SLOT_BYTES;  // 16 KB: MN-major [hh 128 rows][64 tokens]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int h0 = t * HT;
+  const int nkb = p.d / 64;
+  const int nmt = p.d / 128;
+
+  if (tid == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&full[i], NPROD + 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&ug_done, 1);
+    mbar_init(&h_ready, NPROD);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&zfull[i], 1);
+      mbar_init(&zfree[i], NPROD);
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t tU = tmem, tG = tmem + 64, tZ = tmem + 128;
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ producers
+    const float* wu = p.w_up + (size_t)b * p.d * p.h;
+    const float* wg = p.w_gate + (size_t)b * p.d * p.h;
+    int it = 0;
+    for (int kb = 0; kb < nkb; ++kb, ++it) {
+      const int s = it % NSLOT;
+      mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+      uint8_t* sUp = slots + s * SLOT_BYTES;
+      uint8_t* sGa = sUp + 16384;
+      // 64 rows (k) x 128 cols (hidden) per matrix; thread -> 8 float4 per matrix
+      float4 fu[8], fg[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int idx = tid + j * NPROD;  // 0..2047
+        const int kr = idx >> 5, c4 = (idx & 31) * 4;
+        const int col = h0 + c4;
+        const size_t off = (size_t)(kb * 64 + kr) * p.h + col;
+        if (col < p.h) {
+          fu[j] = __ldg(reinterpret_cast<const float4*>(wu + off));
+          fg[j] = __ldg(reinterpret_cast<const float4*>(wg + off));
+        } else {
+          fu[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          fg[j] = fu[j];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int idx = tid + j * NPROD;
+        const int kr = idx >> 5, c4 = (idx & 31) * 4;
+        const uint32_t o = (c4 >> 6) * 8192 + sw128_offset(kr, (c4 & 63) * 2);
+        uint2 pu, pg;
+        pu.x = pack_bf16x2(fu[j].x, fu[j].y);
+        pu.y = pack_bf16x2(fu[j].z, fu[j].w);
+        pg.x = pack_bf16x2(fg[j].x, fg[j].y);
+        pg.y = pack_bf16x2(fg[j].z, fg[j].w);
+        *reinterpret_cast<uint2*>(sUp + o) = pu;
+        *reinterpret_cast<uint2*>(sGa + o) = pg;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&full[s]);
+    }
+
+    // ------------------------------------------------------------ epilogue 1: H
+    mbar_wait(&ug_done, 0, p.status);
+    tc_fence_after();
+    {
+      const int q = warp & 3, half = warp >> 2;
+      const int row = q * 32 + lane;           // hidden row within tile
+      const int c0 = half * 32;                // token columns
+      float u[32], g[32];
+      tmem_ld16(tmem_addr(tU, q * 32, c0), *reinterpret_cast<float(*)[16]>(&u[0]));
+      tmem_ld16(tmem_addr(tU, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&u[16]));
+      tmem_ld16(tmem_addr(tG, q * 32, c0), *reinterpret_cast<float(*)[16]>(&g[0]));
+      tmem_ld16(tmem_addr(tG, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&g[16]));
+      tmem_wait_ld();
+      float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
+      float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        us[(size_t)(c0 + i) * p.hp] = u[i];
+        gs[(size_t)(c0 + i) * p.hp] = g[i];
+      }
+      // H tile, MN-major: row = hidden, 64 token values per 128 B row
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 pk;
+        float hv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float gg = g[i + e];
+          hv[e] = (c0 + i + e < p.Cc) ? gg * sigmoidf_(gg) * u[i + e] : 0.f;
+        }
+        pk.x = pack_bf16x2(hv[0], hv[1]);
+        pk.y = pack_bf16x2(hv[2], hv[3]);
+        pk.z = pack_bf16x2(hv[4], hv[5]);
+        pk.w = pack_bf16x2(hv[6], hv[7]);
+        *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + i) * 2)) = pk;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&h_ready);
+    }
+
+    // ------------------------------------------------------------ W_down tiles + Z drain
+    const float* wd = p.w_down + (size_t)b * p.h * p.d;
+    for (int mt = 0; mt < nmt; ++mt, ++it) {
+      const int s = it % NSLOT;
+      mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+      uint8_t* sA = slots + s * SLOT_BYTES;
+      // A (M = d slice of 128, K = 128 hidden rows), MN-major: [dblk 2][hh 128][64 d]
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {
+        const int idx = tid + j * NPROD;  // 0..4095
+        const int hh = idx >> 5, c4 = (idx & 31) * 4;
+        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (h0 + hh < p.h) f = __ldg(reinterpret_cast<const float4*>(wd + (size_t)(h0 + hh) * p.d + mt * 128 + c4));
+        uint2 pk;
+        pk.x = pack_bf16x2(f.x, f.y);
+        pk.y = pack_bf16x2(f.z, f.w);
+        *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = pk;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&full[s]);
+
+      // drain the previous Z tile while the tensor cores work on this one
+      if (mt > 0) {
+        const int pm = mt - 1, zb = pm & 1;
+        mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
+        tc_fence_after();
+        const int q = warp & 3, half = warp >> 2;
+        const int row = q * 32 + lane, c0 = half * 32;
+        float z[32];
+        tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
+        tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&zfree[zb]);
+        float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < p.Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
+      }
+    }
+    {
+      const int pm = nmt - 1, zb = pm & 1;
+      mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
+      tc_fence_after();
+      const int q = warp & 3, half = warp >> 2;
+      const int row = q * 32 + lane, c0 = half * 32;
+      float z[32];
+      tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
+      tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
+      tmem_wait_ld();
+      float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
+      for (int i = 0; i < 32; ++i)
+        if (c0 + i < p.Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
+    }
+  } else if (warp == TMA_WARP) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      int it = 0;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % NSLOT;
+        mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+        mbar_arrive_expect_tx(&full[s], 8192);
+        tma_load_3d(slots + s * SLOT_BYTES + 32768, &tmK, &full[s], kb * 64, p.tok0, b);
+      }
+      for (int mt = 0; mt < nmt; ++mt, ++it) {
+        const int s = it % NSLOT;
+        mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+        mbar_arrive(&full[s]);
+      }
+    }
+  } else {  // MMA warp
+    if (lane == 0) {
+      const uint32_t id_ug = idesc_bf16(128, 64, true, false);
+      int it = 0;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % NSLOT;
+        mbar_wait(&full[s], (it / NSLOT) & 1, p.status);
+        tc_fence_after();
+        const uint32_t a_up = smem_u32(slots + s * SLOT_BYTES);
+        const uint32_t a_ga = a_up + 16384, bk = a_up + 32768;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t bd = sdesc_sw128(bk + ks * 32, 16, 1024);
+          const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
+          mma_bf16(tU, sdesc_sw128(a_up + ks * 2048, 8192, 1024), bd, id_ug, acc);
+          mma_bf16(tG, sdesc_sw128(a_ga + ks * 2048, 8192, 1024), bd, id_ug, acc);
+        }
+        mma_commit(&empty[s]);
+      }
+      mma_commit(&ug_done);
+      mbar_wait(&h_ready, 0, p.status);
+      tc_fence_after();
+      const uint32_t id_z = idesc_bf16(128, 64, true, true);
+      const uint32_t hb = smem_u32(sH);
+      for (int mt = 0; mt < nmt; ++mt, ++it) {
+        const int s = it % NSLOT, zb = mt & 1;
+        mbar_wait(&full[s], (it / NSLOT) & 1, p.status);
+        mbar_wait(&zfree[zb], ((mt >> 1) & 1) ^ 1, p.status);
+        tc_fence_after();
+        const uint32_t a = smem_u32(slots + s * SLOT_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_bf16(tZ + zb * 64, sdesc_sw128(a + ks * 2048, 16384, 1024), sdesc_sw128(hb + ks * 2048, 8192, 1024),
+                   id_z, ks > 0 ? 1u : 0u);
+        mma_commit(&empty[s]);
+        mma_commit(&zfull[zb]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ============================================================================
+// ln: LayerNorm statistics, v_hat, token loss, analytical LayerNorm backward
+// ============================================================================
+constexpr int LN_THREADS = 256;
+constexpr int LN_MAXV = 16;  // d <= 4096
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < LN_THREADS / 32; ++i) s += red[i];
+  return s;
+}
+
+__global__ void __launch_bounds__(LN_THREADS) chunk_ln_kernel(const ChunkParams p) {
+  __shared__ float red[LN_THREADS / 32];
+  __shared__ ChunkStats st_sh;
+  const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  __nv_bfloat16* dzrow = p.dz + ((size_t)b * CT + c) * p.d;
+  if (c >= p.Cc) {  // padded token row: zero gradient
+    for (int i = tid; i < p.d; i += LN_THREADS) dzrow[i] = __float2bfloat16(0.f);
+    return;
+  }
+  if (tid < 32) {
+    ChunkStats s = chunk_stats(p, b);
+    if (tid == 0) st_sh = s;
+  }
+  if (c == 0 && tid == 0) p.norm2[b] = 0.f;
+  const size_t tok = (size_t)b * p.T + p.tok0 + c;
+  float* zrow = p.zacc + ((size_t)b * CT + c) * p.d;
+  const __nv_bfloat16* krow = p.k + tok * p.d;
+  const __nv_bfloat16* vrow = p.v + tok * p.d;
+  const int nv = p.d / LN_THREADS;  // d % 256 == 0 is not required: handle tail below
+  float z[LN_MAXV];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    z[j] = 0.f;
+    if (i < p.d) {
+      z[j] = zrow[i];
+      zrow[i] = 0.f;
+      sum += z[j];
+    }
+  }
+  (void)nv;
+  const float dinv = 1.f / (float)p.d;
+  const float mean = block_sum(sum, red) * dinv;
+  float sq = 0.f;
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    if (i < p.d) {
+      const float df = z[j] - mean;
+      sq += df * df;
+    }
+  }
+  const float var = block_sum(sq, red) * dinv;
+  const float rstd = rsqrtf(var + p.eps);
+  float err2 = 0.f;
+  float e[LN_MAXV], zh[LN_MAXV];
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    e[j] = 0.f;
+    zh[j] = 0.f;
+    if (i < p.d) {
+      zh[j] = (z[j] - mean) * rstd;
+      const float vhat = __bfloat162float(krow[i]) + (zh[j] * p.ln_w[i] + p.ln_b[i]);
+      e[j] = vhat - __bfloat162float(vrow[i]);
+      err2 += e[j] * e[j];
+      if (p.out) {
+        if (p.out_bf16)
+          reinterpret_cast<__nv_bfloat16*>(p.out)[tok * p.d + i] = __float2bfloat16(vhat);
+        else
+          reinterpret_cast<float*>(p.out)[tok * p.d + i] = vhat;
+      }
+    }
+  }
+  const float loss = 0.5f * block_sum(err2, red) * p.inv_scale;
+  const ChunkStats st = st_sh;
+  const float m = p.mask ? p.mask[tok] : 1.f;
+  if (tid == 0 && p.token_loss) p.token_loss[tok] = loss;
+  const float wf = p.mask ? p.eta[tok] * m / fmaxf(st.count, 1.f) : p.eta[tok] / (float)p.Cc;
+  const float coef = wf * p.inv_scale;
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    if (i < p.d) {
+      const float dzh = coef * e[j] * p.ln_w[i];
+      e[j] = dzh;
+      s1 += dzh;
+      s2 += dzh * zh[j];
+    }
+  }
+  const float mdz = block_sum(s1, red) * dinv;
+  const float mdzz = block_sum(s2, red) * dinv;
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    if (i < p.d) dzrow[i] = __float2bfloat16(rstd * (e[j] - mdz - zh[j] * mdzz));
+  }
+}
+
+// ============================================================================
+// bwd: dH, dU, dG and the three weight gradients; NORM pass accumulates
+// ||grad||^2, UPDATE pass applies momentum / decay / clip in place.
+// ============================================================================
+__global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                const __grid_constant__ CUtensorMap tmDZ,
+                                                                const ChunkParams p, int update) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3[2], empty3[2], dh_done, ops_ready, gfull, gfree;
+  __shared__ uint32_t tmem_slot;
+  __shared__ ChunkStats st_sh;
+  uint8_t* slots = align1024(smem_raw);             // ring 1: NSLOT x 24 KB (W_down rows + dZ tile)
+  uint8_t* slots3 = slots + NSLOT * BWD_SLOT;       // ring 3: 2 x 32 KB (K slice + dZ slice)
+  uint8_t* sDU = slots3 + 2 * 32768;                // K-major [hh 128][64 tokens]
+  uint8_t* sDG = sDU + 16384;
+  uint8_t* sHt = sDG + 16384;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int h0 = t * HT;
+  const int nkb = p.d / 64;
+  const int nch = p.d / 128;
+
+  if (tid == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&full[i], NPROD + 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full3[i], 1);
+      mbar_init(&empty3[i], 1);
+    }
+    mbar_init(&dh_done, 1);
+    mbar_init(&ops_ready, NPROD);
+    mbar_init(&gfull, 1);
+    mbar_init(&gfree, NPROD);
+    fence_mbarrier_init();
+  }
+  if (warp == 0) {
+    ChunkStats s = chunk_stats(p, b);
+    if (lane == 0) st_sh = s;
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t tDH = tmem, tGU = tmem + 128, tGG = tmem + 256, tGD = tmem + 384;
+  const ChunkStats st = st_sh;
+  // A state with no valid token keeps W and S exactly (model/uttt_layer.py:513-520).
+  const bool skip = !st.active;
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ W_down rows -> A (K-major)
+    const float* wd = p.w_down + (size_t)b * p.h * p.d;
+    int it = 0;
+    for (int kb = 0; kb < nkb; ++kb, ++it) {
+      const int s = it % NSLOT;
+      mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+      uint8_t* sA = slots + s * BWD_SLOT;
+      float4 f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int idx = tid + j * NPROD;  // 0..2047 : 128 rows x 16 float4
+        const int hh = idx >> 4, c4 = (idx & 15) * 4;
+        f[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!skip && h0 + hh < p.h)
+          f[j] = __ldg(reinterpret_cast<const float4*>(wd + (size_t)(h0 + hh) * p.d + kb * 64 + c4));
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int idx = tid + j * NPROD;
+        const int hh = idx >> 4, c4 = (idx & 15) * 4;
+        uint2 pk;
+        pk.x = pack_bf16x2(f[j].x, f[j].y);
+        pk.y = pack_bf16x2(f[j].z, f[j].w);
+        *reinterpret_cast<uint2*>(sA + sw128_offset(hh, c4 * 2)) = pk;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&full[s]);
+    }
+
+    // ------------------------------------------------------------ epilogue 1: dU, dG, H
+    mbar_wait(&dh_done, 0, p.status);
+    tc_fence_after();
+    const int q = warp & 3, half = warp >> 2;
+    {
+      const int row = q * 32 + lane, c0 = half * 32;
+      float dh[32];
+      tmem_ld16(tmem_addr(tDH, q * 32, c0), *reinterpret_cast<float(*)[16]>(&dh[0]));
+      tmem_ld16(tmem_addr(tDH, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&dh[16]));
+      tmem_wait_ld();
+      const float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
+      const float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        float du[8], dg[8], hv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = c0 + i + e;
+          const float u = us[(size_t)c * p.hp];
+          const float g = gs[(size_t)c * p.hp];
+          const float sg = sigmoidf_(g);
+          const float a = g * sg;
+          const bool valid = c < p.Cc;
+          hv[e] = valid ? a * u : 0.f;
+          du[e] = valid ? dh[i + e] * a : 0.f;
+          dg[e] = valid ? dh[i + e] * u * (sg * (1.f + g * (1.f - sg))) : 0.f;
+        }
+        uint4 a4, b4, c4;
+        a4.x = pack_bf16x2(du[0], du[1]); a4.y = pack_bf16x2(du[2], du[3]);
+        a4.z = pack_bf16x2(du[4], du[5]); a4.w = pack_bf16x2(du[6], du[7]);
+        b4.x = pack_bf16x2(dg[0], dg[1]); b4.y = pack_bf16x2(dg[2], dg[3]);
+        b4.z = pack_bf16x2(dg[4], dg[5]); b4.w = pack_bf16x2(dg[6], dg[7]);
+        c4.x = pack_bf16x2(hv[0], hv[1]); c4.y = pack_bf16x2(hv[2], hv[3]);
+        c4.z = pack_bf16x2(hv[4], hv[5]); c4.w = pack_bf16x2(hv[6], hv[7]);
+        const uint32_t o = sw128_offset(row, (c0 + i) * 2);
+        *reinterpret_cast<uint4*>(sDU + o) = a4;
+        *reinterpret_cast<uint4*>(sDG + o) = b4;
+        *reinterpret_cast<uint4*>(sHt + o) = c4;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&ops_ready);
+    }
+
+    // ------------------------------------------------------------ epilogue 2: gradients
+    float scale = 1.f;
+    if (update && p.clip > 0.f) scale = fminf(1.f, p.clip * rsqrtf(p.norm2[b] + 1e-8f));
+    if (update && p.clip_out && t == 0 && tid == 0) p.clip_out[(size_t)b * p.n_chunks + p.chunk_index] = scale;
+    const float decay = 1.f - st.alpha_bar;
+    const float beta = p.beta;
+    const size_t wbase_ug = (size_t)b * p.d * p.h;
+    const size_t wbase_d = (size_t)b * p.h * p.d;
+    float acc = 0.f;
+    const int row = q * 32 + lane;
+    for (int j = 0; j < nch; ++j) {
+      mbar_wait(&gfull, j & 1, p.status);
+      tc_fence_after();
+      const int cbase = half * 64;
+#pragma unroll 1
+      for (int cc = 0; cc < 64; cc += 16) {
+        float gu[16], gg[16], gd[16];
+        tmem_ld16(tmem_addr(tGU, q * 32, cbase + cc), gu);
+        tmem_ld16(tmem_addr(tGG, q * 32, cbase + cc), gg);
+        tmem_ld16(tmem_addr(tGD, q * 32, cbase + cc), gd);
+        tmem_wait_ld();
+        if (skip) continue;
+        if (!update) {
+          if (h0 + row < p.h) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (h0 + cbase + cc + e < p.h) acc += gd[e] * gd[e];
+          continue;
+        }
+        // gradW_up^T / gradW_gate^T: (hidden row, d column) -> W[dd][h0 + row]
+        if (h0 + row < p.h) {
+          float wu[16], wg[16], su[16], sg2[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const size_t o = wbase_ug + (size_t)(j * 128 + cbase + cc + e) * p.h + h0 + row;
+            wu[e] = p.w_up[o];
+            wg[e] = p.w_gate[o];
+            su[e] = beta != 0.f ? p.s_up[o] : 0.f;
+            sg2[e] = beta != 0.f ? p.s_gate[o] : 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const size_t o = wbase_ug + (size_t)(j * 128 + cbase + cc + e) * p.h + h0 + row;
+            const float nsu = beta * su[e] - gu[e] * scale;
+            const float nsg = beta * sg2[e] - gg[e] * scale;
+            p.s_up_out[o] = nsu;
+            p.s_gate_out[o] = nsg;
+            p.w_up_out[o] = decay * wu[e] + nsu;
+            p.w_gate_out[o] = decay * wg[e] + nsg;
+          }
+        }
+        // gradW_down^T: (d row, hidden column) -> W_down[h0 + col][dd]
+        {
+          float wdv[16], sdv[16];
+          const int dd = j * 128 + row;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int hh = h0 + cbase + cc + e;
+            const size_t o = wbase_d + (size_t)hh * p.d + dd;
+            wdv[e] = 0.f;
+            sdv[e] = 0.f;
+            if (hh < p.h) {
+              wdv[e] = p.w_down[o];
+              sdv[e] = beta != 0.f ? p.s_down[o] : 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int hh = h0 + cbase + cc + e;
+            if (hh < p.h) {
+              const size_t o = wbase_d + (size_t)hh * p.d + dd;
+              const float ns = beta * sdv[e] - gd[e] * scale;
+              p.s_down_out[o] = ns;
+              p.w_down_out[o] = decay * wdv[e] + ns;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&gfree);
+    }
+    if (!update) {
+      acc = warp_sum(acc);
+      if (lane == 0 && !skip) atomicAdd(p.norm2 + b, acc);
+    }
+  } else if (warp == TMA_WARP) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmDZ);
+      int it = 0;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % NSLOT;
+        mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+        mbar_arrive_expect_tx(&full[s], 8192);
+        tma_load_2d(slots + s * BWD_SLOT + 16384, &tmDZ, &full[s], kb * 64, b * CT);
+      }
+      for (int j = 0; j < nch; ++j) {
+        const int s = j & 1;
+        mbar_wait(&empty3[s], ((j >> 1) & 1) ^ 1, p.status);
+        mbar_arrive_expect_tx(&full3[s], 32768);
+        uint8_t* base = slots3 + s * 32768;
+        // K slice (MN-major B for gradW_up/gate): rows = tokens, 64 d each
+        tma_load_3d(base, &tmK, &full3[s], j * 128, p.tok0, b);
+        tma_load_3d(base + 8192, &tmK, &full3[s], j * 128 + 64, p.tok0, b);
+        // dZ slice (MN-major A for gradW_down^T)
+        tma_load_2d(base + 16384, &tmDZ, &full3[s], j * 128, b * CT);
+        tma_load_2d(base + 24576, &tmDZ, &full3[s], j * 128 + 64, b * CT);
+      }
+    }
+  } else {  // MMA warp
+    if (lane == 0) {
+      const uint32_t id_dh = idesc_bf16(128, 64, false, false);
+      int it = 0;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % NSLOT;
+        mbar_wait(&full[s], (it / NSLOT) & 1, p.status);
+        tc_fence_after();
+        const uint32_t a = smem_u32(slots + s * BWD_SLOT), bz = a + 16384;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_bf16(tDH, sdesc_sw128(a + ks * 32, 16, 1024), sdesc_sw128(bz + ks * 32, 16, 1024), id_dh,
+                   (kb > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(&dh_done);
+      mbar_wait(&ops_ready, 0, p.status);
+      tc_fence_after();
+      const uint32_t id_uw = idesc_bf16(128, 128, false, true);   // A = dU^T K-major, B = K MN-major
+      const uint32_t id_dw = idesc_bf16(128, 128, true, false);   // A = dZ^T MN-major, B = H K-major
+      const uint32_t du = smem_u32(sDU), dg = smem_u32(sDG), ht = smem_u32(sHt);
+      for (int j = 0; j < nch; ++j) {
+        const int s = j & 1;
+        mbar_wait(&full3[s], (j >> 1) & 1, p.status);
+        mbar_wait(&gfree, (j & 1) ^ 1, p.status);
+        tc_fence_after();
+        const uint32_t kk = smem_u32(slots3 + s * 32768), zz = kk + 16384;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t acc = ks > 0 ? 1u : 0u;
+          const uint64_t kd = sdesc_sw128(kk + ks * 2048, 8192, 1024);
+          mma_bf16(tGU, sdesc_sw128(du + ks * 32, 16, 1024), kd, id_uw, acc);
+          mma_bf16(tGG, sdesc_sw128(dg + ks * 32, 16, 1024), kd, id_uw, acc);
+          mma_bf16(tGD, sdesc_sw128(zz + ks * 2048, 8192, 1024), sdesc_sw128(ht + ks * 32, 16, 1024), id_dw, acc);
+        }
+        mma_commit(&empty3[s]);
+        mma_commit(&gfull);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+size_t fwd_smem() { return 1024 + NSLOT * SLOT_BYTES + 16384; }
+size_t bwd_smem() { return 1024 + NSLOT * BWD_SLOT + 2 * 32768 + 3 * 16384; }
+
+}  // namespace
+}  // namespace uttt
+
+using namespace uttt;
+
+extern "C" size_t uttt_chunk_write_workspace(int B, int C, int d, int h) {
+  if (B <= 0 || d <= 0 || h <= 0) return 0;
+  (void)C;
+  const size_t hp = ((size_t)h + 127) / 128 * 128;
+  size_t bytes = 256;
+  bytes += ws_round((size_t)B * CT * d * sizeof(float));      // zacc
+  bytes += 2 * ws_round((size_t)B * CT * hp * sizeof(float));  // u_save, g_save
+  bytes += ws_round((size_t)B * CT * d * 2);                   // dz
+  bytes += ws_round((size_t)B * sizeof(float));                 // norm2
+  return bytes;
+}
+
+extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q,
+                                const void* k, const void* v, const float* eta, const float* alpha,
+                                const float* mask, float* w_up, float* w_gate, float* w_down, float* s_up,
+                                float* s_gate, float* s_down, const float* ln_weight, const float* ln_bias,
+                                float momentum_beta, float max_grad_norm, int normalize_by_dim, float eps,
+                                void* out, int out_dtype, float* token_loss, float* clip_scale, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  UTTT_REQUIRE(B > 0 && T > 0 && C > 0 && d > 0 && h > 0 && n_chunks >= 0 && chunk_begin >= 0, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(k && v && eta && alpha && w_up && w_gate && w_down && s_up && s_gate && s_down && ln_weight &&
+                   ln_bias && workspace,
+               UTTT_ERR_INVALID);
+  UTTT_REQUIRE(C <= CT, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(d % 128 == 0 && d <= 4096, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(h % 8 == 0, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE((long long)(chunk_begin + n_chunks - 1) * C < T || n_chunks == 0, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(out == nullptr || q == k, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(out_dtype == UTTT_DTYPE_F32 || out_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(eps > 0.f && momentum_beta == momentum_beta && max_grad_norm >= 0.f, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(workspace_bytes >= uttt_chunk_write_workspace(B, C, d, h), UTTT_ERR_WORKSPACE);
+  if (n_chunks == 0) return UTTT_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+
+  WsCursor ws(workspace, workspace_bytes);
+  const int hp = (h + 127) / 128 * 128;
+  ChunkParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = B; p.T = T; p.C = C; p.d = d; p.h = h; p.hp = hp;
+  p.w_up = w_up; p.w_gate = w_gate; p.w_down = w_down;
+  p.w_up_out = w_up; p.w_gate_out = w_gate; p.w_down_out = w_down;
+  p.s_up = s_up; p.s_gate = s_gate; p.s_down = s_down;
+  p.s_up_out = s_up; p.s_gate_out = s_gate; p.s_down_out = s_down;
+  p.eta = eta; p.alpha = alpha; p.mask = mask; p.ln_w = ln_weight; p.ln_b = ln_bias;
+  p.k = (const __nv_bfloat16*)k; p.v = (const __nv_bfloat16*)v;
+  p.zacc = ws.take<float>((size_t)B * CT * d);
+  p.u_save = ws.take<float>((size_t)B * CT * hp);
+  p.g_save = ws.take<float>((size_t)B * CT * hp);
+  p.dz = ws.take<__nv_bfloat16>((size_t)B * CT * d);
+  p.norm2 = ws.take<float>(B);
+  p.token_loss = token_loss; p.out = out; p.out_bf16 = out_dtype == UTTT_DTYPE_BF16;
+  p.clip_out = clip_scale;
+  p.n_chunks = n_chunks;
+  p.beta = momentum_beta; p.clip = max_grad_norm; p.eps = eps;
+  p.inv_scale = normalize_by_dim ? 1.f / (float)d : 1.f;
+  p.status = ws_status(workspace);
+  if (!ws.ok()) return UTTT_ERR_WORKSPACE;
+
+  CUtensorMap tmK, tmDZ;
+  {
+    uint64_t dims[3] = {(uint64_t)d, (uint64_t)T, (uint64_t)B};
+    uint64_t str[2] = {(uint64_t)d * 2, (uint64_t)T * d * 2};
+    uint32_t box[3] = {64, 64, 1};
+    UTTT_TRY(make_tmap_bf16(&tmK, k, 3, dims, str, box));
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)d, (uint64_t)B * CT};
+    uint64_t str[1] = {(uint64_t)d * 2};
+    uint32_t box[2] = {64, 64};
+    UTTT_TRY(make_tmap_bf16(&tmDZ, p.dz, 2, dims, str, box));
+  }
+  static bool attr_done = false;
+  if (!attr_done) {
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)fwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)bwd_smem())));
+    attr_done = true;
+  }
+  UTTT_TRY(cuda_status(cudaMemsetAsync(p.zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
+  const dim3 grid((h + HT - 1) / HT, B);
+  for (int ci = 0; ci < n_chunks; ++ci) {
+    p.tok0 = (chunk_begin + ci) * C;
+    p.Cc = (T - p.tok0) < C ? (T - p.tok0) : C;
+    p.chunk_index = ci;
+    chunk_fwd_kernel<<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
+    UTTT_TRY(launch_status());
+    chunk_ln_kernel<<<dim3(CT, B), LN_THREADS, 0, st>>>(p);
+    UTTT_TRY(launch_status());
+    if (max_grad_norm > 0.f) {
+      chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
+      UTTT_TRY(launch_status());
+    }
+    chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+    UTTT_TRY(launch_status());
+  }
+  return UTTT_OK;
+}

@@ -1,0 +1,63 @@
+// Host-side helpers shared by the launchers: CUDA error capture, tensor-map
+// encoding (through the runtime's driver entry point, so the library does not
+// link libcuda), and workspace layout.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/uttt_b200.h"
+
+namespace uttt {
+
+int& last_cuda_error_ref();
+
+inline int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return UTTT_OK;
+  last_cuda_error_ref() = (int)e;
+  return UTTT_ERR_CUDA;
+}
+
+// Check the launch that was just issued.
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
+
+#define UTTT_TRY(expr)              \
+  do {                              \
+    int _s = (expr);                \
+    if (_s != UTTT_OK) return _s;   \
+  } while (0)
+
+#define UTTT_REQUIRE(cond, code) \
+  do {                           \
+    if (!(cond)) return (code);  \
+  } while (0)
+
+// 2-D / 3-D BF16 tensor maps with 128-byte swizzle; out-of-bounds boxes are
+// zero-filled.  `dims` / `strides_bytes` are innermost first.
+int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box);
+
+// Workspace: [status int (256 B slot)] [region 0] [region 1] ... each 256-B aligned.
+struct WsCursor {
+  uint8_t* base;
+  size_t used;
+  size_t cap;
+  explicit WsCursor(void* b, size_t c) : base((uint8_t*)b), used(256), cap(c) {}
+  template <class T>
+  T* take(size_t count) {
+    size_t bytes = (count * sizeof(T) + 255) & ~(size_t)255;
+    T* p = (T*)(base + used);
+    used += bytes;
+    return p;
+  }
+  bool ok() const { return used <= cap; }
+};
+
+inline size_t ws_round(size_t bytes) { return (bytes + 255) & ~(size_t)255; }
+
+inline int* ws_status(void* ws) { return (int*)ws; }
+
+}  // namespace uttt
