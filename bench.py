@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark of the uTTT serving hot path on B200 (one JSON line on rank 0).
+
+Workload (the isolated chunk-TTT write): 64 independent
+FP32 fast-weight states per GPU, d=1024, h=2816; per state T=2048 tokens in
+32 sequential chunks of C=64; keys/values BF16 ~N(0,1) L2-normalised per
+token; MSE (normalize_by_dim) surprise loss; fixed inner lr 1e-2; no decay,
+momentum or clipping.  A step is one full pass: all 32 chunks of all states.
+Synthetic seeded data stands in for real conversations (the reference
+publishes no dataset for this path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank runs its own 64 states (personas partition by user
+id; no data-path collective) -> weak scaling; the timed region is bracketed
+by a barrier + synchronize on every rank and the max over ranks is used.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "chunk-TTT update tok/s (packed multi-persona decode + chunk-TTT update path, BASELINE config 2)"
+UNIT = "tok/s"
+
+CFG = dict(states=64, d=1024, h=2816, tokens=2048, chunk=64, inner_lr=1e-2, momentum=0.0, clip=0.0,
+           init_std=0.02, eps=1e-5)
+
+
+# ----------------------------------------------------------------------------- helpers
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def traffic_record():
+    path = os.path.join(ROOT, "profiles", "chunk_write_config2_traffic.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            return json.load(fh)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------------------------- workload
+def make_states(device, seed):
+    from utttcompanion_b200 import fastweight as fw  # noqa: F401  (loads the library)
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, d, h, T = CFG["states"], CFG["d"], CFG["h"], CFG["tokens"]
+
+    def unit_rows(shape):
+        x = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+        return (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+    st = {
+        "k": unit_rows((B, T, d)),
+        "v": unit_rows((B, T, d)),
+        "eta": torch.full((B, T), CFG["inner_lr"], device=device),
+        "alpha": torch.zeros((B, T), device=device),
+        "w_up": torch.randn((B, d, h), generator=g, device=device) * CFG["init_std"],
+        "w_gate": torch.randn((B, d, h), generator=g, device=device) * CFG["init_std"],
+        "w_down": torch.randn((B, h, d), generator=g, device=device) * CFG["init_std"],
+        "ln_w": torch.ones(d, device=device),
+        "ln_b": torch.zeros(d, device=device),
+        "loss": torch.empty((B, T), device=device),
+    }
+    for n in ("up", "gate", "down"):
+        st["s_" + n] = torch.zeros_like(st["w_" + n])
+    return st
+
+
+def run_step(st):
+    from utttcompanion_b200 import fastweight as fw
+    fw.chunk_write(st["k"], st["v"], st["eta"], st["alpha"], st["w_up"], st["w_gate"], st["w_down"],
+                   st["s_up"], st["s_gate"], st["s_down"], st["ln_w"], st["ln_b"], None, CFG["momentum"],
+                   CFG["clip"], True, CFG["eps"], chunk_size=CFG["chunk"], token_loss=st["loss"])
+
+
+def launches_per_step():
+    n_chunks = CFG["tokens"] // CFG["chunk"]
+    return n_chunks * (3 + (1 if CFG["clip"] > 0 else 0))
+
+
+def algorithmic_bytes(kind: int) -> float:
+    """Minimal HBM bytes one launch of a chunk kernel must move (all states)."""
+    B, d, h = CFG["states"], CFG["d"], CFG["h"]
+    w = 3.0 * d * h * 4.0                       # FP32 W_up + W_gate + W_down of one state
+    if kind == 3:   # bwd+update: read W (+S if momentum), write W and S
+        return B * (w * (3.0 + (1.0 if CFG["momentum"] else 0.0)))
+    if kind == 0:   # fwd: read W once
+        return B * w
+    return 0.0
+
+
+def cpu_baseline(max_seconds=20.0):
+    """The oracle port (numpy FP32, all host threads) on a bounded sample: chunk
+    steps of single config-2 states until ~max_seconds of CPU work."""
+    from oracle import fastweight as ofw
+    from oracle.numerics import Precision
+    rng = np.random.default_rng(0)
+    d, h, C = CFG["d"], CFG["h"], CFG["chunk"]
+    W = [rng.normal(0, CFG["init_std"], s).astype(np.float32) for s in ((1, d, h), (1, d, h), (1, h, d))]
+    S = [np.zeros_like(w) for w in W]
+    lnw, lnb = np.ones(d, np.float32), np.zeros(d, np.float32)
+    prec = Precision("f32")
+    n, t0 = 0, time.perf_counter()
+    while True:
+        k = rng.standard_normal((1, C, d)).astype(np.float32)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+        v = rng.standard_normal((1, C, d)).astype(np.float32)
+        v /= np.linalg.norm(v, axis=-1, keepdims=True)
+        eta = np.full((1, C, 1), CFG["inner_lr"], np.float32)
+        r = ofw.fused_chunk_ttt_step(k, k, v, eta, np.zeros_like(eta), *W, *S, lnw, lnb, None, CFG["momentum"],
+                                     CFG["clip"], True, CFG["eps"], prec=prec)
+        W, S = [r.w_up, r.w_gate, r.w_down], [r.s_up, r.s_gate, r.s_down]
+        n += 1
+        el = time.perf_counter() - t0
+        if el > max_seconds or n >= 400:
+            break
+    return n * C / el, n, el
+
+
+def host_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([int(x.get("num_threads", 1)) for x in threadpool_info()] + [1])
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------- arms
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    # each step: one chunk of one state through the oracle port (numpy FP32)
+    from oracle import fastweight as ofw
+    from oracle.numerics import Precision
+    rng = np.random.default_rng(1)
+    d, h, C = CFG["d"], CFG["h"], CFG["chunk"]
+    W = [rng.normal(0, CFG["init_std"], s).astype(np.float32) for s in ((1, d, h), (1, d, h), (1, h, d))]
+    S = [np.zeros_like(w) for w in W]
+    lnw, lnb = np.ones(d, np.float32), np.zeros(d, np.float32)
+    prec = Precision("f32")
+
+    def step():
+        nonlocal W, S
+        k = rng.standard_normal((1, C, d)).astype(np.float32)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+        v = rng.standard_normal((1, C, d)).astype(np.float32)
+        v /= np.linalg.norm(v, axis=-1, keepdims=True)
+        eta = np.full((1, C, 1), CFG["inner_lr"], np.float32)
+        r = ofw.fused_chunk_ttt_step(k, k, v, eta, np.zeros_like(eta), *W, *S, lnw, lnb, None, CFG["momentum"],
+                                     CFG["clip"], True, CFG["eps"], prec=prec)
+        W, S = [r.w_up, r.w_gate, r.w_down], [r.s_up, r.s_gate, r.s_down]
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = args.steps * C / el
+    cores = host_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "chunk_ttt_write_isolated (BASELINE config 2)", **CFG,
+                   "reference_sample": "one 64-token chunk of one state per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} chunk steps of one d=1024,h=2816 state (64 tokens each), "
+                                   "numpy FP32 restatement of fused_chunk_ttt_step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def ours_arm(args, world, rank, local):
+    from utttcompanion_b200 import _lib
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    lib = _lib.load()
+    st = make_states(device, seed=1234 + rank)
+    B, T = CFG["states"], CFG["tokens"]
+
+    for _ in range(args.warmup):
+        run_step(st)
+    torch.cuda.synchronize()
+
+    # live per-kernel timing on the launch stream (one extra, untimed step)
+    lib.uttt_profile_enable(1)
+    run_step(st)
+    ms = (np.zeros(16, np.float32))
+    cnt = np.zeros(16, np.int32)
+    _lib.check(lib.uttt_profile_read(ms.ctypes.data, cnt.ctypes.data), "profile_read")
+    lib.uttt_profile_enable(0)
+
+    # timed region
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run_step(st)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    value = world * B * T / (step_ms / 1e3)
+
+    # end-to-end through the public API: pinned host K/V/eta/alpha in, token losses out, every step
+    hk = torch.empty_like(st["k"], device="cpu").pin_memory()
+    hv = torch.empty_like(st["v"], device="cpu").pin_memory()
+    he = torch.empty_like(st["eta"], device="cpu").pin_memory()
+    ha = torch.empty_like(st["alpha"], device="cpu").pin_memory()
+    hl = torch.empty_like(st["loss"], device="cpu").pin_memory()
+    hk.copy_(st["k"])
+    hv.copy_(st["v"])
+    he.copy_(st["eta"])
+    ha.copy_(st["alpha"])
+    e2e_steps = max(1, min(args.steps, 5))
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        st["k"].copy_(hk, non_blocking=True)
+        st["v"].copy_(hv, non_blocking=True)
+        st["eta"].copy_(he, non_blocking=True)
+        st["alpha"].copy_(ha, non_blocking=True)
+        run_step(st)
+        hl.copy_(st["loss"], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    h2d = sum(t.numel() * t.element_size() for t in (hk, hv, he, ha))
+    d2h = hl.numel() * hl.element_size()
+    from utttcompanion_b200 import fastweight as fw
+    fw.check_status(fw.workspace(0, device), "bench")
+
+    if rank == 0:
+        hbm, tflops, src = peaks()
+        kinds = {0: "chunk_fwd", 1: "chunk_ln", 2: "chunk_norm", 3: "chunk_bwd_update"}
+        per_kind = {kinds[k]: {"ms_total": float(ms[k]), "launches": int(cnt[k])} for k in kinds if cnt[k]}
+        dom = max(kinds, key=lambda k: ms[k])
+        avg_s = ms[dom] / max(cnt[dom], 1) / 1e3
+        alg = algorithmic_bytes(dom)
+        achieved = alg / avg_s / 1e9
+        traffic = None
+        rec = traffic_record()
+        if rec and rec.get("kernel") == kinds[dom]:
+            traffic = rec.get("bytes_per_launch")
+        total_flops = 14.0 * CFG["chunk"] * CFG["d"] * CFG["h"] * (T // CFG["chunk"]) * B
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "chunk_ttt_write_isolated (BASELINE config 2)", **CFG,
+                       "parallelism": f"states partitioned over {world} GPU(s), no collective",
+                       "l2": "inputs larger than L2 (2.2 GB FP32 state per GPU)"},
+            "e2e": {"value": world * B * T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches_per_step() * args.steps,
+            "roofline": {"bound": "hbm", "kernel": kinds[dom], "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_source": src, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": alg},
+            "tensor_tflops": total_flops / (step_ms / 1e3) / 1e12,
+            "kernels": per_kind,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, n, el = cpu_baseline()
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
+                                    "sample": f"{n} chunk steps of one config-2 state ({n * CFG['chunk']} tokens, "
+                                              f"{el:.1f} s), numpy FP32 restatement of fused_chunk_ttt_step"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")
+    ap.add_argument("--tokens", type=int, default=None, help="override tokens per state (profiling cases)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.states:
+        CFG["states"] = args.states
+    if args.tokens:
+        CFG["tokens"] = args.tokens
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return reference_arm(args, world, rank)
+    return ours_arm(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -44,6 +44,23 @@ int uttt_last_cuda_error(void);
  * workspace.  Synchronises `stream`. */
 int uttt_read_status(void* workspace, int reset, void* stream);
 
+/* ---- live kernel timing ------------------------------------------------- */
+/* When enabled, every launcher brackets its kernels with CUDA events on the
+ * launch stream, per kernel kind.  uttt_profile_read synchronises, writes the
+ * total milliseconds and launch count of each kind (arrays of length
+ * UTTT_PROF_KINDS) and resets the counters.  No counterpart in the reference
+ * (which times with torch.cuda.synchronize + perf_counter,
+ * deploy/benchmark_inference_speed.py:136-183). */
+#define UTTT_PROF_KINDS 16
+#define UTTT_PROF_CHUNK_FWD 0
+#define UTTT_PROF_CHUNK_LN 1
+#define UTTT_PROF_CHUNK_NORM 2
+#define UTTT_PROF_CHUNK_BWD 3
+#define UTTT_PROF_READOUT 4
+#define UTTT_PROF_READOUT_LN 5
+int uttt_profile_enable(int on);
+int uttt_profile_read(float* total_ms, int* launches);
+
 /* ---- diagnostics -------------------------------------------------------- */
 /* D(MxN, fp32) = A * B^T on the tensor cores, used by the self-tests that pin
  * the descriptor / swizzle / TMEM conventions.  mode bit0: A is given

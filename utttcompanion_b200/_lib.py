@@ -39,6 +39,8 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_status_string": (C.c_char_p, [i32]),
     "uttt_last_cuda_error": (i32, []),
     "uttt_read_status": (i32, [vp, i32, vp]),
+    "uttt_profile_enable": (i32, [i32]),
+    "uttt_profile_read": (i32, [vp, vp]),
     "uttt_selftest_gemm": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
     "uttt_chunk_write_workspace": (sz, [i32, i32, i32, i32]),
     "uttt_chunk_write": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,

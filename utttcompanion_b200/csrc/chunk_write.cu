@@ -827,15 +827,25 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     p.tok0 = (chunk_begin + ci) * C;
     p.Cc = (T - p.tok0) < C ? (T - p.tok0) : C;
     p.chunk_index = ci;
-    chunk_fwd_kernel<<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
+    {
+      ProfScope ps(UTTT_PROF_CHUNK_FWD, st);
+      chunk_fwd_kernel<<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
+    }
     UTTT_TRY(launch_status());
-    chunk_ln_kernel<<<dim3(CT, B), LN_THREADS, 0, st>>>(p);
+    {
+      ProfScope ps(UTTT_PROF_CHUNK_LN, st);
+      chunk_ln_kernel<<<dim3(CT, B), LN_THREADS, 0, st>>>(p);
+    }
     UTTT_TRY(launch_status());
     if (max_grad_norm > 0.f) {
+      ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
       chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
-      UTTT_TRY(launch_status());
     }
-    chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+    UTTT_TRY(launch_status());
+    {
+      ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
+      chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+    }
     UTTT_TRY(launch_status());
   }
   return UTTT_OK;

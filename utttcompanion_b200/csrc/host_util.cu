@@ -2,6 +2,10 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+#include <utility>
+#include <vector>
+
 #include "host_util.cuh"
 
 namespace uttt {
@@ -9,6 +13,25 @@ namespace uttt {
 int& last_cuda_error_ref() {
   static thread_local int e = 0;
   return e;
+}
+
+namespace {
+struct ProfState {
+  bool on = false;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> events;
+  std::mutex mu;
+};
+ProfState& prof() {
+  static ProfState s;
+  return s;
+}
+}  // namespace
+
+bool prof_on() { return prof().on; }
+
+void prof_record(int kind, cudaEvent_t start, cudaEvent_t stop) {
+  std::lock_guard<std::mutex> g(prof().mu);
+  prof().events.push_back({kind, {start, stop}});
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -67,6 +90,35 @@ const char* uttt_status_string(int status) {
 }
 
 int uttt_last_cuda_error(void) { return uttt::last_cuda_error_ref(); }
+
+int uttt_profile_enable(int on) {
+  uttt::prof().on = on != 0;
+  return UTTT_OK;
+}
+
+int uttt_profile_read(float* total_ms, int* launches) {
+  if (!total_ms || !launches) return UTTT_ERR_INVALID;
+  for (int i = 0; i < UTTT_PROF_KINDS; ++i) {
+    total_ms[i] = 0.f;
+    launches[i] = 0;
+  }
+  std::lock_guard<std::mutex> g(uttt::prof().mu);
+  int status = UTTT_OK;
+  for (auto& e : uttt::prof().events) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(e.second.second) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, e.second.first, e.second.second) != cudaSuccess)
+      status = UTTT_ERR_CUDA;
+    if (e.first >= 0 && e.first < UTTT_PROF_KINDS) {
+      total_ms[e.first] += ms;
+      launches[e.first] += 1;
+    }
+    cudaEventDestroy(e.second.first);
+    cudaEventDestroy(e.second.second);
+  }
+  uttt::prof().events.clear();
+  return status;
+}
 
 int uttt_read_status(void* workspace, int reset, void* stream) {
   if (!workspace) return UTTT_ERR_INVALID;

@@ -60,4 +60,29 @@ inline size_t ws_round(size_t bytes) { return (bytes + 255) & ~(size_t)255; }
 
 inline int* ws_status(void* ws) { return (int*)ws; }
 
+// Live per-kind kernel timing (see uttt_profile_enable).  Usage in a launcher:
+//   ProfScope ps(UTTT_PROF_CHUNK_FWD, stream);  kernel<<<...>>>(...);
+// The scope records a start event at construction and a stop event at
+// destruction, both on `stream`.
+bool prof_on();
+void prof_record(int kind, cudaEvent_t start, cudaEvent_t stop);
+struct ProfScope {
+  int kind;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(int k, cudaStream_t st) : kind(k), s(st) {
+    if (prof_on()) {
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+      cudaEventRecord(a, s);
+    }
+  }
+  ~ProfScope() {
+    if (a) {
+      cudaEventRecord(b, s);
+      prof_record(kind, a, b);
+    }
+  }
+};
+
 }  // namespace uttt
