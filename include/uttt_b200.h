@@ -101,6 +101,30 @@ int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_c
                      int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss,
                      float* clip_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- fast-weight readout ------------------------------------------------ */
+/*
+ * f_W(x) = x + LayerNorm(silu(x W_gate) * (x W_up) W_down) for B states of T
+ * tokens each.  Replaces swiglu_fast_forward / swiglu_packed_forward
+ * (model/uttt_layer.py:211-257) as called by
+ * SharedFastWeightPool.forward_readout (:670-695).
+ *
+ *   x            BF16 (B, T, d)
+ *   w_dtype      UTTT_DTYPE_F32: w_up, w_gate (S, d, h), w_down (S, h, d) FP32
+ *                masters;  UTTT_DTYPE_BF16: w_up = packed [W_up | W_gate]
+ *                (S, d, 2h) BF16 read copy (inference_read_weights, :648-668),
+ *                w_gate unused, w_down (S, h, d) BF16.
+ *   state_index  int32 (B): row b reads state state_index[b] (NULL: state b).
+ *   ln_*         FP32 (d,) LayerNorm affine, as the reference applies it.
+ *   out          (B, T, d) in out_dtype.
+ * T == 1 with BF16 copies runs the decode GEMV; otherwise 64-token tiles on
+ * the tensor cores.  Requires d % 128 == 0 (d % 256 for the decode GEMV),
+ * h % 8 == 0.
+ */
+size_t uttt_fast_readout_workspace(int B, int d, int h);
+int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up, const void* w_gate,
+                      const void* w_down, const int* state_index, const float* ln_weight, const float* ln_bias,
+                      float eps, void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -99,9 +99,9 @@ def chunk_case(ul, name, dtype, act_dtype, B, C, d, h, mask, beta, clip, q_is_k,
     np.savez_compressed(os.path.join(HERE, f"chunk_{name}.npz"), **arrays)
 
 
-def swiglu_case(ul, name, act_dtype, seed):
+def swiglu_case(ul, name, act_dtype, seed, T=5):
     g = torch.Generator().manual_seed(seed)
-    B, T, d, h = 2, 5, 32, 48
+    B, d, h = 3, 256, 160
     x = torch.randn(B, T, d, generator=g).to(act_dtype)
     w_up = torch.randn(B, d, h, generator=g) * d ** -0.5
     w_gate = torch.randn(B, d, h, generator=g) * d ** -0.5
@@ -261,6 +261,8 @@ def main():
     chunk_case(ul, "bf16_clipbite", f32, bf, 2, 64, 128, 160, None, 0.5, 0.02, False, False, 7)
     swiglu_case(ul, "f32", f32, 21)
     swiglu_case(ul, "bf16", bf, 22)
+    swiglu_case(ul, "bf16_t1", bf, 23, T=1)
+    swiglu_case(ul, "bf16_t70", bf, 24, T=70)
     elastic_case(ul)
     model_case(um, "f64", f64, False)
     model_case(um, "f32", f32, False)

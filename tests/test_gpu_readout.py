@@ -1,0 +1,63 @@
+"""GPU parity of the fast-weight readout (decode GEMV and tensor-core tiles)
+against the reference's fixtures and the oracle.  Tolerance: max |diff| <= 2e-2
+(BF16 activations; the north-star logits bound)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fastweight as ofw
+from oracle.numerics import Precision, round_bf16
+from utttcompanion_b200 import readout as ro
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLDEN, name + ".npz")))
+
+
+def T(x, dtype=torch.float32):
+    return torch.as_tensor(np.ascontiguousarray(x)).to(device="cuda", dtype=dtype)
+
+
+@pytest.mark.parametrize("name", ["swiglu_bf16", "swiglu_bf16_t1", "swiglu_bf16_t70"])
+@pytest.mark.parametrize("form", ["fp32_masters", "packed_bf16"])
+def test_readout_matches_reference_fixture(name, form):
+    g = load(name)
+    x = T(g["x"], torch.bfloat16)
+    if form == "packed_bf16":
+        packed = torch.cat((T(g["w_up"]).to(torch.bfloat16), T(g["w_gate"]).to(torch.bfloat16)), dim=-1)
+        y = ro.swiglu_packed_forward(x, packed, T(g["w_down"]).to(torch.bfloat16), T(g["ln_weight"]),
+                                     T(g["ln_bias"]), 1e-5)
+        ref = g["out_packed"]
+    else:
+        y = ro.swiglu_fast_forward(x, T(g["w_up"]), T(g["w_gate"]), T(g["w_down"]), T(g["ln_weight"]),
+                                   T(g["ln_bias"]), 1e-5)
+        ref = g["out"]
+    torch.cuda.synchronize()
+    assert y.dtype == torch.bfloat16 and y.shape == x.shape
+    err = np.max(np.abs(y.float().cpu().numpy() - ref))
+    assert err < 2e-2, err
+
+
+def test_decode_readout_gathers_personas_by_index():
+    rng = np.random.default_rng(3)
+    S, B, d, h = 5, 7, 512, 1376          # ragged hidden tile (1376 = 5*256 + 96)
+    w_up = rng.normal(0, d ** -0.5, (S, d, h)).astype(np.float32)
+    w_gate = rng.normal(0, d ** -0.5, (S, d, h)).astype(np.float32)
+    w_down = rng.normal(0, 0.1 * h ** -0.5, (S, h, d)).astype(np.float32)
+    lnw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    lnb = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    x = round_bf16(rng.standard_normal((B, 1, d)))
+    idx = np.array([4, 0, 0, 2, 3, 1, 4], np.int32)
+    packed, down = ro.inference_read_weights(T(w_up), T(w_gate), T(w_down))
+    y = ro.fast_readout(T(x, torch.bfloat16), packed, None, down, T(lnw), T(lnb), 1e-5,
+                        state_index=torch.as_tensor(idx), packed=True)
+    torch.cuda.synchronize()
+    ref = ofw.swiglu_fast_forward(x, w_up[idx], w_gate[idx], w_down[idx], lnw, lnb, 1e-5, Precision("bf16"))
+    assert np.max(np.abs(y.float().cpu().numpy() - ref)) < 2e-2

@@ -67,7 +67,7 @@ def test_chunk_grad_and_step_match_reference(name):
         np.testing.assert_array_equal(res.w_up[inactive], g["w_up"][inactive])
 
 
-@pytest.mark.parametrize("name", ["f32", "bf16"])
+@pytest.mark.parametrize("name", ["f32", "bf16", "bf16_t1", "bf16_t70"])
 def test_swiglu_readout_matches_reference(name):
     g = load("swiglu_" + name)
     prec = Precision("bf16" if bool(g["act_is_bf16"]) else "f32")

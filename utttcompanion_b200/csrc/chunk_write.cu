@@ -74,6 +74,39 @@ struct ChunkParams {
   int hp;             // hidden padded to 128
   float beta, clip, eps, inv_scale;
   int* status;
+  // weight source of the fwd kernel: element (state, k, j) of up/gate at
+  // src_up + state*ss_ug + k*ld_ug + j, of down (state, j, dd) at
+  // src_down + state*ss_d + j*d + dd.  state = state_index ? state_index[b] : b.
+  const void* src_up;
+  const void* src_gate;
+  const void* src_down;
+  long long ss_ug, ss_d;
+  int ld_ug;
+  const int* state_index;
+};
+
+template <typename WT>
+struct Quad;
+template <>
+struct Quad<float> {  // 4 FP32 masters -> 4 BF16 (8 bytes)
+  using V = float4;
+  static __device__ __forceinline__ V load(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+  static __device__ __forceinline__ V zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  static __device__ __forceinline__ uint2 pack(V v) {
+    uint2 r;
+    r.x = pack_bf16x2(v.x, v.y);
+    r.y = pack_bf16x2(v.z, v.w);
+    return r;
+  }
+};
+template <>
+struct Quad<__nv_bfloat16> {  // 4 BF16 read-copy values, stored as they are
+  using V = uint2;
+  static __device__ __forceinline__ V load(const __nv_bfloat16* p) {
+    return __ldg(reinterpret_cast<const uint2*>(p));
+  }
+  static __device__ __forceinline__ V zero() { return make_uint2(0u, 0u); }
+  static __device__ __forceinline__ uint2 pack(V v) { return v; }
 };
 
 // Per-state chunk statistics: number of valid tokens, masked mean of alpha,
@@ -111,8 +144,10 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* raw) {
 // ============================================================================
 // fwd: U, G, H and the partial Z of one 128-row hidden tile
 // ============================================================================
+template <typename WT>
 __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const ChunkParams p) {
+  using Q = Quad<WT>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[NSLOT], empty[NSLOT], ug_done, h_ready, zfull[2], zfree[2];
   __shared__ uint32_t tmem_slot;
@@ -145,29 +180,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
   const uint32_t tmem = tmem_slot;
   const uint32_t tU = tmem, tG = tmem + 64, tZ = tmem + 128;
 
+  const int state = p.state_index ? p.state_index[b] : b;
   if (warp < 8) {
     // ------------------------------------------------------------ producers
-    const float* wu = p.w_up + (size_t)b * p.d * p.h;
-    const float* wg = p.w_gate + (size_t)b * p.d * p.h;
+    const WT* wu = reinterpret_cast<const WT*>(p.src_up) + (size_t)state * p.ss_ug;
+    const WT* wg = reinterpret_cast<const WT*>(p.src_gate) + (size_t)state * p.ss_ug;
     int it = 0;
     for (int kb = 0; kb < nkb; ++kb, ++it) {
       const int s = it % NSLOT;
       mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
       uint8_t* sUp = slots + s * SLOT_BYTES;
       uint8_t* sGa = sUp + 16384;
-      // 64 rows (k) x 128 cols (hidden) per matrix; thread -> 8 float4 per matrix
-      float4 fu[8], fg[8];
+      // 64 rows (k) x 128 cols (hidden) per matrix; thread -> 8 quads per matrix
+      typename Q::V fu[8], fg[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int idx = tid + j * NPROD;  // 0..2047
         const int kr = idx >> 5, c4 = (idx & 31) * 4;
         const int col = h0 + c4;
-        const size_t off = (size_t)(kb * 64 + kr) * p.h + col;
+        const size_t off = (size_t)(kb * 64 + kr) * p.ld_ug + col;
         if (col < p.h) {
-          fu[j] = __ldg(reinterpret_cast<const float4*>(wu + off));
-          fg[j] = __ldg(reinterpret_cast<const float4*>(wg + off));
+          fu[j] = Q::load(wu + off);
+          fg[j] = Q::load(wg + off);
         } else {
-          fu[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          fu[j] = Q::zero();
           fg[j] = fu[j];
         }
       }
@@ -176,13 +212,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         const int idx = tid + j * NPROD;
         const int kr = idx >> 5, c4 = (idx & 31) * 4;
         const uint32_t o = (c4 >> 6) * 8192 + sw128_offset(kr, (c4 & 63) * 2);
-        uint2 pu, pg;
-        pu.x = pack_bf16x2(fu[j].x, fu[j].y);
-        pu.y = pack_bf16x2(fu[j].z, fu[j].w);
-        pg.x = pack_bf16x2(fg[j].x, fg[j].y);
-        pg.y = pack_bf16x2(fg[j].z, fg[j].w);
-        *reinterpret_cast<uint2*>(sUp + o) = pu;
-        *reinterpret_cast<uint2*>(sGa + o) = pg;
+        *reinterpret_cast<uint2*>(sUp + o) = Q::pack(fu[j]);
+        *reinterpret_cast<uint2*>(sGa + o) = Q::pack(fg[j]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&full[s]);
@@ -201,12 +232,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       tmem_ld16(tmem_addr(tG, q * 32, c0), *reinterpret_cast<float(*)[16]>(&g[0]));
       tmem_ld16(tmem_addr(tG, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&g[16]));
       tmem_wait_ld();
-      float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
-      float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+      if (p.u_save) {
+        float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
+        float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        us[(size_t)(c0 + i) * p.hp] = u[i];
-        gs[(size_t)(c0 + i) * p.hp] = g[i];
+        for (int i = 0; i < 32; ++i) {
+          us[(size_t)(c0 + i) * p.hp] = u[i];
+          gs[(size_t)(c0 + i) * p.hp] = g[i];
+        }
       }
       // H tile, MN-major: row = hidden, 64 token values per 128 B row
 #pragma unroll
@@ -230,7 +263,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
     }
 
     // ------------------------------------------------------------ W_down tiles + Z drain
-    const float* wd = p.w_down + (size_t)b * p.h * p.d;
+    const WT* wd = reinterpret_cast<const WT*>(p.src_down) + (size_t)state * p.ss_d;
     for (int mt = 0; mt < nmt; ++mt, ++it) {
       const int s = it % NSLOT;
       mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
@@ -240,12 +273,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       for (int j = 0; j < 16; ++j) {
         const int idx = tid + j * NPROD;  // 0..4095
         const int hh = idx >> 5, c4 = (idx & 31) * 4;
-        float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (h0 + hh < p.h) f = __ldg(reinterpret_cast<const float4*>(wd + (size_t)(h0 + hh) * p.d + mt * 128 + c4));
-        uint2 pk;
-        pk.x = pack_bf16x2(f.x, f.y);
-        pk.y = pack_bf16x2(f.z, f.w);
-        *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = pk;
+        typename Q::V f = Q::zero();
+        if (h0 + hh < p.h) f = Q::load(wd + (size_t)(h0 + hh) * p.d + mt * 128 + c4);
+        *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = Q::pack(f);
       }
       fence_proxy_async_smem();
       mbar_arrive(&full[s]);
@@ -448,6 +478,54 @@ __global__ void __launch_bounds__(LN_THREADS) chunk_ln_kernel(const ChunkParams 
   for (int j = 0; j < LN_MAXV; ++j) {
     const int i = tid + j * LN_THREADS;
     if (i < p.d) dzrow[i] = __float2bfloat16(rstd * (e[j] - mdz - zh[j] * mdzz));
+  }
+}
+
+// ============================================================================
+// readout epilogue: out = x + LN(z) * gamma + beta  (swiglu_fast_forward's
+// last line, model/uttt_layer.py:243-247).  Consumes and re-zeroes z.
+// ============================================================================
+__global__ void __launch_bounds__(LN_THREADS) readout_ln_kernel(const float* __restrict__ zbase, int zrows,
+                                                                const __nv_bfloat16* __restrict__ x, int T,
+                                                                int tok0, int Cc, int d, const float* ln_w,
+                                                                const float* ln_b, float eps, void* out,
+                                                                int out_bf16) {
+  __shared__ float red[LN_THREADS / 32];
+  const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  if (c >= Cc) return;
+  float* zrow = const_cast<float*>(zbase) + ((size_t)b * zrows + c) * d;
+  const size_t tok = (size_t)b * T + tok0 + c;
+  float z[LN_MAXV];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    z[j] = 0.f;
+    if (i < d) {
+      z[j] = zrow[i];
+      zrow[i] = 0.f;
+      sum += z[j];
+    }
+  }
+  const float dinv = 1.f / (float)d;
+  const float mean = block_sum(sum, red) * dinv;
+  float sq = 0.f;
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    if (i < d) sq += (z[j] - mean) * (z[j] - mean);
+  }
+  const float rstd = rsqrtf(block_sum(sq, red) * dinv + eps);
+#pragma unroll
+  for (int j = 0; j < LN_MAXV; ++j) {
+    const int i = tid + j * LN_THREADS;
+    if (i < d) {
+      const float y = __bfloat162float(x[tok * d + i]) + ((z[j] - mean) * rstd * ln_w[i] + ln_b[i]);
+      if (out_bf16)
+        reinterpret_cast<__nv_bfloat16*>(out)[tok * d + i] = __float2bfloat16(y);
+      else
+        reinterpret_cast<float*>(out)[tok * d + i] = y;
+    }
   }
 }
 
@@ -798,6 +876,9 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   p.beta = momentum_beta; p.clip = max_grad_norm; p.eps = eps;
   p.inv_scale = normalize_by_dim ? 1.f / (float)d : 1.f;
   p.status = ws_status(workspace);
+  p.src_up = w_up; p.src_gate = w_gate; p.src_down = w_down;
+  p.ss_ug = (long long)d * h; p.ss_d = (long long)h * d; p.ld_ug = h;
+  p.state_index = nullptr;
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
 
   CUtensorMap tmK, tmDZ;
@@ -815,8 +896,10 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   }
   static bool attr_done = false;
   if (!attr_done) {
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)fwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)bwd_smem())));
     attr_done = true;
@@ -829,7 +912,7 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     p.chunk_index = ci;
     {
       ProfScope ps(UTTT_PROF_CHUNK_FWD, st);
-      chunk_fwd_kernel<<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
+      chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
     }
     UTTT_TRY(launch_status());
     {
@@ -845,6 +928,107 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
       chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+    }
+    UTTT_TRY(launch_status());
+  }
+  return UTTT_OK;
+}
+
+// ============================================================================
+// fast-weight readout entry point
+// ============================================================================
+namespace uttt {
+int launch_readout_gemv(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
+                        const __nv_bfloat16* wd, const int* state_index, float* zacc, cudaStream_t st);
+}
+
+extern "C" size_t uttt_fast_readout_workspace(int B, int d, int h) {
+  if (B <= 0 || d <= 0 || h <= 0) return 0;
+  (void)h;
+  return 256 + ws_round((size_t)B * CT * d * sizeof(float));
+}
+
+extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up,
+                                 const void* w_gate, const void* w_down, const int* state_index,
+                                 const float* ln_weight, const float* ln_bias, float eps, void* out, int out_dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  UTTT_REQUIRE(B > 0 && T > 0 && d > 0 && h > 0, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(x && w_up && w_down && ln_weight && ln_bias && out && workspace, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(w_dtype == UTTT_DTYPE_F32 || w_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(w_dtype == UTTT_DTYPE_BF16 || w_gate, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(out_dtype == UTTT_DTYPE_F32 || out_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(eps > 0.f, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(workspace_bytes >= uttt_fast_readout_workspace(B, d, h), UTTT_ERR_WORKSPACE);
+  cudaStream_t st = (cudaStream_t)stream;
+  WsCursor ws(workspace, workspace_bytes);
+  float* zacc = ws.take<float>((size_t)B * CT * d);
+  if (!ws.ok()) return UTTT_ERR_WORKSPACE;
+  const int ob = out_dtype == UTTT_DTYPE_BF16;
+  UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
+  if (T == 1 && w_dtype == UTTT_DTYPE_BF16) {
+    // decode: one token per state, memory-bound GEMV over the BF16 read copies
+    {
+      ProfScope ps(UTTT_PROF_READOUT, st);
+      UTTT_TRY(launch_readout_gemv(B, d, h, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_up,
+                                   (const __nv_bfloat16*)w_down, state_index, zacc, st));
+    }
+    ProfScope ps(UTTT_PROF_READOUT_LN, st);
+    readout_ln_kernel<<<dim3(1, B), LN_THREADS, 0, st>>>(zacc, CT, (const __nv_bfloat16*)x, 1, 0, 1, d, ln_weight,
+                                                         ln_bias, eps, out, ob);
+    return launch_status();
+  }
+  static bool attr_done = false;
+  if (!attr_done) {
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    attr_done = true;
+  }
+  ChunkParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = B; p.T = T; p.C = CT; p.d = d; p.h = h; p.hp = (h + 127) / 128 * 128;
+  p.zacc = zacc;
+  p.status = ws_status(workspace);
+  p.k = (const __nv_bfloat16*)x;
+  if (w_dtype == UTTT_DTYPE_BF16) {
+    p.src_up = w_up;
+    p.src_gate = (const __nv_bfloat16*)w_up + h;
+    p.ld_ug = 2 * h;
+    p.ss_ug = (long long)d * 2 * h;
+  } else {
+    p.src_up = w_up;
+    p.src_gate = w_gate;
+    p.ld_ug = h;
+    p.ss_ug = (long long)d * h;
+  }
+  p.src_down = w_down;
+  p.ss_d = (long long)h * d;
+  p.state_index = state_index;
+  CUtensorMap tmX;
+  {
+    uint64_t dims[3] = {(uint64_t)d, (uint64_t)T, (uint64_t)B};
+    uint64_t str[2] = {(uint64_t)d * 2, (uint64_t)T * d * 2};
+    uint32_t box[3] = {64, 64, 1};
+    UTTT_TRY(make_tmap_bf16(&tmX, x, 3, dims, str, box));
+  }
+  const dim3 grid((h + HT - 1) / HT, B);
+  for (int tok0 = 0; tok0 < T; tok0 += CT) {
+    p.tok0 = tok0;
+    p.Cc = (T - tok0) < CT ? (T - tok0) : CT;
+    {
+      ProfScope ps(UTTT_PROF_READOUT, st);
+      if (w_dtype == UTTT_DTYPE_BF16)
+        chunk_fwd_kernel<__nv_bfloat16><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
+      else
+        chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
+    }
+    UTTT_TRY(launch_status());
+    {
+      ProfScope ps(UTTT_PROF_READOUT_LN, st);
+      readout_ln_kernel<<<dim3(CT, B), LN_THREADS, 0, st>>>(zacc, CT, (const __nv_bfloat16*)x, T, tok0, p.Cc, d,
+                                                            ln_weight, ln_bias, eps, out, ob);
     }
     UTTT_TRY(launch_status());
   }
