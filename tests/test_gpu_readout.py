@@ -1,6 +1,9 @@
 """GPU parity of the fast-weight readout (decode GEMV and tensor-core tiles)
-against the reference's fixtures and the oracle.  Tolerance: max |diff| <= 2e-2
-(BF16 activations; the north-star logits bound)."""
+against the reference's fixtures and the oracle.
+
+Tolerance: |diff| <= 2e-2 + |ref|/128.  The outputs are x + LN(z) with |y| up
+to ~5 and both sides round them to BF16, so one BF16 ULP (|y|/128) is added to
+the north-star 2e-2 absolute bound."""
 
 import os
 
@@ -19,6 +22,11 @@ pytestmark = pytest.mark.gpu
 
 def load(name):
     return dict(np.load(os.path.join(GOLDEN, name + ".npz")))
+
+
+def close(got, ref):
+    bad = np.abs(got - ref) > 2e-2 + np.abs(ref) / 128
+    assert not bad.any(), (np.max(np.abs(got - ref)), int(bad.sum()))
 
 
 def T(x, dtype=torch.float32):
@@ -41,8 +49,7 @@ def test_readout_matches_reference_fixture(name, form):
         ref = g["out"]
     torch.cuda.synchronize()
     assert y.dtype == torch.bfloat16 and y.shape == x.shape
-    err = np.max(np.abs(y.float().cpu().numpy() - ref))
-    assert err < 2e-2, err
+    close(y.float().cpu().numpy(), ref)
 
 
 def test_decode_readout_gathers_personas_by_index():
@@ -60,4 +67,4 @@ def test_decode_readout_gathers_personas_by_index():
                         state_index=torch.as_tensor(idx), packed=True)
     torch.cuda.synchronize()
     ref = ofw.swiglu_fast_forward(x, w_up[idx], w_gate[idx], w_down[idx], lnw, lnb, 1e-5, Precision("bf16"))
-    assert np.max(np.abs(y.float().cpu().numpy() - ref)) < 2e-2
+    close(y.float().cpu().numpy(), ref)
