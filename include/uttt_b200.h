@@ -101,6 +101,32 @@ int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_c
                      int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss,
                      float* clip_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free chunk write.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: serving loops whose HBM is fully
+ * reserved up front (an extra allocation would fail, and cudaMalloc / cudaFree
+ * may synchronise the device and stall the decode streams), and host code in
+ * foreign-language bindings that has no device allocator.  Same arguments and
+ * results as uttt_chunk_write, minus the workspace: the scratch is a fixed
+ * UTTT_NOALLOC_SCRATCH_BYTES device array inside the library, held on every
+ * device that loads it until the process exits.  Sizes whose
+ * uttt_chunk_write_workspace(B, C, d, h) exceeds it are rejected with
+ * UTTT_ERR_WORKSPACE before any work.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU race and must be ordered by the caller.  The array's status word
+ * is cleared at the start of each call, so an expired device wait is not
+ * reported through uttt_read_status for this variant.
+ */
+#define UTTT_NOALLOC_SCRATCH_BYTES (8u << 20)
+int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q,
+                             const void* k, const void* v, const float* eta, const float* alpha, const float* mask,
+                             float* w_up, float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
+                             const float* ln_weight, const float* ln_bias, float momentum_beta,
+                             float max_grad_norm, int normalize_by_dim, float eps, void* out, int out_dtype,
+                             float* token_loss, float* clip_scale, void* stream);
+
 /* ---- fast-weight readout ------------------------------------------------ */
 /*
  * f_W(x) = x + LayerNorm(silu(x W_gate) * (x W_up) W_down) for B states of T
