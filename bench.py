@@ -162,8 +162,10 @@ def algorithmic_bytes(kind: int) -> float:
     """Minimal HBM bytes one launch of a chunk kernel must move (all states)."""
     B, d, h = CFG["states"], CFG["d"], CFG["h"]
     w = 3.0 * d * h * 4.0                       # FP32 W_up + W_gate + W_down of one state
-    if kind == 3:   # bwd+update: read W (+S if momentum), write W and S
-        return B * (w * (3.0 + (1.0 if CFG["momentum"] else 0.0)))
+    if kind == 3:   # bwd+update: read W (+S if momentum), write W (+S when momentum is kept or at the last chunk)
+        n_chunks = CFG["tokens"] // CFG["chunk"]
+        s_writes = 1.0 if CFG["momentum"] else 1.0 / n_chunks
+        return B * w * (2.0 + s_writes + (1.0 if CFG["momentum"] else 0.0))
     if kind == 0:   # fwd: read W once
         return B * w
     return 0.0

@@ -58,6 +58,11 @@ int uttt_read_status(void* workspace, int reset, void* stream);
 #define UTTT_PROF_CHUNK_BWD 3
 #define UTTT_PROF_READOUT 4
 #define UTTT_PROF_READOUT_LN 5
+#define UTTT_PROF_GEMM 6
+#define UTTT_PROF_FINISH 7
+#define UTTT_PROF_ATTN 8
+#define UTTT_PROF_ROWWISE 9
+#define UTTT_PROF_ARGMAX 10
 int uttt_profile_enable(int on);
 int uttt_profile_read(float* total_ms, int* launches);
 
@@ -150,6 +155,38 @@ size_t uttt_fast_readout_workspace(int B, int d, int h);
 int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up, const void* w_gate,
                       const void* w_down, const int* state_index, const float* ln_weight, const float* ln_bias,
                       float eps, void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- slow-weight projections -------------------------------------------- */
+/*
+ * y = x W^T for BF16 x (M, K) and an nn.Linear weight W (N, K), FP32
+ * accumulation on the tensor cores, followed by a per-row finishing pass over
+ * column segments of y.  Replaces the F.linear calls of the reference's
+ * blocks and their epilogues: the packed QKV projection
+ * (model/uttt_layer.py:1068-1074), wo / w_o with the residual add
+ * (:1168, :1305, :1544-1554), fused_fast_q_proj (:1175-1190),
+ * fused_slow_projections (:1193-1231) and the tied lm_head
+ * (model/uttt_model.py:944-950).  Segment ops reproduce the reference's BF16
+ * roundings: STORE  y;  RESID  aux + bf16(y);  RMSNORM  rms_norm(bf16(y)) *
+ * gamma (aux = FP32 gamma or NULL);  SIGMOID  scale * sigmoid(bf16(y + aux)).
+ * Requires K % 64 == 0.  out may alias a RESID segment's aux (in place).
+ */
+#define UTTT_SEG_STORE 0
+#define UTTT_SEG_RESID 1
+#define UTTT_SEG_RMSNORM 2
+#define UTTT_SEG_SIGMOID 3
+typedef struct UtttSegment {
+  int start, len; /* columns [start, start + len) of y */
+  int op;         /* UTTT_SEG_* */
+  int out_f32;    /* 1: FP32 output rows, 0: BF16 */
+  void* out;      /* row r at out + r * out_ld elements */
+  long long out_ld;
+  const void* aux; /* RESID: BF16 rows (aux_ld); RMSNORM: FP32 gamma (len); SIGMOID: FP32 bias (len) */
+  long long aux_ld;
+  float scale; /* SIGMOID multiplier */
+} UtttSegment;
+size_t uttt_linear_workspace(int M, int N);
+int uttt_linear(int M, int N, int K, const void* x, const void* w, int nseg, const UtttSegment* segs, float eps,
+                void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

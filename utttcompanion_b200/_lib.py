@@ -49,7 +49,19 @@ SIGNATURES: Dict[str, tuple] = {
                                        vp, vp, vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp]),
     "uttt_fast_readout_workspace": (sz, [i32, i32, i32]),
     "uttt_fast_readout": (i32, [i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, f32, vp, i32, vp, sz, vp]),
+    "uttt_linear_workspace": (sz, [i32, i32]),
+    "uttt_linear": (i32, [i32, i32, i32, vp, vp, i32, vp, f32, vp, sz, vp]),
 }
+
+
+class Segment(C.Structure):
+    """``UtttSegment`` of include/uttt_b200.h."""
+    _fields_ = [("start", C.c_int), ("len", C.c_int), ("op", C.c_int), ("out_f32", C.c_int),
+                ("out", C.c_void_p), ("out_ld", C.c_longlong), ("aux", C.c_void_p), ("aux_ld", C.c_longlong),
+                ("scale", C.c_float)]
+
+
+SEG_STORE, SEG_RESID, SEG_RMSNORM, SEG_SIGMOID = 0, 1, 2, 3
 
 _lib: Optional[C.CDLL] = None
 

@@ -71,6 +71,7 @@ struct ChunkParams {
   float* clip_out;    // (B, n_chunks) or null
   int chunk_index;
   int n_chunks;
+  int call_end;       // token index one past the last chunk of this call
   int hp;             // hidden padded to 128
   float beta, clip, eps, inv_scale;
   int* status;
@@ -115,6 +116,7 @@ struct ChunkStats {
   float count;   // valid tokens (Cc without a mask)
   float alpha_bar;
   bool active;
+  bool later_active;  // a later chunk of this call changes this state
 };
 
 __device__ ChunkStats chunk_stats(const ChunkParams& p, int b) {
@@ -133,6 +135,15 @@ __device__ ChunkStats chunk_stats(const ChunkParams& p, int b) {
   s.count = cnt;
   s.alpha_bar = p.mask ? asum / fmaxf(cnt, 1.f) : asum / (float)p.Cc;
   s.active = p.mask ? (cnt != 0.f) : true;
+  bool later = false;
+  const int lo = p.tok0 + p.Cc;
+  if (!p.mask) {
+    later = lo < p.call_end;
+  } else {
+    for (int c = lo + lane; c < p.call_end && !later; c += 32) later = p.mask[(size_t)b * p.T + c] != 0.f;
+    later = __any_sync(0xffffffffu, later);
+  }
+  s.later_active = later;
   return s;
 }
 
@@ -533,6 +544,7 @@ __global__ void __launch_bounds__(LN_THREADS) readout_ln_kernel(const float* __r
 // bwd: dH, dU, dG and the three weight gradients; NORM pass accumulates
 // ||grad||^2, UPDATE pass applies momentum / decay / clip in place.
 // ============================================================================
+template <bool kMomentum>
 __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const __grid_constant__ CUtensorMap tmDZ,
                                                                 const ChunkParams p, int update) {
@@ -656,15 +668,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     }
 
     // ------------------------------------------------------------ epilogue 2: gradients
+    // TMEM tiles: gradW_up^T / gradW_gate^T as (hidden row, d column) and
+    // gradW_down^T as (d row, hidden column): the 32 lanes of a warp are 32
+    // consecutive floats of one weight row, so every load / store instruction
+    // moves one full 128-byte line.
     float scale = 1.f;
     if (update && p.clip > 0.f) scale = fminf(1.f, p.clip * rsqrtf(p.norm2[b] + 1e-8f));
     if (update && p.clip_out && t == 0 && tid == 0) p.clip_out[(size_t)b * p.n_chunks + p.chunk_index] = scale;
     const float decay = 1.f - st.alpha_bar;
     const float beta = p.beta;
+    // With beta == 0 the momentum of this chunk is never read again unless this
+    // is the last chunk of the call that changes this state.
+    const bool write_s = kMomentum || !st.later_active;
     const size_t wbase_ug = (size_t)b * p.d * p.h;
     const size_t wbase_d = (size_t)b * p.h * p.d;
     float acc = 0.f;
     const int row = q * 32 + lane;
+    const bool ug_row_ok = h0 + row < p.h;
     for (int j = 0; j < nch; ++j) {
       mbar_wait(&gfull, j & 1, p.status);
       tc_fence_after();
@@ -677,61 +697,75 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         tmem_ld16(tmem_addr(tGD, q * 32, cbase + cc), gd);
         tmem_wait_ld();
         if (skip) continue;
+        const int hc = h0 + cbase + cc;   // first hidden column of this thread's gradW_down^T run
         if (!update) {
-          if (h0 + row < p.h) {
+          if (ug_row_ok) {
 #pragma unroll
             for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e];
           }
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if (h0 + cbase + cc + e < p.h) acc += gd[e] * gd[e];
+            if (hc + e < p.h) acc += gd[e] * gd[e];
           continue;
         }
-        // gradW_up^T / gradW_gate^T: (hidden row, d column) -> W[dd][h0 + row]
-        if (h0 + row < p.h) {
-          float wu[16], wg[16], su[16], sg2[16];
+        // W_up / W_gate element (dd = j*128 + cbase + cc + e, hidden = h0 + row)
+        if (ug_row_ok) {
+          const size_t oug = wbase_ug + (size_t)(j * 128 + cbase + cc) * p.h + h0 + row;
+          float wu[16], wg[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const size_t o = wbase_ug + (size_t)(j * 128 + cbase + cc + e) * p.h + h0 + row;
-            wu[e] = p.w_up[o];
-            wg[e] = p.w_gate[o];
-            su[e] = beta != 0.f ? p.s_up[o] : 0.f;
-            sg2[e] = beta != 0.f ? p.s_gate[o] : 0.f;
+            wu[e] = p.w_up[oug + (size_t)e * p.h];
+            wg[e] = p.w_gate[oug + (size_t)e * p.h];
           }
+          if constexpr (kMomentum) {
+            float su[16], sg[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const size_t o = wbase_ug + (size_t)(j * 128 + cbase + cc + e) * p.h + h0 + row;
-            const float nsu = beta * su[e] - gu[e] * scale;
-            const float nsg = beta * sg2[e] - gg[e] * scale;
-            p.s_up_out[o] = nsu;
-            p.s_gate_out[o] = nsg;
-            p.w_up_out[o] = decay * wu[e] + nsu;
-            p.w_gate_out[o] = decay * wg[e] + nsg;
-          }
-        }
-        // gradW_down^T: (d row, hidden column) -> W_down[h0 + col][dd]
-        {
-          float wdv[16], sdv[16];
-          const int dd = j * 128 + row;
+            for (int e = 0; e < 16; ++e) {
+              su[e] = p.s_up[oug + (size_t)e * p.h];
+              sg[e] = p.s_gate[oug + (size_t)e * p.h];
+            }
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int hh = h0 + cbase + cc + e;
-            const size_t o = wbase_d + (size_t)hh * p.d + dd;
-            wdv[e] = 0.f;
-            sdv[e] = 0.f;
-            if (hh < p.h) {
-              wdv[e] = p.w_down[o];
-              sdv[e] = beta != 0.f ? p.s_down[o] : 0.f;
+            for (int e = 0; e < 16; ++e) {
+              const size_t a = oug + (size_t)e * p.h;
+              const float nsu = beta * su[e] - gu[e] * scale;
+              const float nsg = beta * sg[e] - gg[e] * scale;
+              p.w_up_out[a] = decay * wu[e] + nsu;
+              p.w_gate_out[a] = decay * wg[e] + nsg;
+              p.s_up_out[a] = nsu;
+              p.s_gate_out[a] = nsg;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const size_t a = oug + (size_t)e * p.h;
+              const float nsu = -gu[e] * scale;
+              const float nsg = -gg[e] * scale;
+              p.w_up_out[a] = decay * wu[e] + nsu;
+              p.w_gate_out[a] = decay * wg[e] + nsg;
+              if (write_s) {
+                p.s_up_out[a] = nsu;
+                p.s_gate_out[a] = nsg;
+              }
             }
           }
+        }
+        // W_down element (hidden = hc + e, dd = j*128 + row)
+        {
+          const size_t od = wbase_d + (size_t)hc * p.d + j * 128 + row;
+          float wd[16], sd[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const int hh = h0 + cbase + cc + e;
-            if (hh < p.h) {
-              const size_t o = wbase_d + (size_t)hh * p.d + dd;
-              const float ns = beta * sdv[e] - gd[e] * scale;
-              p.s_down_out[o] = ns;
-              p.w_down_out[o] = decay * wdv[e] + ns;
+            const bool ok = hc + e < p.h;
+            wd[e] = ok ? p.w_down[od + (size_t)e * p.d] : 0.f;
+            if constexpr (kMomentum) sd[e] = ok ? p.s_down[od + (size_t)e * p.d] : 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (hc + e < p.h) {
+              const size_t c = od + (size_t)e * p.d;
+              const float ns = (kMomentum ? beta * sd[e] : 0.f) - gd[e] * scale;
+              p.w_down_out[c] = decay * wd[e] + ns;
+              if (write_s) p.s_down_out[c] = ns;
             }
           }
         }
@@ -873,6 +907,7 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   p.token_loss = token_loss; p.out = out; p.out_bf16 = out_dtype == UTTT_DTYPE_BF16;
   p.clip_out = clip_scale;
   p.n_chunks = n_chunks;
+  p.call_end = (chunk_begin + n_chunks) * C < T ? (chunk_begin + n_chunks) * C : T;
   p.beta = momentum_beta; p.clip = max_grad_norm; p.eps = eps;
   p.inv_scale = normalize_by_dim ? 1.f / (float)d : 1.f;
   p.status = ws_status(workspace);
@@ -900,8 +935,10 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)bwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
     attr_done = true;
   }
   UTTT_TRY(cuda_status(cudaMemsetAsync(p.zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
@@ -922,12 +959,18 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     UTTT_TRY(launch_status());
     if (max_grad_norm > 0.f) {
       ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
-      chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
+      if (momentum_beta != 0.f)
+        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
+      else
+        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
     }
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
-      chunk_bwd_kernel<<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+      if (momentum_beta != 0.f)
+        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+      else
+        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
     }
     UTTT_TRY(launch_status());
   }
