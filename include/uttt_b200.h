@@ -148,8 +148,7 @@ int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int chunk_begin,
  *   ln_*         FP32 (d,) LayerNorm affine, as the reference applies it.
  *   out          (B, T, d) in out_dtype.
  * T == 1 with BF16 copies runs the decode GEMV; otherwise 64-token tiles on
- * the tensor cores.  Requires d % 128 == 0 (d % 256 for the decode GEMV),
- * h % 8 == 0.
+ * the tensor cores.  Requires d % 128 == 0, h % 8 == 0.
  */
 size_t uttt_fast_readout_workspace(int B, int d, int h);
 int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up, const void* w_gate,
@@ -187,6 +186,63 @@ typedef struct UtttSegment {
 size_t uttt_linear_workspace(int M, int N);
 int uttt_linear(int M, int N, int K, const void* x, const void* w, int nseg, const UtttSegment* segs, float eps,
                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- attention ---------------------------------------------------------- */
+/*
+ * Decode step of SlidingWindowAttention (model/uttt_layer.py:1058-1168, the
+ * T == 1 SDPA branch :1119-1124; ring layout of CUDAGraphDecoder,
+ * engine/inference.py:240-259) for B rows of a packed batch.  Row b is persona
+ * slot slot[b] at absolute position pos[b]: q, k get RoPE at pos[b]
+ * (apply_rope :946-958), k / v are written into the ring at slot pos[b] % W,
+ * and the n_heads / n_kv query heads of each group attend over the
+ * min(pos[b]+1, W) valid slots.
+ *   qkv    BF16 rows (B, qkv_ld): [q (n_heads*hd) | k (n_kv*hd) | v (n_kv*hd)]
+ *   k_ring, v_ring  BF16 (slots, n_kv, W, hd) of one layer
+ *   rope_cos/sin    FP32 (positions, hd) tables (RotaryEmbedding, :899-943)
+ *   out    BF16 rows (B, out_ld), heads concatenated.
+ * hd in {32, 64, 128}, n_heads / n_kv <= 8.
+ */
+int uttt_attn_decode(int B, int n_heads, int n_kv, int hd, int W, const void* qkv, int qkv_ld, const int* pos,
+                     const int* slot, void* k_ring, void* v_ring, const float* rope_cos, const float* rope_sin,
+                     void* out, int out_ld, void* stream);
+/*
+ * Multi-token causal sliding-window attention (the prefill / chunk branches
+ * :1125-1148) for B rows of T new tokens at positions start_pos.. with `hist`
+ * history positions already at the start of the KV window buffers:
+ *   k_buf, v_buf  BF16 (B, n_kv, hist + T, hd); this call writes positions
+ *                 hist.. (RoPE'd k, v) and reads all of them.
+ *   q_scratch     BF16 (B, T, n_heads, hd) scratch for the RoPE'd queries.
+ *   out           BF16 (B, T, n_heads*hd).
+ * Query at absolute position p attends keys in (p - W, p].
+ */
+int uttt_attn_prefill(int B, int T, int start_pos, int hist, int n_heads, int n_kv, int hd, int W, const void* qkv,
+                      int qkv_ld, const float* rope_cos, const float* rope_sin, void* q_scratch, void* k_buf,
+                      void* v_buf, void* out, void* stream);
+/* Copy the last min(W, L) positions (ending at absolute position end_pos) of
+ * KV window buffers (B, n_kv, L, hd) into persona rings at slot[b]. */
+int uttt_kv_ring_fill(int B, int L, int end_pos, int n_kv, int hd, int W, const void* k_buf, const void* v_buf,
+                      const int* slot, void* k_ring, void* v_ring, void* stream);
+
+/* ---- row-wise ops -------------------------------------------------------- */
+/* RMSNorm (model/uttt_layer.py:881-896): out = x * rsqrt(mean(x^2) + eps) * weight
+ * (weight FP32, rounded to BF16 as weight.to(x.dtype) does; NULL for none). */
+int uttt_rmsnorm(int rows, int d, const void* x, long long x_ld, const float* weight, float eps, void* out,
+                 long long out_ld, void* stream);
+/* Token embedding gather (model/uttt_model.py:778-780): out[r] = table[ids[r]]. */
+int uttt_embed(int rows, int d, const int* ids, const void* table, void* out, void* stream);
+/* Greedy pick of _sample_next_token at temperature <= 1e-5
+ * (model/uttt_model.py:1204-1221): BF16-rounded logits, PAD/BOS/UNK (ids 0,1,3)
+ * and ids >= active_limit masked (stop_free also masks 2,4,5 as the
+ * reference's graph-vs-eager test does), lowest id on ties.  top2 (optional)
+ * receives the best and second-best values per row. */
+int uttt_greedy_argmax(int rows, int V, const void* logits, int logits_f32, long long ld, int active_limit,
+                       int stop_free, int* ids, float* top2, void* stream);
+
+/* BF16 read copies of S FP32 states (SharedFastWeightPool.inference_read_weights,
+ * model/uttt_layer.py:648-668): packed_up_gate (S, d, 2h) = [w_up | w_gate],
+ * down (S, h, d) = w_down, round-to-nearest-even. */
+int uttt_pack_read_copies(int S, int d, int h, const float* w_up, const float* w_gate, const float* w_down,
+                          void* packed_up_gate, void* down, void* stream);
 
 #ifdef __cplusplus
 }

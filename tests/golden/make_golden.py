@@ -99,9 +99,8 @@ def chunk_case(ul, name, dtype, act_dtype, B, C, d, h, mask, beta, clip, q_is_k,
     np.savez_compressed(os.path.join(HERE, f"chunk_{name}.npz"), **arrays)
 
 
-def swiglu_case(ul, name, act_dtype, seed, T=5):
+def swiglu_case(ul, name, act_dtype, seed, T=5, B=2, d=256, h=160):
     g = torch.Generator().manual_seed(seed)
-    B, d, h = 3, 256, 160
     x = torch.randn(B, T, d, generator=g).to(act_dtype)
     w_up = torch.randn(B, d, h, generator=g) * d ** -0.5
     w_gate = torch.randn(B, d, h, generator=g) * d ** -0.5
@@ -140,7 +139,7 @@ def elastic_case(ul):
         drift_keys=np.array(keys), drift_vals=np.array([drift[k] for k in keys], np.float64))
 
 
-SMALL = dict(vocab_size=512, d_model=64, n_layers=2, n_heads=4, n_kv_heads=2, d_ff_fast=96,
+SMALL = dict(vocab_size=512, d_model=128, n_layers=2, n_heads=4, n_kv_heads=2, d_ff_fast=160,
              sliding_window_size=16, max_seq_len=256, chunk_size=16, gradient_checkpointing=False,
              dropout=0.0)
 
@@ -174,9 +173,9 @@ def model_case(um, name, dtype, autocast_bf16, seed=2024, n_prompt=37, n_gen=20)
         model = model.double()
     elif autocast_bf16:
         model = model.to(torch.bfloat16)
-        # FP32 fast-weight masters, as the persona path keeps them
-        for p in model.fast_weight_pool.parameters():
-            p.data = p.data.float()
+        # FP32 fast-weight masters (W_0 unrounded), as the persona path keeps them
+        for n, p in model.fast_weight_pool.named_parameters():
+            p.data = torch.tensor(weights["fast_weight_pool." + n], dtype=torch.float32)
     gen = torch.Generator().manual_seed(seed + 1)
     prompt = torch.randint(6, cfg.vocab_size, (1, n_prompt), generator=gen)
     state_dtype = torch.float64 if dtype == torch.float64 else torch.float32
@@ -185,7 +184,8 @@ def model_case(um, name, dtype, autocast_bf16, seed=2024, n_prompt=37, n_gen=20)
     pg = torch.Generator().manual_seed(seed + 2)
     for nm in ("w_up", "w_gate", "w_down"):
         t = getattr(state, nm)
-        setattr(state, nm, t + (1e-2 * torch.randn(t.shape, generator=pg, dtype=torch.float64)).to(t.dtype))
+        delta = (1e-2 * torch.randn(t.shape, generator=pg, dtype=torch.float64)).float()
+        setattr(state, nm, (t.float() + delta).to(t.dtype))
     ctx = torch.autocast("cpu", dtype=torch.bfloat16) if autocast_bf16 else torch.autocast("cpu", enabled=False)
     out = {}
     with torch.no_grad(), ctx:
@@ -220,9 +220,16 @@ def model_case(um, name, dtype, autocast_bf16, seed=2024, n_prompt=37, n_gen=20)
                rope_sin=_np(model.layers[0].attn.rope.sin_cached.float()))
     out.pop("weights")
     arrays = dict(out)
-    for k, v in weights.items():
-        arrays["W::" + k] = v
-    arrays["cfg_json"] = np.array(repr(SMALL))
+    # weights and the starting persona state are identical for every dtype case: stored once
+    shared = {"W::" + k: v for k, v in weights.items()}
+    shared.update(cfg_json=np.array(repr(SMALL)), prompt=arrays["prompt"], rope_cos=arrays.pop("rope_cos"),
+                  rope_sin=arrays.pop("rope_sin"), active_limit=arrays["active_limit"],
+                  state_w_up=arrays.pop("state_w_up").astype(np.float32),
+                  state_w_gate=arrays.pop("state_w_gate").astype(np.float32),
+                  state_w_down=arrays.pop("state_w_down").astype(np.float32))
+    path = os.path.join(HERE, "model_shared.npz")
+    if name == "f32":
+        np.savez_compressed(path, **shared)
     np.savez_compressed(os.path.join(HERE, f"model_{name}.npz"), **arrays)
 
 
@@ -259,13 +266,13 @@ def main():
     chunk_case(ul, "bf16_plain", f32, bf, 2, 64, 128, 160, None, 0.0, 0.0, True, False, 5)
     chunk_case(ul, "bf16_full", f32, bf, 3, 64, 128, 160, "ragged", 0.9, 1.0, False, True, 6)
     chunk_case(ul, "bf16_clipbite", f32, bf, 2, 64, 128, 160, None, 0.5, 0.02, False, False, 7)
-    swiglu_case(ul, "f32", f32, 21)
+    swiglu_case(ul, "f32", f32, 21, d=32, h=48)
     swiglu_case(ul, "bf16", bf, 22)
     swiglu_case(ul, "bf16_t1", bf, 23, T=1)
     swiglu_case(ul, "bf16_t70", bf, 24, T=70)
     elastic_case(ul)
-    model_case(um, "f64", f64, False)
     model_case(um, "f32", f32, False)
+    model_case(um, "f64", f64, False)
     model_case(um, "bf16", f32, True)
     init_checksums(um)
     print("golden fixtures written to", HERE)

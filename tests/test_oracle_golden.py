@@ -18,7 +18,10 @@ from conftest import GOLDEN
 
 
 def load(name):
-    return dict(np.load(os.path.join(GOLDEN, name + ".npz"), allow_pickle=False))
+    out = dict(np.load(os.path.join(GOLDEN, name + ".npz"), allow_pickle=False))
+    if name.startswith("model_"):
+        out.update(np.load(os.path.join(GOLDEN, "model_shared.npz"), allow_pickle=False))
+    return out
 
 
 CHUNK_CASES = ["f64_plain", "f64_full", "f32_plain", "f32_full", "bf16_plain", "bf16_full", "bf16_clipbite"]

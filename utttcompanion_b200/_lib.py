@@ -51,6 +51,13 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_fast_readout": (i32, [i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, f32, vp, i32, vp, sz, vp]),
     "uttt_linear_workspace": (sz, [i32, i32]),
     "uttt_linear": (i32, [i32, i32, i32, vp, vp, i32, vp, f32, vp, sz, vp]),
+    "uttt_attn_decode": (i32, [i32, i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, i32, vp]),
+    "uttt_attn_prefill": (i32, [i32, i32, i32, i32, i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp]),
+    "uttt_kv_ring_fill": (i32, [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
+    "uttt_rmsnorm": (i32, [i32, i32, vp, C.c_longlong, vp, f32, vp, C.c_longlong, vp]),
+    "uttt_embed": (i32, [i32, i32, vp, vp, vp, vp]),
+    "uttt_greedy_argmax": (i32, [i32, i32, vp, i32, C.c_longlong, i32, i32, vp, vp, vp]),
+    "uttt_pack_read_copies": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, vp]),
 }
 
 

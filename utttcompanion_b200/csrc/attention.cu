@@ -1,0 +1,315 @@
+// Sliding-window GQA attention of the uTTT blocks (SlidingWindowAttention,
+// model/uttt_layer.py:961-1168) for packed multi-persona batches.
+//
+// Decode (one new token per row): RoPE of q and k at the row's own position,
+// k/v written in place into the persona's KV ring at slot pos % W, then
+// attention over the min(pos+1, W) valid slots.  The ring holds exactly the
+// keys the reference's trimmed cache holds (the last W positions), so the
+// softmax runs over the same set.  One CTA per (row, kv head); the n_rep query
+// heads of the group share every K/V load; warps split the slots, lanes split
+// the head dimension, online softmax per warp, merged through shared memory.
+//
+// Prefill / chunk (T new tokens per row): RoPE into a contiguous per-row KV
+// window buffer that starts with up to W-1 history positions, then causal
+// sliding-window attention (query at absolute position p sees keys in
+// (p - W, p]).  64 queries per CTA, two threads per query (each half of the
+// head dimension), 64-key tiles staged in shared memory.
+//
+// RoPE tables are the reference's FP32 cos/sin (RotaryEmbedding._build_cache,
+// :910-933); like apply_rope on BF16 activations (:946-958) every product and
+// the sum are rounded to BF16.
+#include "common.cuh"
+#include "host_util.cuh"
+
+namespace uttt {
+namespace {
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+// rotate-half RoPE of element i of a head vector x (length hd) at position pos
+__device__ __forceinline__ float rope_elem(const __nv_bfloat16* x, int i, int hd, const float* cosr,
+                                           const float* sinr) {
+  const int half = hd >> 1;
+  const float xi = __bfloat162float(x[i]);
+  const float rot = i < half ? -__bfloat162float(x[i + half]) : __bfloat162float(x[i - half]);
+  return bfr(bfr(xi * bfr(cosr[i])) + bfr(rot * bfr(sinr[i])));
+}
+
+constexpr int DEC_THREADS = 128;
+constexpr int MAX_HD = 128;
+constexpr int MAX_REP = 8;
+
+template <int E>
+__global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int qkv_ld, const int* __restrict__ pos, const int* __restrict__ slot,
+    __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring, int n_heads, int n_kv, int hd, int W,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, float scale, __nv_bfloat16* __restrict__ out,
+    int out_ld) {
+  __shared__ float qs[MAX_REP][MAX_HD];
+  __shared__ float wm[4][MAX_REP], wl[4][MAX_REP];
+  __shared__ float wacc[4][MAX_REP][MAX_HD];
+  const int b = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rep = n_heads / n_kv;
+  const int p = pos[b];
+  const int sl = slot[b];
+  const __nv_bfloat16* row = qkv + (size_t)b * qkv_ld;
+  const float* cr = cos_t + (size_t)p * hd;
+  const float* sr = sin_t + (size_t)p * hd;
+  const size_t ring_base = (((size_t)sl * n_kv + g) * W) * hd;
+  // RoPE q heads of this group, RoPE k, write k / v into the ring slot
+  for (int i = tid; i < rep * hd; i += DEC_THREADS) {
+    const int r = i / hd, e = i % hd;
+    qs[r][e] = rope_elem(row + (size_t)(g * rep + r) * hd, e, hd, cr, sr);
+  }
+  const __nv_bfloat16* krow = row + (size_t)n_heads * hd + (size_t)g * hd;
+  const __nv_bfloat16* vrow = row + (size_t)(n_heads + n_kv) * hd + (size_t)g * hd;
+  const int ws = p % W;
+  for (int e = tid; e < hd; e += DEC_THREADS) {
+    kring[ring_base + (size_t)ws * hd + e] = __float2bfloat16(rope_elem(krow, e, hd, cr, sr));
+    vring[ring_base + (size_t)ws * hd + e] = vrow[e];
+  }
+  __syncthreads();
+  const int nvalid = p + 1 < W ? p + 1 : W;
+  float m[MAX_REP], l[MAX_REP], acc[MAX_REP][E];
+#pragma unroll
+  for (int r = 0; r < MAX_REP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[r][e] = 0.f;
+  }
+  for (int s = warp; s < nvalid; s += 4) {
+    const __nv_bfloat16* kp = kring + ring_base + (size_t)s * hd + lane * E;
+    const __nv_bfloat16* vp = vring + ring_base + (size_t)s * hd + lane * E;
+    float kv[E], vv[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      kv[e] = __bfloat162float(kp[e]);
+      vv[e] = __bfloat162float(vp[e]);
+    }
+#pragma unroll
+    for (int r = 0; r < MAX_REP; ++r) {
+      if (r >= rep) break;
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) d += qs[r][lane * E + e] * kv[e];
+      d = warp_sum(d) * scale;
+      const float mn = fmaxf(m[r], d);
+      const float c = __expf(m[r] - mn);
+      const float pe = __expf(d - mn);
+      l[r] = l[r] * c + pe;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[r][e] = acc[r][e] * c + pe * vv[e];
+      m[r] = mn;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < MAX_REP; ++r) {
+    if (r >= rep) break;
+    if (lane == 0) {
+      wm[warp][r] = m[r];
+      wl[warp][r] = l[r];
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) wacc[warp][r][lane * E + e] = acc[r][e];
+  }
+  __syncthreads();
+  for (int i = tid; i < rep * hd; i += DEC_THREADS) {
+    const int r = i / hd, e = i % hd;
+    float mx = -INFINITY;
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, wm[w][r]);
+    float L = 0.f, A = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      if (wm[w][r] == -INFINITY) continue;
+      const float c = __expf(wm[w][r] - mx);
+      L += wl[w][r] * c;
+      A += wacc[w][r][e] * c;
+    }
+    out[(size_t)b * out_ld + (size_t)(g * rep + r) * hd + e] = __float2bfloat16(A / L);
+  }
+}
+
+// RoPE of the new tokens' k into the KV window buffer (after `hist` history
+// positions) and of q into qout; v copied.  One CTA per token row.
+__global__ void rope_prefill_kernel(const __nv_bfloat16* __restrict__ qkv, int qkv_ld, int T, int start_pos,
+                                    int n_heads, int n_kv, int hd, int hist, int L, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ qout,
+                                    __nv_bfloat16* __restrict__ kbuf, __nv_bfloat16* __restrict__ vbuf) {
+  const int bt = blockIdx.x;
+  const int b = bt / T, t = bt % T;
+  const int p = start_pos + t;
+  const __nv_bfloat16* row = qkv + (size_t)bt * qkv_ld;
+  const float* cr = cos_t + (size_t)p * hd;
+  const float* sr = sin_t + (size_t)p * hd;
+  for (int i = threadIdx.x; i < n_heads * hd; i += blockDim.x) {
+    const int hh = i / hd, e = i % hd;
+    qout[(size_t)bt * n_heads * hd + i] = __float2bfloat16(rope_elem(row + (size_t)hh * hd, e, hd, cr, sr));
+  }
+  for (int i = threadIdx.x; i < n_kv * hd; i += blockDim.x) {
+    const int g = i / hd, e = i % hd;
+    const size_t o = (((size_t)b * n_kv + g) * L + hist + t) * hd + e;
+    kbuf[o] = __float2bfloat16(rope_elem(row + (size_t)n_heads * hd + (size_t)g * hd, e, hd, cr, sr));
+    vbuf[o] = row[(size_t)(n_heads + n_kv) * hd + (size_t)g * hd + e];
+  }
+}
+
+constexpr int PF_Q = 64;        // queries per CTA
+constexpr int PF_KT = 64;       // keys per smem tile
+constexpr int PF_THREADS = 128;  // two threads per query
+
+template <int HD>
+__global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kbuf,
+    const __nv_bfloat16* __restrict__ vbuf, int T, int hist, int L, int n_heads, int n_kv, int hd, int W, float scale,
+    __nv_bfloat16* __restrict__ out) {
+  __shared__ __nv_bfloat16 ks[PF_KT][MAX_HD];
+  __shared__ __nv_bfloat16 vs[PF_KT][MAX_HD];
+  const int qb = blockIdx.x, hh = blockIdx.y, b = blockIdx.z;
+  const int g = hh / (n_heads / n_kv);
+  const int tid = threadIdx.x, qi = tid >> 1, half = tid & 1;
+  const int t = qb * PF_Q + qi;      // new-token index of this thread's query
+  const bool qvalid = t < T;
+  constexpr int hh2 = HD / 2;
+  const int e0 = half * hh2;
+  float qr[hh2], acc[hh2];
+#pragma unroll
+  for (int e = 0; e < hh2; ++e) {
+    qr[e] = 0.f;
+    acc[e] = 0.f;
+  }
+  if (qvalid) {
+    const __nv_bfloat16* qp = q + (((size_t)b * T + t) * n_heads + hh) * HD + e0;
+#pragma unroll
+    for (int e = 0; e < hh2; ++e) qr[e] = __bfloat162float(qp[e]);
+  }
+  float m = -INFINITY, l = 0.f;
+  const int kpos_q = hist + t;                           // this query's index in the KV buffer
+  const int lo_blk = hist + qb * PF_Q - (W - 1);         // first key any query of the block needs
+  const int hi_blk = hist + min(T, (qb + 1) * PF_Q) - 1;  // last key
+  const int k0 = max(0, lo_blk);
+  const __nv_bfloat16* kb = kbuf + (((size_t)b * n_kv + g) * L) * hd;
+  const __nv_bfloat16* vb = vbuf + (((size_t)b * n_kv + g) * L) * hd;
+  for (int kt = k0; kt <= hi_blk; kt += PF_KT) {
+    __syncthreads();
+    for (int i = tid; i < PF_KT * hd; i += PF_THREADS) {
+      const int r = i / hd, e = i % hd;
+      const int kk = kt + r;
+      ks[r][e] = kk <= hi_blk ? kb[(size_t)kk * hd + e] : __float2bfloat16(0.f);
+      vs[r][e] = kk <= hi_blk ? vb[(size_t)kk * hd + e] : __float2bfloat16(0.f);
+    }
+    __syncthreads();
+    const int nk = min(PF_KT, hi_blk - kt + 1);
+    for (int r = 0; r < nk; ++r) {
+      const int kk = kt + r;
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < hh2; ++e) d += qr[e] * __bfloat162float(ks[r][e0 + e]);
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      const bool ok = qvalid && kk <= kpos_q && kpos_q - kk < W;
+      if (!ok) continue;
+      d *= scale;
+      const float mn = fmaxf(m, d);
+      const float c = __expf(m - mn);
+      const float pe = __expf(d - mn);
+      l = l * c + pe;
+#pragma unroll
+      for (int e = 0; e < hh2; ++e) acc[e] = acc[e] * c + pe * __bfloat162float(vs[r][e0 + e]);
+      m = mn;
+    }
+  }
+  if (qvalid) {
+    __nv_bfloat16* op = out + (((size_t)b * T + t) * n_heads + hh) * HD + e0;
+#pragma unroll
+    for (int e = 0; e < hh2; ++e) op[e] = __float2bfloat16(acc[e] / l);
+  }
+}
+
+// Copy the last min(W, L) positions of a KV window buffer into the ring slots
+// of the persona: position p -> slot p % W.
+__global__ void ring_fill_kernel(const __nv_bfloat16* __restrict__ kbuf, const __nv_bfloat16* __restrict__ vbuf,
+                                 int L, int end_pos, const int* __restrict__ slot, int n_kv, int hd, int W,
+                                 __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring) {
+  const int b = blockIdx.y, g = blockIdx.z;
+  const int n = L < W ? L : W;
+  const int sl = slot[b];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * hd; i += gridDim.x * blockDim.x) {
+    const int j = i / hd, e = i % hd;
+    const int li = L - n + j;              // index in the buffer
+    const int p = end_pos - n + j;         // absolute position
+    const size_t src = (((size_t)b * n_kv + g) * L + li) * hd + e;
+    const size_t dst = ((((size_t)sl * n_kv + g) * W) + (p % W)) * hd + e;
+    kring[dst] = kbuf[src];
+    vring[dst] = vbuf[src];
+  }
+}
+
+}  // namespace
+}  // namespace uttt
+
+using namespace uttt;
+
+extern "C" int uttt_attn_decode(int B, int n_heads, int n_kv, int hd, int W, const void* qkv, int qkv_ld,
+                                const int* pos, const int* slot, void* k_ring, void* v_ring, const float* rope_cos,
+                                const float* rope_sin, void* out, int out_ld, void* stream) {
+  UTTT_REQUIRE(B > 0 && n_heads > 0 && n_kv > 0 && hd > 0 && W > 0, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(qkv && pos && slot && k_ring && v_ring && rope_cos && rope_sin && out, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(n_heads % n_kv == 0 && n_heads / n_kv <= MAX_REP, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(hd == 32 || hd == 64 || hd == 128, UTTT_ERR_UNSUPPORTED);
+  cudaStream_t st = (cudaStream_t)stream;
+  ProfScope ps(UTTT_PROF_ATTN, st);
+  const float scale = 1.f / sqrtf((float)hd);
+#define UTTT_DEC(EV)                                                                                          \
+  attn_decode_kernel<EV><<<dim3(B, n_kv), DEC_THREADS, 0, st>>>(                                              \
+      (const __nv_bfloat16*)qkv, qkv_ld, pos, slot, (__nv_bfloat16*)k_ring, (__nv_bfloat16*)v_ring, n_heads, \
+      n_kv, hd, W, rope_cos, rope_sin, scale, (__nv_bfloat16*)out, out_ld)
+  if (hd == 32)
+    UTTT_DEC(1);
+  else if (hd == 64)
+    UTTT_DEC(2);
+  else
+    UTTT_DEC(4);
+#undef UTTT_DEC
+  return launch_status();
+}
+
+extern "C" int uttt_attn_prefill(int B, int T, int start_pos, int hist, int n_heads, int n_kv, int hd, int W,
+                                 const void* qkv, int qkv_ld, const float* rope_cos, const float* rope_sin,
+                                 void* q_scratch, void* k_buf, void* v_buf, void* out, void* stream) {
+  UTTT_REQUIRE(B > 0 && T > 0 && start_pos >= 0 && hist >= 0 && n_heads > 0 && n_kv > 0 && hd > 0 && W > 0,
+               UTTT_ERR_INVALID);
+  UTTT_REQUIRE(qkv && rope_cos && rope_sin && q_scratch && k_buf && v_buf && out, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(hist <= start_pos && hist <= W - 1, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(n_heads % n_kv == 0 && (hd == 32 || hd == 64 || hd == 128), UTTT_ERR_UNSUPPORTED);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int L = hist + T;
+  ProfScope ps(UTTT_PROF_ATTN, st);
+  rope_prefill_kernel<<<B * T, 128, 0, st>>>((const __nv_bfloat16*)qkv, qkv_ld, T, start_pos, n_heads, n_kv, hd,
+                                             hist, L, rope_cos, rope_sin, (__nv_bfloat16*)q_scratch,
+                                             (__nv_bfloat16*)k_buf, (__nv_bfloat16*)v_buf);
+  UTTT_TRY(launch_status());
+  const dim3 grid((T + PF_Q - 1) / PF_Q, n_heads, B);
+  const float scale = 1.f / sqrtf((float)hd);
+#define UTTT_PF(HDV)                                                                                          \
+  attn_prefill_kernel<HDV><<<grid, PF_THREADS, 0, st>>>((const __nv_bfloat16*)q_scratch,                       \
+                                                       (const __nv_bfloat16*)k_buf, (const __nv_bfloat16*)v_buf, \
+                                                       T, hist, L, n_heads, n_kv, hd, W, scale, (__nv_bfloat16*)out)
+  if (hd == 32)
+    UTTT_PF(32);
+  else if (hd == 64)
+    UTTT_PF(64);
+  else
+    UTTT_PF(128);
+#undef UTTT_PF
+  return launch_status();
+}
+
+extern "C" int uttt_kv_ring_fill(int B, int L, int end_pos, int n_kv, int hd, int W, const void* k_buf,
+                                 const void* v_buf, const int* slot, void* k_ring, void* v_ring, void* stream) {
+  UTTT_REQUIRE(B > 0 && L > 0 && end_pos >= L && n_kv > 0 && hd > 0 && W > 0, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(k_buf && v_buf && slot && k_ring && v_ring, UTTT_ERR_INVALID);
+  cudaStream_t st = (cudaStream_t)stream;
+  ring_fill_kernel<<<dim3(8, B, n_kv), 256, 0, st>>>((const __nv_bfloat16*)k_buf, (const __nv_bfloat16*)v_buf, L,
+                                                    end_pos, slot, n_kv, hd, W, (__nv_bfloat16*)k_ring,
+                                                    (__nv_bfloat16*)v_ring);
+  return launch_status();
+}

@@ -89,10 +89,11 @@ __global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloa
   float* zb = zacc + (size_t)b * 64 * d;   // row 0 of this state's 64-row z block
   for (int dc = 0; dc < d; dc += 256) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const bool dval = dc + lane * 8 < d;   // d % 128 == 0: a 256-wide slice may be half full
 #pragma unroll 8
     for (int r = 0; r < 32; ++r) {
       const int j = warp * 32 + r;
-      if (j0 + j < h) {
+      if (dval && j0 + j < h) {
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(drow + (size_t)(j0 + j) * d + dc + lane * 8));
         float f[8];
         bf16x8_to_f32(v, f);
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloa
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) s += part[w][0][tid];
-    red_add_f32(zb + dc + tid, s);
+    if (dc + tid < d) red_add_f32(zb + dc + tid, s);
   }
 }
 
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloa
 
 int launch_readout_gemv(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
                         const __nv_bfloat16* wd, const int* state_index, float* zacc, cudaStream_t st) {
-  if (d % 256 != 0 || d > MAXD) return UTTT_ERR_UNSUPPORTED;
+  if (d % 128 != 0 || d > MAXD) return UTTT_ERR_UNSUPPORTED;
   readout_gemv_kernel<<<dim3((h + GT - 1) / GT, B), GTHREADS, 0, st>>>(x, wp, wd, state_index, d, h, zacc);
   return launch_status();
 }

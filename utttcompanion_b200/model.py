@@ -1,0 +1,404 @@
+"""B200 uTTT model engine behind the reference's model API.
+
+``UtttB200`` holds a reference state dict (``uTTTModel`` parameter names) on
+the GPU and runs the hot path with this package's kernels only:
+
+* ``forward_frozen`` / ``prefill`` -- ``uTTTModel.forward(update_fast_weights=False)``
+  (``model/uttt_model.py:813-830,944-950``): embedding, per block RMSNorm ->
+  packed QKV -> RoPE + sliding-window attention -> wo + residual -> RMSNorm ->
+  q projection + RMSNorm (``fused_fast_q_proj``) -> fast-weight readout through
+  the persona's frozen weights -> w_o + residual; final RMSNorm, tied lm_head.
+* ``decode_step`` -- one token for each of B personas in ONE packed batch,
+  each row with its own fast-weight read copy (``state_index``) and its own
+  KV ring slot and position (the multi-persona decode the reference, which is
+  batch-1, serialises per persona).
+* ``generate_greedy`` -- ``stream_generate`` at temperature 0.
+* ``test_time_update`` -- ``uTTTModel.test_time_update`` with the chunk-first
+  shared schedule (``model/uttt_model.py:453-608``): all layers of a chunk read
+  the chunk-start snapshot; their writes advance one cursor.
+
+Activations are BF16 and masters FP32, the reference's serving dtypes.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+from types import SimpleNamespace
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .fastweight import _stream, chunk_write, check_status, workspace
+from .readout import fast_readout
+from .workloads import ModelConfig
+
+PAD_ID, BOS_ID, EOS_ID, UNK_ID, USER_ID, ASSISTANT_ID = 0, 1, 2, 3, 4, 5
+SIMPLE_ACTIVE_VOCAB_LIMIT = 21478          # SimpleUTF8Tokenizer.ACTIVE_VOCAB_LIMIT, model/uttt_model.py:151
+
+
+@dataclass
+class FastState:
+    """Device mirror of ``FastWeightState`` (``model/uttt_layer.py:59-204``): FP32 masters."""
+    w_up: torch.Tensor
+    w_gate: torch.Tensor
+    w_down: torch.Tensor
+    s_up: torch.Tensor
+    s_gate: torch.Tensor
+    s_down: torch.Tensor
+    ln_weight: torch.Tensor
+    ln_bias: torch.Tensor
+    step: int = 0
+    last_surprise_loss: float = 0.0
+    surprise_history: List[float] = field(default_factory=list)
+
+    def clone(self) -> "FastState":
+        return FastState(*(t.clone() for t in (self.w_up, self.w_gate, self.w_down, self.s_up, self.s_gate,
+                                                self.s_down, self.ln_weight, self.ln_bias)),
+                         int(self.step), float(self.last_surprise_loss), list(self.surprise_history[-100:]))
+
+    def to_state_dict(self) -> Dict[str, object]:
+        """Persona checkpoint payload in the reference's format (``:170-184``)."""
+        d = {k: getattr(self, k).detach().cpu() for k in ("w_up", "w_gate", "w_down", "s_up", "s_gate", "s_down",
+                                                         "ln_weight", "ln_bias")}
+        d.update(step=self.step, last_surprise_loss=self.last_surprise_loss,
+                 surprise_history=list(self.surprise_history[-100:]))
+        return d
+
+    @classmethod
+    def from_state_dict(cls, sd: Dict[str, object], device="cuda") -> "FastState":
+        t = [torch.as_tensor(sd[k]).to(device=device, dtype=torch.float32).contiguous()
+             for k in ("w_up", "w_gate", "w_down", "s_up", "s_gate", "s_down", "ln_weight", "ln_bias")]
+        for i in range(6):
+            if t[i].dim() == 2:
+                t[i] = t[i].unsqueeze(0)
+        return cls(*t, int(sd.get("step", 0)), float(sd.get("last_surprise_loss", 0.0)),
+                   list(sd.get("surprise_history", [])))
+
+
+def rope_tables(head_dim: int, n_pos: int, theta: float):
+    """FP32 cos/sin exactly as ``RotaryEmbedding._build_cache`` (``model/uttt_layer.py:910-933``)."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    t = torch.arange(0, n_pos, dtype=torch.float32)
+    freqs = torch.outer(t, inv_freq)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos(), emb.sin()
+
+
+def _seg(start, length, op, out, out_ld, aux=None, aux_ld=0, scale=0.0, out_f32=False):
+    return _lib.Segment(start, length, op, int(out_f32), out.data_ptr(), out_ld,
+                        None if aux is None else aux.data_ptr(), aux_ld, scale)
+
+
+class UtttB200:
+    def __init__(self, state_dict: Dict[str, torch.Tensor], cfg: ModelConfig, device="cuda",
+                 max_personas: int = 1, max_positions: Optional[int] = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        dev = self.device
+        self.lib = _lib.load()
+        d, hd = cfg.d_model, cfg.head_dim
+        if d % 128 != 0 or cfg.d_ff_fast % 8 != 0:
+            raise ValueError("B200 kernels need d_model % 128 == 0 and d_ff_fast % 8 == 0")
+
+        def bf(t):
+            return t.detach().to(device=dev, dtype=torch.bfloat16).contiguous()
+
+        def f32(t):
+            return t.detach().to(device=dev, dtype=torch.float32).contiguous()
+
+        sd = state_dict
+        self.emb = bf(sd["tok_embeddings.weight"])
+        head = sd.get("lm_head.weight")
+        self.lm_head = self.emb if head is None or head is sd["tok_embeddings.weight"] else bf(head)
+        self.layers = []
+        for i in range(cfg.n_layers):
+            p = f"layers.{i}."
+            self.layers.append(SimpleNamespace(
+                attn_norm=f32(sd[p + "attn_norm.weight"]),
+                wqkv=bf(torch.cat([sd[p + "attn.wq.weight"], sd[p + "attn.wk.weight"], sd[p + "attn.wv.weight"]])),
+                wo=bf(sd[p + "attn.wo.weight"]),
+                uttt_norm=f32(sd[p + "uttt_norm.weight"]),
+                w_q=bf(sd[p + "uttt.w_q.weight"]),
+                slow=bf(torch.cat([sd[p + "uttt.w_q.weight"], sd[p + "uttt.w_k.weight"], sd[p + "uttt.w_v.weight"],
+                                   sd[p + "uttt.w_eta.weight"], sd[p + "uttt.w_alpha.weight"]])),
+                w_o=bf(sd[p + "uttt.w_o.weight"]),
+                q_norm=f32(sd[p + "uttt.q_norm.weight"]),
+                k_norm=f32(sd[p + "uttt.k_norm.weight"]),
+                b_eta=f32(sd[p + "uttt.w_eta.bias"]),
+                b_alpha=f32(sd[p + "uttt.w_alpha.bias"]),
+            ))
+        self.norm = f32(sd["norm.weight"])
+        self.w0 = tuple(f32(sd["fast_weight_pool." + n]) for n in ("w_up_init", "w_gate_init", "w_down_init"))
+        self.ln_w = f32(sd["fast_weight_pool.ln_weight"])
+        self.ln_b = f32(sd["fast_weight_pool.ln_bias"])
+        n_pos = max_positions or (cfg.max_seq_len + 1024)
+        cos, sin = rope_tables(hd, n_pos, cfg.rope_theta)
+        self.rope_cos, self.rope_sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
+        self.n_pos = n_pos
+        self.active_limit = SIMPLE_ACTIVE_VOCAB_LIMIT if cfg.vocab_size >= 24000 else cfg.vocab_size
+        self.qkv_dim = (cfg.n_heads + 2 * cfg.n_kv_heads) * hd
+        self.max_personas = max_personas
+        shape = (max_personas, cfg.n_kv_heads, cfg.sliding_window_size, hd)
+        self.k_ring = [torch.zeros(shape, dtype=torch.bfloat16, device=dev) for _ in range(cfg.n_layers)]
+        self.v_ring = [torch.zeros(shape, dtype=torch.bfloat16, device=dev) for _ in range(cfg.n_layers)]
+
+    # ------------------------------------------------------------------ launch helpers
+    def _st(self) -> int:
+        return _stream(self.device)
+
+    def _linear(self, x: torch.Tensor, w: torch.Tensor, segs: Sequence[_lib.Segment]) -> None:
+        M, K = x.shape
+        N = w.shape[0]
+        arr = (_lib.Segment * len(segs))(*segs)
+        ws = workspace(self.lib.uttt_linear_workspace(M, N), self.device, slot=2)
+        _lib.check(self.lib.uttt_linear(M, N, K, x.data_ptr(), w.data_ptr(), len(segs), arr, self.cfg.rms_norm_eps,
+                                        ws.data_ptr(), ws.numel(), self._st()), "uttt_linear")
+
+    def _rmsnorm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        out = torch.empty_like(x)
+        rows, d = x.shape
+        _lib.check(self.lib.uttt_rmsnorm(rows, d, x.data_ptr(), x.stride(0), w.data_ptr(), self.cfg.rms_norm_eps,
+                                         out.data_ptr(), d, self._st()), "uttt_rmsnorm")
+        return out
+
+    def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        ids = ids.to(device=self.device, dtype=torch.int32).contiguous().reshape(-1)
+        out = torch.empty(ids.numel(), self.cfg.d_model, dtype=torch.bfloat16, device=self.device)
+        _lib.check(self.lib.uttt_embed(ids.numel(), self.cfg.d_model, ids.data_ptr(), self.emb.data_ptr(),
+                                       out.data_ptr(), self._st()), "uttt_embed")
+        return out
+
+    def _resid_linear(self, h: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> None:
+        """h += bf16(x W^T), in place (block residual adds, model/uttt_layer.py:1544-1554)."""
+        d = w.shape[0]
+        self._linear(x, w, [_seg(0, d, _lib.SEG_RESID, h, h.stride(0), h, h.stride(0))])
+
+    def _q_proj(self, layer, x2: torch.Tensor) -> torch.Tensor:
+        """``fused_fast_q_proj`` (model/uttt_layer.py:1175-1190)."""
+        d = self.cfg.d_model
+        q = torch.empty(x2.shape[0], d, dtype=torch.bfloat16, device=self.device)
+        self._linear(x2, layer.w_q, [_seg(0, d, _lib.SEG_RMSNORM, q, d, layer.q_norm)])
+        return q
+
+    def logits(self, h_last: torch.Tensor) -> torch.Tensor:
+        """Final RMSNorm + tied lm_head (BF16 output, as under autocast), returned as FP32."""
+        x = self._rmsnorm(h_last, self.norm)
+        V = self.lm_head.shape[0]
+        out = torch.empty(x.shape[0], V, dtype=torch.bfloat16, device=self.device)
+        self._linear(x, self.lm_head, [_seg(0, V, _lib.SEG_STORE, out, V)])
+        return out.float()
+
+    def greedy(self, logits: torch.Tensor, stop_free: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Device greedy pick; returns (ids int32 (B,), top-1/top-2 values (B, 2))."""
+        B, V = logits.shape
+        logits = logits.contiguous()
+        ids = torch.empty(B, dtype=torch.int32, device=self.device)
+        top2 = torch.empty(B, 2, dtype=torch.float32, device=self.device)
+        _lib.check(self.lib.uttt_greedy_argmax(B, V, logits.data_ptr(), 1, V, self.active_limit, int(stop_free),
+                                               ids.data_ptr(), top2.data_ptr(), self._st()), "uttt_greedy_argmax")
+        return ids, top2
+
+    def read_copies(self, w_up, w_gate, w_down) -> Tuple[torch.Tensor, torch.Tensor]:
+        """BF16 read copies of FP32 states (S, d, h) (``inference_read_weights``)."""
+        S, d, h = w_up.shape
+        packed = torch.empty(S, d, 2 * h, dtype=torch.bfloat16, device=self.device)
+        down = torch.empty(S, h, d, dtype=torch.bfloat16, device=self.device)
+        _lib.check(self.lib.uttt_pack_read_copies(S, d, h, w_up.data_ptr(), w_gate.data_ptr(), w_down.data_ptr(),
+                                                  packed.data_ptr(), down.data_ptr(), self._st()),
+                   "uttt_pack_read_copies")
+        return packed, down
+
+    def init_fast_state(self, batch_size: int = 1) -> FastState:
+        """``SharedFastWeightPool.init_state`` (detach=True), FP32 masters."""
+        rep = [w.unsqueeze(0).expand(batch_size, *w.shape).contiguous() for w in self.w0]
+        return FastState(*rep, *(torch.zeros_like(t) for t in rep), self.ln_w.clone(), self.ln_b.clone())
+
+    # ------------------------------------------------------------------ frozen path
+    def prefill(self, ids: torch.Tensor, slot: int, read_packed: torch.Tensor, read_down: torch.Tensor,
+                state_index: int = 0) -> torch.Tensor:
+        """Frozen forward of one persona's prompt; fills its KV ring; returns last-token logits (V,)."""
+        cfg = self.cfg
+        ids = ids.reshape(-1)
+        T = ids.numel()
+        d, hd, nh, nkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+        if T + 1 >= self.n_pos:
+            raise ValueError("prompt longer than the RoPE table")
+        dev = self.device
+        h = self._embed(ids)
+        slot_t = torch.tensor([slot], dtype=torch.int32, device=dev)
+        sidx = torch.tensor([state_index], dtype=torch.int32, device=dev)
+        qkv = torch.empty(T, self.qkv_dim, dtype=torch.bfloat16, device=dev)
+        qs = torch.empty(T, nh * hd, dtype=torch.bfloat16, device=dev)
+        kb = torch.empty(1, nkv, T, hd, dtype=torch.bfloat16, device=dev)
+        vb = torch.empty_like(kb)
+        att = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
+        for i, lay in enumerate(self.layers):
+            x = self._rmsnorm(h, lay.attn_norm)
+            self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
+            _lib.check(self.lib.uttt_attn_prefill(1, T, 0, 0, nh, nkv, hd, cfg.sliding_window_size, qkv.data_ptr(),
+                                                  self.qkv_dim, self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+                                                  qs.data_ptr(), kb.data_ptr(), vb.data_ptr(), att.data_ptr(),
+                                                  self._st()), "uttt_attn_prefill")
+            _lib.check(self.lib.uttt_kv_ring_fill(1, T, T, nkv, hd, cfg.sliding_window_size, kb.data_ptr(),
+                                                  vb.data_ptr(), slot_t.data_ptr(), self.k_ring[i].data_ptr(),
+                                                  self.v_ring[i].data_ptr(), self._st()), "uttt_kv_ring_fill")
+            self._resid_linear(h, att, lay.wo)
+            q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
+            r = fast_readout(q.unsqueeze(0), read_packed, None, read_down, self.ln_w, self.ln_b, cfg.rms_norm_eps,
+                             state_index=sidx, packed=True)
+            self._resid_linear(h, r.reshape(T, d), lay.w_o)
+        return self.logits(h[-1:].contiguous())[0]
+
+    def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor, read_packed: torch.Tensor,
+                    read_down: torch.Tensor, state_index: torch.Tensor) -> torch.Tensor:
+        """One new token for each of B rows (packed multi-persona decode); returns logits (B, V) FP32."""
+        cfg = self.cfg
+        B = tokens.numel()
+        d, hd, nh, nkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+        dev = self.device
+        pos = pos.to(device=dev, dtype=torch.int32).contiguous()
+        slots = slots.to(device=dev, dtype=torch.int32).contiguous()
+        sidx = state_index.to(device=dev, dtype=torch.int32).contiguous()
+        h = self._embed(tokens)
+        qkv = torch.empty(B, self.qkv_dim, dtype=torch.bfloat16, device=dev)
+        att = torch.empty(B, d, dtype=torch.bfloat16, device=dev)
+        for i, lay in enumerate(self.layers):
+            x = self._rmsnorm(h, lay.attn_norm)
+            self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
+            _lib.check(self.lib.uttt_attn_decode(B, nh, nkv, hd, cfg.sliding_window_size, qkv.data_ptr(),
+                                                 self.qkv_dim, pos.data_ptr(), slots.data_ptr(),
+                                                 self.k_ring[i].data_ptr(), self.v_ring[i].data_ptr(),
+                                                 self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), att.data_ptr(),
+                                                 d, self._st()), "uttt_attn_decode")
+            self._resid_linear(h, att, lay.wo)
+            q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
+            r = fast_readout(q.unsqueeze(1), read_packed, None, read_down, self.ln_w, self.ln_b, cfg.rms_norm_eps,
+                             state_index=sidx, packed=True)
+            self._resid_linear(h, r.reshape(B, d), lay.w_o)
+        return self.logits(h)
+
+    def generate_greedy(self, prompt: torch.Tensor, state: FastState, n_tokens: int, slot: int = 0,
+                        stop_free: bool = True) -> Tuple[List[int], List[float], List[torch.Tensor]]:
+        """``stream_generate`` at temperature 0 for one persona (stop-free greedy by default)."""
+        packed, down = self.read_copies(state.w_up, state.w_gate, state.w_down)
+        logits = self.prefill(prompt, slot, packed, down, 0).unsqueeze(0)
+        pos = prompt.numel()
+        ids, margins, all_logits = [], [], []
+        zero = torch.zeros(1, dtype=torch.int32, device=self.device)
+        slot_t = torch.full((1,), slot, dtype=torch.int32, device=self.device)
+        for _ in range(n_tokens):
+            all_logits.append(logits[0])
+            tok, top2 = self.greedy(logits, stop_free)
+            t = int(tok.item())
+            if not stop_free and t in (USER_ID, ASSISTANT_ID):
+                break
+            ids.append(t)
+            tv = top2[0].tolist()
+            margins.append(tv[0] - tv[1])
+            if len(ids) == n_tokens:
+                break
+            logits = self.decode_step(tok, torch.full((1,), pos, dtype=torch.int32, device=self.device), slot_t,
+                                      packed, down, zero)
+            pos += 1
+        return ids, margins, all_logits
+
+    def teacher_forced_logits(self, prompt: torch.Tensor, forced: Sequence[int], state: FastState,
+                              slot: int = 0) -> List[torch.Tensor]:
+        packed, down = self.read_copies(state.w_up, state.w_gate, state.w_down)
+        out = [self.prefill(prompt, slot, packed, down, 0)]
+        pos = prompt.numel()
+        zero = torch.zeros(1, dtype=torch.int32, device=self.device)
+        slot_t = torch.full((1,), slot, dtype=torch.int32, device=self.device)
+        for tok in list(forced)[:-1]:
+            lg = self.decode_step(torch.tensor([tok], dtype=torch.int32, device=self.device),
+                                  torch.full((1,), pos, dtype=torch.int32, device=self.device), slot_t, packed, down,
+                                  zero)
+            out.append(lg[0])
+            pos += 1
+        return out
+
+    # ------------------------------------------------------------------ write path
+    def test_time_update(self, interaction_ids: torch.Tensor, fast_state: FastState,
+                         attention_mask: Optional[torch.Tensor] = None) -> Tuple[FastState, float, List[float]]:
+        """``uTTTModel.test_time_update`` (model/uttt_model.py:1237-1271) for one persona."""
+        cfg = self.cfg
+        dev = self.device
+        ids = interaction_ids.reshape(-1)
+        T = ids.numel()
+        C, W = cfg.chunk_size, cfg.sliding_window_size
+        d, hd, nh, nkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+        if C > 64:
+            raise ValueError("chunk_size > 64 is not supported by the B200 write kernels")
+        cur = fast_state.clone()
+        mask = None if attention_mask is None else attention_mask.reshape(1, T).to(device=dev,
+                                                                                 dtype=torch.float32).contiguous()
+        h_all = self._embed(ids)
+        hist_k: List[Optional[torch.Tensor]] = [None] * cfg.n_layers
+        hist_v: List[Optional[torch.Tensor]] = [None] * cfg.n_layers
+        chunk_losses, counts = [], []
+        for off in range(0, T, C):
+            Cc = min(C, T - off)
+            rp, rd = self.read_copies(cur.w_up, cur.w_gate, cur.w_down)      # chunk-start snapshot
+            hidden = h_all[off:off + Cc].clone()
+            m = None if mask is None else mask[:, off:off + Cc].contiguous()
+            layer_loss = []
+            for i, lay in enumerate(self.layers):
+                x = self._rmsnorm(hidden, lay.attn_norm)
+                qkv = torch.empty(Cc, self.qkv_dim, dtype=torch.bfloat16, device=dev)
+                self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
+                hist = 0 if hist_k[i] is None else hist_k[i].shape[2]
+                kb = torch.empty(1, nkv, hist + Cc, hd, dtype=torch.bfloat16, device=dev)
+                vb = torch.empty_like(kb)
+                if hist:
+                    kb[:, :, :hist].copy_(hist_k[i])
+                    vb[:, :, :hist].copy_(hist_v[i])
+                qs = torch.empty(Cc, nh * hd, dtype=torch.bfloat16, device=dev)
+                att = torch.empty(Cc, d, dtype=torch.bfloat16, device=dev)
+                _lib.check(self.lib.uttt_attn_prefill(1, Cc, off, hist, nh, nkv, hd, W, qkv.data_ptr(), self.qkv_dim,
+                                                      self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+                                                      qs.data_ptr(), kb.data_ptr(), vb.data_ptr(), att.data_ptr(),
+                                                      self._st()), "uttt_attn_prefill")
+                keep = min(W - 1, hist + Cc)
+                hist_k[i] = kb[:, :, hist + Cc - keep:].contiguous()
+                hist_v[i] = vb[:, :, hist + Cc - keep:].contiguous()
+                hh = hidden.clone()
+                self._resid_linear(hh, att, lay.wo)
+                x2 = self._rmsnorm(hh, lay.uttt_norm)
+                q = torch.empty(Cc, d, dtype=torch.bfloat16, device=dev)
+                k = torch.empty(1, Cc, d, dtype=torch.bfloat16, device=dev)
+                v = torch.empty(1, Cc, d, dtype=torch.bfloat16, device=dev)
+                eta = torch.empty(1, Cc, dtype=torch.float32, device=dev)
+                alpha = torch.empty(1, Cc, dtype=torch.float32, device=dev)
+                self._linear(x2, lay.slow, [                       # fused_slow_projections, :1193-1231
+                    _seg(0, d, _lib.SEG_RMSNORM, q, d, lay.q_norm),
+                    _seg(d, d, _lib.SEG_RMSNORM, k, d, lay.k_norm),
+                    _seg(2 * d, d, _lib.SEG_RMSNORM, v, d),
+                    _seg(3 * d, 1, _lib.SEG_SIGMOID, eta, 1, lay.b_eta, 0, cfg.base_inner_lr, out_f32=True),
+                    _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, alpha, 1, lay.b_alpha, 0, cfg.base_weight_decay,
+                         out_f32=True),
+                ])
+                out = fast_readout(q.unsqueeze(0), rp, None, rd, cur.ln_weight, cur.ln_bias, cfg.rms_norm_eps,
+                                   packed=True)
+                loss = torch.empty(1, Cc, dtype=torch.float32, device=dev)
+                chunk_write(k, v, eta, alpha, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,
+                            cur.ln_weight, cur.ln_bias, m, cfg.momentum_beta, float(cfg.max_inner_grad_norm or 0.0),
+                            cfg.normalize_loss_by_dim, cfg.rms_norm_eps, chunk_size=Cc, token_loss=loss)
+                if m is None:
+                    layer_loss.append(loss.mean())
+                else:
+                    layer_loss.append((loss * m).sum() / m.sum().clamp_min(1.0))
+                self._resid_linear(hh, out.reshape(Cc, d), lay.w_o)
+                hidden = hh
+            chunk_losses.append(torch.stack(layer_loss))
+            counts.append(m.sum() if m is not None else torch.tensor(float(Cc), device=dev))
+            cur.step += cfg.n_layers
+        check_status(workspace(0, dev), "test_time_update")
+        cnt = torch.stack(counts).to(torch.float64)
+        per_layer_t = (torch.stack(chunk_losses).to(torch.float64) * cnt[:, None]).sum(0) / cnt.sum().clamp_min(1.0)
+        per_layer = [float(x) for x in per_layer_t.float().tolist()]
+        cur.last_surprise_loss = sum(per_layer) / max(len(per_layer), 1)
+        cur.surprise_history = (list(fast_state.surprise_history) + per_layer)[-100:]
+        return cur, cur.last_surprise_loss, per_layer
