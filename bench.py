@@ -207,6 +207,122 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+# ----------------------------------------------------------------------------- decode + write (config 3)
+DEC = dict(personas=32, prompt_min=64, prompt_max=1024, new_tokens=128, warmup_tokens=3, perturb_std=1e-3)
+
+
+def decode_workload(device, rank, lib):
+    """32 personas of the ~151M-class model (d=768, 12 layers, h=2048,
+    V=32000, window 512), W_p = W_0 + N(0, 1e-3), ragged prompts uniform in [64, 1024]
+    with uniform ids; greedy decode of 128 tokens per persona as ONE packed batch per
+    step (captured CUDA graph), then one chunk-TTT write per persona on prompt+reply
+    (all personas in one batched write, right-padded to a multiple of 64 with masks)."""
+    from utttcompanion_b200 import _lib
+    from utttcompanion_b200.model import DecodeGraph, FastState, UtttB200
+    from utttcompanion_b200.workloads import CONFIG_151M, perturbed_persona_states, reference_init_state_dict
+    cfg = CONFIG_151M
+    P = DEC["personas"]
+    sd = reference_init_state_dict(cfg, seed=0)
+    eng = UtttB200(sd, cfg, device=device, max_personas=P, max_positions=DEC["prompt_max"] + 512)
+    w_up, w_gate, w_down = perturbed_persona_states(sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"],
+                                                    sd["fast_weight_pool.w_down_init"], P, DEC["perturb_std"],
+                                                    seed=100 + rank, device=device)
+    packed, down = eng.read_copies(w_up, w_gate, w_down)
+    graph = DecodeGraph(eng, P, packed, down)          # before prefill: its warm-up touches ring slot 0
+    g = torch.Generator().manual_seed(7 + rank)
+    lens = torch.randint(DEC["prompt_min"], DEC["prompt_max"] + 1, (P,), generator=g).tolist()
+    prompts = [torch.randint(6, cfg.vocab_size, (n,), generator=g) for n in lens]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = torch.stack([eng.prefill(prompts[p], p, packed, down, p) for p in range(P)])
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    ids, _ = eng.greedy(first)
+    tokens = ids.clone()
+    pos = torch.tensor(lens, dtype=torch.int32, device=device)
+    generated = [tokens.clone()]
+    for _ in range(DEC["warmup_tokens"]):
+        ids, _ = graph.step(tokens, pos)
+        tokens.copy_(ids)
+        pos += 1
+        generated.append(tokens.clone())
+    steps = DEC["new_tokens"] - 1 - DEC["warmup_tokens"]
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        ids, _ = graph.step(tokens, pos)
+        tokens.copy_(ids)
+        pos += 1
+        generated.append(tokens.clone())
+    e1.record()
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1) / steps
+    # end to end: the serving loop reads every step's ids back to the host (as stream_generate's
+    # per-token .item(), model/uttt_model.py:1038) and feeds the next tokens from pinned host memory
+    hid = torch.empty(P, dtype=torch.int32).pin_memory()
+    htok = torch.empty(P, dtype=torch.int32).pin_memory()
+    htok.copy_(tokens)
+    e2e_steps = 16
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        tokens.copy_(htok, non_blocking=True)
+        ids, _ = graph.step(tokens, pos)
+        hid.copy_(ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        htok.copy_(hid)
+        pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    # live kernel timing of one eager step (same kernels as the graph)
+    lib.uttt_profile_enable(1)
+    eng.decode_step(tokens, pos, graph.slots, packed, down, graph.sidx)
+    ms = np.zeros(16, np.float32)
+    cnt = np.zeros(16, np.int32)
+    _lib.check(lib.uttt_profile_read(ms.ctypes.data, cnt.ctypes.data), "profile_read")
+    lib.uttt_profile_enable(0)
+    readout_s = ms[4] / max(cnt[4], 1) / 1e3
+    readout_bytes = P * 3.0 * cfg.d_model * cfg.d_ff_fast * 2.0      # BF16 read copies of every persona
+    # one write per persona on prompt + reply (personalizer.py:483-512), batched over personas
+    gen = torch.stack(generated, dim=1).cpu()                          # (P, new_tokens)
+    turns = [prompts[p].tolist() + gen[p].tolist() for p in range(P)]
+    Tmax = max(len(t) for t in turns)
+    Tpad = ((Tmax + 63) // 64) * 64
+    inter = torch.zeros(P, Tpad, dtype=torch.long)
+    mask = torch.zeros(P, Tpad)
+    for p, t in enumerate(turns):
+        inter[p, :len(t)] = torch.tensor(t)
+        mask[p, :len(t)] = 1.0
+    st = FastState(w_up, w_gate, w_down, torch.zeros_like(w_up), torch.zeros_like(w_gate), torch.zeros_like(w_down),
+                   eng.ln_w.clone(), eng.ln_b.clone())
+    eng.test_time_update_batch(inter[:, :64], st, mask[:, :64])      # warm-up (workspaces); st is not modified
+    torch.cuda.synchronize()
+    e0.record()
+    new, surprises, _ = eng.test_time_update_batch(inter, st, mask)
+    e1.record()
+    torch.cuda.synchronize()
+    write_ms = e0.elapsed_time(e1)
+    valid = float(mask.sum())
+    return {
+        "workload": "packed multi-persona greedy decode + per-turn chunk-TTT write (BASELINE config 3)",
+        "model": "uTTT ~76.5M (d=768, 12 layers, 12/4 heads, h=2048, V=32000, window 512), reference seed-0 init",
+        "personas": P, "prompt_tokens": {"min": min(lens), "max": max(lens), "mean": float(np.mean(lens))},
+        "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,
+        "decode_e2e_tok_s": P / (e2e_ms / 1e3),
+        "prefill_s_total": prefill_s,
+        "write_tok_s": valid / (write_ms / 1e3), "write_padded_tok_s": P * Tpad / (write_ms / 1e3),
+        "write_ms": write_ms, "mean_surprise": float(np.mean(surprises)),
+        "readout_roofline": {"bound": "hbm", "kernel": "readout_gemv (+ read-copy decode path)",
+                             "achieved": readout_bytes / readout_s / 1e9, "unit": "GB/s",
+                             "algorithmic_bytes_per_launch": readout_bytes, "avg_ms": readout_s * 1e3},
+        "decode_kernels_ms": {k: float(ms[i]) for i, k in enumerate(
+            ["chunk_fwd", "chunk_ln", "chunk_norm", "chunk_bwd", "readout", "readout_ln", "gemm", "finish",
+             "attn", "rowwise", "argmax"]) if cnt[i]},
+    }
+
+
 # ----------------------------------------------------------------------------- arms
 def reference_arm(args, world, rank):
     if rank != 0:
@@ -369,6 +485,11 @@ def ours_arm(args, world, rank, local):
             "kernels": per_kind,
             "clocks": clk,
         }
+        if not args.no_decode:
+            dec = decode_workload(device, rank, lib)
+            dec["readout_roofline"]["peak"] = hbm
+            dec["readout_roofline"]["frac"] = dec["readout_roofline"]["achieved"] / hbm
+            line["decode"] = dec
         if world == 1 and not args.no_cpu_baseline:
             v, n, el = cpu_baseline()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
@@ -389,6 +510,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode + write workload")
     ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")
     ap.add_argument("--tokens", type=int, default=None, help="override tokens per state (profiling cases)")
     args = ap.parse_args()

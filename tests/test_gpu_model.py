@@ -182,3 +182,84 @@ def test_packed_multi_persona_decode_equals_per_persona_decode():
         a, b = one[0].cpu().numpy(), packed_logits[p].cpu().numpy()
         assert np.max(np.abs(a - b)) <= 1e-2, p
         assert int(np.argmax(_mask(a, cfg.vocab_size))) == int(np.argmax(_mask(b, cfg.vocab_size)))
+
+
+def _tiny_cfg():
+    return ModelConfig(vocab_size=2048, d_model=256, n_layers=2, n_heads=4, n_kv_heads=2, d_ff_fast=384,
+                       sliding_window_size=32, chunk_size=64, max_seq_len=512)
+
+
+def test_batched_write_equals_per_persona_writes():
+    """test_time_update_batch over ragged personas == each persona's own test_time_update.
+
+    The two runs pack different row counts, so the projection GEMMs pick a
+    different split-K and accumulate in a different order; BF16 rounding of
+    the activations then differs by a ULP here and there.  Bounds: masters
+    rel-L2 <= 1e-4, momentum (the accumulated step) <= 1e-2, surprise 1e-3."""
+    cfg = _tiny_cfg()
+    sd = reference_init_state_dict(cfg, seed=9)
+    eng = UtttB200(sd, cfg)
+    from utttcompanion_b200.workloads import perturbed_persona_states
+    P = 3
+    w = perturbed_persona_states(sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"],
+                                 sd["fast_weight_pool.w_down_init"], P, std=1e-2, seed=4)
+    st = FastState(*w, *(torch.zeros_like(x) for x in w), eng.ln_w.clone(), eng.ln_b.clone())
+    lens = [150, 64, 97]
+    Tpad = 192
+    gen = torch.Generator().manual_seed(2)
+    ids = torch.randint(6, cfg.vocab_size, (P, Tpad), generator=gen)
+    mask = torch.zeros(P, Tpad)
+    for p, n in enumerate(lens):
+        mask[p, :n] = 1
+    new, surprises, per_layer = eng.test_time_update_batch(ids, st, mask)
+    torch.cuda.synchronize()
+    for p in range(P):
+        one = FastState(*(x[p:p + 1].clone() for x in (st.w_up, st.w_gate, st.w_down, st.s_up, st.s_gate, st.s_down)),
+                        st.ln_weight, st.ln_bias)
+        n1, s1, pl1 = eng.test_time_update(ids[p], one, mask[p])
+        torch.cuda.synchronize()
+        for name in ("w_up", "w_gate", "w_down", "s_up", "s_down"):
+            a = getattr(new, name)[p].cpu().numpy()
+            b = getattr(n1, name)[0].cpu().numpy()
+            bound = 1e-4 if name.startswith("w") else 1e-2
+            assert rel_l2(a, b) < bound, (p, name, rel_l2(a, b))
+        assert abs(surprises[p] - s1) <= 1e-3 * abs(s1)
+        np.testing.assert_allclose(per_layer[p], pl1, rtol=1e-3)
+
+
+def test_decode_graph_replay_equals_eager_steps():
+    from utttcompanion_b200.model import DecodeGraph
+    from utttcompanion_b200.workloads import perturbed_persona_states
+    cfg = _tiny_cfg()
+    sd = reference_init_state_dict(cfg, seed=6)
+    P = 3
+    eng = UtttB200(sd, cfg, max_personas=P)
+    w = perturbed_persona_states(sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"],
+                                 sd["fast_weight_pool.w_down_init"], P, std=1e-2, seed=8)
+    packed, down = eng.read_copies(*w)
+    graph = DecodeGraph(eng, P, packed, down)
+    gen = torch.Generator().manual_seed(3)
+    lens = [12, 45, 30]
+    firsts = [eng.prefill(torch.randint(6, cfg.vocab_size, (n,), generator=gen), p, packed, down, p)
+              for p, n in enumerate(lens)]
+    toks, _ = eng.greedy(torch.stack(firsts))
+    pos = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    k_save = [k.clone() for k in eng.k_ring]
+    v_save = [v.clone() for v in eng.v_ring]
+    t_graph, p_graph = toks.clone(), pos.clone()
+    graph_logits = []
+    for _ in range(5):
+        ids, lg = graph.step(t_graph, p_graph)
+        graph_logits.append(lg.clone())
+        t_graph = ids.clone()
+        p_graph = p_graph + 1
+    for i in range(cfg.n_layers):
+        eng.k_ring[i].copy_(k_save[i])
+        eng.v_ring[i].copy_(v_save[i])
+    t_e, p_e = toks.clone(), pos.clone()
+    slots = torch.arange(P, dtype=torch.int32, device="cuda")
+    for s in range(5):
+        lg = eng.decode_step(t_e, p_e, slots, packed, down, slots)
+        assert torch.max(torch.abs(lg - graph_logits[s])).item() <= 1e-2, s
+        t_e, _ = eng.greedy(lg)
+        p_e = p_e + 1

@@ -134,6 +134,9 @@ class UtttB200:
         self.w0 = tuple(f32(sd["fast_weight_pool." + n]) for n in ("w_up_init", "w_gate_init", "w_down_init"))
         self.ln_w = f32(sd["fast_weight_pool.ln_weight"])
         self.ln_b = f32(sd["fast_weight_pool.ln_bias"])
+        # readout LayerNorm affine as the BF16 path applies it (ln.to(x.dtype), model/uttt_layer.py:253-257)
+        self.ln_w_act = self.ln_w.to(torch.bfloat16).float().contiguous()
+        self.ln_b_act = self.ln_b.to(torch.bfloat16).float().contiguous()
         n_pos = max_positions or (cfg.max_seq_len + 1024)
         cos, sin = rope_tables(hd, n_pos, cfg.rope_theta)
         self.rope_cos, self.rope_sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
@@ -247,8 +250,8 @@ class UtttB200:
                                                   self.v_ring[i].data_ptr(), self._st()), "uttt_kv_ring_fill")
             self._resid_linear(h, att, lay.wo)
             q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
-            r = fast_readout(q.unsqueeze(0), read_packed, None, read_down, self.ln_w, self.ln_b, cfg.rms_norm_eps,
-                             state_index=sidx, packed=True)
+            r = fast_readout(q.unsqueeze(0), read_packed, None, read_down, self.ln_w_act, self.ln_b_act,
+                             cfg.rms_norm_eps, state_index=sidx, packed=True, ln_prepared=True)
             self._resid_linear(h, r.reshape(T, d), lay.w_o)
         return self.logits(h[-1:].contiguous())[0]
 
@@ -275,8 +278,8 @@ class UtttB200:
                                                  d, self._st()), "uttt_attn_decode")
             self._resid_linear(h, att, lay.wo)
             q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
-            r = fast_readout(q.unsqueeze(1), read_packed, None, read_down, self.ln_w, self.ln_b, cfg.rms_norm_eps,
-                             state_index=sidx, packed=True)
+            r = fast_readout(q.unsqueeze(1), read_packed, None, read_down, self.ln_w_act, self.ln_b_act,
+                             cfg.rms_norm_eps, state_index=sidx, packed=True, ln_prepared=True)
             self._resid_linear(h, r.reshape(B, d), lay.w_o)
         return self.logits(h)
 
@@ -324,40 +327,58 @@ class UtttB200:
     def test_time_update(self, interaction_ids: torch.Tensor, fast_state: FastState,
                          attention_mask: Optional[torch.Tensor] = None) -> Tuple[FastState, float, List[float]]:
         """``uTTTModel.test_time_update`` (model/uttt_model.py:1237-1271) for one persona."""
+        new, surprises, per_layer = self.test_time_update_batch(interaction_ids.reshape(1, -1), fast_state,
+                                                                None if attention_mask is None
+                                                                else attention_mask.reshape(1, -1))
+        return new, surprises[0], per_layer[0]
+
+    def test_time_update_batch(self, interaction_ids: torch.Tensor, fast_state: FastState,
+                               attention_mask: Optional[torch.Tensor] = None):
+        """The write of B personas at once: rows of ``interaction_ids`` (B, T) with
+        right-padding masks; ``fast_state`` holds B stacked states.  Every chunk of
+        every layer is one packed launch sequence over all rows; a row whose
+        chunk is all padding keeps its state exactly (model/uttt_layer.py:513-520).
+        Returns (new stacked state, per-row mean surprise, per-row per-layer surprise).
+        Per-row statistics follow the reference's single-persona definitions
+        (model/uttt_model.py:598-607, 833-838)."""
         cfg = self.cfg
         dev = self.device
-        ids = interaction_ids.reshape(-1)
-        T = ids.numel()
+        ids = interaction_ids.to(device=dev)
+        B, T = ids.shape
         C, W = cfg.chunk_size, cfg.sliding_window_size
         d, hd, nh, nkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
         if C > 64:
             raise ValueError("chunk_size > 64 is not supported by the B200 write kernels")
+        if fast_state.w_up.shape[0] != B:
+            raise ValueError(f"fast_state holds {fast_state.w_up.shape[0]} states for {B} rows")
         cur = fast_state.clone()
-        mask = None if attention_mask is None else attention_mask.reshape(1, T).to(device=dev,
+        mask = None if attention_mask is None else attention_mask.reshape(B, T).to(device=dev,
                                                                                  dtype=torch.float32).contiguous()
-        h_all = self._embed(ids)
+        h_all = self._embed(ids).reshape(B, T, d)
         hist_k: List[Optional[torch.Tensor]] = [None] * cfg.n_layers
         hist_v: List[Optional[torch.Tensor]] = [None] * cfg.n_layers
+        rows_idx = torch.arange(B, dtype=torch.int32, device=dev)
         chunk_losses, counts = [], []
         for off in range(0, T, C):
             Cc = min(C, T - off)
+            R = B * Cc
             rp, rd = self.read_copies(cur.w_up, cur.w_gate, cur.w_down)      # chunk-start snapshot
-            hidden = h_all[off:off + Cc].clone()
+            hidden = h_all[:, off:off + Cc].reshape(R, d).clone()
             m = None if mask is None else mask[:, off:off + Cc].contiguous()
             layer_loss = []
             for i, lay in enumerate(self.layers):
                 x = self._rmsnorm(hidden, lay.attn_norm)
-                qkv = torch.empty(Cc, self.qkv_dim, dtype=torch.bfloat16, device=dev)
+                qkv = torch.empty(R, self.qkv_dim, dtype=torch.bfloat16, device=dev)
                 self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
                 hist = 0 if hist_k[i] is None else hist_k[i].shape[2]
-                kb = torch.empty(1, nkv, hist + Cc, hd, dtype=torch.bfloat16, device=dev)
+                kb = torch.empty(B, nkv, hist + Cc, hd, dtype=torch.bfloat16, device=dev)
                 vb = torch.empty_like(kb)
                 if hist:
                     kb[:, :, :hist].copy_(hist_k[i])
                     vb[:, :, :hist].copy_(hist_v[i])
-                qs = torch.empty(Cc, nh * hd, dtype=torch.bfloat16, device=dev)
-                att = torch.empty(Cc, d, dtype=torch.bfloat16, device=dev)
-                _lib.check(self.lib.uttt_attn_prefill(1, Cc, off, hist, nh, nkv, hd, W, qkv.data_ptr(), self.qkv_dim,
+                qs = torch.empty(R, nh * hd, dtype=torch.bfloat16, device=dev)
+                att = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
+                _lib.check(self.lib.uttt_attn_prefill(B, Cc, off, hist, nh, nkv, hd, W, qkv.data_ptr(), self.qkv_dim,
                                                       self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
                                                       qs.data_ptr(), kb.data_ptr(), vb.data_ptr(), att.data_ptr(),
                                                       self._st()), "uttt_attn_prefill")
@@ -367,11 +388,11 @@ class UtttB200:
                 hh = hidden.clone()
                 self._resid_linear(hh, att, lay.wo)
                 x2 = self._rmsnorm(hh, lay.uttt_norm)
-                q = torch.empty(Cc, d, dtype=torch.bfloat16, device=dev)
-                k = torch.empty(1, Cc, d, dtype=torch.bfloat16, device=dev)
-                v = torch.empty(1, Cc, d, dtype=torch.bfloat16, device=dev)
-                eta = torch.empty(1, Cc, dtype=torch.float32, device=dev)
-                alpha = torch.empty(1, Cc, dtype=torch.float32, device=dev)
+                q = torch.empty(B, Cc, d, dtype=torch.bfloat16, device=dev)
+                k = torch.empty(B, Cc, d, dtype=torch.bfloat16, device=dev)
+                v = torch.empty(B, Cc, d, dtype=torch.bfloat16, device=dev)
+                eta = torch.empty(B, Cc, dtype=torch.float32, device=dev)
+                alpha = torch.empty(B, Cc, dtype=torch.float32, device=dev)
                 self._linear(x2, lay.slow, [                       # fused_slow_projections, :1193-1231
                     _seg(0, d, _lib.SEG_RMSNORM, q, d, lay.q_norm),
                     _seg(d, d, _lib.SEG_RMSNORM, k, d, lay.k_norm),
@@ -380,25 +401,81 @@ class UtttB200:
                     _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, alpha, 1, lay.b_alpha, 0, cfg.base_weight_decay,
                          out_f32=True),
                 ])
-                out = fast_readout(q.unsqueeze(0), rp, None, rd, cur.ln_weight, cur.ln_bias, cfg.rms_norm_eps,
-                                   packed=True)
-                loss = torch.empty(1, Cc, dtype=torch.float32, device=dev)
+                out = fast_readout(q, rp, None, rd, cur.ln_weight, cur.ln_bias, cfg.rms_norm_eps,
+                                   state_index=rows_idx, packed=True)
+                loss = torch.empty(B, Cc, dtype=torch.float32, device=dev)
                 chunk_write(k, v, eta, alpha, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,
                             cur.ln_weight, cur.ln_bias, m, cfg.momentum_beta, float(cfg.max_inner_grad_norm or 0.0),
                             cfg.normalize_loss_by_dim, cfg.rms_norm_eps, chunk_size=Cc, token_loss=loss)
                 if m is None:
-                    layer_loss.append(loss.mean())
+                    layer_loss.append(loss.mean(dim=1))
                 else:
-                    layer_loss.append((loss * m).sum() / m.sum().clamp_min(1.0))
-                self._resid_linear(hh, out.reshape(Cc, d), lay.w_o)
+                    layer_loss.append((loss * m).sum(dim=1) / m.sum(dim=1).clamp_min(1.0))
+                self._resid_linear(hh, out.reshape(R, d), lay.w_o)
                 hidden = hh
-            chunk_losses.append(torch.stack(layer_loss))
-            counts.append(m.sum() if m is not None else torch.tensor(float(Cc), device=dev))
+            chunk_losses.append(torch.stack(layer_loss, dim=1))                    # (B, L)
+            counts.append(m.sum(dim=1) if m is not None else torch.full((B,), float(Cc), device=dev))
             cur.step += cfg.n_layers
         check_status(workspace(0, dev), "test_time_update")
-        cnt = torch.stack(counts).to(torch.float64)
-        per_layer_t = (torch.stack(chunk_losses).to(torch.float64) * cnt[:, None]).sum(0) / cnt.sum().clamp_min(1.0)
-        per_layer = [float(x) for x in per_layer_t.float().tolist()]
-        cur.last_surprise_loss = sum(per_layer) / max(len(per_layer), 1)
-        cur.surprise_history = (list(fast_state.surprise_history) + per_layer)[-100:]
-        return cur, cur.last_surprise_loss, per_layer
+        cnt = torch.stack(counts, dim=1).to(torch.float64)                          # (B, n_chunks)
+        losses = torch.stack(chunk_losses, dim=1).to(torch.float64)                # (B, n_chunks, L)
+        per_layer_t = (losses * cnt[:, :, None]).sum(1) / cnt.sum(1, keepdim=True).clamp_min(1.0)
+        per_layer = [[float(x) for x in row] for row in per_layer_t.float().tolist()]   # single sync
+        means = [sum(r) / max(len(r), 1) for r in per_layer]
+        cur.last_surprise_loss = means[0] if B == 1 else float(sum(means) / B)
+        cur.surprise_history = (list(fast_state.surprise_history) + (per_layer[0] if B == 1 else []))[-100:]
+        return cur, means, per_layer
+
+
+class DecodeGraph:
+    """A packed decode step (+ greedy pick) captured once in a CUDA graph.
+
+    The B200 counterpart of ``CUDAGraphDecoder`` (``engine/inference.py:71-302``)
+    for a packed batch: static device buffers hold each row's token, position,
+    KV slot and fast-weight state index; ``step`` copies the new inputs in,
+    replays, and returns (greedy ids, logits) from static outputs that stay
+    valid until the next replay.  The read copies and KV rings it captured
+    must stay allocated.
+    """
+
+    def __init__(self, engine: "UtttB200", batch: int, read_packed: torch.Tensor, read_down: torch.Tensor,
+                 stop_free: bool = True):
+        self.engine = engine
+        dev = engine.device
+        self.batch = batch
+        self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
+        self.sidx = torch.arange(batch, dtype=torch.int32, device=dev)
+        self.read_packed, self.read_down = read_packed, read_down
+        self.stop_free = stop_free
+        # warm up (workspaces, kernel attributes) on a side stream, then capture;
+        # the warm-up writes ring slot 0 of every row's persona, which the
+        # caller's next step overwrites before any read (positions start >= 0).
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self._body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=side):
+            self.logits, self.ids, self.top2 = self._body()
+        torch.cuda.synchronize(dev)
+
+    def _body(self):
+        lg = self.engine.decode_step(self.tokens, self.pos, self.slots, self.read_packed, self.read_down, self.sidx)
+        ids, top2 = self.engine.greedy(lg, self.stop_free)
+        return lg, ids, top2
+
+    def step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Tensor] = None,
+             state_index: Optional[torch.Tensor] = None):
+        self.tokens.copy_(tokens, non_blocking=True)
+        self.pos.copy_(pos, non_blocking=True)
+        if slots is not None:
+            self.slots.copy_(slots, non_blocking=True)
+        if state_index is not None:
+            self.sidx.copy_(state_index, non_blocking=True)
+        self.graph.replay()
+        return self.ids, self.logits

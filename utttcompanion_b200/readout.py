@@ -20,8 +20,14 @@ from .fastweight import _ptr, _require_cuda, _stream, workspace
 def fast_readout(x: torch.Tensor, w_up: torch.Tensor, w_gate: Optional[torch.Tensor], w_down: torch.Tensor,
                  ln_weight: torch.Tensor, ln_bias: torch.Tensor, eps: float = 1e-5,
                  state_index: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-                 packed: bool = False) -> torch.Tensor:
-    """f_W(x) for (B, T, d) ``x``.  ``packed``: ``w_up`` is the BF16 [W_up | W_gate] copy."""
+                 packed: bool = False, ln_prepared: bool = False,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """f_W(x) for (B, T, d) ``x``.  ``packed``: ``w_up`` is the BF16 [W_up | W_gate] copy.
+
+    ``ln_prepared``: ``ln_weight``/``ln_bias`` are already FP32 contiguous and
+    rounded to the activation dtype (skips two casts per call, e.g. inside a
+    captured decode graph).  ``out``: preallocated BF16 (B, T, d) output.
+    """
     _require_cuda(x, w_up, w_down)
     if x.dim() != 3:
         raise ValueError("x must be (B, T, d)")
@@ -48,10 +54,15 @@ def fast_readout(x: torch.Tensor, w_up: torch.Tensor, w_gate: Optional[torch.Ten
     if state_index is not None:
         state_index = state_index.to(device=x.device, dtype=torch.int32).contiguous()
     act = x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
-    lw = ln_weight.to(act).to(torch.float32).contiguous()
-    lb = ln_bias.to(act).to(torch.float32).contiguous()
+    if ln_prepared:
+        lw, lb = ln_weight, ln_bias
+    else:
+        lw = ln_weight.to(act).to(torch.float32).contiguous()
+        lb = ln_bias.to(act).to(torch.float32).contiguous()
     odt = out_dtype or x.dtype
-    out = torch.empty(B, T, d, dtype=torch.bfloat16 if odt == torch.bfloat16 else torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty(B, T, d, dtype=torch.bfloat16 if odt == torch.bfloat16 else torch.float32,
+                          device=x.device)
     lib = _lib.load()
     ws = workspace(lib.uttt_fast_readout_workspace(B, d, h), x.device, slot=1)
     st = lib.uttt_fast_readout(B, T, d, h, xb.data_ptr(), wd_kind, wu.data_ptr(), _ptr(wg), wd.data_ptr(),
