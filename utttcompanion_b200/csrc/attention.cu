@@ -35,97 +35,143 @@ __device__ __forceinline__ float rope_elem(const __nv_bfloat16* x, int i, int hd
   return bfr(bfr(xi * bfr(cosr[i])) + bfr(rot * bfr(sinr[i])));
 }
 
-constexpr int DEC_THREADS = 128;
+constexpr int DEC_THREADS = 256;
 constexpr int MAX_HD = 128;
 constexpr int MAX_REP = 8;
+constexpr int MAX_W = 1024;
 
-template <int E>
+// One CTA per (row, kv group).  Scores: every lane owns one ring slot and reads
+// its whole K row with 16-byte loads (all slots' loads in flight at once);
+// softmax over the slots in shared memory; output: threads own one element of
+// the head dimension and a share of the slots, accumulate every query head of
+// the group from one V load, and reduce the shares through shared memory.
+template <int HD>
 __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int qkv_ld, const int* __restrict__ pos, const int* __restrict__ slot,
-    __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring, int n_heads, int n_kv, int hd, int W,
+    __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring, int n_heads, int n_kv, int W,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float scale, __nv_bfloat16* __restrict__ out,
     int out_ld) {
-  __shared__ float qs[MAX_REP][MAX_HD];
-  __shared__ float wm[4][MAX_REP], wl[4][MAX_REP];
-  __shared__ float wacc[4][MAX_REP][MAX_HD];
+  __shared__ float qs[MAX_REP][HD];
+  __shared__ float ps[MAX_REP][MAX_W];
+  __shared__ float red[MAX_REP][DEC_THREADS / 32];
+  __shared__ float part[DEC_THREADS / HD][MAX_REP][HD];
   const int b = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rep = n_heads / n_kv;
   const int p = pos[b];
   const int sl = slot[b];
   const __nv_bfloat16* row = qkv + (size_t)b * qkv_ld;
-  const float* cr = cos_t + (size_t)p * hd;
-  const float* sr = sin_t + (size_t)p * hd;
-  const size_t ring_base = (((size_t)sl * n_kv + g) * W) * hd;
-  // RoPE q heads of this group, RoPE k, write k / v into the ring slot
-  for (int i = tid; i < rep * hd; i += DEC_THREADS) {
-    const int r = i / hd, e = i % hd;
-    qs[r][e] = rope_elem(row + (size_t)(g * rep + r) * hd, e, hd, cr, sr);
+  const float* cr = cos_t + (size_t)p * HD;
+  const float* sr = sin_t + (size_t)p * HD;
+  const size_t ring_base = (((size_t)sl * n_kv + g) * W) * HD;
+  for (int i = tid; i < rep * HD; i += DEC_THREADS) {
+    const int r = i / HD, e = i % HD;
+    qs[r][e] = rope_elem(row + (size_t)(g * rep + r) * HD, e, HD, cr, sr);
   }
-  const __nv_bfloat16* krow = row + (size_t)n_heads * hd + (size_t)g * hd;
-  const __nv_bfloat16* vrow = row + (size_t)(n_heads + n_kv) * hd + (size_t)g * hd;
+  const __nv_bfloat16* krow = row + (size_t)n_heads * HD + (size_t)g * HD;
+  const __nv_bfloat16* vrow = row + (size_t)(n_heads + n_kv) * HD + (size_t)g * HD;
   const int ws = p % W;
-  for (int e = tid; e < hd; e += DEC_THREADS) {
-    kring[ring_base + (size_t)ws * hd + e] = __float2bfloat16(rope_elem(krow, e, hd, cr, sr));
-    vring[ring_base + (size_t)ws * hd + e] = vrow[e];
+  for (int e = tid; e < HD; e += DEC_THREADS) {
+    kring[ring_base + (size_t)ws * HD + e] = __float2bfloat16(rope_elem(krow, e, HD, cr, sr));
+    vring[ring_base + (size_t)ws * HD + e] = vrow[e];
   }
   __syncthreads();
   const int nvalid = p + 1 < W ? p + 1 : W;
-  float m[MAX_REP], l[MAX_REP], acc[MAX_REP][E];
+
+  // ---- scores: one slot per thread
+  float mloc[MAX_REP];
+#pragma unroll
+  for (int r = 0; r < MAX_REP; ++r) mloc[r] = -INFINITY;
+  for (int s0 = 0; s0 < nvalid; s0 += DEC_THREADS) {
+    const int s = s0 + tid;
+    if (s < nvalid) {
+      const uint4* kp = reinterpret_cast<const uint4*>(kring + ring_base + (size_t)s * HD);
+      uint4 kv[HD / 8];
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) kv[c] = kp[c];
+      float dot[MAX_REP];
+#pragma unroll
+      for (int r = 0; r < MAX_REP; ++r) dot[r] = 0.f;
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&kv[c]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h2[j]);
+#pragma unroll
+          for (int r = 0; r < MAX_REP; ++r) {
+            if (r < rep) dot[r] += qs[r][c * 8 + 2 * j] * f.x + qs[r][c * 8 + 2 * j + 1] * f.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < MAX_REP; ++r) {
+        if (r < rep) {
+          const float sc = dot[r] * scale;
+          ps[r][s] = sc;
+          mloc[r] = fmaxf(mloc[r], sc);
+        }
+      }
+    }
+  }
+  // ---- softmax over the slots of every head
 #pragma unroll
   for (int r = 0; r < MAX_REP; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
+    if (r >= rep) break;
+    float m = mloc[r];
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[r][e] = 0.f;
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[r][warp] = m;
   }
-  for (int s = warp; s < nvalid; s += 4) {
-    const __nv_bfloat16* kp = kring + ring_base + (size_t)s * hd + lane * E;
-    const __nv_bfloat16* vp = vring + ring_base + (size_t)s * hd + lane * E;
-    float kv[E], vv[E];
+  __syncthreads();
+  float mx[MAX_REP], lsum[MAX_REP];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      kv[e] = __bfloat162float(kp[e]);
-      vv[e] = __bfloat162float(vp[e]);
-    }
+  for (int r = 0; r < MAX_REP; ++r) {
+    mx[r] = -INFINITY;
+    if (r < rep)
+      for (int w = 0; w < DEC_THREADS / 32; ++w) mx[r] = fmaxf(mx[r], red[r][w]);
+    lsum[r] = 0.f;
+  }
+  __syncthreads();
+  for (int s = tid; s < nvalid; s += DEC_THREADS) {
 #pragma unroll
     for (int r = 0; r < MAX_REP; ++r) {
-      if (r >= rep) break;
-      float d = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) d += qs[r][lane * E + e] * kv[e];
-      d = warp_sum(d) * scale;
-      const float mn = fmaxf(m[r], d);
-      const float c = __expf(m[r] - mn);
-      const float pe = __expf(d - mn);
-      l[r] = l[r] * c + pe;
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[r][e] = acc[r][e] * c + pe * vv[e];
-      m[r] = mn;
+      if (r < rep) {
+        const float e = __expf(ps[r][s] - mx[r]);
+        ps[r][s] = e;
+        lsum[r] += e;
+      }
     }
   }
 #pragma unroll
   for (int r = 0; r < MAX_REP; ++r) {
     if (r >= rep) break;
-    if (lane == 0) {
-      wm[warp][r] = m[r];
-      wl[warp][r] = l[r];
-    }
-#pragma unroll
-    for (int e = 0; e < E; ++e) wacc[warp][r][lane * E + e] = acc[r][e];
+    const float l = warp_sum(lsum[r]);
+    if (lane == 0) red[r][warp] = l;
   }
   __syncthreads();
-  for (int i = tid; i < rep * hd; i += DEC_THREADS) {
-    const int r = i / hd, e = i % hd;
-    float mx = -INFINITY;
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, wm[w][r]);
-    float L = 0.f, A = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      if (wm[w][r] == -INFINITY) continue;
-      const float c = __expf(wm[w][r] - mx);
-      L += wl[w][r] * c;
-      A += wacc[w][r][e] * c;
-    }
-    out[(size_t)b * out_ld + (size_t)(g * rep + r) * hd + e] = __float2bfloat16(A / L);
+  // ---- output: thread = (slot group, head-dim element)
+  constexpr int NG = DEC_THREADS / HD;
+  const int e = tid % HD, grp = tid / HD;
+  float acc[MAX_REP];
+#pragma unroll
+  for (int r = 0; r < MAX_REP; ++r) acc[r] = 0.f;
+#pragma unroll 4
+  for (int s = grp; s < nvalid; s += NG) {
+    const float v = __bfloat162float(vring[ring_base + (size_t)s * HD + e]);
+#pragma unroll
+    for (int r = 0; r < MAX_REP; ++r)
+      if (r < rep) acc[r] += ps[r][s] * v;
+  }
+#pragma unroll
+  for (int r = 0; r < MAX_REP; ++r)
+    if (r < rep) part[grp][r][e] = acc[r];
+  __syncthreads();
+  for (int i = tid; i < rep * HD; i += DEC_THREADS) {
+    const int r = i / HD, ee = i % HD;
+    float a = 0.f, l = 0.f;
+    for (int gg = 0; gg < NG; ++gg) a += part[gg][r][ee];
+    for (int w = 0; w < DEC_THREADS / 32; ++w) l += red[r][w];
+    out[(size_t)b * out_ld + (size_t)(g * rep + r) * HD + ee] = __float2bfloat16(a / l);
   }
 }
 
@@ -255,19 +301,20 @@ extern "C" int uttt_attn_decode(int B, int n_heads, int n_kv, int hd, int W, con
   UTTT_REQUIRE(qkv && pos && slot && k_ring && v_ring && rope_cos && rope_sin && out, UTTT_ERR_INVALID);
   UTTT_REQUIRE(n_heads % n_kv == 0 && n_heads / n_kv <= MAX_REP, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(hd == 32 || hd == 64 || hd == 128, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(W <= MAX_W, UTTT_ERR_UNSUPPORTED);
   cudaStream_t st = (cudaStream_t)stream;
   ProfScope ps(UTTT_PROF_ATTN, st);
   const float scale = 1.f / sqrtf((float)hd);
-#define UTTT_DEC(EV)                                                                                          \
-  attn_decode_kernel<EV><<<dim3(B, n_kv), DEC_THREADS, 0, st>>>(                                              \
-      (const __nv_bfloat16*)qkv, qkv_ld, pos, slot, (__nv_bfloat16*)k_ring, (__nv_bfloat16*)v_ring, n_heads, \
-      n_kv, hd, W, rope_cos, rope_sin, scale, (__nv_bfloat16*)out, out_ld)
+#define UTTT_DEC(HDV)                                                                                          \
+  attn_decode_kernel<HDV><<<dim3(B, n_kv), DEC_THREADS, 0, st>>>(                                              \
+      (const __nv_bfloat16*)qkv, qkv_ld, pos, slot, (__nv_bfloat16*)k_ring, (__nv_bfloat16*)v_ring, n_heads,  \
+      n_kv, W, rope_cos, rope_sin, scale, (__nv_bfloat16*)out, out_ld)
   if (hd == 32)
-    UTTT_DEC(1);
+    UTTT_DEC(32);
   else if (hd == 64)
-    UTTT_DEC(2);
+    UTTT_DEC(64);
   else
-    UTTT_DEC(4);
+    UTTT_DEC(128);
 #undef UTTT_DEC
   return launch_status();
 }

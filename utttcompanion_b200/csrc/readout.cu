@@ -6,8 +6,8 @@
 // 16-byte coalesced loads straight into registers, the K dimension is split
 // across the 8 warps of a CTA and reduced through shared memory.
 //
-// grid = (ceil(h / 256) hidden tiles, B states).  A CTA computes u, g for its
-// 256 hidden units, h = silu(g) * u, then the partial z = h W_down[tile, :]
+// grid = (ceil(h / 128) hidden tiles, B states).  A CTA computes u, g for its
+// 128 hidden units, h = silu(g) * u, then the partial z = h W_down[tile, :]
 // and adds it into z (FP32, L2-resident) with one red.add per element.
 #include "common.cuh"
 #include "host_util.cuh"
@@ -15,18 +15,17 @@
 namespace uttt {
 namespace {
 
-constexpr int GT = 256;        // hidden units per CTA
+constexpr int GT = 128;        // hidden units per CTA
 constexpr int GTHREADS = 256;  // 8 warps
 constexpr int MAXD = 4096;
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+__device__ __forceinline__ void bf16x4_to_f32(const uint2& v, float (&f)[4]) {
   const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __bfloat1622float2(p[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
+  const float2 a = __bfloat1622float2(p[0]), b = __bfloat1622float2(p[1]);
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
 }
 
 __global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloat16* __restrict__ x,
@@ -43,37 +42,36 @@ __global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloa
   for (int i = tid; i < d; i += GTHREADS) xs[i] = __bfloat162float(x[(size_t)b * d + i]);
   __syncthreads();
 
-  // ---- u, g for 256 hidden units; K (= d) split over the 8 warps
+  // ---- u, g for 128 hidden units: lane -> 4 columns, warp -> 1/8 of K (= d)
   const __nv_bfloat16* wrow = wp + (size_t)state * d * 2 * h;
-  const int col = j0 + lane * 8;
+  const int col = j0 + lane * 4;
   const bool cval = col < h;
-  float au[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  float ag[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float au[4] = {0.f, 0.f, 0.f, 0.f}, ag[4] = {0.f, 0.f, 0.f, 0.f};
   const int kper = d / 8;
   const int k0 = warp * kper;
   if (cval) {
-#pragma unroll 4
+#pragma unroll 8
     for (int k = k0; k < k0 + kper; ++k) {
-      const uint4 vu = __ldg(reinterpret_cast<const uint4*>(wrow + (size_t)k * 2 * h + col));
-      const uint4 vg = __ldg(reinterpret_cast<const uint4*>(wrow + (size_t)k * 2 * h + h + col));
-      float fu[8], fg[8];
-      bf16x8_to_f32(vu, fu);
-      bf16x8_to_f32(vg, fg);
+      const uint2 vu = __ldg(reinterpret_cast<const uint2*>(wrow + (size_t)k * 2 * h + col));
+      const uint2 vg = __ldg(reinterpret_cast<const uint2*>(wrow + (size_t)k * 2 * h + h + col));
+      float fu[4], fg[4];
+      bf16x4_to_f32(vu, fu);
+      bf16x4_to_f32(vg, fg);
       const float xv = xs[k];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
         au[i] = fmaf(xv, fu[i], au[i]);
         ag[i] = fmaf(xv, fg[i], ag[i]);
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    part[warp][0][lane * 8 + i] = au[i];
-    part[warp][1][lane * 8 + i] = ag[i];
+  for (int i = 0; i < 4; ++i) {
+    part[warp][0][lane * 4 + i] = au[i];
+    part[warp][1][lane * 4 + i] = ag[i];
   }
   __syncthreads();
-  {
+  if (tid < GT) {
     float u = 0.f, g = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
@@ -84,32 +82,33 @@ __global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloa
   }
   __syncthreads();
 
-  // ---- partial z over this tile's 256 rows of W_down; rows split over warps
+  // ---- partial z over this tile's 128 rows of W_down: warp -> 16 rows, lane -> 4 d columns
   const __nv_bfloat16* drow = wd + (size_t)state * h * d;
   float* zb = zacc + (size_t)b * 64 * d;   // row 0 of this state's 64-row z block
-  for (int dc = 0; dc < d; dc += 256) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const bool dval = dc + lane * 8 < d;   // d % 128 == 0: a 256-wide slice may be half full
+  for (int dc = 0; dc < d; dc += 128) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 8
-    for (int r = 0; r < 32; ++r) {
-      const int j = warp * 32 + r;
-      if (dval && j0 + j < h) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(drow + (size_t)(j0 + j) * d + dc + lane * 8));
-        float f[8];
-        bf16x8_to_f32(v, f);
+    for (int r = 0; r < 16; ++r) {
+      const int j = warp * 16 + r;
+      if (j0 + j < h) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(drow + (size_t)(j0 + j) * d + dc + lane * 4));
+        float f[4];
+        bf16x4_to_f32(v, f);
         const float hv = hs[j];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = fmaf(hv, f[i], acc[i]);
+        for (int i = 0; i < 4; ++i) acc[i] = fmaf(hv, f[i], acc[i]);
       }
     }
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) part[warp][0][lane * 8 + i] = acc[i];
+    for (int i = 0; i < 4; ++i) part[warp][0][lane * 4 + i] = acc[i];
     __syncthreads();
-    float s = 0.f;
+    if (tid < 128) {
+      float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += part[w][0][tid];
-    if (dc + tid < d) red_add_f32(zb + dc + tid, s);
+      for (int w = 0; w < 8; ++w) s += part[w][0][tid];
+      red_add_f32(zb + dc + tid, s);
+    }
   }
 }
 
