@@ -544,12 +544,22 @@ __global__ void __launch_bounds__(LN_THREADS) readout_ln_kernel(const float* __r
 // bwd: dH, dU, dG and the three weight gradients; NORM pass accumulates
 // ||grad||^2, UPDATE pass applies momentum / decay / clip in place.
 // ============================================================================
+// FP32 tensor maps of the masters for the TMA-staged update epilogue:
+// up/gate/s_up/s_gate over (h, d, B) with 128 x 32 boxes, down/s_down over
+// (d, h, B) with 32 x 128 boxes (128-byte swizzle).
+struct WMaps {
+  CUtensorMap up, gate, down, sup, sgate, sdown;
+};
+constexpr int QW = 32;                    // d columns per staged quarter chunk
+constexpr int WTILE = HT * QW * 4;        // 16 KB: one staged FP32 tile
+
 template <bool kMomentum>
 __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const __grid_constant__ CUtensorMap tmDZ,
+                                                                const __grid_constant__ WMaps wm,
                                                                 const ChunkParams p, int update) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3[2], empty3[2], dh_done, ops_ready, gfull, gfree;
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3[2], empty3[2], dh_done, ops_ready, gfull, gfree, wfull[2];
   __shared__ uint32_t tmem_slot;
   __shared__ ChunkStats st_sh;
   uint8_t* slots = align1024(smem_raw);             // ring 1: NSLOT x 24 KB (W_down rows + dZ tile)
@@ -577,6 +587,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     mbar_init(&ops_ready, NPROD);
     mbar_init(&gfull, 1);
     mbar_init(&gfree, NPROD);
+    mbar_init(&wfull[0], 1);
+    mbar_init(&wfull[1], 1);
     fence_mbarrier_init();
   }
   if (warp == 0) {
@@ -668,10 +680,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     }
 
     // ------------------------------------------------------------ epilogue 2: gradients
-    // TMEM tiles: gradW_up^T / gradW_gate^T as (hidden row, d column) and
-    // gradW_down^T as (d row, hidden column): the 32 lanes of a warp are 32
-    // consecutive floats of one weight row, so every load / store instruction
-    // moves one full 128-byte line.
+    // All three TMEM gradient tiles are (hidden row, d column).  The FP32
+    // masters move through shared memory by TMA in quarter chunks of 32 d
+    // columns (W_up / W_gate tiles [32 d][128 hidden], W_down tile
+    // [128 hidden][32 d] 128B-swizzled): the threads only touch TMEM and shared
+    // memory, and the copy engine keeps HBM busy.  Without momentum two W
+    // buffers alternate so the next quarter loads while this one computes.
     float scale = 1.f;
     if (update && p.clip > 0.f) scale = fminf(1.f, p.clip * rsqrtf(p.norm2[b] + 1e-8f));
     if (update && p.clip_out && t == 0 && tid == 0) p.clip_out[(size_t)b * p.n_chunks + p.chunk_index] = scale;
@@ -680,99 +694,114 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     // With beta == 0 the momentum of this chunk is never read again unless this
     // is the last chunk of the call that changes this state.
     const bool write_s = kMomentum || !st.later_active;
-    const size_t wbase_ug = (size_t)b * p.d * p.h;
-    const size_t wbase_d = (size_t)b * p.h * p.d;
+    const bool dbuf = !kMomentum && !write_s;        // W only: two 48 KB buffers
+    const int buf_bytes = dbuf ? 3 * WTILE : 6 * WTILE;
+    uint8_t* wbuf = slots;                           // ring 1 is free once dH is done
+    const int nq = p.d / QW;
+    const int row = q * 32 + lane;                   // hidden row within the tile
+    const int cq = half * 16;                        // this thread's 16 of the quarter's 32 columns
+    const bool row_ok = h0 + row < p.h;
+    const bool leader = tid == 0;
+    const bool move = update && !skip;
+    auto load_q = [&](int qi, int buf) {
+      uint8_t* B0 = wbuf + buf * buf_bytes;
+      mbar_arrive_expect_tx(&wfull[buf], kMomentum ? 6 * WTILE : 3 * WTILE);
+      tma_load_3d(B0, &wm.up, &wfull[buf], h0, qi * QW, b);
+      tma_load_3d(B0 + WTILE, &wm.gate, &wfull[buf], h0, qi * QW, b);
+      tma_load_3d(B0 + 2 * WTILE, &wm.down, &wfull[buf], qi * QW, h0, b);
+      if (kMomentum) {
+        tma_load_3d(B0 + 3 * WTILE, &wm.sup, &wfull[buf], h0, qi * QW, b);
+        tma_load_3d(B0 + 4 * WTILE, &wm.sgate, &wfull[buf], h0, qi * QW, b);
+        tma_load_3d(B0 + 5 * WTILE, &wm.sdown, &wfull[buf], qi * QW, h0, b);
+      }
+    };
+    if (move && leader) {
+      load_q(0, 0);
+      if (dbuf && nq > 1) load_q(1, 1);
+    }
     float acc = 0.f;
-    const int row = q * 32 + lane;
-    const bool ug_row_ok = h0 + row < p.h;
-    for (int j = 0; j < nch; ++j) {
-      mbar_wait(&gfull, j & 1, p.status);
-      tc_fence_after();
-      const int cbase = half * 64;
-#pragma unroll 1
-      for (int cc = 0; cc < 64; cc += 16) {
-        float gu[16], gg[16], gd[16];
-        tmem_ld16(tmem_addr(tGU, q * 32, cbase + cc), gu);
-        tmem_ld16(tmem_addr(tGG, q * 32, cbase + cc), gg);
-        tmem_ld16(tmem_addr(tGD, q * 32, cbase + cc), gd);
-        tmem_wait_ld();
-        if (skip) continue;
-        const int hc = h0 + cbase + cc;   // first hidden column of this thread's gradW_down^T run
-        if (!update) {
-          if (ug_row_ok) {
+    for (int qi = 0; qi < nq; ++qi) {
+      const int j = qi >> 2, qq = qi & 3;
+      if (qq == 0) {
+        mbar_wait(&gfull, j & 1, p.status);
+        tc_fence_after();
+      }
+      float gu[16], gg[16], gd[16];
+      tmem_ld16(tmem_addr(tGU, q * 32, qq * QW + cq), gu);
+      tmem_ld16(tmem_addr(tGG, q * 32, qq * QW + cq), gg);
+      tmem_ld16(tmem_addr(tGD, q * 32, qq * QW + cq), gd);
+      tmem_wait_ld();
+      if (qq == 3) {
+        tc_fence_before();
+        mbar_arrive(&gfree);
+      }
+      if (skip) continue;
+      if (!update) {
+        if (row_ok) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e];
-          }
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (hc + e < p.h) acc += gd[e] * gd[e];
-          continue;
+          for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e] + gd[e] * gd[e];
         }
-        // W_up / W_gate element (dd = j*128 + cbase + cc + e, hidden = h0 + row)
-        if (ug_row_ok) {
-          const size_t oug = wbase_ug + (size_t)(j * 128 + cbase + cc) * p.h + h0 + row;
-          float wu[16], wg[16];
+        continue;
+      }
+      const int buf = dbuf ? (qi & 1) : 0;
+      mbar_wait(&wfull[buf], dbuf ? ((qi >> 1) & 1) : (qi & 1), p.status);
+      uint8_t* B0 = wbuf + buf * buf_bytes;
+      float* wu = reinterpret_cast<float*>(B0);
+      float* wg = reinterpret_cast<float*>(B0 + WTILE);
+      uint8_t* wd = B0 + 2 * WTILE;
+      float* su = reinterpret_cast<float*>(B0 + 3 * WTILE);
+      float* sg = reinterpret_cast<float*>(B0 + 4 * WTILE);
+      uint8_t* sd = B0 + 5 * WTILE;
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            wu[e] = p.w_up[oug + (size_t)e * p.h];
-            wg[e] = p.w_gate[oug + (size_t)e * p.h];
-          }
-          if constexpr (kMomentum) {
-            float su[16], sg[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              su[e] = p.s_up[oug + (size_t)e * p.h];
-              sg[e] = p.s_gate[oug + (size_t)e * p.h];
-            }
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const size_t a = oug + (size_t)e * p.h;
-              const float nsu = beta * su[e] - gu[e] * scale;
-              const float nsg = beta * sg[e] - gg[e] * scale;
-              p.w_up_out[a] = decay * wu[e] + nsu;
-              p.w_gate_out[a] = decay * wg[e] + nsg;
-              p.s_up_out[a] = nsu;
-              p.s_gate_out[a] = nsg;
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const size_t a = oug + (size_t)e * p.h;
-              const float nsu = -gu[e] * scale;
-              const float nsg = -gg[e] * scale;
-              p.w_up_out[a] = decay * wu[e] + nsu;
-              p.w_gate_out[a] = decay * wg[e] + nsg;
-              if (write_s) {
-                p.s_up_out[a] = nsu;
-                p.s_gate_out[a] = nsg;
-              }
-            }
-          }
-        }
-        // W_down element (hidden = hc + e, dd = j*128 + row)
-        {
-          const size_t od = wbase_d + (size_t)hc * p.d + j * 128 + row;
-          float wd[16], sd[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const bool ok = hc + e < p.h;
-            wd[e] = ok ? p.w_down[od + (size_t)e * p.d] : 0.f;
-            if constexpr (kMomentum) sd[e] = ok ? p.s_down[od + (size_t)e * p.d] : 0.f;
-          }
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            if (hc + e < p.h) {
-              const size_t c = od + (size_t)e * p.d;
-              const float ns = (kMomentum ? beta * sd[e] : 0.f) - gd[e] * scale;
-              p.w_down_out[c] = decay * wd[e] + ns;
-              if (write_s) p.s_down_out[c] = ns;
-            }
-          }
+      for (int e = 0; e < 16; ++e) {
+        const int o = (cq + e) * HT + row;            // [32 d][128 hidden]
+        const float nsu = (kMomentum ? beta * su[o] : 0.f) - gu[e] * scale;
+        const float nsg = (kMomentum ? beta * sg[o] : 0.f) - gg[e] * scale;
+        wu[o] = decay * wu[o] + nsu;
+        wg[o] = decay * wg[o] + nsg;
+        if (write_s) {
+          su[o] = nsu;
+          sg[o] = nsg;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&gfree);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {                   // [128 hidden][32 d], 128B swizzle
+        const uint32_t o = sw128_offset(row, (cq + 4 * i) * 4);
+        float4 w4 = *reinterpret_cast<float4*>(wd + o);
+        float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kMomentum) s4 = *reinterpret_cast<float4*>(sd + o);
+        float4 ns;
+        ns.x = (kMomentum ? beta * s4.x : 0.f) - gd[4 * i + 0] * scale;
+        ns.y = (kMomentum ? beta * s4.y : 0.f) - gd[4 * i + 1] * scale;
+        ns.z = (kMomentum ? beta * s4.z : 0.f) - gd[4 * i + 2] * scale;
+        ns.w = (kMomentum ? beta * s4.w : 0.f) - gd[4 * i + 3] * scale;
+        w4.x = decay * w4.x + ns.x;
+        w4.y = decay * w4.y + ns.y;
+        w4.z = decay * w4.z + ns.z;
+        w4.w = decay * w4.w + ns.w;
+        *reinterpret_cast<float4*>(wd + o) = w4;
+        if (write_s) *reinterpret_cast<float4*>(sd + o) = ns;
+      }
+      fence_proxy_async_smem();
+      named_bar(1, NPROD);
+      if (leader) {
+        tma_store_3d(&wm.up, wu, h0, qi * QW, b);
+        tma_store_3d(&wm.gate, wg, h0, qi * QW, b);
+        tma_store_3d(&wm.down, wd, qi * QW, h0, b);
+        if (write_s) {
+          tma_store_3d(&wm.sup, su, h0, qi * QW, b);
+          tma_store_3d(&wm.sgate, sg, h0, qi * QW, b);
+          tma_store_3d(&wm.sdown, sd, qi * QW, h0, b);
+        }
+        bulk_commit();
+        const int nxt = qi + (dbuf ? 2 : 1);
+        if (nxt < nq) {
+          bulk_wait_read<0>();
+          load_q(nxt, buf);
+        }
+      }
     }
+    if (move && leader) bulk_wait_all();
     if (!update) {
       acc = warp_sum(acc);
       if (lane == 0 && !skip) atomicAdd(p.norm2 + b, acc);
@@ -820,7 +849,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       mbar_wait(&ops_ready, 0, p.status);
       tc_fence_after();
       const uint32_t id_uw = idesc_bf16(128, 128, false, true);   // A = dU^T K-major, B = K MN-major
-      const uint32_t id_dw = idesc_bf16(128, 128, true, false);   // A = dZ^T MN-major, B = H K-major
+      const uint32_t id_dw = idesc_bf16(128, 128, false, true);   // A = H^T K-major, B = dZ slice MN-major
       const uint32_t du = smem_u32(sDU), dg = smem_u32(sDG), ht = smem_u32(sHt);
       for (int j = 0; j < nch; ++j) {
         const int s = j & 1;
@@ -834,7 +863,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
           const uint64_t kd = sdesc_sw128(kk + ks * 2048, 8192, 1024);
           mma_bf16(tGU, sdesc_sw128(du + ks * 32, 16, 1024), kd, id_uw, acc);
           mma_bf16(tGG, sdesc_sw128(dg + ks * 32, 16, 1024), kd, id_uw, acc);
-          mma_bf16(tGD, sdesc_sw128(zz + ks * 2048, 8192, 1024), sdesc_sw128(ht + ks * 32, 16, 1024), id_dw, acc);
+          mma_bf16(tGD, sdesc_sw128(ht + ks * 32, 16, 1024), sdesc_sw128(zz + ks * 2048, 8192, 1024), id_dw, acc);
         }
         mma_commit(&empty3[s]);
         mma_commit(&gfull);
@@ -929,6 +958,21 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     uint32_t box[2] = {64, 64};
     UTTT_TRY(make_tmap_bf16(&tmDZ, p.dz, 2, dims, str, box));
   }
+  WMaps wmaps;
+  {
+    uint64_t dims_ug[3] = {(uint64_t)h, (uint64_t)d, (uint64_t)B};
+    uint64_t str_ug[2] = {(uint64_t)h * 4, (uint64_t)d * h * 4};
+    uint32_t box_ug[3] = {HT, QW, 1};
+    uint64_t dims_d[3] = {(uint64_t)d, (uint64_t)h, (uint64_t)B};
+    uint64_t str_d[2] = {(uint64_t)d * 4, (uint64_t)h * d * 4};
+    uint32_t box_d[3] = {QW, HT, 1};
+    UTTT_TRY(make_tmap_f32(&wmaps.up, w_up, 3, dims_ug, str_ug, box_ug, false));
+    UTTT_TRY(make_tmap_f32(&wmaps.gate, w_gate, 3, dims_ug, str_ug, box_ug, false));
+    UTTT_TRY(make_tmap_f32(&wmaps.down, w_down, 3, dims_d, str_d, box_d, true));
+    UTTT_TRY(make_tmap_f32(&wmaps.sup, s_up, 3, dims_ug, str_ug, box_ug, false));
+    UTTT_TRY(make_tmap_f32(&wmaps.sgate, s_gate, 3, dims_ug, str_ug, box_ug, false));
+    UTTT_TRY(make_tmap_f32(&wmaps.sdown, s_down, 3, dims_d, str_d, box_d, true));
+  }
   static bool attr_done = false;
   if (!attr_done) {
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
@@ -960,17 +1004,17 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     if (max_grad_norm > 0.f) {
       ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
       if (momentum_beta != 0.f)
-        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
+        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
       else
-        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 0);
+        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
     }
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
       if (momentum_beta != 0.f)
-        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
       else
-        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, p, 1);
+        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
     }
     UTTT_TRY(launch_status());
   }

@@ -71,6 +71,32 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
   return r == CUDA_SUCCESS ? UTTT_OK : UTTT_ERR_INVALID;
 }
 
+int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  auto fn = encode_fn();
+  if (!fn) return UTTT_ERR_CUDA;
+  if (((uintptr_t)base & 15u) != 0) return UTTT_ERR_INVALID;
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t gbox[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    gbox[i] = box[i];
+    estride[i] = 1;
+    if (i + 1 < rank) {
+      if (strides_bytes[i] % 16 != 0) return UTTT_ERR_INVALID;
+      gstride[i] = strides_bytes[i];
+    }
+  }
+  if ((box[0] * 4) % 16 != 0 || (swizzle128 && box[0] * 4 != 128)) return UTTT_ERR_INVALID;
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride,
+                  gbox, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? UTTT_OK : UTTT_ERR_INVALID;
+}
+
 }  // namespace uttt
 
 extern "C" {

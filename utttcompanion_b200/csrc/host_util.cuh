@@ -39,6 +39,9 @@ inline int launch_status() { return cuda_status(cudaGetLastError()); }
 // zero-filled.  `dims` / `strides_bytes` are innermost first.
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box);
+// FP32 tensor map; swizzle128 selects SWIZZLE_128B (inner box must then be 128 B), else none.
+int make_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
 
 // Workspace: [status int (256 B slot)] [region 0] [region 1] ... each 256-B aligned.
 struct WsCursor {
