@@ -72,6 +72,7 @@ struct ChunkParams {
   int chunk_index;
   int n_chunks;
   int call_end;       // token index one past the last chunk of this call
+  int tok0_next, Cc_next;  // the fused forward's chunk (bwd kernel with kFuse)
   int hp;             // hidden padded to 128
   float beta, clip, eps, inv_scale;
   int* status;
@@ -553,20 +554,28 @@ struct WMaps {
 constexpr int QW = 32;                    // d columns per staged quarter chunk
 constexpr int WTILE = HT * QW * 4;        // 16 KB: one staged FP32 tile
 
-template <bool kMomentum>
+// kFuse: also run the NEXT chunk's forward (U', G', H', partial Z') from the
+// weight tiles this kernel just updated, so the separate forward pass over
+// the FP32 masters disappears for every chunk but the first of a call.
+template <bool kMomentum, bool kFuse>
 __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const __grid_constant__ CUtensorMap tmDZ,
                                                                 const __grid_constant__ WMaps wm,
                                                                 const ChunkParams p, int update) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3[2], empty3[2], dh_done, ops_ready, gfull, gfree, wfull[2];
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3, empty3, dh_done, ops_ready, gfull, gfree, wfull[2];
+  __shared__ uint64_t a_ready, kfull, ug_free, h_ready, fullz[2], emptyz[2], zfull[2], zfree[2];
   __shared__ uint32_t tmem_slot;
   __shared__ ChunkStats st_sh;
-  uint8_t* slots = align1024(smem_raw);             // ring 1: NSLOT x 24 KB (W_down rows + dZ tile)
-  uint8_t* slots3 = slots + NSLOT * BWD_SLOT;       // ring 3: 2 x 32 KB (K slice + dZ slice)
-  uint8_t* sDU = slots3 + 2 * 32768;                // K-major [hh 128][64 tokens]
+  uint8_t* slots = align1024(smem_raw);             // 96 KB: phase-1 ring | W staging | Z' ring
+  uint8_t* slots3 = slots + NSLOT * BWD_SLOT;       // 32 KB: K slice + dZ slice of one 128-wide d chunk
+  uint8_t* sDU = slots3 + 32768;                    // K-major [hh 128][64 tokens]
   uint8_t* sDG = sDU + 16384;
   uint8_t* sHt = sDG + 16384;
+  uint8_t* sAU = sHt + 16384;                       // next chunk: bf16 W'_up^T  K-major [hh 128][64 d]
+  uint8_t* sAG = sAU + 16384;                       //             bf16 W'_gate^T
+  uint8_t* sKN = sAG + 16384;                       //             K' tile [64 tokens][64 d]
+  uint8_t* sH = sDU;                                // next chunk H' (MN-major [hh][64 tokens]) after the loop
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x, b = blockIdx.y;
@@ -579,9 +588,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       mbar_init(&full[i], NPROD + 1);
       mbar_init(&empty[i], 1);
     }
+    mbar_init(&full3, 1);
+    mbar_init(&empty3, 1);
+    mbar_init(&a_ready, 1);
+    mbar_init(&kfull, 1);
+    mbar_init(&ug_free, 1);
+    mbar_init(&h_ready, NPROD);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&full3[i], 1);
-      mbar_init(&empty3[i], 1);
+      mbar_init(&fullz[i], NPROD);
+      mbar_init(&emptyz[i], 1);
+      mbar_init(&zfull[i], 1);
+      mbar_init(&zfree[i], NPROD);
     }
     mbar_init(&dh_done, 1);
     mbar_init(&ops_ready, NPROD);
@@ -601,6 +618,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   const uint32_t tDH = tmem, tGU = tmem + 128, tGG = tmem + 256, tGD = tmem + 384;
+  const uint32_t tUN = tmem, tGN = tmem + 64;       // next chunk U', G' (after dH is drained)
+  const uint32_t tZN = tmem + 128;                   // next chunk Z' tiles (after the gradients)
   const ChunkStats st = st_sh;
   // A state with no valid token keeps W and S exactly (model/uttt_layer.py:513-520).
   const bool skip = !st.active;
@@ -703,6 +722,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     const bool row_ok = h0 + row < p.h;
     const bool leader = tid == 0;
     const bool move = update && !skip;
+    // the next chunk's forward reads the (possibly unchanged) tiles as well
+    const bool stage = (update && !skip) || (kFuse && update);
     auto load_q = [&](int qi, int buf) {
       uint8_t* B0 = wbuf + buf * buf_bytes;
       mbar_arrive_expect_tx(&wfull[buf], kMomentum ? 6 * WTILE : 3 * WTILE);
@@ -715,7 +736,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         tma_load_3d(B0 + 5 * WTILE, &wm.sdown, &wfull[buf], qi * QW, h0, b);
       }
     };
-    if (move && leader) {
+    if (stage && leader) {
       load_q(0, 0);
       if (dbuf && nq > 1) load_q(1, 1);
     }
@@ -735,14 +756,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         tc_fence_before();
         mbar_arrive(&gfree);
       }
-      if (skip) continue;
       if (!update) {
-        if (row_ok) {
+        if (row_ok && !skip) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e] + gd[e] * gd[e];
         }
         continue;
       }
+      if (!stage) continue;
       const int buf = dbuf ? (qi & 1) : 0;
       mbar_wait(&wfull[buf], dbuf ? ((qi >> 1) & 1) : (qi & 1), p.status);
       uint8_t* B0 = wbuf + buf * buf_bytes;
@@ -752,6 +773,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       float* su = reinterpret_cast<float*>(B0 + 3 * WTILE);
       float* sg = reinterpret_cast<float*>(B0 + 4 * WTILE);
       uint8_t* sd = B0 + 5 * WTILE;
+      if (!skip) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         const int o = (cq + e) * HT + row;            // [32 d][128 hidden]
@@ -782,9 +804,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         *reinterpret_cast<float4*>(wd + o) = w4;
         if (write_s) *reinterpret_cast<float4*>(sd + o) = ns;
       }
+      }  // !skip
+      if constexpr (kFuse) {
+        // bf16 W'_up^T / W'_gate^T columns of this quarter into the next-chunk A tiles
+        const int kbi = qi >> 1, half_kb = qi & 1;
+        if (half_kb == 0 && kbi > 0) mbar_wait(&ug_free, (kbi - 1) & 1, p.status);
+#pragma unroll 1
+        for (int i = 0; i < 2; ++i) {
+          const float* pu = wu + (cq + 8 * i) * HT + row;
+          const float* pg = wg + (cq + 8 * i) * HT + row;
+          uint4 a, g;
+          a.x = pack_bf16x2(pu[0 * HT], pu[1 * HT]); a.y = pack_bf16x2(pu[2 * HT], pu[3 * HT]);
+          a.z = pack_bf16x2(pu[4 * HT], pu[5 * HT]); a.w = pack_bf16x2(pu[6 * HT], pu[7 * HT]);
+          g.x = pack_bf16x2(pg[0 * HT], pg[1 * HT]); g.y = pack_bf16x2(pg[2 * HT], pg[3 * HT]);
+          g.z = pack_bf16x2(pg[4 * HT], pg[5 * HT]); g.w = pack_bf16x2(pg[6 * HT], pg[7 * HT]);
+          const uint32_t o = sw128_offset(row, (half_kb * 32 + cq + 8 * i) * 2);
+          *reinterpret_cast<uint4*>(sAU + o) = a;
+          *reinterpret_cast<uint4*>(sAG + o) = g;
+        }
+      }
       fence_proxy_async_smem();
       named_bar(1, NPROD);
-      if (leader) {
+      if (kFuse && leader && (qi & 1)) mbar_arrive(&a_ready);
+      if (leader && !skip) {
         tma_store_3d(&wm.up, wu, h0, qi * QW, b);
         tma_store_3d(&wm.gate, wg, h0, qi * QW, b);
         tma_store_3d(&wm.down, wd, qi * QW, h0, b);
@@ -794,6 +836,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
           tma_store_3d(&wm.sdown, sd, qi * QW, h0, b);
         }
         bulk_commit();
+      }
+      if (leader) {
         const int nxt = qi + (dbuf ? 2 : 1);
         if (nxt < nq) {
           bulk_wait_read<0>();
@@ -801,10 +845,105 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         }
       }
     }
-    if (move && leader) bulk_wait_all();
+    if (stage && leader) {
+      bulk_wait_all();
+      asm volatile("fence.proxy.async.global;" ::: "memory");   // W' stores visible to generic loads
+    }
     if (!update) {
       acc = warp_sum(acc);
       if (lane == 0 && !skip) atomicAdd(p.norm2 + b, acc);
+    }
+    if constexpr (kFuse) {
+      if (update) {
+        // ---------------------------------------------------------- next chunk: H' and partial Z'
+        named_bar(1, NPROD);                                   // W'_down stores visible to all producers
+        mbar_wait(&ug_free, (nkb - 1) & 1, p.status);          // last U'/G' k-block done
+        tc_fence_after();
+        const int c0 = half * 32;
+        float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
+        float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+#pragma unroll 1
+        for (int c16 = 0; c16 < 32; c16 += 16) {
+          float u[16], g[16];
+          tmem_ld16(tmem_addr(tUN, q * 32, c0 + c16), u);
+          tmem_ld16(tmem_addr(tGN, q * 32, c0 + c16), g);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            us[(size_t)(c0 + c16 + i) * p.hp] = u[i];
+            gs[(size_t)(c0 + c16 + i) * p.hp] = g[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 16; i += 8) {
+            uint4 pk;
+            float hv[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float gg2 = g[i + e];
+              hv[e] = (c0 + c16 + i + e < p.Cc_next) ? gg2 * sigmoidf_(gg2) * u[i + e] : 0.f;
+            }
+            pk.x = pack_bf16x2(hv[0], hv[1]);
+            pk.y = pack_bf16x2(hv[2], hv[3]);
+            pk.z = pack_bf16x2(hv[4], hv[5]);
+            pk.w = pack_bf16x2(hv[6], hv[7]);
+            *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + c16 + i) * 2)) = pk;
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&h_ready);
+        // W'_down rows (just stored, L2-resident) -> MN-major A tiles, drained Z' tiles -> zacc
+        const float* wdg = p.w_down + (size_t)b * p.h * p.d;
+        const int nmt = p.d / 128;
+        for (int mt = 0; mt < nmt; ++mt) {
+          const int sz = mt & 1;
+          mbar_wait(&emptyz[sz], ((mt >> 1) & 1) ^ 1, p.status);
+          uint8_t* sA = slots + sz * SLOT_BYTES;
+#pragma unroll 4
+          for (int jj = 0; jj < 16; ++jj) {
+            const int idx = tid + jj * NPROD;  // 0..4095
+            const int hh = idx >> 5, c4 = (idx & 31) * 4;
+            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (h0 + hh < p.h) f = *reinterpret_cast<const float4*>(wdg + (size_t)(h0 + hh) * p.d + mt * 128 + c4);
+            uint2 pk;
+            pk.x = pack_bf16x2(f.x, f.y);
+            pk.y = pack_bf16x2(f.z, f.w);
+            *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = pk;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&fullz[sz]);
+          if (mt > 0) {
+            const int pm = mt - 1, zb = pm & 1;
+            mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
+            tc_fence_after();
+            float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
+#pragma unroll 1
+            for (int c16 = 0; c16 < 32; c16 += 16) {
+              float z[16];
+              tmem_ld16(tmem_addr(tZN + zb * 64, q * 32, c0 + c16), z);
+              tmem_wait_ld();
+              for (int i = 0; i < 16; ++i)
+                if (c0 + c16 + i < p.Cc_next) red_add_f32(za + (size_t)(c0 + c16 + i) * p.d, z[i]);
+            }
+            tc_fence_before();
+            mbar_arrive(&zfree[zb]);
+          }
+        }
+        {
+          const int pm = nmt - 1, zb = pm & 1;
+          mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
+          tc_fence_after();
+          float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
+#pragma unroll 1
+          for (int c16 = 0; c16 < 32; c16 += 16) {
+            float z[16];
+            tmem_ld16(tmem_addr(tZN + zb * 64, q * 32, c0 + c16), z);
+            tmem_wait_ld();
+            for (int i = 0; i < 16; ++i)
+              if (c0 + c16 + i < p.Cc_next) red_add_f32(za + (size_t)(c0 + c16 + i) * p.d, z[i]);
+          }
+        }
+      }
     }
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -818,16 +957,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         tma_load_2d(slots + s * BWD_SLOT + 16384, &tmDZ, &full[s], kb * 64, b * CT);
       }
       for (int j = 0; j < nch; ++j) {
-        const int s = j & 1;
-        mbar_wait(&empty3[s], ((j >> 1) & 1) ^ 1, p.status);
-        mbar_arrive_expect_tx(&full3[s], 32768);
-        uint8_t* base = slots3 + s * 32768;
+        mbar_wait(&empty3, (j & 1) ^ 1, p.status);
+        mbar_arrive_expect_tx(&full3, 32768);
+        uint8_t* base = slots3;
         // K slice (MN-major B for gradW_up/gate): rows = tokens, 64 d each
-        tma_load_3d(base, &tmK, &full3[s], j * 128, p.tok0, b);
-        tma_load_3d(base + 8192, &tmK, &full3[s], j * 128 + 64, p.tok0, b);
-        // dZ slice (MN-major A for gradW_down^T)
-        tma_load_2d(base + 16384, &tmDZ, &full3[s], j * 128, b * CT);
-        tma_load_2d(base + 24576, &tmDZ, &full3[s], j * 128 + 64, b * CT);
+        tma_load_3d(base, &tmK, &full3, j * 128, p.tok0, b);
+        tma_load_3d(base + 8192, &tmK, &full3, j * 128 + 64, p.tok0, b);
+        // dZ slice (B for gradW_down, MN-major)
+        tma_load_2d(base + 16384, &tmDZ, &full3, j * 128, b * CT);
+        tma_load_2d(base + 24576, &tmDZ, &full3, j * 128 + 64, b * CT);
+        if (kFuse && update) {
+          // the next chunk's K tiles for the two 64-wide k-blocks of this d chunk
+          for (int kk2 = 0; kk2 < 2; ++kk2) {
+            const int kbi = 2 * j + kk2;
+            if (kbi > 0) mbar_wait(&ug_free, (kbi - 1) & 1, p.status);
+            mbar_arrive_expect_tx(&kfull, 8192);
+            tma_load_3d(sKN, &tmK, &kfull, kbi * 64, p.tok0_next, b);
+          }
+        }
       }
     }
   } else {  // MMA warp
@@ -851,12 +998,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       const uint32_t id_uw = idesc_bf16(128, 128, false, true);   // A = dU^T K-major, B = K MN-major
       const uint32_t id_dw = idesc_bf16(128, 128, false, true);   // A = H^T K-major, B = dZ slice MN-major
       const uint32_t du = smem_u32(sDU), dg = smem_u32(sDG), ht = smem_u32(sHt);
+      const uint32_t id_ug = idesc_bf16(128, 64, false, false);   // next chunk: A = W'^T K-major, B = K' K-major
       for (int j = 0; j < nch; ++j) {
-        const int s = j & 1;
-        mbar_wait(&full3[s], (j >> 1) & 1, p.status);
+        mbar_wait(&full3, j & 1, p.status);
         mbar_wait(&gfree, (j & 1) ^ 1, p.status);
         tc_fence_after();
-        const uint32_t kk = smem_u32(slots3 + s * 32768), zz = kk + 16384;
+        const uint32_t kk = smem_u32(slots3), zz = kk + 16384;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint32_t acc = ks > 0 ? 1u : 0u;
@@ -865,8 +1012,45 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
           mma_bf16(tGG, sdesc_sw128(dg + ks * 32, 16, 1024), kd, id_uw, acc);
           mma_bf16(tGD, sdesc_sw128(ht + ks * 32, 16, 1024), sdesc_sw128(zz + ks * 2048, 8192, 1024), id_dw, acc);
         }
-        mma_commit(&empty3[s]);
+        mma_commit(&empty3);
         mma_commit(&gfull);
+        if (kFuse && update) {
+          for (int kk2 = 0; kk2 < 2; ++kk2) {
+            const int kbi = 2 * j + kk2;
+            mbar_wait(&a_ready, kbi & 1, p.status);
+            mbar_wait(&kfull, kbi & 1, p.status);
+            tc_fence_after();
+            const uint32_t au = smem_u32(sAU), ag = smem_u32(sAG), kn = smem_u32(sKN);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t bd = sdesc_sw128(kn + ks * 32, 16, 1024);
+              const uint32_t acc = (kbi > 0 || ks > 0) ? 1u : 0u;
+              mma_bf16(tUN, sdesc_sw128(au + ks * 32, 16, 1024), bd, id_ug, acc);
+              mma_bf16(tGN, sdesc_sw128(ag + ks * 32, 16, 1024), bd, id_ug, acc);
+            }
+            mma_commit(&ug_free);
+          }
+        }
+      }
+      if (kFuse && update) {
+        mbar_wait(&h_ready, 0, p.status);
+        tc_fence_after();
+        const uint32_t id_z = idesc_bf16(128, 64, true, true);
+        const uint32_t hb = smem_u32(sH);
+        const int nmt = p.d / 128;
+        for (int mt = 0; mt < nmt; ++mt) {
+          const int sz = mt & 1, zb = mt & 1;
+          mbar_wait(&fullz[sz], (mt >> 1) & 1, p.status);
+          mbar_wait(&zfree[zb], ((mt >> 1) & 1) ^ 1, p.status);
+          tc_fence_after();
+          const uint32_t a = smem_u32(slots + sz * SLOT_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_bf16(tZN + zb * 64, sdesc_sw128(a + ks * 2048, 16384, 1024), sdesc_sw128(hb + ks * 2048, 8192, 1024),
+                     id_z, ks > 0 ? 1u : 0u);
+          mma_commit(&emptyz[sz]);
+          mma_commit(&zfull[zb]);
+        }
       }
     }
   }
@@ -876,7 +1060,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
 }
 
 size_t fwd_smem() { return 1024 + NSLOT * SLOT_BYTES + 16384; }
-size_t bwd_smem() { return 1024 + NSLOT * BWD_SLOT + 2 * 32768 + 3 * 16384; }
+size_t bwd_smem() { return 1024 + NSLOT * BWD_SLOT + 32768 + 3 * 16384 + 2 * 16384 + 8192; }
 
 }  // namespace
 }  // namespace uttt
@@ -979,19 +1163,28 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false>,
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false, false>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true>,
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true, false>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false, true>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true, true>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
     attr_done = true;
   }
   UTTT_TRY(cuda_status(cudaMemsetAsync(p.zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
   const dim3 grid((h + HT - 1) / HT, B);
+  // The forward of every chunk but the first runs inside the previous chunk's
+  // backward kernel (kFuse), from the weight tiles it has just updated.
   for (int ci = 0; ci < n_chunks; ++ci) {
     p.tok0 = (chunk_begin + ci) * C;
     p.Cc = (T - p.tok0) < C ? (T - p.tok0) : C;
     p.chunk_index = ci;
-    {
+    const bool fuse = ci + 1 < n_chunks;
+    p.tok0_next = p.tok0 + C;
+    p.Cc_next = fuse ? ((T - p.tok0_next) < C ? (T - p.tok0_next) : C) : 0;
+    if (ci == 0) {
       ProfScope ps(UTTT_PROF_CHUNK_FWD, st);
       chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
     }
@@ -1004,17 +1197,24 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     if (max_grad_norm > 0.f) {
       ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
       if (momentum_beta != 0.f)
-        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+        chunk_bwd_kernel<true, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
       else
-        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+        chunk_bwd_kernel<false, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
     }
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
-      if (momentum_beta != 0.f)
-        chunk_bwd_kernel<true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
-      else
-        chunk_bwd_kernel<false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+      if (momentum_beta != 0.f) {
+        if (fuse)
+          chunk_bwd_kernel<true, true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+        else
+          chunk_bwd_kernel<true, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+      } else {
+        if (fuse)
+          chunk_bwd_kernel<false, true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+        else
+          chunk_bwd_kernel<false, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+      }
     }
     UTTT_TRY(launch_status());
   }
