@@ -244,6 +244,28 @@ int uttt_greedy_argmax(int rows, int V, const void* logits, int logits_f32, long
 int uttt_pack_read_copies(int S, int d, int h, const float* w_up, const float* w_gate, const float* w_down,
                           void* packed_up_gate, void* down, void* stream);
 
+/* apply_rope (model/uttt_layer.py:946-958) on `rows` = B*H*T head vectors of
+ * length D (row r is token r % T), BF16 in / out, BF16 cos / sin rows (T, D)
+ * (the reference casts its FP32 tables to the activation dtype, :935-943). */
+int uttt_apply_rope(long long rows, int T, int D, const void* x, const void* cos_t, const void* sin_t, void* out,
+                    void* stream);
+
+/* ---- stability guard ------------------------------------------------------ */
+/* Slow-anchor elastic pull of B FP32 states towards the shared W_0, in place,
+ * with the optional drift clamp (SharedFastWeightPool.apply_elastic_pull,
+ * model/uttt_layer.py:773-832): w = W0 + (1-lambda)(W - W0), then if
+ * max_drift_ratio > 0 each state's deviation is scaled by
+ * min(1, ratio * ||W0|| / sqrt(||w - W0||^2 + 1e-8)) (norms over all three
+ * matrices).  lambda <= 0 and ratio <= 0 is a no-op, as in the reference. */
+size_t uttt_guard_workspace(int B);
+int uttt_elastic_pull(int B, int d, int h, float* w_up, float* w_gate, float* w_down, const float* w_up0,
+                      const float* w_gate0, const float* w_down0, float anchor_lambda, float max_drift_ratio,
+                      void* workspace, size_t workspace_bytes, void* stream);
+/* Drift statistics for compute_drift (:834-874): out (device FP32, 4*B + 4):
+ * out[4b+m] = ||W_m[b] - W0_m||^2 for m = up, gate, down; out[4B+m] = ||W0_m||^2. */
+int uttt_drift_sums(int B, int d, int h, const float* w_up, const float* w_gate, const float* w_down,
+                    const float* w_up0, const float* w_gate0, const float* w_down0, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,10 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_embed": (i32, [i32, i32, vp, vp, vp, vp]),
     "uttt_greedy_argmax": (i32, [i32, i32, vp, i32, C.c_longlong, i32, i32, vp, vp, vp]),
     "uttt_pack_read_copies": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, vp]),
+    "uttt_apply_rope": (i32, [C.c_longlong, i32, i32, vp, vp, vp, vp, vp]),
+    "uttt_guard_workspace": (sz, [i32]),
+    "uttt_elastic_pull": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, vp, f32, f32, vp, sz, vp]),
+    "uttt_drift_sums": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp]),
 }
 
 

@@ -117,10 +117,41 @@ __global__ void pack_read_kernel(const float4* __restrict__ w_up, const float4* 
   }
 }
 
+// apply_rope on (B, H, T, D) q and k with (T, D) cos / sin rows, every op rounded
+// to BF16 as the reference's eager BF16 path does (model/uttt_layer.py:946-958).
+__global__ void rope_apply_kernel(__nv_bfloat16* __restrict__ x, long long rows, int T, int D,
+                                  const __nv_bfloat16* __restrict__ cs, const __nv_bfloat16* __restrict__ sn,
+                                  __nv_bfloat16* __restrict__ out) {
+  const long long r = blockIdx.x;          // row = (b, h, t)
+  if (r >= rows) return;
+  const int t = (int)(r % T);
+  const int half = D / 2;
+  const __nv_bfloat16* xr = x + r * D;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float xi = __bfloat162float(xr[i]);
+    const float rot = i < half ? -__bfloat162float(xr[i + half]) : __bfloat162float(xr[i - half]);
+    const float c = __bfloat162float(cs[(size_t)t * D + i]), s = __bfloat162float(sn[(size_t)t * D + i]);
+    const float a = __bfloat162float(__float2bfloat16(xi * c));
+    const float b = __bfloat162float(__float2bfloat16(rot * s));
+    out[r * D + i] = __float2bfloat16(a + b);
+  }
+}
+
 }  // namespace
 }  // namespace uttt
 
 using namespace uttt;
+
+extern "C" int uttt_apply_rope(long long rows, int T, int D, const void* x, const void* cos_t, const void* sin_t,
+                               void* out, void* stream) {
+  UTTT_REQUIRE(rows > 0 && T > 0 && D > 0 && D % 2 == 0 && x && cos_t && sin_t && out, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(rows % T == 0, UTTT_ERR_INVALID);
+  cudaStream_t st = (cudaStream_t)stream;
+  ProfScope ps(UTTT_PROF_ROWWISE, st);
+  rope_apply_kernel<<<(unsigned)rows, 64, 0, st>>>((__nv_bfloat16*)x, rows, T, D, (const __nv_bfloat16*)cos_t,
+                                                   (const __nv_bfloat16*)sin_t, (__nv_bfloat16*)out);
+  return launch_status();
+}
 
 extern "C" int uttt_pack_read_copies(int S, int d, int h, const float* w_up, const float* w_gate,
                                      const float* w_down, void* packed_up_gate, void* down, void* stream) {
