@@ -284,8 +284,11 @@ class UtttB200:
         return self.logits(h)
 
     def generate_greedy(self, prompt: torch.Tensor, state: FastState, n_tokens: int, slot: int = 0,
-                        stop_free: bool = True) -> Tuple[List[int], List[float], List[torch.Tensor]]:
-        """``stream_generate`` at temperature 0 for one persona (stop-free greedy by default)."""
+                        stop_free: bool = True, eos_token_id: Optional[int] = None
+                        ) -> Tuple[List[int], List[float], List[torch.Tensor]]:
+        """``stream_generate`` at temperature 0 for one persona (stop-free greedy by default;
+        otherwise the reference's stops: role ids end the reply unyielded, EOS is yielded last,
+        model/uttt_model.py:1036-1050)."""
         packed, down = self.read_copies(state.w_up, state.w_gate, state.w_down)
         logits = self.prefill(prompt, slot, packed, down, 0).unsqueeze(0)
         pos = prompt.numel()
@@ -301,7 +304,7 @@ class UtttB200:
             ids.append(t)
             tv = top2[0].tolist()
             margins.append(tv[0] - tv[1])
-            if len(ids) == n_tokens:
+            if len(ids) == n_tokens or (not stop_free and eos_token_id is not None and t == eos_token_id):
                 break
             logits = self.decode_step(tok, torch.full((1,), pos, dtype=torch.int32, device=self.device), slot_t,
                                       packed, down, zero)
@@ -439,14 +442,19 @@ class DecodeGraph:
     """
 
     def __init__(self, engine: "UtttB200", batch: int, read_packed: torch.Tensor, read_down: torch.Tensor,
-                 stop_free: bool = True):
+                 stop_free: bool = True, pad_slot: Optional[int] = None):
         self.engine = engine
         dev = engine.device
         self.batch = batch
         self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
-        self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
-        self.sidx = torch.arange(batch, dtype=torch.int32, device=dev)
+        if pad_slot is None:
+            if batch > min(engine.max_personas, read_packed.shape[0]):
+                raise ValueError("batch exceeds the persona slots; pass pad_slot")
+            self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
+        else:
+            self.slots = torch.full((batch,), pad_slot, dtype=torch.int32, device=dev)
+        self.sidx = self.slots.clone()
         self.read_packed, self.read_down = read_packed, read_down
         self.stop_free = stop_free
         # warm up (workspaces, kernel attributes) on a side stream, then capture;

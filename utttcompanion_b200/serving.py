@@ -1,0 +1,331 @@
+"""Multi-persona serving on one B200: persona arena + continuous batching.
+
+The reference serves one turn at a time on one worker thread
+(``server/app.py:163-166,215-217``) and ``stream_generate`` is batch-1
+(``model/uttt_model.py:993-994``).  ``ServingEngine`` keeps the same turn
+semantics per persona -- generate with the persona's frozen fast weights,
+write [prompt + reply] with the chunk-first TTT schedule, gate by surprise,
+pull elastically toward W_0, commit (``engine/personalizer.py:369-584``) --
+but runs every in-flight turn of every persona in ONE packed decode launch
+per token and batches the writes of all turns that finish together.
+
+* ``PersonaArena``: device-resident FP32 masters + momentum and BF16 read
+  copies for up to ``capacity`` personas (plus one padding slot), KV rings in
+  the model engine indexed by the same slot, host spill of evicted personas
+  in the reference's persona-file payload format (``FastWeightState.to_state_dict``).
+* ``ServingEngine``: ``submit`` / ``step`` / ``run`` scheduler; a persona is
+  never in two in-flight turns (later turns of the same user wait for the
+  earlier write to commit, as the reference's serialisation guarantees).
+* ``PersonaRouter``: ``gpu = stable_hash(user_id) mod world_size`` -- personas
+  partition across the GPUs of a node with no data-path collective.
+"""
+
+from __future__ import annotations
+
+import collections
+import hashlib
+import math
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional
+
+import torch
+
+from . import _lib
+from .fastweight import _stream, workspace
+from .model import ASSISTANT_ID, EOS_ID, PAD_ID, USER_ID, DecodeGraph, FastState, UtttB200
+
+
+class PersonaRouter:
+    """Stable user-id -> GPU partition (no collective on the data path)."""
+
+    def __init__(self, world_size: int):
+        if world_size < 1:
+            raise ValueError("world_size must be >= 1")
+        self.world_size = world_size
+
+    def rank_of(self, user_id: str) -> int:
+        digest = hashlib.sha256(str(user_id).encode("utf-8")).digest()
+        return int.from_bytes(digest[:8], "little") % self.world_size
+
+    def partition(self, user_ids) -> Dict[int, List[str]]:
+        out: Dict[int, List[str]] = {r: [] for r in range(self.world_size)}
+        for uid in user_ids:
+            out[self.rank_of(uid)].append(uid)
+        return out
+
+
+class PersonaArena:
+    """Device-resident persona store with LRU spill to host."""
+
+    def __init__(self, engine: UtttB200, capacity: int):
+        if capacity + 1 > engine.max_personas:
+            raise ValueError("the model engine needs max_personas >= capacity + 1 (one padding slot)")
+        self.engine = engine
+        self.capacity = capacity
+        self.pad_slot = capacity
+        d, h = engine.cfg.d_model, engine.cfg.d_ff_fast
+        dev = engine.device
+        n = capacity + 1
+        w0 = engine.w0
+        self.w_up = w0[0].unsqueeze(0).repeat(n, 1, 1).contiguous()
+        self.w_gate = w0[1].unsqueeze(0).repeat(n, 1, 1).contiguous()
+        self.w_down = w0[2].unsqueeze(0).repeat(n, 1, 1).contiguous()
+        self.s_up = torch.zeros_like(self.w_up)
+        self.s_gate = torch.zeros_like(self.w_gate)
+        self.s_down = torch.zeros_like(self.w_down)
+        self.read_packed = torch.empty(n, d, 2 * h, dtype=torch.bfloat16, device=dev)
+        self.read_down = torch.empty(n, h, d, dtype=torch.bfloat16, device=dev)
+        self.meta: List[Optional[dict]] = [None] * n
+        self.slot_of_user: "collections.OrderedDict[str, int]" = collections.OrderedDict()
+        self.host: Dict[str, dict] = {}      # evicted personas: reference persona-file payloads
+        self.pinned: set = set()             # slots with a turn in flight (never evicted)
+        self.refresh(list(range(n)))
+
+    def refresh(self, slots: List[int]) -> None:
+        """Rebuild the BF16 read copies of `slots` (after a write commits)."""
+        e = self.engine
+        d, h = e.cfg.d_model, e.cfg.d_ff_fast
+        for s in slots:
+            _lib.check(e.lib.uttt_pack_read_copies(1, d, h, self.w_up[s].data_ptr(), self.w_gate[s].data_ptr(),
+                                                   self.w_down[s].data_ptr(), self.read_packed[s].data_ptr(),
+                                                   self.read_down[s].data_ptr(), _stream(e.device)),
+                       "uttt_pack_read_copies")
+
+    def _free_slot(self) -> int:
+        used = set(self.slot_of_user.values())
+        for s in range(self.capacity):
+            if s not in used:
+                return s
+        for uid, s in self.slot_of_user.items():           # least recently used, not in flight
+            if s not in self.pinned:
+                self.host[uid] = self.export_slot(s)
+                del self.slot_of_user[uid]
+                return s
+        raise RuntimeError("persona arena full: every slot has a turn in flight")
+
+    def acquire(self, user_id: str) -> int:
+        """Slot of `user_id`: resident hit, host promote, or a fresh W_0 persona."""
+        if user_id in self.slot_of_user:
+            self.slot_of_user.move_to_end(user_id)
+            return self.slot_of_user[user_id]
+        s = self._free_slot()
+        payload = self.host.pop(user_id, None)
+        if payload is None:
+            for i, w in enumerate(self.engine.w0):
+                (self.w_up, self.w_gate, self.w_down)[i][s].copy_(w)
+            for t in (self.s_up, self.s_gate, self.s_down):
+                t[s].zero_()
+            self.meta[s] = {"step": 0, "last_surprise_loss": 0.0, "surprise_history": []}
+        else:
+            self.import_slot(s, payload)
+        self.refresh([s])
+        self.slot_of_user[user_id] = s
+        return s
+
+    def state(self, slots: List[int]) -> FastState:
+        idx = torch.as_tensor(slots, device=self.w_up.device)
+        return FastState(self.w_up[idx], self.w_gate[idx], self.w_down[idx], self.s_up[idx], self.s_gate[idx],
+                         self.s_down[idx], self.engine.ln_w, self.engine.ln_b)
+
+    def export_slot(self, s: int) -> dict:
+        m = self.meta[s] or {}
+        return {"w_up": self.w_up[s:s + 1].cpu(), "w_gate": self.w_gate[s:s + 1].cpu(),
+                "w_down": self.w_down[s:s + 1].cpu(), "s_up": self.s_up[s:s + 1].cpu(),
+                "s_gate": self.s_gate[s:s + 1].cpu(), "s_down": self.s_down[s:s + 1].cpu(),
+                "ln_weight": self.engine.ln_w.cpu(), "ln_bias": self.engine.ln_b.cpu(),
+                "step": int(m.get("step", 0)), "last_surprise_loss": float(m.get("last_surprise_loss", 0.0)),
+                "surprise_history": list(m.get("surprise_history", []))[-100:]}
+
+    def import_slot(self, s: int, payload: dict) -> None:
+        for name in ("w_up", "w_gate", "w_down", "s_up", "s_gate", "s_down"):
+            t = torch.as_tensor(payload[name]).to(self.w_up.device, torch.float32)
+            getattr(self, name)[s].copy_(t.reshape(getattr(self, name)[s].shape))
+        self.meta[s] = {"step": int(payload.get("step", 0)),
+                        "last_surprise_loss": float(payload.get("last_surprise_loss", 0.0)),
+                        "surprise_history": list(payload.get("surprise_history", []))}
+
+    def export_user(self, user_id: str) -> dict:
+        if user_id in self.slot_of_user:
+            return self.export_slot(self.slot_of_user[user_id])
+        return self.host[user_id]
+
+
+@dataclass
+class Turn:
+    user_id: str
+    prompt_ids: List[int]
+    max_new_tokens: int = 128
+    eos_token_id: Optional[int] = EOS_ID
+    reply: List[int] = field(default_factory=list)
+    slot: int = -1
+    pos: int = 0
+    next_token: int = 0
+    decoded: bool = False
+    done: bool = False
+    result: Optional[dict] = None
+
+
+class ServingEngine:
+    """Continuous batching of persona turns on one GPU (greedy decoding)."""
+
+    def __init__(self, engine: UtttB200, capacity: int, max_batch: int, surprise_threshold: float = 0.25,
+                 elastic_anchor_lambda: float = 0.02, max_weight_drift_ratio: Optional[float] = 0.35,
+                 online_ttt: bool = True):
+        self.engine = engine
+        self.arena = PersonaArena(engine, capacity)
+        self.max_batch = max_batch
+        self.surprise_threshold = surprise_threshold
+        self.elastic_anchor_lambda = elastic_anchor_lambda
+        self.max_weight_drift_ratio = max_weight_drift_ratio
+        self.online_ttt = online_ttt
+        # padding rows of the packed graph decode the padding persona at position 0
+        self.graph = DecodeGraph(engine, max_batch, self.arena.read_packed, self.arena.read_down, stop_free=False,
+                                 pad_slot=self.arena.pad_slot)
+        self.waiting: Deque[Turn] = collections.deque()
+        self.active: List[Optional[Turn]] = [None] * max_batch
+        self.finished: List[Turn] = []
+        self.in_flight_users: set = set()
+        from .pool import SharedFastWeightPoolB200
+        self.pool = SharedFastWeightPoolB200(*engine.w0, engine.ln_w, engine.ln_b, engine.cfg.momentum_beta,
+                                             engine.cfg.max_inner_grad_norm, engine.cfg.normalize_loss_by_dim,
+                                             engine.cfg.rms_norm_eps, engine.device)
+
+    # ------------------------------------------------------------------ API
+    def submit(self, user_id: str, prompt_ids: List[int], max_new_tokens: int = 128,
+               eos_token_id: Optional[int] = EOS_ID) -> Turn:
+        if not prompt_ids:
+            raise ValueError("empty prompt")
+        t = Turn(str(user_id), list(prompt_ids), max_new_tokens, eos_token_id)
+        self.waiting.append(t)
+        return t
+
+    def idle(self) -> bool:
+        return not self.waiting and all(a is None for a in self.active)
+
+    def run(self, max_steps: int = 1_000_000) -> List[Turn]:
+        steps = 0
+        while not self.idle() and steps < max_steps:
+            self.step()
+            steps += 1
+        return self.finished
+
+    def interact_and_evolve(self, user_id: str, prompt_ids: List[int], max_new_tokens: int = 128) -> dict:
+        """Synchronous one-turn API with the fields of ``EvolutionResult``
+        (``engine/personalizer.py:44-66``) that do not involve text."""
+        t = self.submit(user_id, prompt_ids, max_new_tokens)
+        while not t.done:
+            self.step()
+        return t.result
+
+    # ------------------------------------------------------------------ scheduler
+    def _admit(self) -> None:
+        e = self.engine
+        deferred: Deque[Turn] = collections.deque()
+        while self.waiting and None in self.active:
+            t = self.waiting.popleft()
+            if t.user_id in self.in_flight_users:       # one in-flight turn per persona
+                deferred.append(t)
+                continue
+            row = self.active.index(None)
+            t.slot = self.arena.acquire(t.user_id)
+            self.arena.pinned.add(t.slot)
+            self.in_flight_users.add(t.user_id)
+            ids = torch.tensor(t.prompt_ids, dtype=torch.long)
+            logits = e.prefill(ids, t.slot, self.arena.read_packed, self.arena.read_down, t.slot)
+            tok, _ = e.greedy(logits.unsqueeze(0), stop_free=False)
+            t.pos = len(t.prompt_ids)
+            t.next_token = int(tok.item())
+            self.active[row] = t
+            self._accept(row, t)
+        self.waiting.extendleft(reversed(deferred))
+
+    def _accept(self, row: int, t: Turn) -> None:
+        """Apply stream_generate's stop rules to the token just picked (model/uttt_model.py:1036-1050)."""
+        tok = t.next_token
+        if tok in (USER_ID, ASSISTANT_ID):
+            t.decoded = True
+        else:
+            t.reply.append(tok)
+            if (t.eos_token_id is not None and tok == t.eos_token_id) or len(t.reply) >= t.max_new_tokens:
+                t.decoded = True
+        if t.decoded:
+            self.active[row] = None
+            self.finished.append(t)
+            self._pending_writes.append(t)
+
+    def step(self) -> None:
+        self._pending_writes: List[Turn] = []
+        self._admit()
+        rows = [(i, t) for i, t in enumerate(self.active) if t is not None]
+        if rows:
+            B = self.max_batch
+            tokens = torch.zeros(B, dtype=torch.int32)
+            pos = torch.zeros(B, dtype=torch.int32)
+            slots = torch.full((B,), self.arena.pad_slot, dtype=torch.int32)
+            for i, t in rows:
+                tokens[i], pos[i], slots[i] = t.next_token, t.pos, t.slot
+            ids, _ = self.graph.step(tokens.to(self.engine.device), pos.to(self.engine.device),
+                                     slots.to(self.engine.device), slots.to(self.engine.device))
+            host_ids = ids.cpu().tolist()
+            for i, t in rows:
+                t.pos += 1
+                t.next_token = int(host_ids[i])
+                self._accept(i, t)
+        if self._pending_writes:
+            self._write(self._pending_writes)
+
+    def _write(self, turns: List[Turn]) -> None:
+        """Step 2 + 3 of a turn for every finished turn at once (personalizer.py:480-551)."""
+        cfg = self.engine.cfg
+        slots = [t.slot for t in turns]
+        if not self.online_ttt:
+            for t in turns:
+                self._finish(t, None, [], False)
+            return
+        seqs = [t.prompt_ids + t.reply for t in turns]
+        align = min(cfg.chunk_size, 64)
+        Tpad = max(((len(s) + align - 1) // align) * align for s in seqs)
+        ids = torch.full((len(turns), Tpad), PAD_ID, dtype=torch.long)
+        mask = torch.zeros(len(turns), Tpad)
+        for r, s in enumerate(seqs):
+            ids[r, :len(s)] = torch.tensor(s)
+            mask[r, :len(s)] = 1.0
+        state = self.arena.state(slots)
+        new, surprises, per_layer = self.engine.test_time_update_batch(ids, state, mask)
+        for r, t in enumerate(turns):
+            s = surprises[r]
+            if not math.isfinite(s) or s < 0:
+                raise ValueError("Test-time update returned a non-finite or negative surprise loss; "
+                                 "persona was not changed")
+            gate = s > self.surprise_threshold
+            if gate:
+                one = FastState(*(x[r:r + 1] for x in (new.w_up, new.w_gate, new.w_down, new.s_up, new.s_gate,
+                                                      new.s_down)), new.ln_weight, new.ln_bias)
+                pulled = self.pool.apply_elastic_pull(one, self.elastic_anchor_lambda, self.max_weight_drift_ratio)
+                a = self.arena
+                for name, src in (("w_up", pulled.w_up), ("w_gate", pulled.w_gate), ("w_down", pulled.w_down),
+                                  ("s_up", pulled.s_up), ("s_gate", pulled.s_gate), ("s_down", pulled.s_down)):
+                    getattr(a, name)[t.slot].copy_(src[0])
+                meta = a.meta[t.slot]
+                meta["step"] = int(meta.get("step", 0)) + new.step
+                meta["last_surprise_loss"] = s
+                meta["surprise_history"] = (meta.get("surprise_history", []) + per_layer[r])[-100:]
+                a.refresh([t.slot])
+            else:
+                meta = self.arena.meta[t.slot]
+                meta["last_surprise_loss"] = s
+                meta["surprise_history"] = (meta.get("surprise_history", []) + [s])[-100:]
+            self._finish(t, s, per_layer[r], gate)
+
+    def _finish(self, t: Turn, surprise, per_layer, gate) -> None:
+        drift = self.pool.compute_drift(self.arena.state([t.slot]))
+        t.result = {
+            "user_id": t.user_id, "prompt_ids": t.prompt_ids, "reply_ids": list(t.reply),
+            "surprise_loss": surprise, "surprise_threshold": self.surprise_threshold,
+            "gate_triggered": bool(gate), "weight_drift_frobenius": drift["drift_frobenius"],
+            "weight_drift_pct": drift["drift_pct"], "step": int(self.arena.meta[t.slot].get("step", 0)),
+            "layer_surprise_losses": per_layer, "drift_details": drift,
+        }
+        t.done = True
+        self.arena.pinned.discard(t.slot)
+        self.in_flight_users.discard(t.user_id)
