@@ -37,6 +37,8 @@ constexpr int NTHREADS = NPROD + 64;  // + TMA warp + MMA warp
 constexpr int NSLOT = 4;
 constexpr int SLOT_BYTES = 40 * 1024;
 constexpr int TMA_WARP = 8, MMA_WARP = 9;
+constexpr int STORE_WARP = 10;            // bwd only: W' stores and staging refills
+constexpr int BWD_THREADS = NPROD + 96;
 constexpr int BWD_SLOT = 24 * 1024;
 
 struct ChunkParams {
@@ -402,94 +404,154 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-__global__ void __launch_bounds__(LN_THREADS) chunk_ln_kernel(const ChunkParams p) {
-  __shared__ float red[LN_THREADS / 32];
-  __shared__ ChunkStats st_sh;
-  const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  __nv_bfloat16* dzrow = p.dz + ((size_t)b * CT + c) * p.d;
+// One warp per token row (d = 128 * NV, NV float4 per lane), shuffle-only
+// reductions: the chunk's 64 rows of a state are 8 blocks of 8 warps.
+constexpr int LN_ROWS = 8;
+
+template <int NV>
+__global__ void __launch_bounds__(LN_ROWS * 32) chunk_ln_kernel(const ChunkParams p) {
+  const int lane = threadIdx.x & 31;
+  const int c = blockIdx.x * LN_ROWS + (threadIdx.x >> 5), b = blockIdx.y;
+  constexpr int d = NV * 128;
+  uint2* dzrow = reinterpret_cast<uint2*>(p.dz + ((size_t)b * CT + c) * d);
   if (c >= p.Cc) {  // padded token row: zero gradient
-    for (int i = tid; i < p.d; i += LN_THREADS) dzrow[i] = __float2bfloat16(0.f);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) dzrow[i * 32 + lane] = make_uint2(0u, 0u);
     return;
   }
-  if (tid < 32) {
-    ChunkStats s = chunk_stats(p, b);
-    if (tid == 0) st_sh = s;
-  }
-  if (c == 0 && tid == 0) p.norm2[b] = 0.f;
+  if (c == 0 && lane == 0) p.norm2[b] = 0.f;
   const size_t tok = (size_t)b * p.T + p.tok0 + c;
-  float* zrow = p.zacc + ((size_t)b * CT + c) * p.d;
-  const __nv_bfloat16* krow = p.k + tok * p.d;
-  const __nv_bfloat16* vrow = p.v + tok * p.d;
-  const int nv = p.d / LN_THREADS;  // d % 256 == 0 is not required: handle tail below
-  float z[LN_MAXV];
+  float cnt = (float)p.Cc;  // valid tokens of this chunk (model/uttt_layer.py:371-378)
+  if (p.mask) {
+    float s = 0.f;
+    for (int i = lane; i < p.Cc; i += 32) s += p.mask[(size_t)b * p.T + p.tok0 + i];
+    cnt = warp_sum(s);
+  }
+  float4* zrow = reinterpret_cast<float4*>(p.zacc + ((size_t)b * CT + c) * d);
+  const uint2* krow = reinterpret_cast<const uint2*>(p.k + tok * d);
+  const uint2* vrow = reinterpret_cast<const uint2*>(p.v + tok * d);
+  const float4* lw4 = reinterpret_cast<const float4*>(p.ln_w);
+  const float4* lb4 = reinterpret_cast<const float4*>(p.ln_b);
+  float z[4 * NV];
   float sum = 0.f;
 #pragma unroll
-  for (int j = 0; j < LN_MAXV; ++j) {
-    const int i = tid + j * LN_THREADS;
-    z[j] = 0.f;
-    if (i < p.d) {
-      z[j] = zrow[i];
-      zrow[i] = 0.f;
-      sum += z[j];
-    }
+  for (int i = 0; i < NV; ++i) {
+    const float4 v = zrow[i * 32 + lane];
+    zrow[i * 32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);   // ready for the next chunk's partial sums
+    z[4 * i] = v.x; z[4 * i + 1] = v.y; z[4 * i + 2] = v.z; z[4 * i + 3] = v.w;
+    sum += (v.x + v.y) + (v.z + v.w);
   }
-  (void)nv;
-  const float dinv = 1.f / (float)p.d;
-  const float mean = block_sum(sum, red) * dinv;
+  const float dinv = 1.f / (float)d;
+  const float mean = warp_sum(sum) * dinv;
   float sq = 0.f;
 #pragma unroll
-  for (int j = 0; j < LN_MAXV; ++j) {
-    const int i = tid + j * LN_THREADS;
-    if (i < p.d) {
-      const float df = z[j] - mean;
-      sq += df * df;
-    }
+  for (int j = 0; j < 4 * NV; ++j) {
+    z[j] -= mean;
+    sq += z[j] * z[j];
   }
-  const float var = block_sum(sq, red) * dinv;
-  const float rstd = rsqrtf(var + p.eps);
+  const float rstd = rsqrtf(warp_sum(sq) * dinv + p.eps);
+  // above d = 2560 the residual is recomputed in the second pass instead of
+  // being kept in registers
+  constexpr bool kKeepE = NV <= 20;
+  float e[kKeepE ? 4 * NV : 1];
   float err2 = 0.f;
-  float e[LN_MAXV], zh[LN_MAXV];
 #pragma unroll
-  for (int j = 0; j < LN_MAXV; ++j) {
-    const int i = tid + j * LN_THREADS;
-    e[j] = 0.f;
-    zh[j] = 0.f;
-    if (i < p.d) {
-      zh[j] = (z[j] - mean) * rstd;
-      const float vhat = __bfloat162float(krow[i]) + (zh[j] * p.ln_w[i] + p.ln_b[i]);
-      e[j] = vhat - __bfloat162float(vrow[i]);
-      err2 += e[j] * e[j];
-      if (p.out) {
-        if (p.out_bf16)
-          reinterpret_cast<__nv_bfloat16*>(p.out)[tok * p.d + i] = __float2bfloat16(vhat);
-        else
-          reinterpret_cast<float*>(p.out)[tok * p.d + i] = vhat;
+  for (int i = 0; i < NV; ++i) {
+    const uint2 kk = krow[i * 32 + lane], vv = vrow[i * 32 + lane];
+    const float4 w = lw4[i * 32 + lane], bb = lb4[i * 32 + lane];
+    const float kf[4] = {bf16_lo(kk.x), bf16_hi(kk.x), bf16_lo(kk.y), bf16_hi(kk.y)};
+    const float vf[4] = {bf16_lo(vv.x), bf16_hi(vv.x), bf16_lo(vv.y), bf16_hi(vv.y)};
+    const float wf4[4] = {w.x, w.y, w.z, w.w}, bf4[4] = {bb.x, bb.y, bb.z, bb.w};
+    float vh[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = 4 * i + u;
+      z[j] *= rstd;                                   // z now holds the normalised zh
+      vh[u] = kf[u] + (z[j] * wf4[u] + bf4[u]);
+      const float ej = vh[u] - vf[u];
+      if constexpr (kKeepE) e[j] = ej;
+      err2 += ej * ej;
+    }
+    if (p.out) {
+      const size_t o = tok * d + (size_t)(i * 32 + lane) * 4;
+      if (p.out_bf16) {
+        uint2 pk;
+        pk.x = pack_bf16x2(vh[0], vh[1]);
+        pk.y = pack_bf16x2(vh[2], vh[3]);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + o) = pk;
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + o) = make_float4(vh[0], vh[1], vh[2], vh[3]);
       }
     }
   }
-  const float loss = 0.5f * block_sum(err2, red) * p.inv_scale;
-  const ChunkStats st = st_sh;
+  const float loss = 0.5f * warp_sum(err2) * p.inv_scale;
+  if (lane == 0 && p.token_loss) p.token_loss[tok] = loss;
   const float m = p.mask ? p.mask[tok] : 1.f;
-  if (tid == 0 && p.token_loss) p.token_loss[tok] = loss;
-  const float wf = p.mask ? p.eta[tok] * m / fmaxf(st.count, 1.f) : p.eta[tok] / (float)p.Cc;
+  const float wf = p.mask ? p.eta[tok] * m / fmaxf(cnt, 1.f) : p.eta[tok] / (float)p.Cc;
   const float coef = wf * p.inv_scale;
+  // d(zh) = coef * e * gamma
+  auto dzh = [&](int i, float (&out)[4]) {
+    const float4 w = lw4[i * 32 + lane];
+    const float wf4[4] = {w.x, w.y, w.z, w.w};
+    if constexpr (kKeepE) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) out[u] = coef * e[4 * i + u] * wf4[u];
+    } else {
+      const uint2 kk = krow[i * 32 + lane], vv = vrow[i * 32 + lane];
+      const float4 bb = lb4[i * 32 + lane];
+      const float kf[4] = {bf16_lo(kk.x), bf16_hi(kk.x), bf16_lo(kk.y), bf16_hi(kk.y)};
+      const float vf[4] = {bf16_lo(vv.x), bf16_hi(vv.x), bf16_lo(vv.y), bf16_hi(vv.y)};
+      const float bf4[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float ej = (kf[u] + (z[4 * i + u] * wf4[u] + bf4[u])) - vf[u];
+        out[u] = coef * ej * wf4[u];
+      }
+    }
+  };
   float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-  for (int j = 0; j < LN_MAXV; ++j) {
-    const int i = tid + j * LN_THREADS;
-    if (i < p.d) {
-      const float dzh = coef * e[j] * p.ln_w[i];
-      e[j] = dzh;
-      s1 += dzh;
-      s2 += dzh * zh[j];
+  for (int i = 0; i < NV; ++i) {
+    float g[4];
+    dzh(i, g);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if constexpr (kKeepE) e[4 * i + u] = g[u];
+      s1 += g[u];
+      s2 += g[u] * z[4 * i + u];
     }
   }
-  const float mdz = block_sum(s1, red) * dinv;
-  const float mdzz = block_sum(s2, red) * dinv;
+  const float mdz = warp_sum(s1) * dinv;
+  const float mdzz = warp_sum(s2) * dinv;
 #pragma unroll
-  for (int j = 0; j < LN_MAXV; ++j) {
-    const int i = tid + j * LN_THREADS;
-    if (i < p.d) dzrow[i] = __float2bfloat16(rstd * (e[j] - mdz - zh[j] * mdzz));
+  for (int i = 0; i < NV; ++i) {
+    float g[4];
+    if constexpr (kKeepE) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) g[u] = e[4 * i + u];
+    } else {
+      dzh(i, g);
+    }
+    uint2 pk;
+    pk.x = pack_bf16x2(rstd * (g[0] - mdz - z[4 * i] * mdzz), rstd * (g[1] - mdz - z[4 * i + 1] * mdzz));
+    pk.y = pack_bf16x2(rstd * (g[2] - mdz - z[4 * i + 2] * mdzz), rstd * (g[3] - mdz - z[4 * i + 3] * mdzz));
+    dzrow[i * 32 + lane] = pk;
+  }
+}
+
+using LnKernel = void (*)(const ChunkParams);
+
+LnKernel chunk_ln_for(int d) {
+  switch (d / 128) {
+#define UTTT_LN_CASE(n) case n: return chunk_ln_kernel<n>;
+    UTTT_LN_CASE(1) UTTT_LN_CASE(2) UTTT_LN_CASE(3) UTTT_LN_CASE(4) UTTT_LN_CASE(5) UTTT_LN_CASE(6)
+    UTTT_LN_CASE(7) UTTT_LN_CASE(8) UTTT_LN_CASE(9) UTTT_LN_CASE(10) UTTT_LN_CASE(11) UTTT_LN_CASE(12)
+    UTTT_LN_CASE(13) UTTT_LN_CASE(14) UTTT_LN_CASE(15) UTTT_LN_CASE(16) UTTT_LN_CASE(17) UTTT_LN_CASE(18)
+    UTTT_LN_CASE(19) UTTT_LN_CASE(20) UTTT_LN_CASE(21) UTTT_LN_CASE(22) UTTT_LN_CASE(23) UTTT_LN_CASE(24)
+    UTTT_LN_CASE(25) UTTT_LN_CASE(26) UTTT_LN_CASE(27) UTTT_LN_CASE(28) UTTT_LN_CASE(29) UTTT_LN_CASE(30)
+    UTTT_LN_CASE(31) UTTT_LN_CASE(32)
+#undef UTTT_LN_CASE
+    default: return nullptr;
   }
 }
 
@@ -550,21 +612,25 @@ __global__ void __launch_bounds__(LN_THREADS) readout_ln_kernel(const float* __r
 // (d, h, B) with 32 x 128 boxes (128-byte swizzle).
 struct WMaps {
   CUtensorMap up, gate, down, sup, sgate, sdown;
+  CUtensorMap zacc;   // FP32 (d, B * 64) partial-Z accumulator, 128 x 32 boxes
 };
 constexpr int QW = 32;                    // d columns per staged quarter chunk
 constexpr int WTILE = HT * QW * 4;        // 16 KB: one staged FP32 tile
+constexpr int NF = 4;                     // FP32 W_down quarter tiles in flight (operand rings)
+constexpr int ZSLOT = 32 * 1024;          // one BF16 [128 d][128 hidden] A tile of the next chunk's Z'
 
 // kFuse: also run the NEXT chunk's forward (U', G', H', partial Z') from the
 // weight tiles this kernel just updated, so the separate forward pass over
 // the FP32 masters disappears for every chunk but the first of a call.
 template <bool kMomentum, bool kFuse>
-__global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
+__global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const __grid_constant__ CUtensorMap tmDZ,
                                                                 const __grid_constant__ WMaps wm,
                                                                 const ChunkParams p, int update) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3, empty3, dh_done, ops_ready, gfull, gfree, wfull[2];
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3, empty3, dh_done, ops_ready, gfull, gfree, wfullA[3], wfullB[4];
   __shared__ uint64_t a_ready, kfull, ug_free, h_ready, fullz[2], emptyz[2], zfull[2], zfree[2];
+  __shared__ uint64_t ffull[NF], fempty[NF], qdoneA[3], qdoneB[4];
   __shared__ uint32_t tmem_slot;
   __shared__ ChunkStats st_sh;
   uint8_t* slots = align1024(smem_raw);             // 96 KB: phase-1 ring | W staging | Z' ring
@@ -576,6 +642,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
   uint8_t* sAG = sAU + 16384;                       //             bf16 W'_gate^T
   uint8_t* sKN = sAG + 16384;                       //             K' tile [64 tokens][64 d]
   uint8_t* sH = sDU;                                // next chunk H' (MN-major [hh][64 tokens]) after the loop
+  // FP32 W_down quarter tiles [128 hidden][32 d] (TMA, 128B swizzle) of
+  // phase 1, NF deep, in sDU..sAU (free until dH is done)
+  uint8_t* fring1 = sDU;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x, b = blockIdx.y;
@@ -590,7 +659,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     }
     mbar_init(&full3, 1);
     mbar_init(&empty3, 1);
-    mbar_init(&a_ready, 1);
+    mbar_init(&a_ready, NPROD);
     mbar_init(&kfull, 1);
     mbar_init(&ug_free, 1);
     mbar_init(&h_ready, NPROD);
@@ -604,8 +673,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     mbar_init(&ops_ready, NPROD);
     mbar_init(&gfull, 1);
     mbar_init(&gfree, NPROD);
-    mbar_init(&wfull[0], 1);
-    mbar_init(&wfull[1], 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&wfullA[i], 1);
+      mbar_init(&qdoneA[i], NPROD);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&wfullB[i], 1);
+      mbar_init(&qdoneB[i], NPROD);
+    }
+    for (int i = 0; i < NF; ++i) {
+      mbar_init(&ffull[i], 1);
+      mbar_init(&fempty[i], NPROD);
+    }
     fence_mbarrier_init();
   }
   if (warp == 0) {
@@ -624,31 +703,83 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
   // A state with no valid token keeps W and S exactly (model/uttt_layer.py:513-520).
   const bool skip = !st.active;
 
+  // ------------------------------------------------------------ update set-up
+  // The FP32 masters move through shared memory by TMA in quarter chunks of
+  // 32 d columns: W_up / W_gate tiles [32 d][128 hidden], W_down tiles
+  // [128 hidden][32 d] 128B-swizzled.  Loop A updates W_up / W_gate (and
+  // feeds the next chunk's U', G'), loop B updates W_down and turns each
+  // updated quarter straight into the next chunk's Z' operand, so W'_down is
+  // never read back.  The threads only touch TMEM and shared memory; the copy
+  // engine keeps HBM busy with up to 3 (A) / 4 (B) quarters in flight.
+  float scale = 1.f;
+  if (update && p.clip > 0.f) scale = fminf(1.f, p.clip * rsqrtf(p.norm2[b] + 1e-8f));
+  if (update && p.clip_out && t == 0 && tid == 0) p.clip_out[(size_t)b * p.n_chunks + p.chunk_index] = scale;
+  const float decay = 1.f - st.alpha_bar;
+  const float beta = p.beta;
+  // With beta == 0 the momentum of this chunk is never read again unless this
+  // is the last chunk of the call that changes this state.
+  const bool write_s = kMomentum || !st.later_active;
+  const bool wide = kMomentum || write_s;          // staging holds S tiles as well
+  const int bytesA = wide ? 4 * WTILE : 2 * WTILE, nbufA = wide ? 1 : 3;
+  const int bytesB = wide ? 2 * WTILE : WTILE, nbufB = wide ? 2 : 4;
+  const int nq = p.d / QW;
+  const bool fuse = kFuse && update;
+  // the next chunk's forward reads the (possibly unchanged) tiles as well
+  const bool stage = (update && !skip) || fuse;
+  auto load_a = [&](int qi) {
+    const int buf = qi % nbufA;
+    uint8_t* B0 = slots + buf * bytesA;
+    mbar_arrive_expect_tx(&wfullA[buf], kMomentum ? 4 * WTILE : 2 * WTILE);
+    tma_load_3d(B0, &wm.up, &wfullA[buf], h0, qi * QW, b);
+    tma_load_3d(B0 + WTILE, &wm.gate, &wfullA[buf], h0, qi * QW, b);
+    if (kMomentum) {
+      tma_load_3d(B0 + 2 * WTILE, &wm.sup, &wfullA[buf], h0, qi * QW, b);
+      tma_load_3d(B0 + 3 * WTILE, &wm.sgate, &wfullA[buf], h0, qi * QW, b);
+    }
+  };
+  auto load_b = [&](int qi) {
+    const int buf = qi % nbufB;
+    uint8_t* B0 = slots + buf * bytesB;
+    mbar_arrive_expect_tx(&wfullB[buf], kMomentum ? 2 * WTILE : WTILE);
+    tma_load_3d(B0, &wm.down, &wfullB[buf], qi * QW, h0, b);
+    if (kMomentum) tma_load_3d(B0 + WTILE, &wm.sdown, &wfullB[buf], qi * QW, h0, b);
+  };
+
   if (warp < 8) {
     // ------------------------------------------------------------ W_down rows -> A (K-major)
-    const float* wd = p.w_down + (size_t)b * p.h * p.d;
+    // Two FP32 quarter tiles (TMA; rows past h arrive as zeros) make one BF16
+    // k-block of 64 d columns.
     int it = 0;
     for (int kb = 0; kb < nkb; ++kb, ++it) {
       const int s = it % NSLOT;
       mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
       uint8_t* sA = slots + s * BWD_SLOT;
-      float4 f[8];
+#pragma unroll 1
+      for (int hq = 0; hq < 2; ++hq) {
+        const int qi = 2 * kb + hq, fs = qi % NF;
+        float4 f[4];
+        if (!skip) {
+          mbar_wait(&ffull[fs], (qi / NF) & 1, p.status);
+          const uint8_t* src = fring1 + fs * WTILE;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int idx = tid + j * NPROD;  // 0..2047 : 128 rows x 16 float4
-        const int hh = idx >> 4, c4 = (idx & 15) * 4;
-        f[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (!skip && h0 + hh < p.h)
-          f[j] = __ldg(reinterpret_cast<const float4*>(wd + (size_t)(h0 + hh) * p.d + kb * 64 + c4));
-      }
+          for (int j = 0; j < 4; ++j) {
+            const int idx = tid + j * NPROD;  // 0..1023 : 128 rows x 8 float4
+            f[j] = *reinterpret_cast<const float4*>(src + sw128_offset(idx >> 3, (idx & 7) * 16));
+          }
+          mbar_arrive(&fempty[fs]);
+        } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int idx = tid + j * NPROD;
-        const int hh = idx >> 4, c4 = (idx & 15) * 4;
-        uint2 pk;
-        pk.x = pack_bf16x2(f[j].x, f[j].y);
-        pk.y = pack_bf16x2(f[j].z, f[j].w);
-        *reinterpret_cast<uint2*>(sA + sw128_offset(hh, c4 * 2)) = pk;
+          for (int j = 0; j < 4; ++j) f[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int idx = tid + j * NPROD;
+          const int hh = idx >> 3, c4 = (idx & 7) * 4;
+          uint2 pk;
+          pk.x = pack_bf16x2(f[j].x, f[j].y);
+          pk.y = pack_bf16x2(f[j].z, f[j].w);
+          *reinterpret_cast<uint2*>(sA + sw128_offset(hh, (hq * QW + c4) * 2)) = pk;
+        }
       }
       fence_proxy_async_smem();
       mbar_arrive(&full[s]);
@@ -658,8 +789,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
     mbar_wait(&dh_done, 0, p.status);
     tc_fence_after();
     const int q = warp & 3, half = warp >> 2;
+    const int row = q * 32 + lane;                   // hidden row within the tile
     {
-      const int row = q * 32 + lane, c0 = half * 32;
+      const int c0 = half * 32;
       float dh[32];
       tmem_ld16(tmem_addr(tDH, q * 32, c0), *reinterpret_cast<float(*)[16]>(&dh[0]));
       tmem_ld16(tmem_addr(tDH, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&dh[16]));
@@ -698,48 +830,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       mbar_arrive(&ops_ready);
     }
 
-    // ------------------------------------------------------------ epilogue 2: gradients
-    // All three TMEM gradient tiles are (hidden row, d column).  The FP32
-    // masters move through shared memory by TMA in quarter chunks of 32 d
-    // columns (W_up / W_gate tiles [32 d][128 hidden], W_down tile
-    // [128 hidden][32 d] 128B-swizzled): the threads only touch TMEM and shared
-    // memory, and the copy engine keeps HBM busy.  Without momentum two W
-    // buffers alternate so the next quarter loads while this one computes.
-    float scale = 1.f;
-    if (update && p.clip > 0.f) scale = fminf(1.f, p.clip * rsqrtf(p.norm2[b] + 1e-8f));
-    if (update && p.clip_out && t == 0 && tid == 0) p.clip_out[(size_t)b * p.n_chunks + p.chunk_index] = scale;
-    const float decay = 1.f - st.alpha_bar;
-    const float beta = p.beta;
-    // With beta == 0 the momentum of this chunk is never read again unless this
-    // is the last chunk of the call that changes this state.
-    const bool write_s = kMomentum || !st.later_active;
-    const bool dbuf = !kMomentum && !write_s;        // W only: two 48 KB buffers
-    const int buf_bytes = dbuf ? 3 * WTILE : 6 * WTILE;
-    uint8_t* wbuf = slots;                           // ring 1 is free once dH is done
-    const int nq = p.d / QW;
-    const int row = q * 32 + lane;                   // hidden row within the tile
+    // ------------------------------------------------------------ loop A: W_up, W_gate
     const int cq = half * 16;                        // this thread's 16 of the quarter's 32 columns
     const bool row_ok = h0 + row < p.h;
-    const bool leader = tid == 0;
-    const bool move = update && !skip;
-    // the next chunk's forward reads the (possibly unchanged) tiles as well
-    const bool stage = (update && !skip) || (kFuse && update);
-    auto load_q = [&](int qi, int buf) {
-      uint8_t* B0 = wbuf + buf * buf_bytes;
-      mbar_arrive_expect_tx(&wfull[buf], kMomentum ? 6 * WTILE : 3 * WTILE);
-      tma_load_3d(B0, &wm.up, &wfull[buf], h0, qi * QW, b);
-      tma_load_3d(B0 + WTILE, &wm.gate, &wfull[buf], h0, qi * QW, b);
-      tma_load_3d(B0 + 2 * WTILE, &wm.down, &wfull[buf], qi * QW, h0, b);
-      if (kMomentum) {
-        tma_load_3d(B0 + 3 * WTILE, &wm.sup, &wfull[buf], h0, qi * QW, b);
-        tma_load_3d(B0 + 4 * WTILE, &wm.sgate, &wfull[buf], h0, qi * QW, b);
-        tma_load_3d(B0 + 5 * WTILE, &wm.sdown, &wfull[buf], qi * QW, h0, b);
-      }
-    };
-    if (stage && leader) {
-      load_q(0, 0);
-      if (dbuf && nq > 1) load_q(1, 1);
-    }
     float acc = 0.f;
     for (int qi = 0; qi < nq; ++qi) {
       const int j = qi >> 2, qq = qi & 3;
@@ -747,10 +840,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         mbar_wait(&gfull, j & 1, p.status);
         tc_fence_after();
       }
-      float gu[16], gg[16], gd[16];
+      float gu[16], gg[16];
       tmem_ld16(tmem_addr(tGU, q * 32, qq * QW + cq), gu);
       tmem_ld16(tmem_addr(tGG, q * 32, qq * QW + cq), gg);
-      tmem_ld16(tmem_addr(tGD, q * 32, qq * QW + cq), gd);
       tmem_wait_ld();
       if (qq == 3) {
         tc_fence_before();
@@ -759,53 +851,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       if (!update) {
         if (row_ok && !skip) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e] + gd[e] * gd[e];
+          for (int e = 0; e < 16; ++e) acc += gu[e] * gu[e] + gg[e] * gg[e];
         }
         continue;
       }
       if (!stage) continue;
-      const int buf = dbuf ? (qi & 1) : 0;
-      mbar_wait(&wfull[buf], dbuf ? ((qi >> 1) & 1) : (qi & 1), p.status);
-      uint8_t* B0 = wbuf + buf * buf_bytes;
+      const int buf = qi % nbufA;
+      mbar_wait(&wfullA[buf], (qi / nbufA) & 1, p.status);
+      uint8_t* B0 = slots + buf * bytesA;
       float* wu = reinterpret_cast<float*>(B0);
       float* wg = reinterpret_cast<float*>(B0 + WTILE);
-      uint8_t* wd = B0 + 2 * WTILE;
-      float* su = reinterpret_cast<float*>(B0 + 3 * WTILE);
-      float* sg = reinterpret_cast<float*>(B0 + 4 * WTILE);
-      uint8_t* sd = B0 + 5 * WTILE;
+      float* su = reinterpret_cast<float*>(B0 + 2 * WTILE);
+      float* sg = reinterpret_cast<float*>(B0 + 3 * WTILE);
       if (!skip) {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int o = (cq + e) * HT + row;            // [32 d][128 hidden]
-        const float nsu = (kMomentum ? beta * su[o] : 0.f) - gu[e] * scale;
-        const float nsg = (kMomentum ? beta * sg[o] : 0.f) - gg[e] * scale;
-        wu[o] = decay * wu[o] + nsu;
-        wg[o] = decay * wg[o] + nsg;
-        if (write_s) {
-          su[o] = nsu;
-          sg[o] = nsg;
+        for (int e = 0; e < 16; ++e) {
+          const int o = (cq + e) * HT + row;            // [32 d][128 hidden]
+          const float nsu = (kMomentum ? beta * su[o] : 0.f) - gu[e] * scale;
+          const float nsg = (kMomentum ? beta * sg[o] : 0.f) - gg[e] * scale;
+          wu[o] = decay * wu[o] + nsu;
+          wg[o] = decay * wg[o] + nsg;
+          if (write_s) {
+            su[o] = nsu;
+            sg[o] = nsg;
+          }
         }
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {                   // [128 hidden][32 d], 128B swizzle
-        const uint32_t o = sw128_offset(row, (cq + 4 * i) * 4);
-        float4 w4 = *reinterpret_cast<float4*>(wd + o);
-        float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (kMomentum) s4 = *reinterpret_cast<float4*>(sd + o);
-        float4 ns;
-        ns.x = (kMomentum ? beta * s4.x : 0.f) - gd[4 * i + 0] * scale;
-        ns.y = (kMomentum ? beta * s4.y : 0.f) - gd[4 * i + 1] * scale;
-        ns.z = (kMomentum ? beta * s4.z : 0.f) - gd[4 * i + 2] * scale;
-        ns.w = (kMomentum ? beta * s4.w : 0.f) - gd[4 * i + 3] * scale;
-        w4.x = decay * w4.x + ns.x;
-        w4.y = decay * w4.y + ns.y;
-        w4.z = decay * w4.z + ns.z;
-        w4.w = decay * w4.w + ns.w;
-        *reinterpret_cast<float4*>(wd + o) = w4;
-        if (write_s) *reinterpret_cast<float4*>(sd + o) = ns;
-      }
-      }  // !skip
-      if constexpr (kFuse) {
+      if (fuse) {
         // bf16 W'_up^T / W'_gate^T columns of this quarter into the next-chunk A tiles
         const int kbi = qi >> 1, half_kb = qi & 1;
         if (half_kb == 0 && kbi > 0) mbar_wait(&ug_free, (kbi - 1) & 1, p.status);
@@ -824,126 +896,193 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
         }
       }
       fence_proxy_async_smem();
-      named_bar(1, NPROD);
-      if (kFuse && leader && (qi & 1)) mbar_arrive(&a_ready);
-      if (leader && !skip) {
-        tma_store_3d(&wm.up, wu, h0, qi * QW, b);
-        tma_store_3d(&wm.gate, wg, h0, qi * QW, b);
-        tma_store_3d(&wm.down, wd, qi * QW, h0, b);
-        if (write_s) {
-          tma_store_3d(&wm.sup, su, h0, qi * QW, b);
-          tma_store_3d(&wm.sgate, sg, h0, qi * QW, b);
-          tma_store_3d(&wm.sdown, sd, qi * QW, h0, b);
+      mbar_arrive(&qdoneA[buf]);                     // the store warp takes the quarter from here
+      if (fuse && (qi & 1)) mbar_arrive(&a_ready);
+    }
+
+    // ------------------------------------------------------------ next chunk: H'
+    if (fuse) {
+      mbar_wait(&ug_free, (nkb - 1) & 1, p.status);          // last U'/G' k-block done
+      tc_fence_after();
+      const int c0 = half * 32;
+      float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
+      float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+#pragma unroll 1
+      for (int c16 = 0; c16 < 32; c16 += 16) {
+        float u[16], g[16];
+        tmem_ld16(tmem_addr(tUN, q * 32, c0 + c16), u);
+        tmem_ld16(tmem_addr(tGN, q * 32, c0 + c16), g);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          us[(size_t)(c0 + c16 + i) * p.hp] = u[i];
+          gs[(size_t)(c0 + c16 + i) * p.hp] = g[i];
         }
+#pragma unroll
+        for (int i = 0; i < 16; i += 8) {
+          uint4 pk;
+          float hv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float gg2 = g[i + e];
+            hv[e] = (c0 + c16 + i + e < p.Cc_next) ? gg2 * sigmoidf_(gg2) * u[i + e] : 0.f;
+          }
+          pk.x = pack_bf16x2(hv[0], hv[1]);
+          pk.y = pack_bf16x2(hv[2], hv[3]);
+          pk.z = pack_bf16x2(hv[4], hv[5]);
+          pk.w = pack_bf16x2(hv[6], hv[7]);
+          *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + c16 + i) * 2)) = pk;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&h_ready);
+    }
+
+    // Drains the next chunk's Z' tile mt (TMEM rows = d, columns = tokens)
+    // into zacc: each half (warps 0-3: tokens 0-31, warps 4-7: tokens 32-63)
+    // stages [32 tokens][128 d] FP32 (slots3's free K-slice half, or sDG, both
+    // idle in loop B) and adds it with one bulk tensor reduction.
+    uint8_t* zstage = half ? sDG : slots3;
+    const bool zissuer = (tid & 127) == 0;
+    auto drain_z = [&](int mt) {
+      const int zb = mt & 1;
+      mbar_wait(&zfull[zb], (mt >> 1) & 1, p.status);
+      tc_fence_after();
+      float z[32];
+      tmem_ld16(tmem_addr(tZN + zb * 64, q * 32, half * 32), *reinterpret_cast<float(*)[16]>(&z[0]));
+      tmem_ld16(tmem_addr(tZN + zb * 64, q * 32, half * 32 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&zfree[zb]);
+      if (zissuer) bulk_wait_read<0>();               // the previous add has left the staging tile
+      named_bar(2 + half, 128);
+      float* zs = reinterpret_cast<float*>(zstage);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) zs[i * 128 + row] = (half * 32 + i < p.Cc_next) ? z[i] : 0.f;
+      fence_proxy_async_smem();
+      named_bar(2 + half, 128);
+      if (zissuer) {
+        tma_reduce_add_2d(&wm.zacc, zstage, mt * 128, b * CT + half * 32);
         bulk_commit();
       }
-      if (leader) {
-        const int nxt = qi + (dbuf ? 2 : 1);
-        if (nxt < nq) {
-          bulk_wait_read<0>();
-          load_q(nxt, buf);
+    };
+
+    // ------------------------------------------------------------ loop B: W_down
+    for (int qi = 0; qi < nq; ++qi) {
+      const int j = qi >> 2, qq = qi & 3, jj = nch + j;
+      if (qq == 0) {
+        mbar_wait(&gfull, jj & 1, p.status);
+        tc_fence_after();
+      }
+      float gd[16];
+      tmem_ld16(tmem_addr(tGD, q * 32, qq * QW + cq), gd);
+      tmem_wait_ld();
+      if (qq == 3) {
+        tc_fence_before();
+        mbar_arrive(&gfree);
+      }
+      if (!update) {
+        if (row_ok && !skip) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc += gd[e] * gd[e];
+        }
+        continue;
+      }
+      if (!stage) continue;
+      const int buf = qi % nbufB;
+      mbar_wait(&wfullB[buf], (qi / nbufB) & 1, p.status);
+      uint8_t* wd = slots + buf * bytesB;
+      uint8_t* sd = wd + WTILE;
+      float4 w4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {                     // [128 hidden][32 d], 128B swizzle
+        const uint32_t o = sw128_offset(row, (cq + 4 * i) * 4);
+        w4[i] = *reinterpret_cast<float4*>(wd + o);
+        if (!skip) {
+          float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (kMomentum) s4 = *reinterpret_cast<float4*>(sd + o);
+          float4 ns;
+          ns.x = (kMomentum ? beta * s4.x : 0.f) - gd[4 * i + 0] * scale;
+          ns.y = (kMomentum ? beta * s4.y : 0.f) - gd[4 * i + 1] * scale;
+          ns.z = (kMomentum ? beta * s4.z : 0.f) - gd[4 * i + 2] * scale;
+          ns.w = (kMomentum ? beta * s4.w : 0.f) - gd[4 * i + 3] * scale;
+          w4[i].x = decay * w4[i].x + ns.x;
+          w4[i].y = decay * w4[i].y + ns.y;
+          w4[i].z = decay * w4[i].z + ns.z;
+          w4[i].w = decay * w4[i].w + ns.w;
+          *reinterpret_cast<float4*>(wd + o) = w4[i];
+          if (write_s) *reinterpret_cast<float4*>(sd + o) = ns;
         }
       }
+      uint8_t* zA = (j & 1) ? sAU : slots + 4 * WTILE;  // Z' A tiles [128 d][128 hidden], MN-major
+      if (fuse) {
+        // this thread's 16 W'_down values of its hidden row -> BF16 A tile of d tile j
+        if (qq == 0) mbar_wait(&emptyz[j & 1], ((j >> 1) & 1) ^ 1, p.status);
+        const int dd = qq * QW + cq;                    // d within the 128-wide tile
+        uint4 p0, p1;
+        p0.x = pack_bf16x2(w4[0].x, w4[0].y); p0.y = pack_bf16x2(w4[0].z, w4[0].w);
+        p0.z = pack_bf16x2(w4[1].x, w4[1].y); p0.w = pack_bf16x2(w4[1].z, w4[1].w);
+        p1.x = pack_bf16x2(w4[2].x, w4[2].y); p1.y = pack_bf16x2(w4[2].z, w4[2].w);
+        p1.z = pack_bf16x2(w4[3].x, w4[3].y); p1.w = pack_bf16x2(w4[3].z, w4[3].w);
+        uint8_t* blk = zA + (dd >> 6) * 16384;
+        *reinterpret_cast<uint4*>(blk + sw128_offset(row, (dd & 63) * 2)) = p0;
+        *reinterpret_cast<uint4*>(blk + sw128_offset(row, (dd & 63) * 2 + 16)) = p1;
+      }
+      fence_proxy_async_smem();
+      if (fuse && qq == 3) mbar_arrive(&fullz[j & 1]);
+      mbar_arrive(&qdoneB[buf]);
+      if (fuse && qq == 3 && j > 0) drain_z(j - 1);
     }
-    if (stage && leader) {
-      bulk_wait_all();
-      asm volatile("fence.proxy.async.global;" ::: "memory");   // W' stores visible to generic loads
+    if (fuse) {
+      drain_z(nch - 1);
+      if (zissuer) bulk_wait_all();
     }
     if (!update) {
       acc = warp_sum(acc);
       if (lane == 0 && !skip) atomicAdd(p.norm2 + b, acc);
     }
-    if constexpr (kFuse) {
-      if (update) {
-        // ---------------------------------------------------------- next chunk: H' and partial Z'
-        named_bar(1, NPROD);                                   // W'_down stores visible to all producers
-        mbar_wait(&ug_free, (nkb - 1) & 1, p.status);          // last U'/G' k-block done
-        tc_fence_after();
-        const int c0 = half * 32;
-        float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
-        float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
-#pragma unroll 1
-        for (int c16 = 0; c16 < 32; c16 += 16) {
-          float u[16], g[16];
-          tmem_ld16(tmem_addr(tUN, q * 32, c0 + c16), u);
-          tmem_ld16(tmem_addr(tGN, q * 32, c0 + c16), g);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            us[(size_t)(c0 + c16 + i) * p.hp] = u[i];
-            gs[(size_t)(c0 + c16 + i) * p.hp] = g[i];
+  } else if (warp == STORE_WARP) {
+    // W' stores of loops A and B and the staging refills behind them, so the
+    // producers never wait for a store to leave shared memory
+    if (lane == 0 && stage) {
+      mbar_wait(&dh_done, 0, p.status);              // the phase-1 ring is free
+      for (int qi = 0; qi < nbufA && qi < nq; ++qi) load_a(qi);
+      for (int qi = 0; qi < nq; ++qi) {
+        const int buf = qi % nbufA;
+        mbar_wait(&qdoneA[buf], (qi / nbufA) & 1, p.status);
+        uint8_t* B0 = slots + buf * bytesA;
+        if (!skip) {
+          tma_store_3d(&wm.up, B0, h0, qi * QW, b);
+          tma_store_3d(&wm.gate, B0 + WTILE, h0, qi * QW, b);
+          if (write_s) {
+            tma_store_3d(&wm.sup, B0 + 2 * WTILE, h0, qi * QW, b);
+            tma_store_3d(&wm.sgate, B0 + 3 * WTILE, h0, qi * QW, b);
           }
-#pragma unroll
-          for (int i = 0; i < 16; i += 8) {
-            uint4 pk;
-            float hv[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float gg2 = g[i + e];
-              hv[e] = (c0 + c16 + i + e < p.Cc_next) ? gg2 * sigmoidf_(gg2) * u[i + e] : 0.f;
-            }
-            pk.x = pack_bf16x2(hv[0], hv[1]);
-            pk.y = pack_bf16x2(hv[2], hv[3]);
-            pk.z = pack_bf16x2(hv[4], hv[5]);
-            pk.w = pack_bf16x2(hv[6], hv[7]);
-            *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + c16 + i) * 2)) = pk;
-          }
+          bulk_commit();
         }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&h_ready);
-        // W'_down rows (just stored, L2-resident) -> MN-major A tiles, drained Z' tiles -> zacc
-        const float* wdg = p.w_down + (size_t)b * p.h * p.d;
-        const int nmt = p.d / 128;
-        for (int mt = 0; mt < nmt; ++mt) {
-          const int sz = mt & 1;
-          mbar_wait(&emptyz[sz], ((mt >> 1) & 1) ^ 1, p.status);
-          uint8_t* sA = slots + sz * SLOT_BYTES;
-#pragma unroll 4
-          for (int jj = 0; jj < 16; ++jj) {
-            const int idx = tid + jj * NPROD;  // 0..4095
-            const int hh = idx >> 5, c4 = (idx & 31) * 4;
-            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (h0 + hh < p.h) f = *reinterpret_cast<const float4*>(wdg + (size_t)(h0 + hh) * p.d + mt * 128 + c4);
-            uint2 pk;
-            pk.x = pack_bf16x2(f.x, f.y);
-            pk.y = pack_bf16x2(f.z, f.w);
-            *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = pk;
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(&fullz[sz]);
-          if (mt > 0) {
-            const int pm = mt - 1, zb = pm & 1;
-            mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
-            tc_fence_after();
-            float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
-#pragma unroll 1
-            for (int c16 = 0; c16 < 32; c16 += 16) {
-              float z[16];
-              tmem_ld16(tmem_addr(tZN + zb * 64, q * 32, c0 + c16), z);
-              tmem_wait_ld();
-              for (int i = 0; i < 16; ++i)
-                if (c0 + c16 + i < p.Cc_next) red_add_f32(za + (size_t)(c0 + c16 + i) * p.d, z[i]);
-            }
-            tc_fence_before();
-            mbar_arrive(&zfree[zb]);
-          }
-        }
-        {
-          const int pm = nmt - 1, zb = pm & 1;
-          mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
-          tc_fence_after();
-          float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
-#pragma unroll 1
-          for (int c16 = 0; c16 < 32; c16 += 16) {
-            float z[16];
-            tmem_ld16(tmem_addr(tZN + zb * 64, q * 32, c0 + c16), z);
-            tmem_wait_ld();
-            for (int i = 0; i < 16; ++i)
-              if (c0 + c16 + i < p.Cc_next) red_add_f32(za + (size_t)(c0 + c16 + i) * p.d, z[i]);
-          }
+        if (qi + nbufA < nq) {
+          bulk_wait_read<0>();
+          load_a(qi + nbufA);
         }
       }
+      bulk_wait_read<0>();                           // loop B's staging overlaps loop A's
+      for (int qi = 0; qi < nbufB && qi < nq; ++qi) load_b(qi);
+      for (int qi = 0; qi < nq; ++qi) {
+        const int buf = qi % nbufB;
+        mbar_wait(&qdoneB[buf], (qi / nbufB) & 1, p.status);
+        uint8_t* B0 = slots + buf * bytesB;
+        if (!skip) {
+          tma_store_3d(&wm.down, B0, qi * QW, h0, b);
+          if (write_s) tma_store_3d(&wm.sdown, B0 + WTILE, qi * QW, h0, b);
+          bulk_commit();
+        }
+        if (qi + nbufB < nq) {
+          bulk_wait_read<0>();
+          load_b(qi + nbufB);
+        }
+      }
+      bulk_wait_all();
     }
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -951,30 +1090,46 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       tma_prefetch_desc(&tmDZ);
       int it = 0;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
+        if (!skip) {
+          for (int hq = 0; hq < 2; ++hq) {
+            const int qi = 2 * kb + hq, fs = qi % NF;
+            mbar_wait(&fempty[fs], ((qi / NF) & 1) ^ 1, p.status);
+            mbar_arrive_expect_tx(&ffull[fs], WTILE);
+            tma_load_3d(fring1 + fs * WTILE, &wm.down, &ffull[fs], qi * QW, h0, b);
+          }
+        }
         const int s = it % NSLOT;
         mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full[s], 8192);
         tma_load_2d(slots + s * BWD_SLOT + 16384, &tmDZ, &full[s], kb * 64, b * CT);
       }
-      for (int j = 0; j < nch; ++j) {
+      // loop A, in the MMA warp's order of use: K slice 0, then per d chunk j
+      // the next chunk's K tile 2j, K slice j+1, K tile 2j+1
+      auto kslice = [&](int j) {   // MN-major B of gradW_up / gradW_gate, 128 d
         mbar_wait(&empty3, (j & 1) ^ 1, p.status);
-        mbar_arrive_expect_tx(&full3, 32768);
-        uint8_t* base = slots3;
-        // K slice (MN-major B for gradW_up/gate): rows = tokens, 64 d each
-        tma_load_3d(base, &tmK, &full3, j * 128, p.tok0, b);
-        tma_load_3d(base + 8192, &tmK, &full3, j * 128 + 64, p.tok0, b);
-        // dZ slice (B for gradW_down, MN-major)
-        tma_load_2d(base + 16384, &tmDZ, &full3, j * 128, b * CT);
-        tma_load_2d(base + 24576, &tmDZ, &full3, j * 128 + 64, b * CT);
-        if (kFuse && update) {
-          // the next chunk's K tiles for the two 64-wide k-blocks of this d chunk
-          for (int kk2 = 0; kk2 < 2; ++kk2) {
-            const int kbi = 2 * j + kk2;
-            if (kbi > 0) mbar_wait(&ug_free, (kbi - 1) & 1, p.status);
-            mbar_arrive_expect_tx(&kfull, 8192);
-            tma_load_3d(sKN, &tmK, &kfull, kbi * 64, p.tok0_next, b);
-          }
-        }
+        mbar_arrive_expect_tx(&full3, 16384);
+        tma_load_3d(slots3, &tmK, &full3, j * 128, p.tok0, b);
+        tma_load_3d(slots3 + 8192, &tmK, &full3, j * 128 + 64, p.tok0, b);
+      };
+      auto knext = [&](int kbi) {  // the next chunk's K tile of 64 d
+        if (kbi > 0) mbar_wait(&ug_free, (kbi - 1) & 1, p.status);
+        mbar_arrive_expect_tx(&kfull, 8192);
+        tma_load_3d(sKN, &tmK, &kfull, kbi * 64, p.tok0_next, b);
+      };
+      const bool fuse = kFuse && update;
+      kslice(0);
+      for (int j = 0; j < nch; ++j) {
+        if (fuse) knext(2 * j);
+        if (j + 1 < nch) kslice(j + 1);
+        if (fuse) knext(2 * j + 1);
+      }
+      // loop B: dZ slices (MN-major B of gradW_down)
+      for (int j = 0; j < nch; ++j) {
+        const int jj = nch + j;
+        mbar_wait(&empty3, (jj & 1) ^ 1, p.status);
+        mbar_arrive_expect_tx(&full3, 16384);
+        tma_load_2d(slots3 + 16384, &tmDZ, &full3, j * 128, b * CT);
+        tma_load_2d(slots3 + 24576, &tmDZ, &full3, j * 128 + 64, b * CT);
       }
     }
   } else {  // MMA warp
@@ -999,59 +1154,79 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_bwd_kernel(const __grid_con
       const uint32_t id_dw = idesc_bf16(128, 128, false, true);   // A = H^T K-major, B = dZ slice MN-major
       const uint32_t du = smem_u32(sDU), dg = smem_u32(sDG), ht = smem_u32(sHt);
       const uint32_t id_ug = idesc_bf16(128, 64, false, false);   // next chunk: A = W'^T K-major, B = K' K-major
-      for (int j = 0; j < nch; ++j) {
+      const bool fuse = kFuse && update;
+      auto grad_ug = [&](int j) {                 // gradW_up^T, gradW_gate^T of d chunk j
         mbar_wait(&full3, j & 1, p.status);
         mbar_wait(&gfree, (j & 1) ^ 1, p.status);
         tc_fence_after();
-        const uint32_t kk = smem_u32(slots3), zz = kk + 16384;
+        const uint32_t kk = smem_u32(slots3);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint32_t acc = ks > 0 ? 1u : 0u;
           const uint64_t kd = sdesc_sw128(kk + ks * 2048, 8192, 1024);
           mma_bf16(tGU, sdesc_sw128(du + ks * 32, 16, 1024), kd, id_uw, acc);
           mma_bf16(tGG, sdesc_sw128(dg + ks * 32, 16, 1024), kd, id_uw, acc);
-          mma_bf16(tGD, sdesc_sw128(ht + ks * 32, 16, 1024), sdesc_sw128(zz + ks * 2048, 8192, 1024), id_dw, acc);
         }
         mma_commit(&empty3);
         mma_commit(&gfull);
-        if (kFuse && update) {
-          for (int kk2 = 0; kk2 < 2; ++kk2) {
-            const int kbi = 2 * j + kk2;
-            mbar_wait(&a_ready, kbi & 1, p.status);
-            mbar_wait(&kfull, kbi & 1, p.status);
-            tc_fence_after();
-            const uint32_t au = smem_u32(sAU), ag = smem_u32(sAG), kn = smem_u32(sKN);
+      };
+      auto next_ug = [&](int kbi) {               // U', G' += K'[kbi] W'[kbi]
+        mbar_wait(&a_ready, kbi & 1, p.status);
+        mbar_wait(&kfull, kbi & 1, p.status);
+        tc_fence_after();
+        const uint32_t au = smem_u32(sAU), ag = smem_u32(sAG), kn = smem_u32(sKN);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t bd = sdesc_sw128(kn + ks * 32, 16, 1024);
-              const uint32_t acc = (kbi > 0 || ks > 0) ? 1u : 0u;
-              mma_bf16(tUN, sdesc_sw128(au + ks * 32, 16, 1024), bd, id_ug, acc);
-              mma_bf16(tGN, sdesc_sw128(ag + ks * 32, 16, 1024), bd, id_ug, acc);
-            }
-            mma_commit(&ug_free);
-          }
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t bd = sdesc_sw128(kn + ks * 32, 16, 1024);
+          const uint32_t acc = (kbi > 0 || ks > 0) ? 1u : 0u;
+          mma_bf16(tUN, sdesc_sw128(au + ks * 32, 16, 1024), bd, id_ug, acc);
+          mma_bf16(tGN, sdesc_sw128(ag + ks * 32, 16, 1024), bd, id_ug, acc);
         }
+        mma_commit(&ug_free);
+      };
+      // loop A: the gradient tiles of d chunk j+1 are issued as soon as the
+      // producers have drained chunk j, ahead of the second U'/G' k-block
+      grad_ug(0);
+      for (int j = 0; j < nch; ++j) {
+        if (fuse) next_ug(2 * j);
+        if (j + 1 < nch) grad_ug(j + 1);
+        if (fuse) next_ug(2 * j + 1);
       }
-      if (kFuse && update) {
+      // loop B: gradW_down^T of d chunk j, then Z' of d tile j - 1
+      const uint32_t id_z = idesc_bf16(128, 64, true, true);
+      const uint32_t hb = smem_u32(sH);
+      auto next_z = [&](int mt) {
+        const int zb = mt & 1;
+        mbar_wait(&fullz[zb], (mt >> 1) & 1, p.status);
+        mbar_wait(&zfree[zb], ((mt >> 1) & 1) ^ 1, p.status);
+        tc_fence_after();
+        const uint32_t a = smem_u32(zb ? sAU : slots + 4 * WTILE);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_bf16(tZN + zb * 64, sdesc_sw128(a + ks * 2048, 16384, 1024), sdesc_sw128(hb + ks * 2048, 8192, 1024),
+                   id_z, ks > 0 ? 1u : 0u);
+        mma_commit(&emptyz[zb]);
+        mma_commit(&zfull[zb]);
+      };
+      if (fuse) {
         mbar_wait(&h_ready, 0, p.status);
         tc_fence_after();
-        const uint32_t id_z = idesc_bf16(128, 64, true, true);
-        const uint32_t hb = smem_u32(sH);
-        const int nmt = p.d / 128;
-        for (int mt = 0; mt < nmt; ++mt) {
-          const int sz = mt & 1, zb = mt & 1;
-          mbar_wait(&fullz[sz], (mt >> 1) & 1, p.status);
-          mbar_wait(&zfree[zb], ((mt >> 1) & 1) ^ 1, p.status);
-          tc_fence_after();
-          const uint32_t a = smem_u32(slots + sz * SLOT_BYTES);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            mma_bf16(tZN + zb * 64, sdesc_sw128(a + ks * 2048, 16384, 1024), sdesc_sw128(hb + ks * 2048, 8192, 1024),
-                     id_z, ks > 0 ? 1u : 0u);
-          mma_commit(&emptyz[sz]);
-          mma_commit(&zfull[zb]);
-        }
       }
+      for (int j = 0; j < nch; ++j) {
+        const int jj = nch + j;
+        mbar_wait(&full3, jj & 1, p.status);
+        mbar_wait(&gfree, (jj & 1) ^ 1, p.status);
+        tc_fence_after();
+        const uint32_t zz = smem_u32(slots3) + 16384;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_bf16(tGD, sdesc_sw128(ht + ks * 32, 16, 1024), sdesc_sw128(zz + ks * 2048, 8192, 1024), id_dw,
+                   ks > 0 ? 1u : 0u);
+        mma_commit(&empty3);
+        mma_commit(&gfull);
+        if (fuse && j > 0) next_z(j - 1);
+      }
+      if (fuse) next_z(nch - 1);
     }
   }
   tc_fence_before();
@@ -1156,6 +1331,10 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     UTTT_TRY(make_tmap_f32(&wmaps.sup, s_up, 3, dims_ug, str_ug, box_ug, false));
     UTTT_TRY(make_tmap_f32(&wmaps.sgate, s_gate, 3, dims_ug, str_ug, box_ug, false));
     UTTT_TRY(make_tmap_f32(&wmaps.sdown, s_down, 3, dims_d, str_d, box_d, true));
+    uint64_t dims_z[2] = {(uint64_t)d, (uint64_t)B * CT};
+    uint64_t str_z[1] = {(uint64_t)d * 4};
+    uint32_t box_z[2] = {128, 32};
+    UTTT_TRY(make_tmap_f32(&wmaps.zacc, p.zacc, 2, dims_z, str_z, box_z, false));
   }
   static bool attr_done = false;
   if (!attr_done) {
@@ -1191,29 +1370,29 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_LN, st);
-      chunk_ln_kernel<<<dim3(CT, B), LN_THREADS, 0, st>>>(p);
+      chunk_ln_for(d)<<<dim3(CT / LN_ROWS, B), LN_ROWS * 32, 0, st>>>(p);
     }
     UTTT_TRY(launch_status());
     if (max_grad_norm > 0.f) {
       ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
       if (momentum_beta != 0.f)
-        chunk_bwd_kernel<true, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+        chunk_bwd_kernel<true, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
       else
-        chunk_bwd_kernel<false, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+        chunk_bwd_kernel<false, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
     }
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
       if (momentum_beta != 0.f) {
         if (fuse)
-          chunk_bwd_kernel<true, true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          chunk_bwd_kernel<true, true><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
         else
-          chunk_bwd_kernel<true, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          chunk_bwd_kernel<true, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
       } else {
         if (fuse)
-          chunk_bwd_kernel<false, true><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          chunk_bwd_kernel<false, true><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
         else
-          chunk_bwd_kernel<false, false><<<grid, NTHREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          chunk_bwd_kernel<false, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
       }
     }
     UTTT_TRY(launch_status());

@@ -123,6 +123,13 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem_src))
                : "memory");
 }
+// element-wise FP32 add of a shared-memory tile into global memory (bulk group)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(smem_src))
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until at most N committed bulk groups are still reading their shared-memory source
 template <int N>
@@ -243,6 +250,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+
+// the two BF16 halves of a packed pair (low half = lower address)
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
