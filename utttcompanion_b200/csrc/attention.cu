@@ -40,32 +40,40 @@ constexpr int MAX_HD = 128;
 constexpr int MAX_REP = 8;
 constexpr int MAX_W = 1024;
 
-// One CTA per (row, kv group).  Scores: every lane owns one ring slot and reads
-// its whole K row with 16-byte loads (all slots' loads in flight at once);
-// softmax over the slots in shared memory; output: threads own one element of
-// the head dimension and a share of the slots, accumulate every query head of
-// the group from one V load, and reduce the shares through shared memory.
-template <int HD>
+__host__ __device__ constexpr size_t dec_smem_floats(int hd, int rep, int w) {
+  return (size_t)rep * (hd + w + DEC_THREADS / 32 + (DEC_THREADS / 32) * hd);
+}
+
+// One CTA per (row, kv group), REP query heads per group.  Scores: every
+// thread owns one ring slot and reads its whole K row with 16-byte loads (all
+// slots' loads in flight at once); softmax over the slots in shared memory;
+// output: HD/8 threads cover one V row with 16-byte loads, so a pass reads
+// 256*8/HD rows; every query head of the group accumulates from the same V
+// load, the rows of a warp are combined by shuffles and the warps through
+// shared memory.  Shared memory (dynamic): q [REP][HD], p [REP][W],
+// reductions [REP][8], partial outputs [8][REP][HD].
+template <int HD, int REP>
 __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int qkv_ld, const int* __restrict__ pos, const int* __restrict__ slot,
-    __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring, int n_heads, int n_kv, int W,
+    __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring, int n_kv, int W,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float scale, __nv_bfloat16* __restrict__ out,
     int out_ld) {
-  __shared__ float qs[MAX_REP][HD];
-  __shared__ float ps[MAX_REP][MAX_W];
-  __shared__ float red[MAX_REP][DEC_THREADS / 32];
-  __shared__ float part[DEC_THREADS / HD][MAX_REP][HD];
+  extern __shared__ float dsm[];
+  float* qs = dsm;                                    // [REP][HD]
+  float* ps = qs + REP * HD;                          // [REP][W]
+  float* red = ps + (size_t)REP * W;                  // [REP][8]
+  float* part = red + REP * (DEC_THREADS / 32);       // [8][REP][HD]
   const int b = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rep = n_heads / n_kv;
+  const int n_heads = n_kv * REP;
   const int p = pos[b];
   const int sl = slot[b];
   const __nv_bfloat16* row = qkv + (size_t)b * qkv_ld;
   const float* cr = cos_t + (size_t)p * HD;
   const float* sr = sin_t + (size_t)p * HD;
   const size_t ring_base = (((size_t)sl * n_kv + g) * W) * HD;
-  for (int i = tid; i < rep * HD; i += DEC_THREADS) {
+  for (int i = tid; i < REP * HD; i += DEC_THREADS) {
     const int r = i / HD, e = i % HD;
-    qs[r][e] = rope_elem(row + (size_t)(g * rep + r) * HD, e, HD, cr, sr);
+    qs[i] = rope_elem(row + (size_t)(g * REP + r) * HD, e, HD, cr, sr);
   }
   const __nv_bfloat16* krow = row + (size_t)n_heads * HD + (size_t)g * HD;
   const __nv_bfloat16* vrow = row + (size_t)(n_heads + n_kv) * HD + (size_t)g * HD;
@@ -78,9 +86,9 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
   const int nvalid = p + 1 < W ? p + 1 : W;
 
   // ---- scores: one slot per thread
-  float mloc[MAX_REP];
+  float mloc[REP];
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) mloc[r] = -INFINITY;
+  for (int r = 0; r < REP; ++r) mloc[r] = -INFINITY;
   for (int s0 = 0; s0 < nvalid; s0 += DEC_THREADS) {
     const int s = s0 + tid;
     if (s < nvalid) {
@@ -88,9 +96,9 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
       uint4 kv[HD / 8];
 #pragma unroll
       for (int c = 0; c < HD / 8; ++c) kv[c] = kp[c];
-      float dot[MAX_REP];
+      float dot[REP];
 #pragma unroll
-      for (int r = 0; r < MAX_REP; ++r) dot[r] = 0.f;
+      for (int r = 0; r < REP; ++r) dot[r] = 0.f;
 #pragma unroll
       for (int c = 0; c < HD / 8; ++c) {
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&kv[c]);
@@ -98,80 +106,122 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
         for (int j = 0; j < 4; ++j) {
           const float2 f = __bfloat1622float2(h2[j]);
 #pragma unroll
-          for (int r = 0; r < MAX_REP; ++r) {
-            if (r < rep) dot[r] += qs[r][c * 8 + 2 * j] * f.x + qs[r][c * 8 + 2 * j + 1] * f.y;
-          }
+          for (int r = 0; r < REP; ++r) dot[r] += qs[r * HD + c * 8 + 2 * j] * f.x + qs[r * HD + c * 8 + 2 * j + 1] * f.y;
         }
       }
 #pragma unroll
-      for (int r = 0; r < MAX_REP; ++r) {
-        if (r < rep) {
-          const float sc = dot[r] * scale;
-          ps[r][s] = sc;
-          mloc[r] = fmaxf(mloc[r], sc);
-        }
+      for (int r = 0; r < REP; ++r) {
+        const float sc = dot[r] * scale;
+        ps[(size_t)r * W + s] = sc;
+        mloc[r] = fmaxf(mloc[r], sc);
       }
     }
   }
   // ---- softmax over the slots of every head
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) {
-    if (r >= rep) break;
+  for (int r = 0; r < REP; ++r) {
     float m = mloc[r];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[r][warp] = m;
+    if (lane == 0) red[r * 8 + warp] = m;
   }
   __syncthreads();
-  float mx[MAX_REP], lsum[MAX_REP];
+  float mx[REP], lsum[REP];
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) {
+  for (int r = 0; r < REP; ++r) {
     mx[r] = -INFINITY;
-    if (r < rep)
-      for (int w = 0; w < DEC_THREADS / 32; ++w) mx[r] = fmaxf(mx[r], red[r][w]);
+    for (int w = 0; w < DEC_THREADS / 32; ++w) mx[r] = fmaxf(mx[r], red[r * 8 + w]);
     lsum[r] = 0.f;
   }
   __syncthreads();
   for (int s = tid; s < nvalid; s += DEC_THREADS) {
 #pragma unroll
-    for (int r = 0; r < MAX_REP; ++r) {
-      if (r < rep) {
-        const float e = __expf(ps[r][s] - mx[r]);
-        ps[r][s] = e;
-        lsum[r] += e;
-      }
+    for (int r = 0; r < REP; ++r) {
+      const float e = __expf(ps[(size_t)r * W + s] - mx[r]);
+      ps[(size_t)r * W + s] = e;
+      lsum[r] += e;
     }
   }
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) {
-    if (r >= rep) break;
+  for (int r = 0; r < REP; ++r) {
     const float l = warp_sum(lsum[r]);
-    if (lane == 0) red[r][warp] = l;
+    if (lane == 0) red[r * 8 + warp] = l;
   }
   __syncthreads();
-  // ---- output: thread = (slot group, head-dim element)
-  constexpr int NG = DEC_THREADS / HD;
-  const int e = tid % HD, grp = tid / HD;
-  float acc[MAX_REP];
+  // ---- output: TPR threads per V row, 8 head-dim elements (16 bytes) each
+  constexpr int TPR = HD / 8, RPI = DEC_THREADS / TPR;
+  const int e8 = (tid % TPR) * 8, rsub = tid / TPR;
+  float acc[REP][8];
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r) acc[r] = 0.f;
-#pragma unroll 4
-  for (int s = grp; s < nvalid; s += NG) {
-    const float v = __bfloat162float(vring[ring_base + (size_t)s * HD + e]);
+  for (int r = 0; r < REP; ++r)
 #pragma unroll
-    for (int r = 0; r < MAX_REP; ++r)
-      if (r < rep) acc[r] += ps[r][s] * v;
+    for (int i = 0; i < 8; ++i) acc[r][i] = 0.f;
+#pragma unroll 2
+  for (int s = rsub; s < nvalid; s += RPI) {
+    const uint4 v4 = *reinterpret_cast<const uint4*>(vring + ring_base + (size_t)s * HD + e8);
+    const float f[8] = {bf16_lo(v4.x), bf16_hi(v4.x), bf16_lo(v4.y), bf16_hi(v4.y),
+                        bf16_lo(v4.z), bf16_hi(v4.z), bf16_lo(v4.w), bf16_hi(v4.w)};
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float pr = ps[(size_t)r * W + s];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[r][i] = fmaf(pr, f[i], acc[r][i]);
+    }
   }
 #pragma unroll
-  for (int r = 0; r < MAX_REP; ++r)
-    if (r < rep) part[grp][r][e] = acc[r];
+  for (int o = TPR; o < 32; o <<= 1)
+#pragma unroll
+    for (int r = 0; r < REP; ++r)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[r][i] += __shfl_xor_sync(0xffffffffu, acc[r][i], o);
+  if (lane < TPR) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float4* pw = reinterpret_cast<float4*>(part + ((size_t)warp * REP + r) * HD + e8);
+      pw[0] = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+      pw[1] = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+    }
+  }
   __syncthreads();
-  for (int i = tid; i < rep * HD; i += DEC_THREADS) {
+  for (int i = tid; i < REP * HD; i += DEC_THREADS) {
     const int r = i / HD, ee = i % HD;
     float a = 0.f, l = 0.f;
-    for (int gg = 0; gg < NG; ++gg) a += part[gg][r][ee];
-    for (int w = 0; w < DEC_THREADS / 32; ++w) l += red[r][w];
-    out[(size_t)b * out_ld + (size_t)(g * rep + r) * HD + ee] = __float2bfloat16(a / l);
+#pragma unroll
+    for (int w = 0; w < DEC_THREADS / 32; ++w) {
+      a += part[((size_t)w * REP + r) * HD + ee];
+      l += red[r * 8 + w];
+    }
+    out[(size_t)b * out_ld + (size_t)(g * REP + r) * HD + ee] = __float2bfloat16(a / l);
+  }
+}
+
+template <int HD, int REP>
+int launch_attn_decode(int B, int n_kv, int W, const __nv_bfloat16* qkv, int qkv_ld, const int* pos, const int* slot,
+                       __nv_bfloat16* kring, __nv_bfloat16* vring, const float* cos_t, const float* sin_t, float scale,
+                       __nv_bfloat16* out, int out_ld, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(attn_decode_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)(dec_smem_floats(HD, REP, MAX_W) * sizeof(float)))));
+    attr = true;
+  }
+  attn_decode_kernel<HD, REP><<<dim3(B, n_kv), DEC_THREADS, dec_smem_floats(HD, REP, W) * sizeof(float), st>>>(
+      qkv, qkv_ld, pos, slot, kring, vring, n_kv, W, cos_t, sin_t, scale, out, out_ld);
+  return launch_status();
+}
+
+template <int HD>
+int attn_decode_rep(int rep, int B, int n_kv, int W, const __nv_bfloat16* qkv, int qkv_ld, const int* pos,
+                    const int* slot, __nv_bfloat16* kring, __nv_bfloat16* vring, const float* cos_t, const float* sin_t,
+                    float scale, __nv_bfloat16* out, int out_ld, cudaStream_t st) {
+  switch (rep) {
+#define UTTT_REP(R) \
+  case R:           \
+    return launch_attn_decode<HD, R>(B, n_kv, W, qkv, qkv_ld, pos, slot, kring, vring, cos_t, sin_t, scale, out, out_ld, st);
+    UTTT_REP(1) UTTT_REP(2) UTTT_REP(3) UTTT_REP(4) UTTT_REP(5) UTTT_REP(6) UTTT_REP(7) UTTT_REP(8)
+#undef UTTT_REP
+    default:
+      return UTTT_ERR_UNSUPPORTED;
   }
 }
 
@@ -305,18 +355,14 @@ extern "C" int uttt_attn_decode(int B, int n_heads, int n_kv, int hd, int W, con
   cudaStream_t st = (cudaStream_t)stream;
   ProfScope ps(UTTT_PROF_ATTN, st);
   const float scale = 1.f / sqrtf((float)hd);
-#define UTTT_DEC(HDV)                                                                                          \
-  attn_decode_kernel<HDV><<<dim3(B, n_kv), DEC_THREADS, 0, st>>>(                                              \
-      (const __nv_bfloat16*)qkv, qkv_ld, pos, slot, (__nv_bfloat16*)k_ring, (__nv_bfloat16*)v_ring, n_heads,  \
-      n_kv, W, rope_cos, rope_sin, scale, (__nv_bfloat16*)out, out_ld)
-  if (hd == 32)
-    UTTT_DEC(32);
-  else if (hd == 64)
-    UTTT_DEC(64);
-  else
-    UTTT_DEC(128);
-#undef UTTT_DEC
-  return launch_status();
+  const int rep = n_heads / n_kv;
+  auto q = (const __nv_bfloat16*)qkv;
+  auto kr = (__nv_bfloat16*)k_ring;
+  auto vr = (__nv_bfloat16*)v_ring;
+  auto o = (__nv_bfloat16*)out;
+  if (hd == 32) return attn_decode_rep<32>(rep, B, n_kv, W, q, qkv_ld, pos, slot, kr, vr, rope_cos, rope_sin, scale, o, out_ld, st);
+  if (hd == 64) return attn_decode_rep<64>(rep, B, n_kv, W, q, qkv_ld, pos, slot, kr, vr, rope_cos, rope_sin, scale, o, out_ld, st);
+  return attn_decode_rep<128>(rep, B, n_kv, W, q, qkv_ld, pos, slot, kr, vr, rope_cos, rope_sin, scale, o, out_ld, st);
 }
 
 extern "C" int uttt_attn_prefill(int B, int T, int start_pos, int hist, int n_heads, int n_kv, int hd, int W,

@@ -1404,8 +1404,9 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
 // fast-weight readout entry point
 // ============================================================================
 namespace uttt {
-int launch_readout_gemv(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
-                        const __nv_bfloat16* wd, const int* state_index, float* zacc, cudaStream_t st);
+int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
+                          const __nv_bfloat16* wd, const int* state_index, const float* ln_w, const float* ln_b,
+                          float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st);
 }
 
 extern "C" size_t uttt_fast_readout_workspace(int B, int d, int h) {
@@ -1431,19 +1432,18 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
   float* zacc = ws.take<float>((size_t)B * CT * d);
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
   const int ob = out_dtype == UTTT_DTYPE_BF16;
-  UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
   if (T == 1 && w_dtype == UTTT_DTYPE_BF16) {
     // decode: one token per state, memory-bound GEMV over the BF16 read copies
-    {
-      ProfScope ps(UTTT_PROF_READOUT, st);
-      UTTT_TRY(launch_readout_gemv(B, d, h, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_up,
-                                   (const __nv_bfloat16*)w_down, state_index, zacc, st));
-    }
-    ProfScope ps(UTTT_PROF_READOUT_LN, st);
-    readout_ln_kernel<<<dim3(1, B), LN_THREADS, 0, st>>>(zacc, CT, (const __nv_bfloat16*)x, 1, 0, 1, d, ln_weight,
-                                                         ln_bias, eps, out, ob);
-    return launch_status();
+    // with the LayerNorm + residual in its last CTA per state; z (B, d) and the
+    // per-state completion counters (B) sit at the front of the z buffer
+    unsigned* done = reinterpret_cast<unsigned*>(zacc + (size_t)B * d);
+    UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * d * sizeof(float) + (size_t)B * sizeof(unsigned), st)));
+    ProfScope ps(UTTT_PROF_READOUT, st);
+    return launch_readout_decode(B, d, h, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_up,
+                                 (const __nv_bfloat16*)w_down, state_index, ln_weight, ln_bias, eps, zacc, done, out,
+                                 ob, st);
   }
+  UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
   static bool attr_done = false;
   if (!attr_done) {
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,

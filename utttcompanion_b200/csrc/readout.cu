@@ -1,14 +1,19 @@
 // Decode-time fast-weight readout: one token per state, each state reading its
 // own BF16 read copies (packed [W_up | W_gate] (d, 2h) and W_down (h, d)),
 // the layout of SharedFastWeightPool.inference_read_weights
-// (model/uttt_layer.py:648-668).  The work is a pair of GEMVs per state, so
-// the kernel is bound by HBM: every weight byte is read exactly once with
-// 16-byte coalesced loads straight into registers, the K dimension is split
-// across the 8 warps of a CTA and reduced through shared memory.
+// (model/uttt_layer.py:648-668), and returning x + LN(z) as
+// swiglu_packed_forward does (:211-257).  The work is a pair of GEMVs per
+// state, so the kernel is bound by HBM: every weight byte is read exactly
+// once with 16-byte coalesced loads straight into registers.
 //
-// grid = (ceil(h / 128) hidden tiles, B states).  A CTA computes u, g for its
-// 128 hidden units, h = silu(g) * u, then the partial z = h W_down[tile, :]
-// and adds it into z (FP32, L2-resident) with one red.add per element.
+// grid = (ceil(h / 128) hidden tiles, B states), 8 warps.  A CTA computes u, g
+// for its 128 hidden units (one warp instruction covers a row of both: lanes
+// 0-15 read u, lanes 16-31 read g; the warps split K = d), h = silu(g) * u,
+// then the partial z = h W_down[tile, :] (the warps split the tile's rows),
+// reduced in shared memory and added into z (FP32) with one red.add per
+// column.  The last CTA of a state to finish (device-scope counter) applies
+// the LayerNorm and the residual.  u, g, silu(g), h and z are rounded to BF16
+// where the reference's autocast rounds them.
 #include "common.cuh"
 #include "host_util.cuh"
 
@@ -18,106 +23,188 @@ namespace {
 constexpr int GT = 128;        // hidden units per CTA
 constexpr int GTHREADS = 256;  // 8 warps
 constexpr int MAXD = 4096;
+constexpr int ZG = 512;        // z columns reduced per shared-memory pass
 
-__device__ __forceinline__ void bf16x4_to_f32(const uint2& v, float (&f)[4]) {
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
-  const float2 a = __bfloat1622float2(p[0]), b = __bfloat1622float2(p[1]);
-  f[0] = a.x;
-  f[1] = a.y;
-  f[2] = b.x;
-  f[3] = b.y;
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x);
+  f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
+  f[4] = bf16_lo(v.z); f[5] = bf16_hi(v.z);
+  f[6] = bf16_lo(v.w); f[7] = bf16_hi(v.w);
 }
 
-__global__ void __launch_bounds__(GTHREADS) readout_gemv_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                const __nv_bfloat16* __restrict__ wp,
-                                                                const __nv_bfloat16* __restrict__ wd,
-                                                                const int* __restrict__ state_index, int d, int h,
-                                                                float* __restrict__ zacc) {
-  __shared__ float xs[MAXD];
-  __shared__ float part[8][2][GT];
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16(v)); }
+
+__device__ __forceinline__ float cta_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < GTHREADS / 32; ++i) s += red[i];
+  return s;
+}
+
+// MD: the largest d of the instantiation (sizes the x stage and the LayerNorm
+// registers); MINB: resident CTAs per SM the registers are budgeted for.
+template <int MD, int MINB>
+__global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wp, const __nv_bfloat16* __restrict__ wd,
+    const int* __restrict__ state_index, int d, int h, const float* __restrict__ ln_w,
+    const float* __restrict__ ln_b, float eps, float* __restrict__ zacc, unsigned* __restrict__ done, void* out,
+    int out_bf16) {
+  __shared__ __align__(16) float xs[MD];
+  __shared__ __align__(16) float part[8][ZG];
+  __shared__ float ug[2 * GT];
   __shared__ float hs[GT];
+  __shared__ float red[GTHREADS / 32];
+  __shared__ int last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y, j0 = blockIdx.x * GT;
   const int state = state_index ? state_index[b] : b;
-  for (int i = tid; i < d; i += GTHREADS) xs[i] = __bfloat162float(x[(size_t)b * d + i]);
+  for (int i = tid; i < d / 8; i += GTHREADS) {
+    float f[8];
+    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + (size_t)b * d) + i), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xs[i * 8 + e] = f[e];
+  }
   __syncthreads();
 
-  // ---- u, g for 128 hidden units: lane -> 4 columns, warp -> 1/8 of K (= d)
-  const __nv_bfloat16* wrow = wp + (size_t)state * d * 2 * h;
-  const int col = j0 + lane * 4;
-  const bool cval = col < h;
-  float au[4] = {0.f, 0.f, 0.f, 0.f}, ag[4] = {0.f, 0.f, 0.f, 0.f};
-  const int kper = d / 8;
-  const int k0 = warp * kper;
-  if (cval) {
+  // ---- u (lanes 0-15) and g (lanes 16-31), 8 columns per lane; warp w takes rows w, w+8, ...
+  {
+    const int c8 = (lane & 15) * 8;
+    const size_t ld = (size_t)2 * h;
+    const __nv_bfloat16* col = wp + (size_t)state * d * ld + (lane >> 4) * h + j0 + c8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (j0 + c8 < h) {
 #pragma unroll 8
-    for (int k = k0; k < k0 + kper; ++k) {
-      const uint2 vu = __ldg(reinterpret_cast<const uint2*>(wrow + (size_t)k * 2 * h + col));
-      const uint2 vg = __ldg(reinterpret_cast<const uint2*>(wrow + (size_t)k * 2 * h + h + col));
-      float fu[4], fg[4];
-      bf16x4_to_f32(vu, fu);
-      bf16x4_to_f32(vg, fg);
-      const float xv = xs[k];
+      for (int k = warp; k < d; k += 8) {
+        float f[8];
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(col + (size_t)k * ld)), f);
+        const float xv = xs[k];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        au[i] = fmaf(xv, fu[i], au[i]);
-        ag[i] = fmaf(xv, fg[i], ag[i]);
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(xv, f[e], acc[e]);
       }
     }
+    float4* pw = reinterpret_cast<float4*>(&part[warp][lane * 8]);
+    pw[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    pw[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
+  __syncthreads();
+  {
+    float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    part[warp][0][lane * 4 + i] = au[i];
-    part[warp][1][lane * 4 + i] = ag[i];
+    for (int w = 0; w < 8; ++w) s += part[w][tid];
+    ug[tid] = round_bf16(s);
   }
   __syncthreads();
   if (tid < GT) {
-    float u = 0.f, g = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      u += part[w][0][tid];
-      g += part[w][1][tid];
-    }
-    hs[tid] = (j0 + tid < h) ? g * sigmoidf_(g) * u : 0.f;
+    const float u = ug[tid], g = ug[GT + tid];
+    const float sg = round_bf16(g * sigmoidf_(g));
+    hs[tid] = (j0 + tid < h) ? round_bf16(sg * u) : 0.f;
   }
   __syncthreads();
 
-  // ---- partial z over this tile's 128 rows of W_down: warp -> 16 rows, lane -> 4 d columns
-  const __nv_bfloat16* drow = wd + (size_t)state * h * d;
-  float* zb = zacc + (size_t)b * 64 * d;   // row 0 of this state's 64-row z block
-  for (int dc = 0; dc < d; dc += 128) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
+  // ---- partial z: warp w takes the tile's rows 16w..16w+15, lane 8 columns of a 256-column chunk
+  const __nv_bfloat16* drow = wd + (size_t)state * h * d + (size_t)j0 * d;
+  float* zrow = zacc + (size_t)b * d;
+  for (int c0 = 0; c0 < d; c0 += ZG) {
+    const int ncol = min(ZG, d - c0);
+    float acc[2][8];
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[cc][e] = 0.f;
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
       const int j = warp * 16 + r;
       if (j0 + j < h) {
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(drow + (size_t)(j0 + j) * d + dc + lane * 4));
-        float f[4];
-        bf16x4_to_f32(v, f);
         const float hv = hs[j];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i] = fmaf(hv, f[i], acc[i]);
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = cc * 256 + lane * 8;
+          if (c < ncol) {
+            float f[8];
+            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(drow + (size_t)j * d + c0 + c)), f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[cc][e] = fmaf(hv, f[e], acc[cc][e]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = cc * 256 + lane * 8;
+      if (c < ncol) {
+        float4* pw = reinterpret_cast<float4*>(&part[warp][c]);
+        pw[0] = make_float4(acc[cc][0], acc[cc][1], acc[cc][2], acc[cc][3]);
+        pw[1] = make_float4(acc[cc][4], acc[cc][5], acc[cc][6], acc[cc][7]);
       }
     }
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) part[warp][0][lane * 4 + i] = acc[i];
-    __syncthreads();
-    if (tid < 128) {
+    for (int t = tid; t < ncol; t += GTHREADS) {
       float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) s += part[w][0][tid];
-      red_add_f32(zb + dc + tid, s);
+      for (int w = 0; w < 8; ++w) s += part[w][t];
+      red_add_f32(zrow + c0 + t, s);
+    }
+    __syncthreads();
+  }
+
+  // ---- the state's last CTA: out = x + LN(bf16(z)) * gamma + beta
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(done + b, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  constexpr int NZ = MD / GTHREADS;
+  float zv[NZ];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NZ; ++i) {
+    const int c = tid + i * GTHREADS;
+    zv[i] = 0.f;
+    if (c < d) {
+      zv[i] = round_bf16(__ldcg(zrow + c));
+      sum += zv[i];
+    }
+  }
+  const float dinv = 1.f / (float)d;
+  const float mean = cta_sum(sum, red) * dinv;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NZ; ++i)
+    if (tid + i * GTHREADS < d) sq += (zv[i] - mean) * (zv[i] - mean);
+  const float rstd = rsqrtf(cta_sum(sq, red) * dinv + eps);
+#pragma unroll
+  for (int i = 0; i < NZ; ++i) {
+    const int c = tid + i * GTHREADS;
+    if (c < d) {
+      const float y = xs[c] + ((zv[i] - mean) * rstd * ln_w[c] + ln_b[c]);
+      if (out_bf16)
+        reinterpret_cast<__nv_bfloat16*>(out)[(size_t)b * d + c] = __float2bfloat16(y);
+      else
+        reinterpret_cast<float*>(out)[(size_t)b * d + c] = y;
     }
   }
 }
 
 }  // namespace
 
-int launch_readout_gemv(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
-                        const __nv_bfloat16* wd, const int* state_index, float* zacc, cudaStream_t st) {
-  if (d % 128 != 0 || d > MAXD) return UTTT_ERR_UNSUPPORTED;
-  readout_gemv_kernel<<<dim3((h + GT - 1) / GT, B), GTHREADS, 0, st>>>(x, wp, wd, state_index, d, h, zacc);
+// zacc: (B, d) FP32 and done: (B) counters, both zero on entry.
+int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
+                          const __nv_bfloat16* wd, const int* state_index, const float* ln_w, const float* ln_b,
+                          float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st) {
+  if (d % 128 != 0 || d > MAXD || h % 8 != 0) return UTTT_ERR_UNSUPPORTED;
+  const dim3 grid((h + GT - 1) / GT, B);
+  if (d <= 1024)   // small states: 4 CTAs per SM keep a short launch in one wave
+    readout_decode_kernel<1024, 4><<<grid, GTHREADS, 0, st>>>(x, wp, wd, state_index, d, h, ln_w, ln_b, eps, zacc,
+                                                              done, out, out_bf16);
+  else
+    readout_decode_kernel<MAXD, 3><<<grid, GTHREADS, 0, st>>>(x, wp, wd, state_index, d, h, ln_w, ln_b, eps, zacc,
+                                                              done, out, out_bf16);
   return launch_status();
 }
 
