@@ -95,6 +95,13 @@ int uttt_selftest_gemm(int mode, int M, int N, int K, const void* a, const void*
  *   token_loss     FP32 (B, T): 0.5*||f_W(k_t) - v_t||^2 (/d if normalize)
  *                  per token (the unweighted surprise terms), or NULL.
  *   clip_scale     FP32 (B, n_chunks): applied clip factor per chunk, or NULL.
+ *   n_states,      ragged batches: row b of the activations (and of mask,
+ *   state_rows     token_loss, clip_scale, out) updates fast-weight state
+ *                  state_rows[b] (int32 device array, B entries, distinct)
+ *                  of w_* / s_*, which hold n_states states.  NULL: row b
+ *                  updates state b and n_states must be B (or <= 0).  A row
+ *                  whose entry is not below n_states touches nothing and
+ *                  records UTTT_ERR_INVALID in the workspace status word.
  *
  * Requires d % 128 == 0, 1 <= C <= 64.
  */
@@ -104,10 +111,12 @@ int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_c
                      float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
                      const float* ln_weight, const float* ln_bias, float momentum_beta, float max_grad_norm,
                      int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss,
-                     float* clip_scale, void* workspace, size_t workspace_bytes, void* stream);
+                     float* clip_scale, int n_states, const int* state_rows, void* workspace,
+                     size_t workspace_bytes, void* stream);
 
 /*
- * Allocation-free chunk write.  No counterpart in the reference.
+ * Allocation-free chunk write.  No counterpart in the reference.  (Rows map
+ * to states one to one: n_states = B, state_rows = NULL.)
  *
  * For callers that cannot call cudaMalloc: serving loops whose HBM is fully
  * reserved up front (an extra allocation would fail, and cudaMalloc / cudaFree

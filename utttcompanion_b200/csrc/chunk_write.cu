@@ -87,6 +87,7 @@ struct ChunkParams {
   long long ss_ug, ss_d;
   int ld_ug;
   const int* state_index;
+  int n_states;        // > 0: state_index entries must be below it (checked on the device)
 };
 
 template <typename WT>
@@ -173,6 +174,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
   const int h0 = t * HT;
   const int nkb = p.d / 64;
   const int nmt = p.d / 128;
+  if (p.state_index && p.n_states > 0 && (unsigned)p.state_index[b] >= (unsigned)p.n_states) {
+    if (tid == 0) set_status(p.status, UTTT_ERR_INVALID);   // a bad row -> state map entry: touch nothing
+    return;
+  }
 
   if (tid == 0) {
     for (int i = 0; i < NSLOT; ++i) {
@@ -607,11 +612,11 @@ __global__ void __launch_bounds__(LN_THREADS) readout_ln_kernel(const float* __r
 // bwd: dH, dU, dG and the three weight gradients; NORM pass accumulates
 // ||grad||^2, UPDATE pass applies momentum / decay / clip in place.
 // ============================================================================
-// FP32 tensor maps of the masters for the TMA-staged update epilogue:
-// up/gate/s_up/s_gate over (h, d, B) with 128 x 32 boxes, down/s_down over
-// (d, h, B) with 32 x 128 boxes (128-byte swizzle).
+// FP32 tensor maps of the W masters for the TMA-staged update epilogue:
+// up/gate over (h, d, states) with 128 x 32 boxes, down over (d, h, states)
+// with 32 x 128 boxes (128-byte swizzle).
 struct WMaps {
-  CUtensorMap up, gate, down, sup, sgate, sdown;
+  CUtensorMap up, gate, down;
   CUtensorMap zacc;   // FP32 (d, B * 64) partial-Z accumulator, 128 x 32 boxes
 };
 constexpr int QW = 32;                    // d columns per staged quarter chunk
@@ -648,6 +653,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x, b = blockIdx.y;
+  // row b's activations and workspace rows are compact; its fast-weight state is sb
+  const int sb = p.state_index ? p.state_index[b] : b;
+  if (p.state_index && (unsigned)sb >= (unsigned)p.n_states) {
+    if (tid == 0) set_status(p.status, UTTT_ERR_INVALID);
+    return;
+  }
   const int h0 = t * HT;
   const int nkb = p.d / 64;
   const int nch = p.d / 128;
@@ -719,9 +730,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   // With beta == 0 the momentum of this chunk is never read again unless this
   // is the last chunk of the call that changes this state.
   const bool write_s = kMomentum || !st.later_active;
-  const bool wide = kMomentum || write_s;          // staging holds S tiles as well
-  const int bytesA = wide ? 4 * WTILE : 2 * WTILE, nbufA = wide ? 1 : 3;
-  const int bytesB = wide ? 2 * WTILE : WTILE, nbufB = wide ? 2 : 4;
+  // Staging holds W only (3 quarters of W_up + W_gate, 4 of W_down in flight);
+  // each producer moves its own momentum values between registers and HBM
+  // (lanes are consecutive hidden rows, so S_up / S_gate accesses coalesce).
+  constexpr int bytesA = 2 * WTILE, nbufA = 3;
+  constexpr int bytesB = WTILE, nbufB = 4;
   const int nq = p.d / QW;
   const bool fuse = kFuse && update;
   // the next chunk's forward reads the (possibly unchanged) tiles as well
@@ -729,21 +742,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   auto load_a = [&](int qi) {
     const int buf = qi % nbufA;
     uint8_t* B0 = slots + buf * bytesA;
-    mbar_arrive_expect_tx(&wfullA[buf], kMomentum ? 4 * WTILE : 2 * WTILE);
-    tma_load_3d(B0, &wm.up, &wfullA[buf], h0, qi * QW, b);
-    tma_load_3d(B0 + WTILE, &wm.gate, &wfullA[buf], h0, qi * QW, b);
-    if (kMomentum) {
-      tma_load_3d(B0 + 2 * WTILE, &wm.sup, &wfullA[buf], h0, qi * QW, b);
-      tma_load_3d(B0 + 3 * WTILE, &wm.sgate, &wfullA[buf], h0, qi * QW, b);
-    }
+    mbar_arrive_expect_tx(&wfullA[buf], 2 * WTILE);
+    tma_load_3d(B0, &wm.up, &wfullA[buf], h0, qi * QW, sb);
+    tma_load_3d(B0 + WTILE, &wm.gate, &wfullA[buf], h0, qi * QW, sb);
   };
   auto load_b = [&](int qi) {
     const int buf = qi % nbufB;
     uint8_t* B0 = slots + buf * bytesB;
-    mbar_arrive_expect_tx(&wfullB[buf], kMomentum ? 2 * WTILE : WTILE);
-    tma_load_3d(B0, &wm.down, &wfullB[buf], qi * QW, h0, b);
-    if (kMomentum) tma_load_3d(B0 + WTILE, &wm.sdown, &wfullB[buf], qi * QW, h0, b);
+    mbar_arrive_expect_tx(&wfullB[buf], WTILE);
+    tma_load_3d(B0, &wm.down, &wfullB[buf], qi * QW, h0, sb);
   };
+  // momentum of this state: s_* (d, h) for up / gate, (h, d) for down
+  const size_t s_off = (size_t)sb * p.d * p.h;
 
   if (warp < 8) {
     // ------------------------------------------------------------ W_down rows -> A (K-major)
@@ -836,6 +846,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     float acc = 0.f;
     for (int qi = 0; qi < nq; ++qi) {
       const int j = qi >> 2, qq = qi & 3;
+      // this quarter's momentum (issued before the waits so its latency overlaps them)
+      const bool s_io = update && !skip && row_ok;
+      float su[16], sg[16];
+      const size_t so = s_off + (size_t)(qi * QW + cq) * p.h + h0 + row;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        su[e] = (kMomentum && s_io) ? p.s_up[so + (size_t)e * p.h] : 0.f;
+        sg[e] = (kMomentum && s_io) ? p.s_gate[so + (size_t)e * p.h] : 0.f;
+      }
       if (qq == 0) {
         mbar_wait(&gfull, j & 1, p.status);
         tc_fence_after();
@@ -861,19 +880,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       uint8_t* B0 = slots + buf * bytesA;
       float* wu = reinterpret_cast<float*>(B0);
       float* wg = reinterpret_cast<float*>(B0 + WTILE);
-      float* su = reinterpret_cast<float*>(B0 + 2 * WTILE);
-      float* sg = reinterpret_cast<float*>(B0 + 3 * WTILE);
       if (!skip) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int o = (cq + e) * HT + row;            // [32 d][128 hidden]
-          const float nsu = (kMomentum ? beta * su[o] : 0.f) - gu[e] * scale;
-          const float nsg = (kMomentum ? beta * sg[o] : 0.f) - gg[e] * scale;
+          const float nsu = (kMomentum ? beta * su[e] : 0.f) - gu[e] * scale;
+          const float nsg = (kMomentum ? beta * sg[e] : 0.f) - gg[e] * scale;
           wu[o] = decay * wu[o] + nsu;
           wg[o] = decay * wg[o] + nsg;
-          if (write_s) {
-            su[o] = nsu;
-            sg[o] = nsg;
+          su[e] = nsu;
+          sg[e] = nsg;
+        }
+        if (write_s && row_ok) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            p.s_up_out[so + (size_t)e * p.h] = su[e];
+            p.s_gate_out[so + (size_t)e * p.h] = sg[e];
           }
         }
       }
@@ -991,17 +1013,23 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       }
       if (!stage) continue;
       const int buf = qi % nbufB;
+      // this thread's 16 momentum values of S_down row h0 + row (64 contiguous bytes)
+      const bool sd_io = update && !skip && row_ok;
+      const size_t sdo = s_off + (size_t)(h0 + row) * p.d + qi * QW + cq;
+      float4 sdv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        sdv[i] = (kMomentum && sd_io) ? reinterpret_cast<const float4*>(p.s_down + sdo)[i]
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
       mbar_wait(&wfullB[buf], (qi / nbufB) & 1, p.status);
       uint8_t* wd = slots + buf * bytesB;
-      uint8_t* sd = wd + WTILE;
       float4 w4[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {                     // [128 hidden][32 d], 128B swizzle
         const uint32_t o = sw128_offset(row, (cq + 4 * i) * 4);
         w4[i] = *reinterpret_cast<float4*>(wd + o);
         if (!skip) {
-          float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (kMomentum) s4 = *reinterpret_cast<float4*>(sd + o);
+          const float4 s4 = sdv[i];
           float4 ns;
           ns.x = (kMomentum ? beta * s4.x : 0.f) - gd[4 * i + 0] * scale;
           ns.y = (kMomentum ? beta * s4.y : 0.f) - gd[4 * i + 1] * scale;
@@ -1012,8 +1040,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
           w4[i].z = decay * w4[i].z + ns.z;
           w4[i].w = decay * w4[i].w + ns.w;
           *reinterpret_cast<float4*>(wd + o) = w4[i];
-          if (write_s) *reinterpret_cast<float4*>(sd + o) = ns;
+          sdv[i] = ns;
         }
+      }
+      if (write_s && sd_io) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(p.s_down_out + sdo)[i] = sdv[i];
       }
       uint8_t* zA = (j & 1) ? sAU : slots + 4 * WTILE;  // Z' A tiles [128 d][128 hidden], MN-major
       if (fuse) {
@@ -1053,12 +1085,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         mbar_wait(&qdoneA[buf], (qi / nbufA) & 1, p.status);
         uint8_t* B0 = slots + buf * bytesA;
         if (!skip) {
-          tma_store_3d(&wm.up, B0, h0, qi * QW, b);
-          tma_store_3d(&wm.gate, B0 + WTILE, h0, qi * QW, b);
-          if (write_s) {
-            tma_store_3d(&wm.sup, B0 + 2 * WTILE, h0, qi * QW, b);
-            tma_store_3d(&wm.sgate, B0 + 3 * WTILE, h0, qi * QW, b);
-          }
+          tma_store_3d(&wm.up, B0, h0, qi * QW, sb);
+          tma_store_3d(&wm.gate, B0 + WTILE, h0, qi * QW, sb);
           bulk_commit();
         }
         if (qi + nbufA < nq) {
@@ -1073,8 +1101,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         mbar_wait(&qdoneB[buf], (qi / nbufB) & 1, p.status);
         uint8_t* B0 = slots + buf * bytesB;
         if (!skip) {
-          tma_store_3d(&wm.down, B0, qi * QW, h0, b);
-          if (write_s) tma_store_3d(&wm.sdown, B0 + WTILE, qi * QW, h0, b);
+          tma_store_3d(&wm.down, B0, qi * QW, h0, sb);
           bulk_commit();
         }
         if (qi + nbufB < nq) {
@@ -1095,7 +1122,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
             const int qi = 2 * kb + hq, fs = qi % NF;
             mbar_wait(&fempty[fs], ((qi / NF) & 1) ^ 1, p.status);
             mbar_arrive_expect_tx(&ffull[fs], WTILE);
-            tma_load_3d(fring1 + fs * WTILE, &wm.down, &ffull[fs], qi * QW, h0, b);
+            tma_load_3d(fring1 + fs * WTILE, &wm.down, &ffull[fs], qi * QW, h0, sb);
           }
         }
         const int s = it % NSLOT;
@@ -1259,9 +1286,11 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
                                 const float* mask, float* w_up, float* w_gate, float* w_down, float* s_up,
                                 float* s_gate, float* s_down, const float* ln_weight, const float* ln_bias,
                                 float momentum_beta, float max_grad_norm, int normalize_by_dim, float eps,
-                                void* out, int out_dtype, float* token_loss, float* clip_scale, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+                                void* out, int out_dtype, float* token_loss, float* clip_scale, int n_states,
+                                const int* state_rows, void* workspace, size_t workspace_bytes, void* stream) {
   UTTT_REQUIRE(B > 0 && T > 0 && C > 0 && d > 0 && h > 0 && n_chunks >= 0 && chunk_begin >= 0, UTTT_ERR_INVALID);
+  if (n_states <= 0) n_states = B;
+  UTTT_REQUIRE(state_rows != nullptr || n_states == B, UTTT_ERR_INVALID);
   UTTT_REQUIRE(k && v && eta && alpha && w_up && w_gate && w_down && s_up && s_gate && s_down && ln_weight &&
                    ln_bias && workspace,
                UTTT_ERR_INVALID);
@@ -1301,7 +1330,8 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   p.status = ws_status(workspace);
   p.src_up = w_up; p.src_gate = w_gate; p.src_down = w_down;
   p.ss_ug = (long long)d * h; p.ss_d = (long long)h * d; p.ld_ug = h;
-  p.state_index = nullptr;
+  p.state_index = state_rows;
+  p.n_states = n_states;
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
 
   CUtensorMap tmK, tmDZ;
@@ -1319,18 +1349,15 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   }
   WMaps wmaps;
   {
-    uint64_t dims_ug[3] = {(uint64_t)h, (uint64_t)d, (uint64_t)B};
+    uint64_t dims_ug[3] = {(uint64_t)h, (uint64_t)d, (uint64_t)n_states};
     uint64_t str_ug[2] = {(uint64_t)h * 4, (uint64_t)d * h * 4};
     uint32_t box_ug[3] = {HT, QW, 1};
-    uint64_t dims_d[3] = {(uint64_t)d, (uint64_t)h, (uint64_t)B};
+    uint64_t dims_d[3] = {(uint64_t)d, (uint64_t)h, (uint64_t)n_states};
     uint64_t str_d[2] = {(uint64_t)d * 4, (uint64_t)h * d * 4};
     uint32_t box_d[3] = {QW, HT, 1};
     UTTT_TRY(make_tmap_f32(&wmaps.up, w_up, 3, dims_ug, str_ug, box_ug, false));
     UTTT_TRY(make_tmap_f32(&wmaps.gate, w_gate, 3, dims_ug, str_ug, box_ug, false));
     UTTT_TRY(make_tmap_f32(&wmaps.down, w_down, 3, dims_d, str_d, box_d, true));
-    UTTT_TRY(make_tmap_f32(&wmaps.sup, s_up, 3, dims_ug, str_ug, box_ug, false));
-    UTTT_TRY(make_tmap_f32(&wmaps.sgate, s_gate, 3, dims_ug, str_ug, box_ug, false));
-    UTTT_TRY(make_tmap_f32(&wmaps.sdown, s_down, 3, dims_d, str_d, box_d, true));
     uint64_t dims_z[2] = {(uint64_t)d, (uint64_t)B * CT};
     uint64_t str_z[1] = {(uint64_t)d * 4};
     uint32_t box_z[2] = {128, 32};

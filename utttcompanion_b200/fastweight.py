@@ -61,22 +61,36 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
                 momentum_beta: float, max_inner_grad_norm: float, normalize_by_dim: bool, eps: float,
                 chunk_size: int = 64, chunk_begin: int = 0, n_chunks: Optional[int] = None,
                 out: Optional[torch.Tensor] = None, token_loss: Optional[torch.Tensor] = None,
-                clip_scale: Optional[torch.Tensor] = None) -> None:
+                clip_scale: Optional[torch.Tensor] = None, state_rows: Optional[torch.Tensor] = None) -> None:
     """In-place multi-chunk write over ``(B, T, d)`` BF16 keys/values.
 
     Applies ``n_chunks`` consecutive chunk steps (``SharedFastWeightPool.chunk_step``
     chained by ``uTTTLayer.forward``, ``model/uttt_layer.py:1447-1475``) to FP32
     masters ``w_*``/``s_*`` in place.  ``out`` (optional) receives ``v_hat``,
     which is the readout f_W(k) when the caller reads with q = k.
+    ``state_rows`` (int32 (B,), distinct): row b updates state ``state_rows[b]``
+    of masters holding any number of states (ragged batches); by default row b
+    updates state b.
     """
-    _require_cuda(k, v, eta, alpha, w_up, w_gate, w_down, s_up, s_gate, s_down, ln_weight, ln_bias, token_mask)
+    _require_cuda(k, v, eta, alpha, w_up, w_gate, w_down, s_up, s_gate, s_down, ln_weight, ln_bias, token_mask,
+                  state_rows)
     B, T, d = k.shape
     h = w_up.shape[-1]
+    S = w_up.shape[0]
     for t in (w_up, w_gate, w_down, s_up, s_gate, s_down):
         if t.dtype != torch.float32 or not t.is_contiguous():
             raise ValueError("fast-weight masters must be contiguous FP32")
-    if w_up.shape != (B, d, h) or w_gate.shape != (B, d, h) or w_down.shape != (B, h, d):
-        raise ValueError("fast-weight shapes must be (B,d,h),(B,d,h),(B,h,d)")
+    if w_up.shape != (S, d, h) or w_gate.shape != (S, d, h) or w_down.shape != (S, h, d):
+        raise ValueError("fast-weight shapes must be (S,d,h),(S,d,h),(S,h,d)")
+    if state_rows is None:
+        if S != B:
+            raise ValueError(f"{S} fast-weight states for {B} rows: pass state_rows")
+    else:
+        if state_rows.dtype != torch.int32 or state_rows.numel() != B or not state_rows.is_contiguous():
+            raise ValueError("state_rows must be a contiguous int32 tensor with one entry per row")
+    for t in (s_up, s_gate, s_down):
+        if t.shape[0] != S:
+            raise ValueError("momentum buffers must hold as many states as the masters")
     if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or not k.is_contiguous() or not v.is_contiguous():
         raise ValueError("k and v must be contiguous BF16 (B, T, d)")
     if n_chunks is None:
@@ -92,7 +106,7 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
         _ptr(token_mask), _ptr(w_up), _ptr(w_gate), _ptr(w_down), _ptr(s_up), _ptr(s_gate), _ptr(s_down),
         _ptr(ln_weight), _ptr(ln_bias), float(momentum_beta), float(max_inner_grad_norm),
         int(bool(normalize_by_dim)), float(eps), _ptr(out), out_dtype, _ptr(token_loss), _ptr(clip_scale),
-        ws.data_ptr(), ws.numel(), _stream(k.device))
+        S, _ptr(state_rows), ws.data_ptr(), ws.numel(), _stream(k.device))
     _lib.check(st, "uttt_chunk_write")
 
 

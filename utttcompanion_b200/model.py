@@ -338,9 +338,11 @@ class UtttB200:
     def test_time_update_batch(self, interaction_ids: torch.Tensor, fast_state: FastState,
                                attention_mask: Optional[torch.Tensor] = None):
         """The write of B personas at once: rows of ``interaction_ids`` (B, T) with
-        right-padding masks; ``fast_state`` holds B stacked states.  Every chunk of
-        every layer is one packed launch sequence over all rows; a row whose
-        chunk is all padding keeps its state exactly (model/uttt_layer.py:513-520).
+        masks; ``fast_state`` holds B stacked states.  Every chunk of every layer is
+        one packed launch sequence over the rows still in the batch: a row leaves
+        it once no valid token is left (its state is final, since a chunk without
+        valid tokens keeps W and S exactly, model/uttt_layer.py:513-520), so a
+        ragged batch costs what its rows' own lengths cost.
         Returns (new stacked state, per-row mean surprise, per-row per-layer surprise).
         Per-row statistics follow the reference's single-persona definitions
         (model/uttt_model.py:598-607, 833-838)."""
@@ -350,38 +352,64 @@ class UtttB200:
         B, T = ids.shape
         C, W = cfg.chunk_size, cfg.sliding_window_size
         d, hd, nh, nkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+        L = cfg.n_layers
         if C > 64:
             raise ValueError("chunk_size > 64 is not supported by the B200 write kernels")
         if fast_state.w_up.shape[0] != B:
             raise ValueError(f"fast_state holds {fast_state.w_up.shape[0]} states for {B} rows")
         cur = fast_state.clone()
-        mask = None if attention_mask is None else attention_mask.reshape(B, T).to(device=dev,
-                                                                                 dtype=torch.float32).contiguous()
+        if attention_mask is None:
+            mask_all, last = None, [T - 1] * B
+        else:
+            m_host = attention_mask.reshape(B, T).to(dtype=torch.float32).cpu()
+            pos_idx = torch.arange(T).expand(B, T)
+            last = torch.where(m_host != 0, pos_idx, torch.full_like(pos_idx, -1)).max(dim=1).values.tolist()
+            mask_all = m_host.to(device=dev).contiguous()
         h_all = self._embed(ids).reshape(B, T, d)
-        hist_k: List[Optional[torch.Tensor]] = [None] * cfg.n_layers
-        hist_v: List[Optional[torch.Tensor]] = [None] * cfg.n_layers
-        rows_idx = torch.arange(B, dtype=torch.int32, device=dev)
+        hist_k: List[Optional[torch.Tensor]] = [None] * L
+        hist_v: List[Optional[torch.Tensor]] = [None] * L
+        alive = list(range(B))
+        rows = torch.arange(B, dtype=torch.int32, device=dev)
         chunk_losses, counts = [], []
         for off in range(0, T, C):
             Cc = min(C, T - off)
-            R = B * Cc
+            keep_rows = [r for r in alive if last[r] >= off]
+            if not keep_rows:
+                cur.step += L                      # the reference still steps through padded chunks
+                continue
+            if len(keep_rows) < len(alive):        # compact: rows with nothing left leave the batch
+                sel = torch.tensor([alive.index(r) for r in keep_rows], dtype=torch.long, device=dev)
+                for i in range(L):
+                    if hist_k[i] is not None:
+                        hist_k[i] = hist_k[i].index_select(0, sel)
+                        hist_v[i] = hist_v[i].index_select(0, sel)
+                alive = keep_rows
+                rows = torch.tensor(alive, dtype=torch.int32, device=dev)
+            Bc = len(alive)
+            R = Bc * Cc
+            rows_l = rows.long()
             rp, rd = self.read_copies(cur.w_up, cur.w_gate, cur.w_down)      # chunk-start snapshot
-            hidden = h_all[:, off:off + Cc].reshape(R, d).clone()
-            m = None if mask is None else mask[:, off:off + Cc].contiguous()
-            layer_loss = []
+            hidden = h_all[rows_l, off:off + Cc].reshape(R, d).contiguous()
+            m = None if mask_all is None else mask_all[rows_l, off:off + Cc].contiguous()
+            # Every layer reads the chunk-start snapshot, so the slow forward of all L
+            # layers runs first and produces each layer's write inputs (layer-major) ...
+            K = torch.empty(L, R, d, dtype=torch.bfloat16, device=dev)
+            V = torch.empty_like(K)
+            ETA = torch.empty(L, R, dtype=torch.float32, device=dev)
+            ALPHA = torch.empty_like(ETA)
             for i, lay in enumerate(self.layers):
                 x = self._rmsnorm(hidden, lay.attn_norm)
                 qkv = torch.empty(R, self.qkv_dim, dtype=torch.bfloat16, device=dev)
                 self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
                 hist = 0 if hist_k[i] is None else hist_k[i].shape[2]
-                kb = torch.empty(B, nkv, hist + Cc, hd, dtype=torch.bfloat16, device=dev)
+                kb = torch.empty(Bc, nkv, hist + Cc, hd, dtype=torch.bfloat16, device=dev)
                 vb = torch.empty_like(kb)
                 if hist:
                     kb[:, :, :hist].copy_(hist_k[i])
                     vb[:, :, :hist].copy_(hist_v[i])
                 qs = torch.empty(R, nh * hd, dtype=torch.bfloat16, device=dev)
                 att = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
-                _lib.check(self.lib.uttt_attn_prefill(B, Cc, off, hist, nh, nkv, hd, W, qkv.data_ptr(), self.qkv_dim,
+                _lib.check(self.lib.uttt_attn_prefill(Bc, Cc, off, hist, nh, nkv, hd, W, qkv.data_ptr(), self.qkv_dim,
                                                       self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
                                                       qs.data_ptr(), kb.data_ptr(), vb.data_ptr(), att.data_ptr(),
                                                       self._st()), "uttt_attn_prefill")
@@ -391,39 +419,52 @@ class UtttB200:
                 hh = hidden.clone()
                 self._resid_linear(hh, att, lay.wo)
                 x2 = self._rmsnorm(hh, lay.uttt_norm)
-                q = torch.empty(B, Cc, d, dtype=torch.bfloat16, device=dev)
-                k = torch.empty(B, Cc, d, dtype=torch.bfloat16, device=dev)
-                v = torch.empty(B, Cc, d, dtype=torch.bfloat16, device=dev)
-                eta = torch.empty(B, Cc, dtype=torch.float32, device=dev)
-                alpha = torch.empty(B, Cc, dtype=torch.float32, device=dev)
+                q = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
                 self._linear(x2, lay.slow, [                       # fused_slow_projections, :1193-1231
                     _seg(0, d, _lib.SEG_RMSNORM, q, d, lay.q_norm),
-                    _seg(d, d, _lib.SEG_RMSNORM, k, d, lay.k_norm),
-                    _seg(2 * d, d, _lib.SEG_RMSNORM, v, d),
-                    _seg(3 * d, 1, _lib.SEG_SIGMOID, eta, 1, lay.b_eta, 0, cfg.base_inner_lr, out_f32=True),
-                    _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, alpha, 1, lay.b_alpha, 0, cfg.base_weight_decay,
+                    _seg(d, d, _lib.SEG_RMSNORM, K[i], d, lay.k_norm),
+                    _seg(2 * d, d, _lib.SEG_RMSNORM, V[i], d),
+                    _seg(3 * d, 1, _lib.SEG_SIGMOID, ETA[i], 1, lay.b_eta, 0, cfg.base_inner_lr, out_f32=True),
+                    _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, ALPHA[i], 1, lay.b_alpha, 0, cfg.base_weight_decay,
                          out_f32=True),
                 ])
-                out = fast_readout(q, rp, None, rd, cur.ln_weight, cur.ln_bias, cfg.rms_norm_eps,
-                                   state_index=rows_idx, packed=True)
-                loss = torch.empty(B, Cc, dtype=torch.float32, device=dev)
-                chunk_write(k, v, eta, alpha, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,
-                            cur.ln_weight, cur.ln_bias, m, cfg.momentum_beta, float(cfg.max_inner_grad_norm or 0.0),
-                            cfg.normalize_loss_by_dim, cfg.rms_norm_eps, chunk_size=Cc, token_loss=loss)
-                if m is None:
-                    layer_loss.append(loss.mean(dim=1))
-                else:
-                    layer_loss.append((loss * m).sum(dim=1) / m.sum(dim=1).clamp_min(1.0))
+                out = fast_readout(q.reshape(Bc, Cc, d), rp, None, rd, cur.ln_weight, cur.ln_bias, cfg.rms_norm_eps,
+                                   state_index=rows, packed=True)
                 self._resid_linear(hh, out.reshape(R, d), lay.w_o)
                 hidden = hh
-            chunk_losses.append(torch.stack(layer_loss, dim=1))                    # (B, L)
-            counts.append(m.sum(dim=1) if m is not None else torch.full((B,), float(Cc), device=dev))
-            cur.step += cfg.n_layers
+            # ... then the L writes chain through the state as ONE call whose chunks are the
+            # layers (row b's tokens: layer 0's chunk, layer 1's chunk, ...), so every write
+            # after the first reuses the previous one's freshly updated tiles for its forward.
+            Kr = K.reshape(L, Bc, Cc, d).permute(1, 0, 2, 3).reshape(Bc, L * Cc, d).contiguous()
+            Vr = V.reshape(L, Bc, Cc, d).permute(1, 0, 2, 3).reshape(Bc, L * Cc, d).contiguous()
+            Er = ETA.reshape(L, Bc, Cc).permute(1, 0, 2).reshape(Bc, L * Cc).contiguous()
+            Ar = ALPHA.reshape(L, Bc, Cc).permute(1, 0, 2).reshape(Bc, L * Cc).contiguous()
+            Mr = None if m is None else m.repeat(1, L).contiguous()
+            loss = torch.empty(Bc, L * Cc, dtype=torch.float32, device=dev)
+            chunk_write(Kr, Vr, Er, Ar, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,
+                        cur.ln_weight, cur.ln_bias, Mr, cfg.momentum_beta, float(cfg.max_inner_grad_norm or 0.0),
+                        cfg.normalize_loss_by_dim, cfg.rms_norm_eps, chunk_size=Cc, token_loss=loss,
+                        state_rows=rows)
+            lz = loss.reshape(Bc, L, Cc)
+            if m is None:
+                layer_loss = lz.mean(dim=2)                                        # (Bc, L)
+            else:
+                layer_loss = (lz * m[:, None, :]).sum(dim=2) / m.sum(dim=1, keepdim=True).clamp_min(1.0)
+            chunk_loss = torch.zeros(B, L, dtype=torch.float32, device=dev)
+            chunk_loss[rows_l] = layer_loss                                     # (B, L), zero off the batch
+            count = torch.zeros(B, dtype=torch.float32, device=dev)
+            count[rows_l] = m.sum(dim=1) if m is not None else float(Cc)
+            chunk_losses.append(chunk_loss)
+            counts.append(count)
+            cur.step += L
         check_status(workspace(0, dev), "test_time_update")
-        cnt = torch.stack(counts, dim=1).to(torch.float64)                          # (B, n_chunks)
-        losses = torch.stack(chunk_losses, dim=1).to(torch.float64)                # (B, n_chunks, L)
-        per_layer_t = (losses * cnt[:, :, None]).sum(1) / cnt.sum(1, keepdim=True).clamp_min(1.0)
-        per_layer = [[float(x) for x in row] for row in per_layer_t.float().tolist()]   # single sync
+        if not chunk_losses:
+            per_layer = [[0.0] * L for _ in range(B)]
+        else:
+            cnt = torch.stack(counts, dim=1).to(torch.float64)                      # (B, n_chunks)
+            losses = torch.stack(chunk_losses, dim=1).to(torch.float64)            # (B, n_chunks, L)
+            per_layer_t = (losses * cnt[:, :, None]).sum(1) / cnt.sum(1, keepdim=True).clamp_min(1.0)
+            per_layer = [[float(x) for x in row] for row in per_layer_t.float().tolist()]   # single sync
         means = [sum(r) / max(len(r), 1) for r in per_layer]
         cur.last_surprise_loss = means[0] if B == 1 else float(sum(means) / B)
         cur.surprise_history = (list(fast_state.surprise_history) + (per_layer[0] if B == 1 else []))[-100:]
