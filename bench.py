@@ -207,30 +207,58 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-# ----------------------------------------------------------------------------- decode + write (config 3)
-DEC = dict(personas=32, prompt_min=64, prompt_max=1024, new_tokens=128, warmup_tokens=3, perturb_std=1e-3)
+# ----------------------------------------------------------------------------- decode + write (configs 3, 4)
+def _uniform_prompts(lo, hi):
+    def draw(g, n):
+        return torch.randint(lo, hi + 1, (n,), generator=g).tolist()
+    return draw
 
 
-def decode_workload(device, rank, lib):
-    """32 personas of the ~151M-class model (d=768, 12 layers, h=2048,
-    V=32000, window 512), W_p = W_0 + N(0, 1e-3), ragged prompts uniform in [64, 1024]
-    with uniform ids; greedy decode of 128 tokens per persona as ONE packed batch per
-    step (captured CUDA graph), then one chunk-TTT write per persona on prompt+reply
-    (all personas in one batched write, right-padded to a multiple of 64 with masks)."""
+def _lognormal_prompts(median, sigma, lo, hi):
+    def draw(g, n):
+        z = torch.randn(n, generator=g, dtype=torch.float64)
+        return [int(min(max(round(median * math.exp(sigma * float(x))), lo), hi)) for x in z]
+    return draw
+
+
+DEC = dict(
+    key="decode", label="BASELINE config 3", config="151M", personas=32, prompts=_uniform_prompts(64, 1024),
+    prompt_desc="uniform in [64, 1024]", prompt_max=1024, new_tokens=128, warmup_tokens=3, perturb_std=1e-3,
+    init="reference")
+DEC4 = dict(
+    key="decode_1p58b", label="BASELINE config 4", config="1P58B", personas=64,
+    prompts=_lognormal_prompts(512, 1.0, 32, 4096), prompt_desc="lognormal, median 512, sigma 1.0 (BASELINE gives "
+    "no sigma), clipped to [32, 4096]", prompt_max=4096, new_tokens=256, warmup_tokens=3, perturb_std=1e-3,
+    init="random")
+
+
+def decode_workload(device, rank, lib, spec):
+    """Packed multi-persona greedy decode + per-turn chunk-TTT write.  ``spec``'s
+    personas start from W_p = W_0 + N(0, perturb_std) with ragged prompts of
+    uniform-random ids; they decode ``new_tokens`` greedy tokens as ONE packed
+    batch per step (captured CUDA graph), then write prompt + reply with one
+    batched chunk-TTT write (right-padded to a multiple of 64, masks; rows leave
+    the batch when only padding is left)."""
     from utttcompanion_b200 import _lib
+    from utttcompanion_b200 import workloads as wl
     from utttcompanion_b200.model import DecodeGraph, FastState, UtttB200
-    from utttcompanion_b200.workloads import CONFIG_151M, perturbed_persona_states, reference_init_state_dict
-    cfg = CONFIG_151M
-    P = DEC["personas"]
-    sd = reference_init_state_dict(cfg, seed=0)
-    eng = UtttB200(sd, cfg, device=device, max_personas=P, max_positions=DEC["prompt_max"] + 512)
-    w_up, w_gate, w_down = perturbed_persona_states(sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"],
-                                                    sd["fast_weight_pool.w_down_init"], P, DEC["perturb_std"],
-                                                    seed=100 + rank, device=device)
+    cfg = {"151M": wl.CONFIG_151M, "1P58B": wl.CONFIG_1P58B}[spec["config"]]
+    P = spec["personas"]
+    if spec["init"] == "reference":
+        sd = wl.reference_init_state_dict(cfg, seed=0)
+        init_desc = "reference seed-0 init"
+    else:
+        sd = wl.random_state_dict(cfg, seed=0, device=device)
+        init_desc = "random init with the reference's distributions (generated on the GPU)"
+    eng = UtttB200(sd, cfg, device=device, max_personas=P, max_positions=spec["prompt_max"] + spec["new_tokens"] + 64)
+    w0 = (sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"], sd["fast_weight_pool.w_down_init"])
+    del sd
+    w_up, w_gate, w_down = wl.perturbed_persona_states(*w0, P, spec["perturb_std"], seed=100 + rank, device=device)
+    del w0
     packed, down = eng.read_copies(w_up, w_gate, w_down)
     graph = DecodeGraph(eng, P, packed, down)          # before prefill: its warm-up touches ring slot 0
     g = torch.Generator().manual_seed(7 + rank)
-    lens = torch.randint(DEC["prompt_min"], DEC["prompt_max"] + 1, (P,), generator=g).tolist()
+    lens = spec["prompts"](g, P)
     prompts = [torch.randint(6, cfg.vocab_size, (n,), generator=g) for n in lens]
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -241,12 +269,13 @@ def decode_workload(device, rank, lib):
     tokens = ids.clone()
     pos = torch.tensor(lens, dtype=torch.int32, device=device)
     generated = [tokens.clone()]
-    for _ in range(DEC["warmup_tokens"]):
+    for _ in range(spec["warmup_tokens"]):
         ids, _ = graph.step(tokens, pos)
         tokens.copy_(ids)
         pos += 1
         generated.append(tokens.clone())
-    steps = DEC["new_tokens"] - 1 - DEC["warmup_tokens"]
+    steps = spec["new_tokens"] - 1 - spec["warmup_tokens"]
+    kv_pos = [[min(n + spec["warmup_tokens"] + i, cfg.sliding_window_size - 1) + 1 for n in lens] for i in range(steps)]
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -285,6 +314,13 @@ def decode_workload(device, rank, lib):
     lib.uttt_profile_enable(0)
     readout_s = ms[4] / max(cnt[4], 1) / 1e3
     readout_bytes = P * 3.0 * cfg.d_model * cfg.d_ff_fast * 2.0      # BF16 read copies of every persona
+    # bytes one decode step must move: every persona's read copies in every layer, the shared
+    # slow weights once, and each persona's valid KV slots (K and V) in every layer
+    slow_bytes = sum(t.numel() * t.element_size() for lay in eng.layers for t in (lay.wqkv, lay.wo, lay.w_q, lay.w_o))
+    slow_bytes += eng.lm_head.numel() * eng.lm_head.element_size()
+    kv_bytes = float(np.mean([sum(kp) for kp in kv_pos])) * cfg.n_kv_heads * cfg.head_dim * 2 * 2 * cfg.n_layers
+    step_bytes = readout_bytes * cfg.n_layers + slow_bytes + kv_bytes
+    del graph, packed, down
     # one write per persona on prompt + reply (personalizer.py:483-512), batched over personas
     gen = torch.stack(generated, dim=1).cpu()                          # (P, new_tokens)
     turns = [prompts[p].tolist() + gen[p].tolist() for p in range(P)]
@@ -304,17 +340,24 @@ def decode_workload(device, rank, lib):
     e1.record()
     torch.cuda.synchronize()
     write_ms = e0.elapsed_time(e1)
+    del new
     valid = float(mask.sum())
     return {
-        "workload": "packed multi-persona greedy decode + per-turn chunk-TTT write (BASELINE config 3)",
-        "model": "uTTT ~76.5M (d=768, 12 layers, 12/4 heads, h=2048, V=32000, window 512), reference seed-0 init",
-        "personas": P, "prompt_tokens": {"min": min(lens), "max": max(lens), "mean": float(np.mean(lens))},
+        "workload": f"packed multi-persona greedy decode + per-turn chunk-TTT write ({spec['label']})",
+        "model": f"uTTT d={cfg.d_model}, {cfg.n_layers} layers, {cfg.n_heads}/{cfg.n_kv_heads} heads, "
+                 f"h={cfg.d_ff_fast}, V={cfg.vocab_size}, window {cfg.sliding_window_size}; {init_desc}",
+        "personas": P, "prompts": spec["prompt_desc"], "new_tokens": spec["new_tokens"],
+        "prompt_tokens": {"min": min(lens), "max": max(lens), "mean": float(np.mean(lens))},
         "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,
         "decode_e2e_tok_s": P / (e2e_ms / 1e3),
+        "decode_step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes,
+                                 "achieved": step_bytes / (dec_ms / 1e3) / 1e9, "unit": "GB/s"},
         "prefill_s_total": prefill_s,
         "write_tok_s": valid / (write_ms / 1e3), "write_padded_tok_s": P * Tpad / (write_ms / 1e3),
         "write_ms": write_ms, "mean_surprise": float(np.mean(surprises)),
-        "readout_roofline": {"bound": "hbm", "kernel": "readout_gemv (+ read-copy decode path)",
+        "write_config": {"momentum": cfg.momentum_beta, "clip": cfg.max_inner_grad_norm,
+                         "inner_lr": cfg.base_inner_lr},
+        "readout_roofline": {"bound": "hbm", "kernel": "readout_decode (GEMV + fused LayerNorm)",
                              "achieved": readout_bytes / readout_s / 1e9, "unit": "GB/s",
                              "algorithmic_bytes_per_launch": readout_bytes, "avg_ms": readout_s * 1e3},
         "decode_kernels_ms": {k: float(ms[i]) for i, k in enumerate(
@@ -485,11 +528,14 @@ def ours_arm(args, world, rank, local):
             "kernels": per_kind,
             "clocks": clk,
         }
-        if not args.no_decode:
-            dec = decode_workload(device, rank, lib)
-            dec["readout_roofline"]["peak"] = hbm
-            dec["readout_roofline"]["frac"] = dec["readout_roofline"]["achieved"] / hbm
-            line["decode"] = dec
+        specs = ([] if args.no_decode else [DEC]) + ([] if args.no_decode or args.no_1p58b else [DEC4])
+        for spec in specs:
+            dec = decode_workload(device, rank, lib, spec)
+            for key in ("readout_roofline", "decode_step_roofline"):
+                dec[key]["peak"] = hbm
+                dec[key]["frac"] = dec[key]["achieved"] / hbm
+            line[spec["key"]] = dec
+            torch.cuda.empty_cache()
         if world == 1 and not args.no_cpu_baseline:
             v, n, el = cpu_baseline()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
@@ -510,7 +556,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode + write workload")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode + write workloads (configs 3, 4)")
+    ap.add_argument("--no-1p58b", action="store_true", help="skip the 1.58B (config 4) decode + write workload")
     ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")
     ap.add_argument("--tokens", type=int, default=None, help="override tokens per state (profiling cases)")
     args = ap.parse_args()

@@ -237,8 +237,10 @@ int uttt_kv_ring_fill(int B, int L, int end_pos, int n_kv, int hd, int W, const 
  * (weight FP32, rounded to BF16 as weight.to(x.dtype) does; NULL for none). */
 int uttt_rmsnorm(int rows, int d, const void* x, long long x_ld, const float* weight, float eps, void* out,
                  long long out_ld, void* stream);
-/* Token embedding gather (model/uttt_model.py:778-780): out[r] = table[ids[r]]. */
-int uttt_embed(int rows, int d, const int* ids, const void* table, void* out, void* stream);
+/* Token embedding gather (model/uttt_model.py:778-780): out[r] = table[ids[r]]
+ * for a (V, d) table; ids outside [0, V) are clamped into it on the device
+ * (callers validate ids on the host, as nn.Embedding raises for them). */
+int uttt_embed(int rows, int d, int V, const int* ids, const void* table, void* out, void* stream);
 /* Greedy pick of _sample_next_token at temperature <= 1e-5
  * (model/uttt_model.py:1204-1221): BF16-rounded logits, PAD/BOS/UNK (ids 0,1,3)
  * and ids >= active_limit masked (stop_free also masks 2,4,5 as the

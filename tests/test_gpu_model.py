@@ -263,3 +263,88 @@ def test_decode_graph_replay_equals_eager_steps():
         assert torch.max(torch.abs(lg - graph_logits[s])).item() <= 1e-2, s
         t_e, _ = eng.greedy(lg)
         p_e = p_e + 1
+
+
+def test_head_dim_128_gqa4_model_against_oracle():
+    """The 1.58B configuration's attention shape (head dim 128, 4 query heads per
+    KV head) at a small width: a prompt longer than the window, teacher-forced
+    decode steps and a masked write, against the oracle's BF16 path."""
+    cfg = ModelConfig(vocab_size=1024, d_model=512, n_layers=2, n_heads=4, n_kv_heads=1, d_ff_fast=384,
+                      sliding_window_size=32, chunk_size=64, max_seq_len=512)
+    assert cfg.head_dim == 128
+    sd = reference_init_state_dict(cfg, seed=3)
+    eng = UtttB200(sd, cfg, max_personas=1)
+    ocfg = om.ModelConfig(**{k: v for k, v in cfg.to_dict().items() if k in om.ModelConfig.__dataclass_fields__})
+    oracle = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "bf16",
+                            *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
+    gen = torch.Generator().manual_seed(5)
+    prompt = torch.randint(6, cfg.vocab_size, (80,), generator=gen)
+    ost = oracle.state_for_forward(1, update=True)
+    n_steps = 24
+    oid, omargins, olog = oracle.generate_greedy(prompt.numpy(), ost, n_steps)
+    st = eng.init_fast_state(1)
+    tf = eng.teacher_forced_logits(prompt, oid, st)
+    torch.cuda.synchronize()
+    for step in range(n_steps):
+        ours = tf[step].cpu().numpy()
+        assert logits_close(ours, olog[step]).all(), (step, float(np.max(np.abs(ours - olog[step]))))
+        if int(np.argmax(_mask(ours, oracle.active_limit))) != oid[step]:
+            assert omargins[step] <= 2 * LOGIT_TOL, (step, omargins[step])
+    turn = prompt.tolist() + oid
+    padded = ((len(turn) + 63) // 64) * 64
+    inter = np.array(turn + [0] * (padded - len(turn)))
+    mask = np.array([1.0] * len(turn) + [0.0] * (padded - len(turn)), np.float32)
+    on, _, opl, _ = oracle.test_time_update(inter[None], ost, mask[None])
+    new, _, pl = eng.test_time_update(torch.tensor(inter), st, torch.tensor(mask))
+    torch.cuda.synchronize()
+    for n in ("w_up", "w_gate", "w_down"):
+        got, ref, base = getattr(new, n).cpu().numpy(), getattr(on, n), getattr(ost, n)
+        assert rel_l2(got, ref) < 5e-3, (n, rel_l2(got, ref))
+        assert rel_l2(got - base, ref - base) < 3e-2, (n, rel_l2(got - base, ref - base))
+    np.testing.assert_allclose(pl, opl, rtol=1e-2)
+
+
+def test_decode_graph_survives_workspace_growth():
+    """A captured decode graph keeps the workspace pointers it was recorded with;
+    a later, larger call that grows those workspaces must not free them under
+    the graph (the replays still match eager steps after the freed memory has
+    been handed out again)."""
+    from utttcompanion_b200.fastweight import workspace
+    from utttcompanion_b200.model import DecodeGraph
+    from utttcompanion_b200.workloads import perturbed_persona_states
+    cfg = _tiny_cfg()
+    sd = reference_init_state_dict(cfg, seed=9)
+    P = 2
+    eng = UtttB200(sd, cfg, max_personas=P)
+    w = perturbed_persona_states(sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"],
+                                 sd["fast_weight_pool.w_down_init"], P, std=1e-2, seed=4)
+    packed, down = eng.read_copies(*w)
+    graph = DecodeGraph(eng, P, packed, down)
+    dev = torch.device("cuda")
+    for slot in range(3):                      # grow every workspace slot the decode step uses
+        workspace(workspace(0, dev, slot).numel() * 4, dev, slot)
+    junk = [torch.full((1 << 20,), 7.0, device=dev) for _ in range(16)]   # take the allocator's free blocks
+    gen = torch.Generator().manual_seed(2)
+    lens = [20, 33]
+    firsts = [eng.prefill(torch.randint(6, cfg.vocab_size, (n,), generator=gen), p, packed, down, p)
+              for p, n in enumerate(lens)]
+    toks, _ = eng.greedy(torch.stack(firsts))
+    pos = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    k_save = [k.clone() for k in eng.k_ring]
+    v_save = [v.clone() for v in eng.v_ring]
+    t_g, p_g, graph_logits = toks.clone(), pos.clone(), []
+    for _ in range(4):
+        ids, lg = graph.step(t_g, p_g)
+        graph_logits.append(lg.clone())
+        t_g, p_g = ids.clone(), p_g + 1
+    for i in range(cfg.n_layers):
+        eng.k_ring[i].copy_(k_save[i])
+        eng.v_ring[i].copy_(v_save[i])
+    t_e, p_e = toks.clone(), pos.clone()
+    slots = torch.arange(P, dtype=torch.int32, device="cuda")
+    for s in range(4):
+        lg = eng.decode_step(t_e, p_e, slots, packed, down, slots)
+        assert torch.max(torch.abs(lg - graph_logits[s])).item() <= 1e-2, s
+        t_e, _ = eng.greedy(lg)
+        p_e = p_e + 1
+    assert all(float(j[0]) == 7.0 for j in junk)   # the graph wrote into none of them

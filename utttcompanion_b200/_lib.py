@@ -55,7 +55,7 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_attn_prefill": (i32, [i32, i32, i32, i32, i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp]),
     "uttt_kv_ring_fill": (i32, [i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "uttt_rmsnorm": (i32, [i32, i32, vp, C.c_longlong, vp, f32, vp, C.c_longlong, vp]),
-    "uttt_embed": (i32, [i32, i32, vp, vp, vp, vp]),
+    "uttt_embed": (i32, [i32, i32, i32, vp, vp, vp, vp]),
     "uttt_greedy_argmax": (i32, [i32, i32, vp, i32, C.c_longlong, i32, i32, vp, vp, vp]),
     "uttt_pack_read_copies": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "uttt_apply_rope": (i32, [C.c_longlong, i32, i32, vp, vp, vp, vp, vp]),

@@ -41,16 +41,19 @@ __global__ void __launch_bounds__(R_THREADS) rmsnorm_kernel(const __nv_bfloat16*
   }
 }
 
-__global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int d,
+// ids outside [0, V) are clamped, so no id can address memory outside the table
+__global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int d, int V,
                              __nv_bfloat16* __restrict__ out) {
   const int r = blockIdx.x;
-  const __nv_bfloat16* src = table + (size_t)ids[r] * d;
+  const int id = min(max(ids[r], 0), V - 1);
+  const __nv_bfloat16* src = table + (size_t)id * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) out[(size_t)r * d + i] = src[i];
 }
 
 // Greedy pick over BF16-rounded logits with ids 0,1,3 (PAD/BOS/UNK) masked, or
 // 0..5 in stop-free mode, and ids >= active_limit masked.  Ties go to the
-// lowest id.  Writes the id and the top-1 / top-2 values.
+// lowest id.  Writes the id and the top-1 / top-2 values.  A NaN logit counts
+// as -inf, and a row with no finite candidate still returns an allowed id.
 __global__ void __launch_bounds__(R_THREADS) argmax_kernel(const void* __restrict__ logits, int logits_f32,
                                                            long long ld, int V, int active_limit, int stop_free,
                                                            int* __restrict__ ids, float* __restrict__ top2) {
@@ -65,6 +68,7 @@ __global__ void __launch_bounds__(R_THREADS) argmax_kernel(const void* __restric
     float v = logits_f32 ? reinterpret_cast<const float*>(logits)[(size_t)r * ld + i]
                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[(size_t)r * ld + i]);
     v = __bfloat162float(__float2bfloat16(v));
+    if (v != v) v = -INFINITY;
     if (v > v1 || (v == v1 && i < i1)) {
       v2 = v1;
       v1 = v;
@@ -92,7 +96,7 @@ __global__ void __launch_bounds__(R_THREADS) argmax_kernel(const void* __restric
     __syncthreads();
   }
   if (tid == 0) {
-    ids[r] = si1[0];
+    ids[r] = si1[0] < lim ? si1[0] : (stop_free ? 6 : 2) % lim;   // only when no candidate was finite
     if (top2) {
       top2[2 * r] = sv1[0];
       top2[2 * r + 1] = sv2[0];
@@ -175,11 +179,11 @@ extern "C" int uttt_rmsnorm(int rows, int d, const void* x, long long x_ld, cons
   return launch_status();
 }
 
-extern "C" int uttt_embed(int rows, int d, const int* ids, const void* table, void* out, void* stream) {
+extern "C" int uttt_embed(int rows, int d, int V, const int* ids, const void* table, void* out, void* stream) {
   UTTT_REQUIRE(rows > 0 && d > 0 && ids && table && out, UTTT_ERR_INVALID);
   cudaStream_t st = (cudaStream_t)stream;
   ProfScope ps(UTTT_PROF_ROWWISE, st);
-  embed_kernel<<<rows, 256, 0, st>>>(ids, (const __nv_bfloat16*)table, d, (__nv_bfloat16*)out);
+  embed_kernel<<<rows, 256, 0, st>>>(ids, (const __nv_bfloat16*)table, d, V, (__nv_bfloat16*)out);
   return launch_status();
 }
 

@@ -19,15 +19,27 @@ from . import _lib
 
 _ws_lock = threading.Lock()
 _workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+# Every buffer ever handed out stays allocated: a captured CUDA graph keeps the
+# raw pointers of the workspaces it was recorded with, so a buffer outgrown by
+# a later, larger call must not return to the allocator while a graph could
+# still replay into it.
+_retired: Dict[Tuple[int, int], list] = {}
 
 
 def workspace(nbytes: int, device: torch.device, slot: int = 0) -> torch.Tensor:
-    """A cached, zero-initialised device workspace of at least ``nbytes`` (per device and slot)."""
+    """A cached, zero-initialised device workspace of at least ``nbytes`` (per device and slot).
+
+    Growing a slot allocates a new buffer (at least twice the old size) and keeps
+    the old one alive for the life of the process, so pointers captured by CUDA
+    graphs stay valid."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
-            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            size = max(nbytes, 1 << 20, 0 if ws is None else 2 * ws.numel())
+            if ws is not None:
+                _retired.setdefault(key, []).append(ws)
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
             _workspaces[key] = ws
         return ws
 

@@ -168,10 +168,12 @@ class UtttB200:
         return out
 
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        if not ids.is_cuda and ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.emb.shape[0]):
+            raise ValueError("token id outside the vocabulary")       # nn.Embedding raises as well
         ids = ids.to(device=self.device, dtype=torch.int32).contiguous().reshape(-1)
         out = torch.empty(ids.numel(), self.cfg.d_model, dtype=torch.bfloat16, device=self.device)
-        _lib.check(self.lib.uttt_embed(ids.numel(), self.cfg.d_model, ids.data_ptr(), self.emb.data_ptr(),
-                                       out.data_ptr(), self._st()), "uttt_embed")
+        _lib.check(self.lib.uttt_embed(ids.numel(), self.cfg.d_model, self.emb.shape[0], ids.data_ptr(),
+                                       self.emb.data_ptr(), out.data_ptr(), self._st()), "uttt_embed")
         return out
 
     def _resid_linear(self, h: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> None:

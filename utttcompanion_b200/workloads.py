@@ -137,6 +137,43 @@ def reference_init_state_dict(cfg: ModelConfig, seed: int = 0) -> Dict[str, torc
     return sd
 
 
+def random_state_dict(cfg: ModelConfig, seed: int = 0, device="cuda") -> Dict[str, torch.Tensor]:
+    """A randomly initialised model of ``cfg``'s architecture, generated on ``device``:
+    the reference's init distributions (embeddings and projections N(0, 0.02), the
+    eta / alpha gates at their init values, W_0 as SharedFastWeightPool draws it,
+    model/uttt_layer.py:573-580, 1269-1273) but not its RNG stream, so large
+    configurations initialise in seconds.  Projections are BF16, the rest FP32."""
+    d, h, V, L, hd = cfg.d_model, cfg.d_ff_fast, cfg.vocab_size, cfg.n_layers, cfg.head_dim
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def normal(*shape, std=0.02, dtype=torch.bfloat16):
+        return (torch.randn(shape, generator=g, device=device) * std).to(dtype)
+
+    sd: Dict[str, torch.Tensor] = {"tok_embeddings.weight": normal(V, d)}
+    sd["fast_weight_pool.w_up_init"] = normal(d, h, std=1.0 / math.sqrt(d), dtype=torch.float32)
+    sd["fast_weight_pool.w_gate_init"] = normal(d, h, std=1.0 / math.sqrt(d), dtype=torch.float32)
+    sd["fast_weight_pool.w_down_init"] = normal(h, d, std=0.1 / math.sqrt(h), dtype=torch.float32)
+    sd["fast_weight_pool.ln_weight"] = torch.ones(d, device=device)
+    sd["fast_weight_pool.ln_bias"] = torch.zeros(d, device=device)
+    for i in range(L):
+        p = f"layers.{i}."
+        for n in ("attn_norm", "uttt_norm", "uttt.q_norm", "uttt.k_norm"):
+            sd[p + n + ".weight"] = torch.ones(d, device=device)
+        sd[p + "attn.wq.weight"] = normal(cfg.n_heads * hd, d)
+        sd[p + "attn.wk.weight"] = normal(cfg.n_kv_heads * hd, d)
+        sd[p + "attn.wv.weight"] = normal(cfg.n_kv_heads * hd, d)
+        sd[p + "attn.wo.weight"] = normal(d, cfg.n_heads * hd)
+        for n in ("w_q", "w_k", "w_v", "w_o"):
+            sd[p + f"uttt.{n}.weight"] = normal(d, d)
+        sd[p + "uttt.w_eta.weight"] = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
+        sd[p + "uttt.w_eta.bias"] = torch.zeros(1, device=device)
+        sd[p + "uttt.w_alpha.weight"] = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
+        sd[p + "uttt.w_alpha.bias"] = torch.full((1,), -1.386, device=device)
+    sd["norm.weight"] = torch.ones(d, device=device)
+    sd["lm_head.weight"] = sd["tok_embeddings.weight"]     # tied (model/uttt_model.py:337-338)
+    return sd
+
+
 def perturbed_persona_states(w_up0, w_gate0, w_down0, n: int, std: float = 1e-3, seed: int = 0,
                              device="cuda"):
     """Persona states W_0 + N(0, std) (BASELINE configs 3/4), FP32 (n, d, h) / (n, h, d)."""
