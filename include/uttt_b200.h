@@ -164,6 +164,25 @@ int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, co
                       const void* w_down, const int* state_index, const float* ln_weight, const float* ln_bias,
                       float eps, void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Hidden-dimension split of the decode readout (the 1.58B configuration over
+ * P GPUs): each rank holds hidden units [r*h, (r+1)*h) of every persona, as
+ * packed BF16 [W_up | W_gate] (S, d, 2h) and W_down (S, h, d) slices.
+ * uttt_fast_readout_partial writes that slice's z = h_slice W_down_slice,
+ * FP32 (B, T, d) for T <= 64 tokens per state (z is zeroed first; T == 1 runs
+ * the decode GEMV, T > 1 the tensor-core tile; the workspace only holds the
+ * status word).  After the ranks' z are summed (an all-reduce),
+ * uttt_readout_finish applies out = x + LayerNorm(bf16(z)) * ln_weight +
+ * ln_bias to `rows` rows of (rows, d).  Together they equal uttt_fast_readout
+ * (swiglu_packed_forward, model/uttt_layer.py:250-257): every hidden unit's
+ * u, g and h are computed whole on one rank.
+ */
+int uttt_fast_readout_partial(int B, int T, int d, int h, const void* x, const void* w_packed, const void* w_down,
+                              const int* state_index, float* z, void* workspace, size_t workspace_bytes,
+                              void* stream);
+int uttt_readout_finish(int rows, int d, const float* z, const void* x, const float* ln_weight, const float* ln_bias,
+                        float eps, void* out, int out_dtype, void* stream);
+
 /* ---- slow-weight projections -------------------------------------------- */
 /*
  * y = x W^T for BF16 x (M, K) and an nn.Linear weight W (N, K), FP32

@@ -1,0 +1,86 @@
+"""GPU (2 ranks, NCCL): the hidden-dimension split of the decode path.
+
+Each rank holds half of every persona's hidden units (read copies of its
+slices); prefill and packed decode steps sum the readout's z across the
+ranks.  The logits must match an unsplit engine on the same inputs (both
+teacher-forced on the same tokens) within the logits bound, on both ranks.
+Skipped with fewer than two visible GPUs."""
+
+import datetime
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+
+
+def _cfg():
+    from utttcompanion_b200.workloads import ModelConfig
+    return ModelConfig(vocab_size=2048, d_model=256, n_layers=2, n_heads=2, n_kv_heads=1, d_ff_fast=384,
+                       sliding_window_size=32, chunk_size=64, max_seq_len=512)     # head dim 128
+
+
+def _run(eng, packed, down, prompts, forced):
+    """Prefill every persona, then packed decode steps fed with ``forced`` tokens."""
+    P = len(prompts)
+    logits = [torch.stack([eng.prefill(prompts[p], p, packed, down, p) for p in range(P)])]
+    pos = torch.tensor([len(t) for t in prompts], dtype=torch.int32, device=eng.device)
+    slots = torch.arange(P, dtype=torch.int32, device=eng.device)
+    for step in forced:
+        logits.append(eng.decode_step(step.to(eng.device), pos, slots, packed, down, slots))
+        pos = pos + 1
+    return [lg.float().cpu() for lg in logits]
+
+
+def _rank_main(rank, world, port, out_dir):
+    from utttcompanion_b200.hsplit import HiddenSplit
+    from utttcompanion_b200.model import UtttB200
+    from utttcompanion_b200.workloads import perturbed_persona_states, reference_init_state_dict
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    cfg = _cfg()
+    sd = reference_init_state_dict(cfg, seed=2)
+    P = 2
+    full = perturbed_persona_states(sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"],
+                                    sd["fast_weight_pool.w_down_init"], P, std=1e-2, seed=5, device="cpu")
+    gen = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(6, cfg.vocab_size, (n,), generator=gen) for n in (40, 70)]
+    forced = [torch.randint(6, cfg.vocab_size, (P,), generator=gen, dtype=torch.int32) for _ in range(6)]
+    hs = HiddenSplit()
+    eng = UtttB200(sd, cfg, device=dev, max_personas=P, hsplit=hs)
+    packed, down = eng.read_copies(*(w.to(dev) for w in hs.shard(*full)))
+    split = _run(eng, packed, down, prompts, forced)
+    torch.cuda.synchronize()
+    dist.barrier()
+    dist.destroy_process_group()
+    ref_eng = UtttB200(sd, cfg, device=dev, max_personas=P)
+    rp, rd = ref_eng.read_copies(*(w.to(dev) for w in full))
+    ref = _run(ref_eng, rp, rd, prompts, forced)
+    worst = 0.0
+    for a, b in zip(split, ref):
+        excess = (torch.abs(a - b) - (LOGIT_TOL + torch.abs(b) / 128)).max().item()
+        worst = max(worst, excess)
+    np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array([worst]))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_hidden_split_decode_matches_unsplit(tmp_path):
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, 29541, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    for r in range(2):
+        worst = float(np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))[0])
+        assert worst <= 0.0, (r, worst)

@@ -76,6 +76,7 @@ struct ChunkParams {
   int call_end;       // token index one past the last chunk of this call
   int tok0_next, Cc_next;  // the fused forward's chunk (bwd kernel with kFuse)
   int hp;             // hidden padded to 128
+  int z_rows;         // rows of zacc per state (0: 64, the chunk tile)
   float beta, clip, eps, inv_scale;
   int* status;
   // weight source of the fwd kernel: element (state, k, j) of up/gate at
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&zfree[zb]);
-        float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
+        float* za = p.zacc + (size_t)b * (p.z_rows ? p.z_rows : CT) * p.d + pm * 128 + row;
         for (int i = 0; i < 32; ++i)
           if (c0 + i < p.Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
       }
@@ -327,7 +328,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
       tmem_wait_ld();
-      float* za = p.zacc + (size_t)b * CT * p.d + pm * 128 + row;
+      float* za = p.zacc + (size_t)b * (p.z_rows ? p.z_rows : CT) * p.d + pm * 128 + row;
       for (int i = 0; i < 32; ++i)
         if (c0 + i < p.Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
     }
@@ -1434,6 +1435,65 @@ namespace uttt {
 int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
                           const __nv_bfloat16* wd, const int* state_index, const float* ln_w, const float* ln_b,
                           float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st);
+int launch_readout_finish(int B, int d, const float* z, const __nv_bfloat16* x, const float* ln_w, const float* ln_b,
+                          float eps, void* out, int out_bf16, cudaStream_t st);
+}
+
+extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void* x, const void* w_packed,
+                                         const void* w_down, const int* state_index, float* z, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  UTTT_REQUIRE(B > 0 && T > 0 && d > 0 && h > 0 && x && w_packed && w_down && z && workspace, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(T <= CT && d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(workspace_bytes >= 256, UTTT_ERR_WORKSPACE);
+  cudaStream_t st = (cudaStream_t)stream;
+  UTTT_TRY(cuda_status(cudaMemsetAsync(z, 0, (size_t)B * T * d * sizeof(float), st)));
+  ProfScope ps(UTTT_PROF_READOUT, st);
+  if (T == 1)
+    return launch_readout_decode(B, d, h, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_packed,
+                                 (const __nv_bfloat16*)w_down, state_index, nullptr, nullptr, 1.f, z, nullptr, nullptr,
+                                 1, st);
+  static bool attr_done = false;
+  if (!attr_done) {
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    attr_done = true;
+  }
+  ChunkParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = B; p.T = T; p.C = CT; p.d = d; p.h = h; p.hp = (h + 127) / 128 * 128;
+  p.zacc = z;
+  p.z_rows = T;
+  p.status = ws_status(workspace);
+  p.k = (const __nv_bfloat16*)x;
+  p.src_up = w_packed;
+  p.src_gate = (const __nv_bfloat16*)w_packed + h;
+  p.ld_ug = 2 * h;
+  p.ss_ug = (long long)d * 2 * h;
+  p.src_down = w_down;
+  p.ss_d = (long long)h * d;
+  p.state_index = state_index;
+  p.tok0 = 0;
+  p.Cc = T;
+  CUtensorMap tmX;
+  {
+    uint64_t dims[3] = {(uint64_t)d, (uint64_t)T, (uint64_t)B};
+    uint64_t str[2] = {(uint64_t)d * 2, (uint64_t)T * d * 2};
+    uint32_t box[3] = {64, 64, 1};
+    UTTT_TRY(make_tmap_bf16(&tmX, x, 3, dims, str, box));
+  }
+  chunk_fwd_kernel<__nv_bfloat16><<<dim3((h + HT - 1) / HT, B), NTHREADS, fwd_smem(), st>>>(tmX, p);
+  return launch_status();
+}
+
+extern "C" int uttt_readout_finish(int B, int d, const float* z, const void* x, const float* ln_weight,
+                                   const float* ln_bias, float eps, void* out, int out_dtype, void* stream) {
+  UTTT_REQUIRE(B > 0 && d > 0 && z && x && ln_weight && ln_bias && out, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(out_dtype == UTTT_DTYPE_F32 || out_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && eps > 0.f, UTTT_ERR_UNSUPPORTED);
+  cudaStream_t st = (cudaStream_t)stream;
+  ProfScope ps(UTTT_PROF_READOUT_LN, st);
+  return launch_readout_finish(B, d, z, (const __nv_bfloat16*)x, ln_weight, ln_bias, eps, out,
+                               out_dtype == UTTT_DTYPE_BF16, st);
 }
 
 extern "C" size_t uttt_fast_readout_workspace(int B, int d, int h) {

@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
     const int* __restrict__ state_index, int d, int h, const float* __restrict__ ln_w,
     const float* __restrict__ ln_b, float eps, float* __restrict__ zacc, unsigned* __restrict__ done, void* out,
     int out_bf16) {
+  // done == nullptr: partial mode (a slice of the hidden units): z only, no LayerNorm
   __shared__ __align__(16) float xs[MD];
   __shared__ __align__(16) float part[8][ZG];
   __shared__ float ug[2 * GT];
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   }
 
   // ---- the state's last CTA: out = x + LN(bf16(z)) * gamma + beta
+  if (done == nullptr) return;
   __threadfence();
   __syncthreads();
   if (tid == 0) last = atomicAdd(done + b, 1u) == gridDim.x - 1;
@@ -191,9 +193,62 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   }
 }
 
+// out = x + LN(bf16(z)) * gamma + beta for one row per CTA: the LayerNorm of a
+// readout whose z was summed across ranks (hidden-dimension split).
+template <int MD>
+__global__ void __launch_bounds__(GTHREADS) readout_finish_kernel(const float* __restrict__ z,
+                                                                  const __nv_bfloat16* __restrict__ x, int d,
+                                                                  const float* __restrict__ ln_w,
+                                                                  const float* __restrict__ ln_b, float eps,
+                                                                  void* out, int out_bf16) {
+  __shared__ float red[GTHREADS / 32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  constexpr int NZ = MD / GTHREADS;
+  float zv[NZ];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NZ; ++i) {
+    const int c = tid + i * GTHREADS;
+    zv[i] = 0.f;
+    if (c < d) {
+      zv[i] = round_bf16(z[(size_t)b * d + c]);
+      sum += zv[i];
+    }
+  }
+  const float dinv = 1.f / (float)d;
+  const float mean = cta_sum(sum, red) * dinv;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NZ; ++i)
+    if (tid + i * GTHREADS < d) sq += (zv[i] - mean) * (zv[i] - mean);
+  const float rstd = rsqrtf(cta_sum(sq, red) * dinv + eps);
+#pragma unroll
+  for (int i = 0; i < NZ; ++i) {
+    const int c = tid + i * GTHREADS;
+    if (c < d) {
+      const float y = __bfloat162float(x[(size_t)b * d + c]) + ((zv[i] - mean) * rstd * ln_w[c] + ln_b[c]);
+      if (out_bf16)
+        reinterpret_cast<__nv_bfloat16*>(out)[(size_t)b * d + c] = __float2bfloat16(y);
+      else
+        reinterpret_cast<float*>(out)[(size_t)b * d + c] = y;
+    }
+  }
+}
+
 }  // namespace
 
-// zacc: (B, d) FP32 and done: (B) counters, both zero on entry.
+int launch_readout_finish(int B, int d, const float* z, const __nv_bfloat16* x, const float* ln_w, const float* ln_b,
+                          float eps, void* out, int out_bf16, cudaStream_t st) {
+  if (d % 128 != 0 || d > MAXD) return UTTT_ERR_UNSUPPORTED;
+  if (d <= 1024)
+    readout_finish_kernel<1024><<<B, GTHREADS, 0, st>>>(z, x, d, ln_w, ln_b, eps, out, out_bf16);
+  else
+    readout_finish_kernel<MAXD><<<B, GTHREADS, 0, st>>>(z, x, d, ln_w, ln_b, eps, out, out_bf16);
+  return launch_status();
+}
+
+// zacc: (B, d) FP32 zero on entry; done: (B) zero counters, or nullptr for a
+// partial readout (z only).
 int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __nv_bfloat16* wp,
                           const __nv_bfloat16* wd, const int* state_index, const float* ln_w, const float* ln_b,
                           float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st) {

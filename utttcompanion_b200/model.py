@@ -94,8 +94,12 @@ def _seg(start, length, op, out, out_ld, aux=None, aux_ld=0, scale=0.0, out_f32=
 
 class UtttB200:
     def __init__(self, state_dict: Dict[str, torch.Tensor], cfg: ModelConfig, device="cuda",
-                 max_personas: int = 1, max_positions: Optional[int] = None):
+                 max_personas: int = 1, max_positions: Optional[int] = None, hsplit=None):
+        """``hsplit``: a ``hsplit.HiddenSplit``; persona states and read copies are then
+        this rank's slices of the hidden units and every readout sums its z across
+        the group (decode and prefill; the batched write needs unsplit states)."""
         self.cfg = cfg
+        self.hsplit = hsplit
         self.device = torch.device(device)
         dev = self.device
         self.lib = _lib.load()
@@ -181,6 +185,13 @@ class UtttB200:
         d = w.shape[0]
         self._linear(x, w, [_seg(0, d, _lib.SEG_RESID, h, h.stride(0), h, h.stride(0))])
 
+    def _readout(self, q: torch.Tensor, packed: torch.Tensor, down: torch.Tensor, sidx: torch.Tensor) -> torch.Tensor:
+        """Frozen readout f_W(q) of (B, T, d) BF16 queries through BF16 read copies."""
+        if self.hsplit is not None:
+            return self.hsplit.readout(q, packed, down, sidx, self.ln_w_act, self.ln_b_act, self.cfg.rms_norm_eps)
+        return fast_readout(q, packed, None, down, self.ln_w_act, self.ln_b_act, self.cfg.rms_norm_eps,
+                            state_index=sidx, packed=True, ln_prepared=True)
+
     def _q_proj(self, layer, x2: torch.Tensor) -> torch.Tensor:
         """``fused_fast_q_proj`` (model/uttt_layer.py:1175-1190)."""
         d = self.cfg.d_model
@@ -217,8 +228,10 @@ class UtttB200:
         return packed, down
 
     def init_fast_state(self, batch_size: int = 1) -> FastState:
-        """``SharedFastWeightPool.init_state`` (detach=True), FP32 masters."""
-        rep = [w.unsqueeze(0).expand(batch_size, *w.shape).contiguous() for w in self.w0]
+        """``SharedFastWeightPool.init_state`` (detach=True), FP32 masters (this rank's
+        hidden-unit slices when the engine splits them)."""
+        w0 = self.w0 if self.hsplit is None else self.hsplit.shard(*(w.unsqueeze(0) for w in self.w0))
+        rep = [w.reshape(w.shape[-2:]).unsqueeze(0).expand(batch_size, *w.shape[-2:]).contiguous() for w in w0]
         return FastState(*rep, *(torch.zeros_like(t) for t in rep), self.ln_w.clone(), self.ln_b.clone())
 
     # ------------------------------------------------------------------ frozen path
@@ -252,8 +265,7 @@ class UtttB200:
                                                   self.v_ring[i].data_ptr(), self._st()), "uttt_kv_ring_fill")
             self._resid_linear(h, att, lay.wo)
             q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
-            r = fast_readout(q.unsqueeze(0), read_packed, None, read_down, self.ln_w_act, self.ln_b_act,
-                             cfg.rms_norm_eps, state_index=sidx, packed=True, ln_prepared=True)
+            r = self._readout(q.unsqueeze(0), read_packed, read_down, sidx)
             self._resid_linear(h, r.reshape(T, d), lay.w_o)
         return self.logits(h[-1:].contiguous())[0]
 
@@ -280,8 +292,7 @@ class UtttB200:
                                                  d, self._st()), "uttt_attn_decode")
             self._resid_linear(h, att, lay.wo)
             q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
-            r = fast_readout(q.unsqueeze(1), read_packed, None, read_down, self.ln_w_act, self.ln_b_act,
-                             cfg.rms_norm_eps, state_index=sidx, packed=True, ln_prepared=True)
+            r = self._readout(q.unsqueeze(1), read_packed, read_down, sidx)
             self._resid_linear(h, r.reshape(B, d), lay.w_o)
         return self.logits(h)
 
@@ -350,6 +361,8 @@ class UtttB200:
         (model/uttt_model.py:598-607, 833-838)."""
         cfg = self.cfg
         dev = self.device
+        if self.hsplit is not None:
+            raise ValueError("the batched write needs unsplit fast-weight states (hidden split: decode and prefill)")
         ids = interaction_ids.to(device=dev)
         B, T = ids.shape
         C, W = cfg.chunk_size, cfg.sliding_window_size
