@@ -1,13 +1,18 @@
 #!/usr/bin/env python
 """Benchmark of the uTTT serving hot path on B200 (one JSON line on rank 0).
 
-Workload (the isolated chunk-TTT write): 64 independent
-FP32 fast-weight states per GPU, d=1024, h=2816; per state T=2048 tokens in
-32 sequential chunks of C=64; keys/values BF16 ~N(0,1) L2-normalised per
-token; MSE (normalize_by_dim) surprise loss; fixed inner lr 1e-2; no decay,
-momentum or clipping.  A step is one full pass: all 32 chunks of all states.
-Synthetic seeded data stands in for real conversations (the reference
-publishes no dataset for this path).
+Headline workload (the isolated chunk-TTT write): 64
+independent FP32 fast-weight states per GPU, d=1024, h=2816; per state T=2048
+tokens in 32 sequential chunks of C=64; keys/values BF16 ~N(0,1)
+L2-normalised per token; MSE (normalize_by_dim) surprise loss; fixed inner lr
+1e-2; no decay, momentum or clipping.  A step is one full pass: all 32 chunks
+of all states.  Synthetic seeded data stands in for real conversations (the
+reference publishes no dataset for this path).
+
+Sub-objects of the same line: packed multi-persona decode + per-turn write of
+BASELINE config 3 (N = 1) and config 4 (the 1.58B model; personas partitioned
+by user id over the N GPUs), and at N > 1 the 1.58B decode with every
+persona's hidden units split over all GPUs (NCCL).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -366,6 +371,65 @@ def decode_workload(device, rank, lib, spec):
     }
 
 
+def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
+    """The 1.58B decode with every persona's hidden units split over all ranks
+    (NCCL all-reduce of the readout's z per layer): the same personas, prompts
+    and tokens on every rank; eager packed steps; max-over-ranks step time."""
+    import torch.distributed as dist
+    from utttcompanion_b200 import workloads as wl
+    from utttcompanion_b200.hsplit import HiddenSplit
+    from utttcompanion_b200.model import UtttB200
+    cfg = wl.CONFIG_1P58B
+    P = spec["personas"]
+    hs = HiddenSplit()
+    sd = wl.random_state_dict(cfg, seed=0, device=device)          # identical on every rank
+    eng = UtttB200(sd, cfg, device=device, max_personas=P, max_positions=spec["prompt_max"] + steps + 64,
+                   hsplit=hs)
+    w0 = (sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"], sd["fast_weight_pool.w_down_init"])
+    del sd
+    full = wl.perturbed_persona_states(*w0, P, spec["perturb_std"], seed=100, device=device)
+    del w0
+    local = hs.shard(*full)
+    del full
+    packed, down = eng.read_copies(*local)
+    del local
+    g = torch.Generator().manual_seed(7)
+    lens = spec["prompts"](g, P)
+    prompts = [torch.randint(6, cfg.vocab_size, (n,), generator=g) for n in lens]
+    first = torch.stack([eng.prefill(prompts[p], p, packed, down, p) for p in range(P)])
+    tokens, _ = eng.greedy(first)
+    pos = torch.tensor(lens, dtype=torch.int32, device=device)
+    slots = torch.arange(P, dtype=torch.int32, device=device)
+    for _ in range(3):
+        tokens, _ = eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))
+        pos += 1
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        tokens, _ = eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))
+        pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dec_ms = float(t.item())
+    slow_bytes = sum(x.numel() * x.element_size() for lay in eng.layers for x in (lay.wqkv, lay.wo, lay.w_q, lay.w_o))
+    slow_bytes += eng.lm_head.numel() * eng.lm_head.element_size()
+    per_gpu = P * 3.0 * cfg.d_model * (cfg.d_ff_fast // world) * 2.0 * cfg.n_layers + slow_bytes
+    del packed, down, eng
+    return {
+        "workload": f"1.58B packed greedy decode, every persona's fast-weight hidden units split over {world} GPUs "
+                    "(NCCL all-reduce of the readout z per layer), eager steps",
+        "personas": P, "prompts": spec["prompt_desc"],
+        "prompt_tokens": {"min": min(lens), "max": max(lens), "mean": float(np.mean(lens))},
+        "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,
+        "per_gpu_fast_weight_bytes_per_step": per_gpu,
+        "per_gpu_hbm_gbs": per_gpu / (dec_ms / 1e3) / 1e9,
+    }
+
+
 # ----------------------------------------------------------------------------- arms
 def reference_arm(args, world, rank):
     if rank != 0:
@@ -436,6 +500,14 @@ def ours_arm(args, world, rank, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
     lib = _lib.load()
     st = make_states(device, seed=1234 + rank)
     B, T = CFG["states"], CFG["tokens"]
@@ -498,6 +570,37 @@ def ours_arm(args, world, rank, local):
     from utttcompanion_b200 import fastweight as fw
     fw.check_status(fw.workspace(0, device), "bench")
 
+    # decode + write workloads: at N = 1 configs 3 and 4; at N > 1 every rank serves its own
+    # config-4 personas (64 per GPU below 4 GPUs, 256 in total from 4 GPUs up), then all
+    # ranks decode 64 personas with the hidden units split across them
+    extra = {}
+    if not args.no_decode:
+        import copy
+        specs = [DEC] if world == 1 else []
+        if not args.no_1p58b:
+            spec4 = copy.copy(DEC4)
+            spec4["personas"] = 64 if world < 4 else 256 // world
+            specs.append(spec4)
+        for spec in specs:
+            dec = decode_workload(device, rank, lib, spec)
+            torch.cuda.empty_cache()
+            if world > 1:
+                dec_ms = max_over_ranks(dec["decode_ms_per_step"])
+                e2e_ms = max_over_ranks(spec["personas"] / dec["decode_e2e_tok_s"] * 1e3)
+                write_ms = max_over_ranks(dec["write_ms"])
+                valid = sum_over_ranks(dec["write_tok_s"] * dec["write_ms"] / 1e3)
+                padded = sum_over_ranks(dec["write_padded_tok_s"] * dec["write_ms"] / 1e3)
+                total = spec["personas"] * world
+                dec.update({"personas_per_gpu": spec["personas"], "personas": total, "n_gpus": world,
+                            "decode_tok_s": total / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
+                            "decode_e2e_tok_s": total / (e2e_ms / 1e3), "write_ms": write_ms,
+                            "write_tok_s": valid / (write_ms / 1e3), "write_padded_tok_s": padded / (write_ms / 1e3),
+                            "partition": "personas by user id, no collective; step times max over ranks"})
+            extra[spec["key"]] = dec
+        if world > 1 and not args.no_1p58b:
+            extra["decode_1p58b_hsplit"] = hsplit_decode_workload(device, rank, world, lib, DEC4)
+            torch.cuda.empty_cache()
+
     if rank == 0:
         hbm, tflops, src = peaks()
         kinds = {0: "chunk_fwd", 1: "chunk_ln", 2: "chunk_norm", 3: "chunk_bwd_update"}
@@ -528,14 +631,14 @@ def ours_arm(args, world, rank, local):
             "kernels": per_kind,
             "clocks": clk,
         }
-        specs = ([] if args.no_decode else [DEC]) + ([] if args.no_decode or args.no_1p58b else [DEC4])
-        for spec in specs:
-            dec = decode_workload(device, rank, lib, spec)
-            for key in ("readout_roofline", "decode_step_roofline"):
-                dec[key]["peak"] = hbm
-                dec[key]["frac"] = dec[key]["achieved"] / hbm
-            line[spec["key"]] = dec
-            torch.cuda.empty_cache()
+        for key, dec in extra.items():
+            for rkey in ("readout_roofline", "decode_step_roofline"):
+                if rkey in dec:
+                    dec[rkey]["peak"] = hbm
+                    dec[rkey]["frac"] = dec[rkey]["achieved"] / hbm
+            if "per_gpu_hbm_gbs" in dec:
+                dec["per_gpu_hbm_frac"] = dec["per_gpu_hbm_gbs"] / hbm
+            line[key] = dec
         if world == 1 and not args.no_cpu_baseline:
             v, n, el = cpu_baseline()
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
