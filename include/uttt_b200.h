@@ -76,6 +76,11 @@ int uttt_selftest_gemm(int mode, int M, int N, int K, const void* a, const void*
                        size_t workspace_bytes, void* stream);
 
 /* ---- chunk-wise TTT write ---------------------------------------------- */
+/* Host hook of a hidden-dimension split: replaces `count` FP32 values at
+ * device address `data` by their sum over every rank of the split (an
+ * all-reduce), ordered on `stream`; returns 0 on success. */
+typedef int (*uttt_partial_sum_fn)(float* data, size_t count, void* ctx, void* stream);
+
 /*
  * Replaces fused_chunk_ttt_step (model/uttt_layer.py:414-534) and its
  * analytical gradient analytical_swiglu_chunk_grad (:279-411), for B
@@ -102,6 +107,12 @@ int uttt_selftest_gemm(int mode, int M, int N, int K, const void* a, const void*
  *                  updates state b and n_states must be B (or <= 0).  A row
  *                  whose entry is not below n_states touches nothing and
  *                  records UTTT_ERR_INVALID in the workspace status word.
+ *   partial_sum,   hidden split over P ranks: w_* / s_* hold this rank's
+ *   partial_sum_ctx hidden units (h = its slice width) and the call sums the
+ *                  partial Z of every chunk (B*64*d floats of the workspace)
+ *                  and, with clipping, the squared gradient norms (B floats)
+ *                  through the hook between its launches; NULL: unsplit.
+ *                  A hook that fails ends the call with UTTT_ERR_CUDA.
  *
  * Requires d % 128 == 0, 1 <= C <= 64.
  */
@@ -111,8 +122,8 @@ int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_c
                      float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
                      const float* ln_weight, const float* ln_bias, float momentum_beta, float max_grad_norm,
                      int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss,
-                     float* clip_scale, int n_states, const int* state_rows, void* workspace,
-                     size_t workspace_bytes, void* stream);
+                     float* clip_scale, int n_states, const int* state_rows, uttt_partial_sum_fn partial_sum,
+                     void* partial_sum_ctx, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Allocation-free chunk write.  No counterpart in the reference.  (Rows map

@@ -1,10 +1,14 @@
-"""GPU (2 ranks, NCCL): the hidden-dimension split of the decode path.
+"""GPU (2 ranks, NCCL): the hidden-dimension split of decode and write.
 
-Each rank holds half of every persona's hidden units (read copies of its
-slices); prefill and packed decode steps sum the readout's z across the
-ranks.  The logits must match an unsplit engine on the same inputs (both
-teacher-forced on the same tokens) within the logits bound, on both ranks.
-Skipped with fewer than two visible GPUs."""
+Each rank holds half of every persona's hidden units (FP32 masters and read
+copies of its slices).  Prefill and packed decode steps sum the readout's z
+across the ranks: the logits must match an unsplit engine on the same inputs
+(both teacher-forced on the same tokens) within the logits bound, on both
+ranks.  The batched chunk-TTT write (momentum + clipping, ragged masks) sums
+every chunk's partial Z and the clip norms across the ranks: each rank's
+updated slices must equal the same slices of the unsplit write (state rel-L2
+<= 1e-3, update rel-L2 <= 1e-2) with the same per-layer surprise.  Skipped
+with fewer than two visible GPUs."""
 
 import datetime
 import os
@@ -40,7 +44,7 @@ def _run(eng, packed, down, prompts, forced):
 
 def _rank_main(rank, world, port, out_dir):
     from utttcompanion_b200.hsplit import HiddenSplit
-    from utttcompanion_b200.model import UtttB200
+    from utttcompanion_b200.model import FastState, UtttB200
     from utttcompanion_b200.workloads import perturbed_persona_states, reference_init_state_dict
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dev = torch.device("cuda", rank)
@@ -57,8 +61,19 @@ def _rank_main(rank, world, port, out_dir):
     forced = [torch.randint(6, cfg.vocab_size, (P,), generator=gen, dtype=torch.int32) for _ in range(6)]
     hs = HiddenSplit()
     eng = UtttB200(sd, cfg, device=dev, max_personas=P, hsplit=hs)
-    packed, down = eng.read_copies(*(w.to(dev) for w in hs.shard(*full)))
+    local = [w.to(dev) for w in hs.shard(*full)]
+    packed, down = eng.read_copies(*local)
     split = _run(eng, packed, down, prompts, forced)
+    # batched write on prompt + forced tokens, ragged (right-padded) with masks
+    turns = [prompts[p].tolist() + [int(f[p]) for f in forced] for p in range(P)]
+    Tpad = ((max(len(t) for t in turns) + 63) // 64) * 64
+    inter = torch.zeros(P, Tpad, dtype=torch.long)
+    mask = torch.zeros(P, Tpad)
+    for p, t in enumerate(turns):
+        inter[p, :len(t)] = torch.tensor(t)
+        mask[p, :len(t)] = 1.0
+    st = FastState(*local, *(torch.zeros_like(w) for w in local), eng.ln_w.clone(), eng.ln_b.clone())
+    new_split, _, pl_split = eng.test_time_update_batch(inter, st, mask)
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
@@ -69,11 +84,21 @@ def _rank_main(rank, world, port, out_dir):
     for a, b in zip(split, ref):
         excess = (torch.abs(a - b) - (LOGIT_TOL + torch.abs(b) / 128)).max().item()
         worst = max(worst, excess)
-    np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array([worst]))
+    fullw = [w.to(dev) for w in full]
+    st_ref = FastState(*fullw, *(torch.zeros_like(w) for w in fullw), ref_eng.ln_w.clone(), ref_eng.ln_b.clone())
+    new_ref, _, pl_ref = ref_eng.test_time_update_batch(inter, st_ref, mask)
+    ref_slices = hs.shard(new_ref.w_up, new_ref.w_gate, new_ref.w_down)
+    base = hs.shard(*fullw)
+    state_err, delta_err = 0.0, 0.0
+    for got, want, w0 in zip((new_split.w_up, new_split.w_gate, new_split.w_down), ref_slices, base):
+        state_err = max(state_err, float(torch.linalg.norm(got - want) / torch.linalg.norm(want)))
+        delta_err = max(delta_err, float(torch.linalg.norm((got - w0) - (want - w0)) / torch.linalg.norm(want - w0)))
+    surprise_err = float(np.max(np.abs(np.array(pl_split) - np.array(pl_ref)) / np.abs(np.array(pl_ref))))
+    np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array([worst, state_err, delta_err, surprise_err]))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_rank_hidden_split_decode_matches_unsplit(tmp_path):
+def test_two_rank_hidden_split_decode_and_write_match_unsplit(tmp_path):
     ctx = mp.get_context("spawn")
     procs = [ctx.Process(target=_rank_main, args=(r, 2, 29541, str(tmp_path))) for r in range(2)]
     for p in procs:
@@ -82,5 +107,7 @@ def test_two_rank_hidden_split_decode_matches_unsplit(tmp_path):
         p.join(timeout=300)
         assert p.exitcode == 0
     for r in range(2):
-        worst = float(np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))[0])
+        worst, state_err, delta_err, surprise_err = np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))
         assert worst <= 0.0, (r, worst)
+        assert state_err <= 1e-3 and delta_err <= 1e-2, (r, state_err, delta_err)
+        assert surprise_err <= 1e-3, (r, surprise_err)

@@ -64,8 +64,8 @@ def test_noalloc_chunk_write_matches_workspace_entry_point_twice():
     names = ("w_up", "w_gate", "w_down", "s_up", "s_gate", "s_down")
     for call in range(2):
         before = {n: ref[n].clone() for n in names}
-        _lib.check(lib.uttt_chunk_write(*_args(ref, B, Tn, C, d, h, loss_ref), B, None, ws.data_ptr(), ws_bytes,
-                                        stream),
+        _lib.check(lib.uttt_chunk_write(*_args(ref, B, Tn, C, d, h, loss_ref), B, None, None, None, ws.data_ptr(),
+                                        ws_bytes, stream),
                    "uttt_chunk_write")
         _lib.check(lib.uttt_chunk_write_noalloc(*_args(na, B, Tn, C, d, h, loss_na), stream),
                    "uttt_chunk_write_noalloc")

@@ -34,6 +34,9 @@ f32 = C.c_float
 sz = C.c_size_t
 
 # argtypes per exported symbol; kept in the same order as include/uttt_b200.h
+# uttt_partial_sum_fn: int (*)(float* data, size_t count, void* ctx, void* stream)
+PARTIAL_SUM_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+
 SIGNATURES: Dict[str, tuple] = {
     "uttt_version": (i32, []),
     "uttt_status_string": (C.c_char_p, [i32]),
@@ -44,7 +47,7 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_selftest_gemm": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
     "uttt_chunk_write_workspace": (sz, [i32, i32, i32, i32]),
     "uttt_chunk_write": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                               vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, i32, vp, vp, sz, vp]),
+                               vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, i32, vp, vp, vp, vp, sz, vp]),
     "uttt_chunk_write_noalloc": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp]),
     "uttt_fast_readout_workspace": (sz, [i32, i32, i32]),

@@ -1288,7 +1288,8 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
                                 float* s_gate, float* s_down, const float* ln_weight, const float* ln_bias,
                                 float momentum_beta, float max_grad_norm, int normalize_by_dim, float eps,
                                 void* out, int out_dtype, float* token_loss, float* clip_scale, int n_states,
-                                const int* state_rows, void* workspace, size_t workspace_bytes, void* stream) {
+                                const int* state_rows, uttt_partial_sum_fn partial_sum, void* partial_sum_ctx,
+                                void* workspace, size_t workspace_bytes, void* stream) {
   UTTT_REQUIRE(B > 0 && T > 0 && C > 0 && d > 0 && h > 0 && n_chunks >= 0 && chunk_begin >= 0, UTTT_ERR_INVALID);
   if (n_states <= 0) n_states = B;
   UTTT_REQUIRE(state_rows != nullptr || n_states == B, UTTT_ERR_INVALID);
@@ -1396,6 +1397,9 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
       chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
     }
     UTTT_TRY(launch_status());
+    // hidden split: this chunk's Z is the sum of every rank's partial Z
+    if (ci == 0 && partial_sum && partial_sum(p.zacc, (size_t)B * CT * d, partial_sum_ctx, stream) != 0)
+      return UTTT_ERR_CUDA;
     {
       ProfScope ps(UTTT_PROF_CHUNK_LN, st);
       chunk_ln_for(d)<<<dim3(CT / LN_ROWS, B), LN_ROWS * 32, 0, st>>>(p);
@@ -1407,6 +1411,9 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
         chunk_bwd_kernel<true, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
       else
         chunk_bwd_kernel<false, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+      UTTT_TRY(launch_status());
+      // hidden split: the clip norm runs over every rank's gradient slices
+      if (partial_sum && partial_sum(p.norm2, (size_t)B, partial_sum_ctx, stream) != 0) return UTTT_ERR_CUDA;
     }
     UTTT_TRY(launch_status());
     {
@@ -1424,6 +1431,9 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
       }
     }
     UTTT_TRY(launch_status());
+    // hidden split: the next chunk's Z (computed by the fused kernel) from every rank's slices
+    if (fuse && partial_sum && partial_sum(p.zacc, (size_t)B * CT * d, partial_sum_ctx, stream) != 0)
+      return UTTT_ERR_CUDA;
   }
   return UTTT_OK;
 }

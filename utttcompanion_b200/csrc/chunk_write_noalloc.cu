@@ -64,6 +64,6 @@ extern "C" int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int c
   UTTT_TRY(cuda_status(cudaMemsetAsync(scratch, 0, sizeof(int), (cudaStream_t)stream)));
   return uttt_chunk_write(B, T, C, d, h, chunk_begin, n_chunks, q, k, v, eta, alpha, mask, w_up, w_gate, w_down,
                           s_up, s_gate, s_down, ln_weight, ln_bias, momentum_beta, max_grad_norm, normalize_by_dim,
-                          eps, out, out_dtype, token_loss, clip_scale, B, nullptr, scratch, (size_t)UTTT_NOALLOC_SCRATCH_BYTES,
+                          eps, out, out_dtype, token_loss, clip_scale, B, nullptr, nullptr, nullptr, scratch, (size_t)UTTT_NOALLOC_SCRATCH_BYTES,
                           stream);
 }

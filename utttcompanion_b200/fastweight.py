@@ -10,6 +10,7 @@ CPU tensors raise ``ValueError``.
 
 from __future__ import annotations
 
+import ctypes
 import threading
 from typing import Dict, Optional, Tuple
 
@@ -73,7 +74,8 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
                 momentum_beta: float, max_inner_grad_norm: float, normalize_by_dim: bool, eps: float,
                 chunk_size: int = 64, chunk_begin: int = 0, n_chunks: Optional[int] = None,
                 out: Optional[torch.Tensor] = None, token_loss: Optional[torch.Tensor] = None,
-                clip_scale: Optional[torch.Tensor] = None, state_rows: Optional[torch.Tensor] = None) -> None:
+                clip_scale: Optional[torch.Tensor] = None, state_rows: Optional[torch.Tensor] = None,
+                partial_sum=None) -> None:
     """In-place multi-chunk write over ``(B, T, d)`` BF16 keys/values.
 
     Applies ``n_chunks`` consecutive chunk steps (``SharedFastWeightPool.chunk_step``
@@ -82,7 +84,11 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
     which is the readout f_W(k) when the caller reads with q = k.
     ``state_rows`` (int32 (B,), distinct): row b updates state ``state_rows[b]``
     of masters holding any number of states (ragged batches); by default row b
-    updates state b.
+    updates state b.  ``partial_sum`` (hidden split): the masters are this
+    rank's slices of the hidden units and ``partial_sum(t)`` must replace the
+    FP32 tensor ``t`` by its sum over the ranks (e.g. ``HiddenSplit.all_reduce``);
+    it is called between launches for every chunk's partial Z and, with
+    clipping, the squared gradient norms.
     """
     _require_cuda(k, v, eta, alpha, w_up, w_gate, w_down, s_up, s_gate, s_down, ln_weight, ln_bias, token_mask,
                   state_rows)
@@ -113,12 +119,27 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
     out_dtype = _lib.DTYPE_F32
     if out is not None:
         out_dtype = _lib.DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    hook = None
+    if partial_sum is not None:
+        base = ws.data_ptr()
+
+        def _sum(ptr, count, ctx, stream):
+            try:
+                off = ptr - base
+                partial_sum(ws[off:off + 4 * count].view(torch.float32))
+                return 0
+            except Exception:                           # reported as UTTT_ERR_CUDA by the call
+                import traceback
+                traceback.print_exc()
+                return 1
+        hook = _lib.PARTIAL_SUM_FN(_sum)
     st = lib.uttt_chunk_write(
         B, T, chunk_size, d, h, chunk_begin, n_chunks, _ptr(k), _ptr(k), _ptr(v), _ptr(eta), _ptr(alpha),
         _ptr(token_mask), _ptr(w_up), _ptr(w_gate), _ptr(w_down), _ptr(s_up), _ptr(s_gate), _ptr(s_down),
         _ptr(ln_weight), _ptr(ln_bias), float(momentum_beta), float(max_inner_grad_norm),
         int(bool(normalize_by_dim)), float(eps), _ptr(out), out_dtype, _ptr(token_loss), _ptr(clip_scale),
-        S, _ptr(state_rows), ws.data_ptr(), ws.numel(), _stream(k.device))
+        S, _ptr(state_rows), None if hook is None else ctypes.cast(hook, ctypes.c_void_p), None, ws.data_ptr(),
+        ws.numel(), _stream(k.device))
     _lib.check(st, "uttt_chunk_write")
 
 

@@ -185,12 +185,18 @@ class UtttB200:
         d = w.shape[0]
         self._linear(x, w, [_seg(0, d, _lib.SEG_RESID, h, h.stride(0), h, h.stride(0))])
 
-    def _readout(self, q: torch.Tensor, packed: torch.Tensor, down: torch.Tensor, sidx: torch.Tensor) -> torch.Tensor:
-        """Frozen readout f_W(q) of (B, T, d) BF16 queries through BF16 read copies."""
+    def _readout(self, q: torch.Tensor, packed: torch.Tensor, down: torch.Tensor, sidx: torch.Tensor,
+                 ln: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+        """Frozen readout f_W(q) of (B, T, d) BF16 queries through BF16 read copies, with the
+        engine's LayerNorm affine or a state's own ``ln`` (weight, bias)."""
+        if ln is None:
+            lw, lb = self.ln_w_act, self.ln_b_act
+        else:   # as the BF16 path applies it (ln.to(x.dtype), model/uttt_layer.py:253-257)
+            lw, lb = (t.to(torch.bfloat16).float().contiguous() for t in ln)
         if self.hsplit is not None:
-            return self.hsplit.readout(q, packed, down, sidx, self.ln_w_act, self.ln_b_act, self.cfg.rms_norm_eps)
-        return fast_readout(q, packed, None, down, self.ln_w_act, self.ln_b_act, self.cfg.rms_norm_eps,
-                            state_index=sidx, packed=True, ln_prepared=True)
+            return self.hsplit.readout(q, packed, down, sidx, lw, lb, self.cfg.rms_norm_eps)
+        return fast_readout(q, packed, None, down, lw, lb, self.cfg.rms_norm_eps, state_index=sidx, packed=True,
+                            ln_prepared=True)
 
     def _q_proj(self, layer, x2: torch.Tensor) -> torch.Tensor:
         """``fused_fast_q_proj`` (model/uttt_layer.py:1175-1190)."""
@@ -361,8 +367,6 @@ class UtttB200:
         (model/uttt_model.py:598-607, 833-838)."""
         cfg = self.cfg
         dev = self.device
-        if self.hsplit is not None:
-            raise ValueError("the batched write needs unsplit fast-weight states (hidden split: decode and prefill)")
         ids = interaction_ids.to(device=dev)
         B, T = ids.shape
         C, W = cfg.chunk_size, cfg.sliding_window_size
@@ -443,8 +447,7 @@ class UtttB200:
                     _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, ALPHA[i], 1, lay.b_alpha, 0, cfg.base_weight_decay,
                          out_f32=True),
                 ])
-                out = fast_readout(q.reshape(Bc, Cc, d), rp, None, rd, cur.ln_weight, cur.ln_bias, cfg.rms_norm_eps,
-                                   state_index=rows, packed=True)
+                out = self._readout(q.reshape(Bc, Cc, d), rp, rd, rows, (cur.ln_weight, cur.ln_bias))
                 self._resid_linear(hh, out.reshape(R, d), lay.w_o)
                 hidden = hh
             # ... then the L writes chain through the state as ONE call whose chunks are the
@@ -459,7 +462,7 @@ class UtttB200:
             chunk_write(Kr, Vr, Er, Ar, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,
                         cur.ln_weight, cur.ln_bias, Mr, cfg.momentum_beta, float(cfg.max_inner_grad_norm or 0.0),
                         cfg.normalize_loss_by_dim, cfg.rms_norm_eps, chunk_size=Cc, token_loss=loss,
-                        state_rows=rows)
+                        state_rows=rows, partial_sum=None if self.hsplit is None else self.hsplit.all_reduce)
             lz = loss.reshape(Bc, L, Cc)
             if m is None:
                 layer_loss = lz.mean(dim=2)                                        # (Bc, L)
