@@ -622,7 +622,7 @@ struct WMaps {
 };
 constexpr int QW = 32;                    // d columns per staged quarter chunk
 constexpr int WTILE = HT * QW * 4;        // 16 KB: one staged FP32 tile
-constexpr int NF = 4;                     // FP32 W_down quarter tiles in flight (operand rings)
+constexpr int NF = 5;                     // FP32 W_down quarter tiles in flight (phase-1 ring)
 constexpr int ZSLOT = 32 * 1024;          // one BF16 [128 d][128 hidden] A tile of the next chunk's Z'
 
 // kFuse: also run the NEXT chunk's forward (U', G', H', partial Z') from the
@@ -649,7 +649,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   uint8_t* sKN = sAG + 16384;                       //             K' tile [64 tokens][64 d]
   uint8_t* sH = sDU;                                // next chunk H' (MN-major [hh][64 tokens]) after the loop
   // FP32 W_down quarter tiles [128 hidden][32 d] (TMA, 128B swizzle) of
-  // phase 1, NF deep, in sDU..sAU (free until dH is done)
+  // phase 1, NF deep, in sDU..sAG (free until dH is done)
   uint8_t* fring1 = sDU;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -797,26 +797,33 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     }
 
     // ------------------------------------------------------------ epilogue 1: dU, dG, H
-    mbar_wait(&dh_done, 0, p.status);
-    tc_fence_after();
     const int q = warp & 3, half = warp >> 2;
     const int row = q * 32 + lane;                   // hidden row within the tile
     {
       const int c0 = half * 32;
+      // the saved U / G of this thread's row are loaded while the dH MMAs finish
+      const float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
+      const float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+      float uv[32], gv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        uv[i] = us[(size_t)(c0 + i) * p.hp];
+        gv[i] = gs[(size_t)(c0 + i) * p.hp];
+      }
+      mbar_wait(&dh_done, 0, p.status);
+      tc_fence_after();
       float dh[32];
       tmem_ld16(tmem_addr(tDH, q * 32, c0), *reinterpret_cast<float(*)[16]>(&dh[0]));
       tmem_ld16(tmem_addr(tDH, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&dh[16]));
       tmem_wait_ld();
-      const float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
-      const float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         float du[8], dg[8], hv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = c0 + i + e;
-          const float u = us[(size_t)c * p.hp];
-          const float g = gs[(size_t)c * p.hp];
+          const float u = uv[i + e];
+          const float g = gv[i + e];
           const float sg = sigmoidf_(g);
           const float a = g * sg;
           const bool valid = c < p.Cc;
