@@ -170,7 +170,7 @@ int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int chunk_begin,
  * T == 1 with BF16 copies runs the decode GEMV; otherwise 64-token tiles on
  * the tensor cores.  Requires d % 128 == 0, h % 8 == 0.
  */
-size_t uttt_fast_readout_workspace(int B, int d, int h);
+size_t uttt_fast_readout_workspace(int B, int T, int d, int h);
 int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up, const void* w_gate,
                       const void* w_down, const int* state_index, const float* ln_weight, const float* ln_bias,
                       float eps, void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
@@ -180,9 +180,8 @@ int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, co
  * P GPUs): each rank holds hidden units [r*h, (r+1)*h) of every persona, as
  * packed BF16 [W_up | W_gate] (S, d, 2h) and W_down (S, h, d) slices.
  * uttt_fast_readout_partial writes that slice's z = h_slice W_down_slice,
- * FP32 (B, T, d) for T <= 64 tokens per state (z is zeroed first; T == 1 runs
- * the decode GEMV, T > 1 the tensor-core tile; the workspace only holds the
- * status word).  After the ranks' z are summed (an all-reduce),
+ * FP32 (B, T, d) (z is zeroed first; T == 1 runs the decode GEMV, T > 1 the
+ * tensor-core tiles; the workspace only holds the status word).  After the ranks' z are summed (an all-reduce),
  * uttt_readout_finish applies out = x + LayerNorm(bf16(z)) * ln_weight +
  * ln_bias to `rows` rows of (rows, d).  Together they equal uttt_fast_readout
  * (swiglu_packed_forward, model/uttt_layer.py:250-257): every hidden unit's

@@ -50,7 +50,7 @@ SIGNATURES: Dict[str, tuple] = {
                                vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, i32, vp, vp, vp, vp, sz, vp]),
     "uttt_chunk_write_noalloc": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp]),
-    "uttt_fast_readout_workspace": (sz, [i32, i32, i32]),
+    "uttt_fast_readout_workspace": (sz, [i32, i32, i32, i32]),
     "uttt_fast_readout": (i32, [i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, f32, vp, i32, vp, sz, vp]),
     "uttt_fast_readout_partial": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]),
     "uttt_readout_finish": (i32, [i32, i32, vp, vp, vp, vp, f32, vp, i32, vp]),

@@ -77,6 +77,7 @@ struct ChunkParams {
   int tok0_next, Cc_next;  // the fused forward's chunk (bwd kernel with kFuse)
   int hp;             // hidden padded to 128
   int z_rows;         // rows of zacc per state (0: 64, the chunk tile)
+  int tiles;          // fwd readout over all token tiles in one launch: grid (T/64, h/128, B)
   float beta, clip, eps, inv_scale;
   int* status;
   // weight source of the fwd kernel: element (state, k, j) of up/gate at
@@ -171,7 +172,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
   uint8_t* sH = slots + NSLOT * SLOT_BYTES;  // 16 KB: MN-major [hh 128 rows][64 tokens]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t = blockIdx.x, b = blockIdx.y;
+  // one chunk (t = hidden tile, b = state) or, in tiles mode, every 64-token tile of a readout
+  // (x = token tile, fastest, so the CTAs that share a hidden tile's weights run together)
+  const int t = p.tiles ? blockIdx.y : blockIdx.x, b = p.tiles ? blockIdx.z : blockIdx.y;
+  const int tok0 = p.tiles ? blockIdx.x * CT : p.tok0;
+  const int Cc = p.tiles ? min(CT, p.T - tok0) : p.Cc;
+  const int zr = p.z_rows ? p.z_rows : CT;
+  const size_t zrow0 = (size_t)b * zr + (p.tiles ? tok0 : 0);   // this tile's first zacc row
   const int h0 = t * HT;
   const int nkb = p.d / 64;
   const int nmt = p.d / 128;
@@ -269,7 +276,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const float gg = g[i + e];
-          hv[e] = (c0 + i + e < p.Cc) ? gg * sigmoidf_(gg) * u[i + e] : 0.f;
+          hv[e] = (c0 + i + e < Cc) ? gg * sigmoidf_(gg) * u[i + e] : 0.f;
         }
         pk.x = pack_bf16x2(hv[0], hv[1]);
         pk.y = pack_bf16x2(hv[2], hv[3]);
@@ -313,9 +320,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&zfree[zb]);
-        float* za = p.zacc + (size_t)b * (p.z_rows ? p.z_rows : CT) * p.d + pm * 128 + row;
+        float* za = p.zacc + zrow0 * p.d + pm * 128 + row;
         for (int i = 0; i < 32; ++i)
-          if (c0 + i < p.Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
+          if (c0 + i < Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
       }
     }
     {
@@ -328,9 +335,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
       tmem_wait_ld();
-      float* za = p.zacc + (size_t)b * (p.z_rows ? p.z_rows : CT) * p.d + pm * 128 + row;
+      float* za = p.zacc + zrow0 * p.d + pm * 128 + row;
       for (int i = 0; i < 32; ++i)
-        if (c0 + i < p.Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
+        if (c0 + i < Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
     }
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -340,7 +347,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         const int s = it % NSLOT;
         mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full[s], 8192);
-        tma_load_3d(slots + s * SLOT_BYTES + 32768, &tmK, &full[s], kb * 64, p.tok0, b);
+        tma_load_3d(slots + s * SLOT_BYTES + 32768, &tmK, &full[s], kb * 64, tok0, b);
       }
       for (int mt = 0; mt < nmt; ++mt, ++it) {
         const int s = it % NSLOT;
@@ -1376,8 +1383,6 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   if (!attr_done) {
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false, false>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true, false>,
@@ -1460,7 +1465,7 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
                                          const void* w_down, const int* state_index, float* z, void* workspace,
                                          size_t workspace_bytes, void* stream) {
   UTTT_REQUIRE(B > 0 && T > 0 && d > 0 && h > 0 && x && w_packed && w_down && z && workspace, UTTT_ERR_INVALID);
-  UTTT_REQUIRE(T <= CT && d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
+  UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(workspace_bytes >= 256, UTTT_ERR_WORKSPACE);
   cudaStream_t st = (cudaStream_t)stream;
   UTTT_TRY(cuda_status(cudaMemsetAsync(z, 0, (size_t)B * T * d * sizeof(float), st)));
@@ -1489,8 +1494,7 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
   p.src_down = w_down;
   p.ss_d = (long long)h * d;
   p.state_index = state_index;
-  p.tok0 = 0;
-  p.Cc = T;
+  p.tiles = 1;
   CUtensorMap tmX;
   {
     uint64_t dims[3] = {(uint64_t)d, (uint64_t)T, (uint64_t)B};
@@ -1498,7 +1502,8 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
     uint32_t box[3] = {64, 64, 1};
     UTTT_TRY(make_tmap_bf16(&tmX, x, 3, dims, str, box));
   }
-  chunk_fwd_kernel<__nv_bfloat16><<<dim3((h + HT - 1) / HT, B), NTHREADS, fwd_smem(), st>>>(tmX, p);
+  chunk_fwd_kernel<__nv_bfloat16><<<dim3((T + CT - 1) / CT, (h + HT - 1) / HT, B), NTHREADS, fwd_smem(), st>>>(tmX,
+                                                                                                           p);
   return launch_status();
 }
 
@@ -1513,10 +1518,10 @@ extern "C" int uttt_readout_finish(int B, int d, const float* z, const void* x, 
                                out_dtype == UTTT_DTYPE_BF16, st);
 }
 
-extern "C" size_t uttt_fast_readout_workspace(int B, int d, int h) {
-  if (B <= 0 || d <= 0 || h <= 0) return 0;
+extern "C" size_t uttt_fast_readout_workspace(int B, int T, int d, int h) {
+  if (B <= 0 || T <= 0 || d <= 0 || h <= 0) return 0;
   (void)h;
-  return 256 + ws_round((size_t)B * CT * d * sizeof(float));
+  return 256 + ws_round((size_t)B * (T > CT ? T : CT) * d * sizeof(float));
 }
 
 extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up,
@@ -1530,10 +1535,10 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
   UTTT_REQUIRE(out_dtype == UTTT_DTYPE_F32 || out_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
   UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(eps > 0.f, UTTT_ERR_INVALID);
-  UTTT_REQUIRE(workspace_bytes >= uttt_fast_readout_workspace(B, d, h), UTTT_ERR_WORKSPACE);
+  UTTT_REQUIRE(workspace_bytes >= uttt_fast_readout_workspace(B, T, d, h), UTTT_ERR_WORKSPACE);
   cudaStream_t st = (cudaStream_t)stream;
   WsCursor ws(workspace, workspace_bytes);
-  float* zacc = ws.take<float>((size_t)B * CT * d);
+  float* zacc = ws.take<float>((size_t)B * (T > CT ? T : CT) * d);
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
   const int ob = out_dtype == UTTT_DTYPE_BF16;
   if (T == 1 && w_dtype == UTTT_DTYPE_BF16) {
@@ -1547,7 +1552,7 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
                                  (const __nv_bfloat16*)w_down, state_index, ln_weight, ln_bias, eps, zacc, done, out,
                                  ob, st);
   }
-  UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
+  UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * T * d * sizeof(float), st)));
   static bool attr_done = false;
   if (!attr_done) {
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
@@ -1576,6 +1581,10 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
   p.src_down = w_down;
   p.ss_d = (long long)h * d;
   p.state_index = state_index;
+  // every 64-token tile in one launch (token tiles fastest: the CTAs of a hidden tile share
+  // its weight slice through L2), z rows (B, T, d), then one LayerNorm launch over all rows
+  p.tiles = 1;
+  p.z_rows = T;
   CUtensorMap tmX;
   {
     uint64_t dims[3] = {(uint64_t)d, (uint64_t)T, (uint64_t)B};
@@ -1583,24 +1592,19 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
     uint32_t box[3] = {64, 64, 1};
     UTTT_TRY(make_tmap_bf16(&tmX, x, 3, dims, str, box));
   }
-  const dim3 grid((h + HT - 1) / HT, B);
-  for (int tok0 = 0; tok0 < T; tok0 += CT) {
-    p.tok0 = tok0;
-    p.Cc = (T - tok0) < CT ? (T - tok0) : CT;
-    {
-      ProfScope ps(UTTT_PROF_READOUT, st);
-      if (w_dtype == UTTT_DTYPE_BF16)
-        chunk_fwd_kernel<__nv_bfloat16><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
-      else
-        chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
-    }
-    UTTT_TRY(launch_status());
-    {
-      ProfScope ps(UTTT_PROF_READOUT_LN, st);
-      readout_ln_kernel<<<dim3(CT, B), LN_THREADS, 0, st>>>(zacc, CT, (const __nv_bfloat16*)x, T, tok0, p.Cc, d,
-                                                            ln_weight, ln_bias, eps, out, ob);
-    }
-    UTTT_TRY(launch_status());
+  const dim3 grid((T + CT - 1) / CT, (h + HT - 1) / HT, B);
+  {
+    ProfScope ps(UTTT_PROF_READOUT, st);
+    if (w_dtype == UTTT_DTYPE_BF16)
+      chunk_fwd_kernel<__nv_bfloat16><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
+    else
+      chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
   }
-  return UTTT_OK;
+  UTTT_TRY(launch_status());
+  {
+    ProfScope ps(UTTT_PROF_READOUT_LN, st);
+    readout_ln_kernel<<<dim3(T, B), LN_THREADS, 0, st>>>(zacc, T, (const __nv_bfloat16*)x, T, 0, T, d, ln_weight,
+                                                         ln_bias, eps, out, ob);
+  }
+  return launch_status();
 }

@@ -56,7 +56,8 @@ class HiddenSplit:
     def readout(self, x: torch.Tensor, packed: torch.Tensor, down: torch.Tensor, state_index: torch.Tensor,
                 ln_weight: torch.Tensor, ln_bias: torch.Tensor, eps: float) -> torch.Tensor:
         """x + LN(z) for (B, T, d) BF16 ``x`` over this rank's BF16 slices
-        ``packed`` (S, d, 2h_local) / ``down`` (S, h_local, d); 64-token tiles."""
+        ``packed`` (S, d, 2h_local) / ``down`` (S, h_local, d): one partial readout,
+        one all-reduce of z (B, T, d) FP32, one LayerNorm finish."""
         lib = _lib.load()
         B, T, d = x.shape
         h = down.shape[-2]
@@ -67,18 +68,12 @@ class HiddenSplit:
         out = torch.empty(B, T, d, dtype=torch.bfloat16, device=x.device)
         ws = workspace(256, x.device, slot=3)
         stream = _stream(x.device)
-        for t0 in range(0, T, 64):
-            tt = min(64, T - t0)
-            xt = x if tt == T else x[:, t0:t0 + tt].contiguous()
-            z = torch.empty(B, tt, d, dtype=torch.float32, device=x.device)
-            _lib.check(lib.uttt_fast_readout_partial(B, tt, d, h, xt.data_ptr(), packed.data_ptr(), down.data_ptr(),
-                                                     _ptr(sidx), z.data_ptr(), ws.data_ptr(), ws.numel(), stream),
-                       "uttt_fast_readout_partial")
-            self.all_reduce(z)
-            ot = out if tt == T else torch.empty(B, tt, d, dtype=torch.bfloat16, device=x.device)
-            _lib.check(lib.uttt_readout_finish(B * tt, d, z.data_ptr(), xt.data_ptr(), ln_weight.data_ptr(),
-                                               ln_bias.data_ptr(), float(eps), ot.data_ptr(), _lib.DTYPE_BF16,
-                                               stream), "uttt_readout_finish")
-            if tt != T:
-                out[:, t0:t0 + tt] = ot
+        z = torch.empty(B, T, d, dtype=torch.float32, device=x.device)
+        _lib.check(lib.uttt_fast_readout_partial(B, T, d, h, x.data_ptr(), packed.data_ptr(), down.data_ptr(),
+                                                 _ptr(sidx), z.data_ptr(), ws.data_ptr(), ws.numel(), stream),
+                   "uttt_fast_readout_partial")
+        self.all_reduce(z)
+        _lib.check(lib.uttt_readout_finish(B * T, d, z.data_ptr(), x.data_ptr(), ln_weight.data_ptr(),
+                                           ln_bias.data_ptr(), float(eps), out.data_ptr(), _lib.DTYPE_BF16, stream),
+                   "uttt_readout_finish")
         return out

@@ -64,7 +64,7 @@ def fast_readout(x: torch.Tensor, w_up: torch.Tensor, w_gate: Optional[torch.Ten
         out = torch.empty(B, T, d, dtype=torch.bfloat16 if odt == torch.bfloat16 else torch.float32,
                           device=x.device)
     lib = _lib.load()
-    ws = workspace(lib.uttt_fast_readout_workspace(B, d, h), x.device, slot=1)
+    ws = workspace(lib.uttt_fast_readout_workspace(B, T, d, h), x.device, slot=1)
     st = lib.uttt_fast_readout(B, T, d, h, xb.data_ptr(), wd_kind, wu.data_ptr(), _ptr(wg), wd.data_ptr(),
                                _ptr(state_index), lw.data_ptr(), lb.data_ptr(), float(eps), out.data_ptr(),
                                _lib.DTYPE_BF16 if out.dtype == torch.bfloat16 else _lib.DTYPE_F32,
