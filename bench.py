@@ -509,6 +509,10 @@ def ours_arm(args, world, rank, local):
         return float(t.item())
 
     lib = _lib.load()
+    if args.only_decode:          # profiling case: the config-3 decode + write workload alone
+        if rank == 0:
+            print(json.dumps(decode_workload(device, rank, lib, DEC)), flush=True)
+        return 0
     st = make_states(device, seed=1234 + rank)
     B, T = CFG["states"], CFG["tokens"]
 
@@ -661,6 +665,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode + write workloads (configs 3, 4)")
     ap.add_argument("--no-1p58b", action="store_true", help="skip the 1.58B (config 4) decode + write workload")
+    ap.add_argument("--only-decode", action="store_true",
+                    help="profiling: run only the config-3 decode + write workload (one JSON object, 1 GPU)")
     ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")
     ap.add_argument("--tokens", type=int, default=None, help="override tokens per state (profiling cases)")
     args = ap.parse_args()

@@ -204,13 +204,20 @@ int uttt_readout_finish(int rows, int d, const float* z, const void* x, const fl
  * fused_slow_projections (:1193-1231) and the tied lm_head
  * (model/uttt_model.py:944-950).  Segment ops reproduce the reference's BF16
  * roundings: STORE  y;  RESID  aux + bf16(y);  RMSNORM  rms_norm(bf16(y)) *
- * gamma (aux = FP32 gamma or NULL);  SIGMOID  scale * sigmoid(bf16(y + aux)).
+ * gamma (aux = FP32 gamma or NULL);  SIGMOID  scale * sigmoid(bf16(y + aux));
+ * NORM  rms_norm(aux row) * gamma for a BF16 row `aux` written by an earlier
+ * segment of the same call (aux2 = FP32 gamma or NULL; y is not read): a
+ * residual projection can emit the next block's normalised input
+ * (uTTTBlock.forward, :1544-1554).  Segments of a row run in order.
  * Requires K % 64 == 0.  out may alias a RESID segment's aux (in place).
+ * The workspace must be zero on entry (a fresh uttt_linear_workspace buffer
+ * is); every call leaves it zero again.
  */
 #define UTTT_SEG_STORE 0
 #define UTTT_SEG_RESID 1
 #define UTTT_SEG_RMSNORM 2
 #define UTTT_SEG_SIGMOID 3
+#define UTTT_SEG_NORM 4
 typedef struct UtttSegment {
   int start, len; /* columns [start, start + len) of y */
   int op;         /* UTTT_SEG_* */
@@ -219,7 +226,8 @@ typedef struct UtttSegment {
   long long out_ld;
   const void* aux; /* RESID: BF16 rows (aux_ld); RMSNORM: FP32 gamma (len); SIGMOID: FP32 bias (len) */
   long long aux_ld;
-  float scale; /* SIGMOID multiplier */
+  float scale;      /* SIGMOID multiplier */
+  const void* aux2; /* NORM: FP32 gamma (len) or NULL */
 } UtttSegment;
 size_t uttt_linear_workspace(int M, int N);
 int uttt_linear(int M, int N, int K, const void* x, const void* w, int nseg, const UtttSegment* segs, float eps,

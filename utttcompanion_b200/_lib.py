@@ -74,10 +74,10 @@ class Segment(C.Structure):
     """``UtttSegment`` of include/uttt_b200.h."""
     _fields_ = [("start", C.c_int), ("len", C.c_int), ("op", C.c_int), ("out_f32", C.c_int),
                 ("out", C.c_void_p), ("out_ld", C.c_longlong), ("aux", C.c_void_p), ("aux_ld", C.c_longlong),
-                ("scale", C.c_float)]
+                ("scale", C.c_float), ("aux2", C.c_void_p)]
 
 
-SEG_STORE, SEG_RESID, SEG_RMSNORM, SEG_SIGMOID = 0, 1, 2, 3
+SEG_STORE, SEG_RESID, SEG_RMSNORM, SEG_SIGMOID, SEG_NORM = 0, 1, 2, 3, 4
 
 _lib: Optional[C.CDLL] = None
 

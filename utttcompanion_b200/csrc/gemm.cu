@@ -119,9 +119,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// Row-wise finishing of a projection: up to 6 column segments per row.
+// Row-wise finishing of a projection: up to 6 column segments per row, one CTA
+// per row (4 independent loads per thread in flight).  The FP32 accumulator
+// row is zeroed after use, so the next projection can accumulate into it
+// without a memset.
 // ---------------------------------------------------------------------------
 constexpr int F_THREADS = 256;
+constexpr int F_UNROLL = 4;
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
@@ -137,60 +141,92 @@ __device__ __forceinline__ float fblock_sum(float v, float* red) {
   return s;
 }
 
-__global__ void __launch_bounds__(F_THREADS) finish_kernel(const float* __restrict__ y, int N, int nseg,
-                                                           UtttSegment seg0, UtttSegment seg1, UtttSegment seg2,
-                                                           UtttSegment seg3, UtttSegment seg4, UtttSegment seg5,
-                                                           float eps, int zero_y) {
+struct SegPack {
+  UtttSegment s[6];
+};
+
+__device__ __forceinline__ float seg_value(const UtttSegment& sg, float v, int r, int i, float rinv) {
+  switch (sg.op) {
+    case UTTT_SEG_RESID:
+      return __bfloat162float((reinterpret_cast<const __nv_bfloat16*>(sg.aux) + (size_t)r * sg.aux_ld)[i]) + bf16r(v);
+    case UTTT_SEG_RMSNORM: {
+      // F.rms_norm of the BF16 projection: FP32 statistics, weight applied in FP32
+      float o = bf16r(v) * rinv;
+      if (sg.aux) o *= bf16r(reinterpret_cast<const float*>(sg.aux)[i]);
+      return o;
+    }
+    case UTTT_SEG_SIGMOID: {
+      // scale * sigmoid(linear + bias) with the BF16 roundings of F.linear, sigmoid and the product
+      const float lin = bf16r(v + (sg.aux ? reinterpret_cast<const float*>(sg.aux)[i] : 0.f));
+      return bf16r(sg.scale * bf16r(sigmoidf_(lin)));
+    }
+    default:
+      return v;
+  }
+}
+
+__global__ void __launch_bounds__(F_THREADS) finish_kernel(float* __restrict__ y, int N, int nseg,
+                                                           const __grid_constant__ SegPack sp, float eps) {
   __shared__ float red[F_THREADS / 32];
   const int r = blockIdx.x, tid = threadIdx.x;
-  float* yrow = const_cast<float*>(y) + (size_t)r * N;
-  const UtttSegment segs[6] = {seg0, seg1, seg2, seg3, seg4, seg5};
+  float* yrow = y + (size_t)r * N;
   for (int si = 0; si < nseg; ++si) {
-    const UtttSegment sg = segs[si];
+    const UtttSegment& sg = sp.s[si];
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(sg.out) + (size_t)r * sg.out_ld;
-    float ss = 0.f;
-    if (sg.op == UTTT_SEG_RMSNORM) {
+    float* outf = reinterpret_cast<float*>(sg.out) + (size_t)r * sg.out_ld;
+    if (sg.op == UTTT_SEG_NORM) {
+      // rms_norm of a BF16 row an earlier segment of this row has just written
+      __syncthreads();
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(sg.aux) + (size_t)r * sg.aux_ld;
+      const float* gamma = reinterpret_cast<const float*>(sg.aux2);
+      float ss = 0.f;
       for (int i = tid; i < sg.len; i += F_THREADS) {
-        const float v = bf16r(yrow[sg.start + i]);
+        const float v = __bfloat162float(src[i]);
         ss += v * v;
       }
-      ss = fblock_sum(ss, red);
-    }
-    const float rinv = rsqrtf(ss / (float)sg.len + eps);
-    for (int i = tid; i < sg.len; i += F_THREADS) {
-      float v = yrow[sg.start + i];
-      float o;
-      switch (sg.op) {
-        case UTTT_SEG_RESID: {
-          const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(sg.aux) + (size_t)r * sg.aux_ld;
-          o = __bfloat162float(res[i]) + bf16r(v);
-          break;
-        }
-        case UTTT_SEG_RMSNORM: {
-          // F.rms_norm of the BF16 projection: FP32 statistics, weight applied in FP32
-          o = bf16r(v) * rinv;
-          if (sg.aux) o *= bf16r(reinterpret_cast<const float*>(sg.aux)[i]);
-          break;
-        }
-        case UTTT_SEG_SIGMOID: {
-          // scale * sigmoid(linear + bias) with the BF16 roundings of F.linear, sigmoid and the product
-          const float lin = bf16r(v + (sg.aux ? reinterpret_cast<const float*>(sg.aux)[i] : 0.f));
-          o = bf16r(sg.scale * bf16r(sigmoidf_(lin)));
-          break;
-        }
-        default:
-          o = v;
+      const float rinv = rsqrtf(fblock_sum(ss, red) / (float)sg.len + eps);
+      for (int i = tid; i < sg.len; i += F_THREADS) {
+        float v = __bfloat162float(src[i]) * rinv;
+        if (gamma) v *= bf16r(gamma[i]);
+        if (sg.out_f32)
+          outf[i] = v;
+        else
+          out[i] = __float2bfloat16(v);
       }
-      if (sg.out_f32)
-        reinterpret_cast<float*>(sg.out)[(size_t)r * sg.out_ld + i] = o;
-      else
-        out[i] = __float2bfloat16(o);
+      continue;
+    }
+    const float* ys = yrow + sg.start;
+    float rinv = 1.f;
+    if (sg.op == UTTT_SEG_RMSNORM) {
+      float ss = 0.f;
+      for (int i = tid; i < sg.len; i += F_THREADS) {
+        const float v = bf16r(ys[i]);
+        ss += v * v;
+      }
+      rinv = rsqrtf(fblock_sum(ss, red) / (float)sg.len + eps);
+    }
+    for (int i0 = tid; i0 < sg.len; i0 += F_THREADS * F_UNROLL) {
+      float v[F_UNROLL];
+#pragma unroll
+      for (int u = 0; u < F_UNROLL; ++u) {
+        const int i = i0 + u * F_THREADS;
+        v[u] = i < sg.len ? ys[i] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < F_UNROLL; ++u) {
+        const int i = i0 + u * F_THREADS;
+        if (i < sg.len) {
+          const float o = seg_value(sg, v[u], r, i, rinv);
+          if (sg.out_f32)
+            outf[i] = o;
+          else
+            out[i] = __float2bfloat16(o);
+        }
+      }
     }
   }
-  if (zero_y) {
-    __syncthreads();
-    for (int i = tid; i < N; i += F_THREADS) yrow[i] = 0.f;
-  }
+  __syncthreads();   // every segment has read this row before it is cleared
+  for (int i = tid; i < N; i += F_THREADS) yrow[i] = 0.f;   // leave the accumulator zero for the next call
 }
 
 }  // namespace
@@ -210,10 +246,11 @@ extern "C" int uttt_linear(int M, int N, int K, const void* x, const void* w, in
   UTTT_REQUIRE(K % 64 == 0, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(workspace_bytes >= uttt_linear_workspace(M, N), UTTT_ERR_WORKSPACE);
   for (int i = 0; i < nseg; ++i) {
-    UTTT_REQUIRE(segs[i].start >= 0 && segs[i].len > 0 && segs[i].start + segs[i].len <= N && segs[i].out,
+    UTTT_REQUIRE(segs[i].op >= UTTT_SEG_STORE && segs[i].op <= UTTT_SEG_NORM, UTTT_ERR_INVALID);
+    UTTT_REQUIRE(segs[i].len > 0 && segs[i].out, UTTT_ERR_INVALID);
+    UTTT_REQUIRE(segs[i].op == UTTT_SEG_NORM || (segs[i].start >= 0 && segs[i].start + segs[i].len <= N),
                  UTTT_ERR_INVALID);
-    UTTT_REQUIRE(segs[i].op >= UTTT_SEG_STORE && segs[i].op <= UTTT_SEG_SIGMOID, UTTT_ERR_INVALID);
-    UTTT_REQUIRE(segs[i].op != UTTT_SEG_RESID || segs[i].aux, UTTT_ERR_INVALID);
+    UTTT_REQUIRE((segs[i].op != UTTT_SEG_RESID && segs[i].op != UTTT_SEG_NORM) || segs[i].aux, UTTT_ERR_INVALID);
   }
   cudaStream_t st = (cudaStream_t)stream;
   WsCursor ws(workspace, workspace_bytes);
@@ -253,18 +290,17 @@ extern "C" int uttt_linear(int M, int N, int K, const void* x, const void* w, in
                                               (int)(1024 + G_STAGES * (16384 + 256 * 128)))));
     attr = true;
   }
-  if (p.atomic) UTTT_TRY(cuda_status(cudaMemsetAsync(y, 0, (size_t)M * N * sizeof(float), st)));
   {
     ProfScope ps(UTTT_PROF_GEMM, st);
     gemm_kernel<<<dim3(ntiles, mtiles, splits), G_THREADS, smem, st>>>(tmW, tmX, p);
   }
   UTTT_TRY(launch_status());
-  UtttSegment s6[6];
-  memset(s6, 0, sizeof(s6));
-  for (int i = 0; i < nseg; ++i) s6[i] = segs[i];
+  SegPack sp;
+  memset(&sp, 0, sizeof(sp));
+  for (int i = 0; i < nseg; ++i) sp.s[i] = segs[i];
   {
     ProfScope ps(UTTT_PROF_FINISH, st);
-    finish_kernel<<<M, F_THREADS, 0, st>>>(y, N, nseg, s6[0], s6[1], s6[2], s6[3], s6[4], s6[5], eps, 0);
+    finish_kernel<<<M, F_THREADS, 0, st>>>(y, N, nseg, sp, eps);
   }
   return launch_status();
 }

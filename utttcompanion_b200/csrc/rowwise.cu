@@ -54,52 +54,82 @@ __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* _
 // 0..5 in stop-free mode, and ids >= active_limit masked.  Ties go to the
 // lowest id.  Writes the id and the top-1 / top-2 values.  A NaN logit counts
 // as -inf, and a row with no finite candidate still returns an allowed id.
-__global__ void __launch_bounds__(R_THREADS) argmax_kernel(const void* __restrict__ logits, int logits_f32,
+// One CTA of 512 threads per row; 8 logits per 16-byte load when the rows
+// are aligned; top-1 / top-2 merged by warp shuffles, then across warps.
+constexpr int A_THREADS = 512;
+
+struct Top2 {
+  float v1, v2;
+  int i1;
+};
+
+__device__ __forceinline__ Top2 top2_merge(Top2 a, Top2 b) {
+  const bool bwins = b.v1 > a.v1 || (b.v1 == a.v1 && b.i1 < a.i1);
+  Top2 o;
+  o.v1 = bwins ? b.v1 : a.v1;
+  o.i1 = bwins ? b.i1 : a.i1;
+  o.v2 = bwins ? fmaxf(a.v1, b.v2) : fmaxf(a.v2, b.v1);
+  return o;
+}
+
+__global__ void __launch_bounds__(A_THREADS) argmax_kernel(const void* __restrict__ logits, int logits_f32,
                                                            long long ld, int V, int active_limit, int stop_free,
                                                            int* __restrict__ ids, float* __restrict__ top2) {
-  __shared__ float sv1[R_THREADS], sv2[R_THREADS];
-  __shared__ int si1[R_THREADS];
-  const int r = blockIdx.x, tid = threadIdx.x;
-  float v1 = -INFINITY, v2 = -INFINITY;
-  int i1 = 0x7fffffff;
+  __shared__ Top2 red[A_THREADS / 32];
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lim = active_limit < V ? active_limit : V;
-  for (int i = tid; i < lim; i += R_THREADS) {
-    if (i == 0 || i == 1 || i == 3 || (stop_free && i < 6)) continue;
-    float v = logits_f32 ? reinterpret_cast<const float*>(logits)[(size_t)r * ld + i]
-                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[(size_t)r * ld + i]);
+  Top2 t = {-INFINITY, -INFINITY, 0x7fffffff};
+  auto consider = [&](int i, float v) {
+    if (i >= lim || i == 0 || i == 1 || i == 3 || (stop_free && i < 6)) return;
     v = __bfloat162float(__float2bfloat16(v));
     if (v != v) v = -INFINITY;
-    if (v > v1 || (v == v1 && i < i1)) {
-      v2 = v1;
-      v1 = v;
-      i1 = i;
-    } else if (v > v2) {
-      v2 = v;
+    if (v > t.v1 || (v == t.v1 && i < t.i1)) {
+      t.v2 = t.v1;
+      t.v1 = v;
+      t.i1 = i;
+    } else if (v > t.v2) {
+      t.v2 = v;
     }
+  };
+  const float* lf = reinterpret_cast<const float*>(logits) + (size_t)r * ld;
+  const __nv_bfloat16* lb = reinterpret_cast<const __nv_bfloat16*>(logits) + (size_t)r * ld;
+  // vector loads only when every 8-logit group stays inside an aligned row
+  const bool vec = (ld % 8 == 0) && (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15u) == 0);
+  if (vec) {
+    for (int j = tid; j * 8 < lim; j += A_THREADS) {
+      float v[8];
+      if (logits_f32) {
+        const float4 a = reinterpret_cast<const float4*>(lf)[2 * j], b = reinterpret_cast<const float4*>(lf)[2 * j + 1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 a = reinterpret_cast<const uint4*>(lb)[j];
+        v[0] = bf16_lo(a.x); v[1] = bf16_hi(a.x); v[2] = bf16_lo(a.y); v[3] = bf16_hi(a.y);
+        v[4] = bf16_lo(a.z); v[5] = bf16_hi(a.z); v[6] = bf16_lo(a.w); v[7] = bf16_hi(a.w);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) consider(j * 8 + e, v[e]);
+    }
+  } else {
+    for (int i = tid; i < lim; i += A_THREADS)
+      consider(i, logits_f32 ? lf[i] : __bfloat162float(lb[i]));
   }
-  sv1[tid] = v1;
-  sv2[tid] = v2;
-  si1[tid] = i1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Top2 u;
+    u.v1 = __shfl_down_sync(0xffffffffu, t.v1, o);
+    u.v2 = __shfl_down_sync(0xffffffffu, t.v2, o);
+    u.i1 = __shfl_down_sync(0xffffffffu, t.i1, o);
+    t = top2_merge(t, u);
+  }
+  if (lane == 0) red[warp] = t;
   __syncthreads();
-  for (int s = R_THREADS / 2; s > 0; s >>= 1) {
-    if (tid < s) {
-      const float a1 = sv1[tid], a2 = sv2[tid], b1 = sv1[tid + s], b2 = sv2[tid + s];
-      const int ai = si1[tid], bi = si1[tid + s];
-      const bool bwins = b1 > a1 || (b1 == a1 && bi < ai);
-      const float n1 = bwins ? b1 : a1;
-      const int ni = bwins ? bi : ai;
-      const float n2 = bwins ? fmaxf(a1, b2) : fmaxf(a2, b1);
-      sv1[tid] = n1;
-      sv2[tid] = n2;
-      si1[tid] = ni;
-    }
-    __syncthreads();
-  }
   if (tid == 0) {
-    ids[r] = si1[0] < lim ? si1[0] : (stop_free ? 6 : 2) % lim;   // only when no candidate was finite
+    Top2 a = red[0];
+    for (int w = 1; w < A_THREADS / 32; ++w) a = top2_merge(a, red[w]);
+    ids[r] = a.i1 < lim ? a.i1 : (stop_free ? 6 : 2) % lim;   // only when no candidate was finite
     if (top2) {
-      top2[2 * r] = sv1[0];
-      top2[2 * r + 1] = sv2[0];
+      top2[2 * r] = a.v1;
+      top2[2 * r + 1] = a.v2;
     }
   }
 }
@@ -192,6 +222,6 @@ extern "C" int uttt_greedy_argmax(int rows, int V, const void* logits, int logit
   UTTT_REQUIRE(rows > 0 && V > 6 && logits && ids && active_limit > 2, UTTT_ERR_INVALID);
   cudaStream_t st = (cudaStream_t)stream;
   ProfScope ps(UTTT_PROF_ARGMAX, st);
-  argmax_kernel<<<rows, R_THREADS, 0, st>>>(logits, logits_f32, ld, V, active_limit, stop_free, ids, top2);
+  argmax_kernel<<<rows, A_THREADS, 0, st>>>(logits, logits_f32, ld, V, active_limit, stop_free, ids, top2);
   return launch_status();
 }

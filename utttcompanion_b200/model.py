@@ -87,9 +87,10 @@ def rope_tables(head_dim: int, n_pos: int, theta: float):
     return emb.cos(), emb.sin()
 
 
-def _seg(start, length, op, out, out_ld, aux=None, aux_ld=0, scale=0.0, out_f32=False):
+def _seg(start, length, op, out, out_ld, aux=None, aux_ld=0, scale=0.0, out_f32=False, aux2=None):
     return _lib.Segment(start, length, op, int(out_f32), out.data_ptr(), out_ld,
-                        None if aux is None else aux.data_ptr(), aux_ld, scale)
+                        None if aux is None else aux.data_ptr(), aux_ld, scale,
+                        None if aux2 is None else aux2.data_ptr())
 
 
 class UtttB200:
@@ -180,10 +181,18 @@ class UtttB200:
                                        self.emb.data_ptr(), out.data_ptr(), self._st()), "uttt_embed")
         return out
 
-    def _resid_linear(self, h: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> None:
-        """h += bf16(x W^T), in place (block residual adds, model/uttt_layer.py:1544-1554)."""
+    def _resid_linear(self, h: torch.Tensor, x: torch.Tensor, w: torch.Tensor,
+                      norm: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        """h += bf16(x W^T), in place (block residual adds, model/uttt_layer.py:1544-1554);
+        with ``norm`` (an RMSNorm weight) also returns rms_norm(h) * norm from the same launch."""
         d = w.shape[0]
-        self._linear(x, w, [_seg(0, d, _lib.SEG_RESID, h, h.stride(0), h, h.stride(0))])
+        segs = [_seg(0, d, _lib.SEG_RESID, h, h.stride(0), h, h.stride(0))]
+        out = None
+        if norm is not None:
+            out = torch.empty(h.shape[0], d, dtype=torch.bfloat16, device=self.device)
+            segs.append(_seg(0, d, _lib.SEG_NORM, out, d, h, h.stride(0), aux2=norm))
+        self._linear(x, w, segs)
+        return out
 
     def _readout(self, q: torch.Tensor, packed: torch.Tensor, down: torch.Tensor, sidx: torch.Tensor,
                  ln: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
@@ -207,7 +216,10 @@ class UtttB200:
 
     def logits(self, h_last: torch.Tensor) -> torch.Tensor:
         """Final RMSNorm + tied lm_head (BF16 output, as under autocast), returned as FP32."""
-        x = self._rmsnorm(h_last, self.norm)
+        return self._lm_head(self._rmsnorm(h_last, self.norm))
+
+    def _lm_head(self, x: torch.Tensor) -> torch.Tensor:
+        """Tied lm_head of final-normalised rows (BF16 output), returned as FP32."""
         V = self.lm_head.shape[0]
         out = torch.empty(x.shape[0], V, dtype=torch.bfloat16, device=self.device)
         self._linear(x, self.lm_head, [_seg(0, V, _lib.SEG_STORE, out, V)])
@@ -259,8 +271,9 @@ class UtttB200:
         kb = torch.empty(1, nkv, T, hd, dtype=torch.bfloat16, device=dev)
         vb = torch.empty_like(kb)
         att = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
+        x = self._rmsnorm(h, self.layers[0].attn_norm)
+        L = len(self.layers)
         for i, lay in enumerate(self.layers):
-            x = self._rmsnorm(h, lay.attn_norm)
             self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
             _lib.check(self.lib.uttt_attn_prefill(1, T, 0, 0, nh, nkv, hd, cfg.sliding_window_size, qkv.data_ptr(),
                                                   self.qkv_dim, self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
@@ -269,11 +282,11 @@ class UtttB200:
             _lib.check(self.lib.uttt_kv_ring_fill(1, T, T, nkv, hd, cfg.sliding_window_size, kb.data_ptr(),
                                                   vb.data_ptr(), slot_t.data_ptr(), self.k_ring[i].data_ptr(),
                                                   self.v_ring[i].data_ptr(), self._st()), "uttt_kv_ring_fill")
-            self._resid_linear(h, att, lay.wo)
-            q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
+            x2 = self._resid_linear(h, att, lay.wo, lay.uttt_norm)
+            q = self._q_proj(lay, x2)
             r = self._readout(q.unsqueeze(0), read_packed, read_down, sidx)
-            self._resid_linear(h, r.reshape(T, d), lay.w_o)
-        return self.logits(h[-1:].contiguous())[0]
+            x = self._resid_linear(h, r.reshape(T, d), lay.w_o, self.layers[i + 1].attn_norm if i + 1 < L else self.norm)
+        return self._lm_head(x[-1:].contiguous())[0]
 
     def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor, read_packed: torch.Tensor,
                     read_down: torch.Tensor, state_index: torch.Tensor) -> torch.Tensor:
@@ -288,19 +301,20 @@ class UtttB200:
         h = self._embed(tokens)
         qkv = torch.empty(B, self.qkv_dim, dtype=torch.bfloat16, device=dev)
         att = torch.empty(B, d, dtype=torch.bfloat16, device=dev)
+        L = len(self.layers)
+        x = self._rmsnorm(h, self.layers[0].attn_norm)
         for i, lay in enumerate(self.layers):
-            x = self._rmsnorm(h, lay.attn_norm)
             self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
             _lib.check(self.lib.uttt_attn_decode(B, nh, nkv, hd, cfg.sliding_window_size, qkv.data_ptr(),
                                                  self.qkv_dim, pos.data_ptr(), slots.data_ptr(),
                                                  self.k_ring[i].data_ptr(), self.v_ring[i].data_ptr(),
                                                  self.rope_cos.data_ptr(), self.rope_sin.data_ptr(), att.data_ptr(),
                                                  d, self._st()), "uttt_attn_decode")
-            self._resid_linear(h, att, lay.wo)
-            q = self._q_proj(lay, self._rmsnorm(h, lay.uttt_norm))
+            x2 = self._resid_linear(h, att, lay.wo, lay.uttt_norm)
+            q = self._q_proj(lay, x2)
             r = self._readout(q.unsqueeze(1), read_packed, read_down, sidx)
-            self._resid_linear(h, r.reshape(B, d), lay.w_o)
-        return self.logits(h)
+            x = self._resid_linear(h, r.reshape(B, d), lay.w_o, self.layers[i + 1].attn_norm if i + 1 < L else self.norm)
+        return self._lm_head(x)
 
     def generate_greedy(self, prompt: torch.Tensor, state: FastState, n_tokens: int, slot: int = 0,
                         stop_free: bool = True, eos_token_id: Optional[int] = None
@@ -416,8 +430,8 @@ class UtttB200:
             V = torch.empty_like(K)
             ETA = torch.empty(L, R, dtype=torch.float32, device=dev)
             ALPHA = torch.empty_like(ETA)
+            x = self._rmsnorm(hidden, self.layers[0].attn_norm)
             for i, lay in enumerate(self.layers):
-                x = self._rmsnorm(hidden, lay.attn_norm)
                 qkv = torch.empty(R, self.qkv_dim, dtype=torch.bfloat16, device=dev)
                 self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
                 hist = 0 if hist_k[i] is None else hist_k[i].shape[2]
@@ -436,8 +450,7 @@ class UtttB200:
                 hist_k[i] = kb[:, :, hist + Cc - keep:].contiguous()
                 hist_v[i] = vb[:, :, hist + Cc - keep:].contiguous()
                 hh = hidden.clone()
-                self._resid_linear(hh, att, lay.wo)
-                x2 = self._rmsnorm(hh, lay.uttt_norm)
+                x2 = self._resid_linear(hh, att, lay.wo, lay.uttt_norm)
                 q = torch.empty(R, d, dtype=torch.bfloat16, device=dev)
                 self._linear(x2, lay.slow, [                       # fused_slow_projections, :1193-1231
                     _seg(0, d, _lib.SEG_RMSNORM, q, d, lay.q_norm),
@@ -448,7 +461,10 @@ class UtttB200:
                          out_f32=True),
                 ])
                 out = self._readout(q.reshape(Bc, Cc, d), rp, rd, rows, (cur.ln_weight, cur.ln_bias))
-                self._resid_linear(hh, out.reshape(R, d), lay.w_o)
+                if i + 1 < L:
+                    x = self._resid_linear(hh, out.reshape(R, d), lay.w_o, self.layers[i + 1].attn_norm)
+                else:
+                    self._resid_linear(hh, out.reshape(R, d), lay.w_o)
                 hidden = hh
             # ... then the L writes chain through the state as ONE call whose chunks are the
             # layers (row b's tokens: layer 0's chunk, layer 1's chunk, ...), so every write
