@@ -430,6 +430,81 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     }
 
 
+# ----------------------------------------------------------------------------- serve sweep (config 5)
+def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=64, seed=0):
+    """continuous batching of persona turns on one GPU.  Turns arrive as
+    a Poisson process at each rate; each picks a user uniformly among ``personas``, a prompt
+    of lognormal length (median 256, sigma 1.0, clipped to [16, 2048]) with uniform ids and a
+    forced reply length uniform in [32, 256] (greedy); every completed turn is written into its
+    user's state (chunk-TTT write, surprise gate, elastic pull).  Reports generated and written
+    tokens per second and the arrival -> result latency of every turn."""
+    from utttcompanion_b200 import workloads as wl
+    from utttcompanion_b200.model import UtttB200
+    from utttcompanion_b200.serving import ServingEngine
+    cfg = {"151M": wl.CONFIG_151M, "1P58B": wl.CONFIG_1P58B}[config]
+    sd = wl.random_state_dict(cfg, seed=seed, device=device)
+    eng = UtttB200(sd, cfg, device=device, max_personas=personas + 1, max_positions=2048 + 256 + 64)
+    del sd
+    srv = ServingEngine(eng, capacity=personas, max_batch=max_batch, surprise_threshold=cfg.surprise_threshold,
+                        stop_free=True)
+    g = torch.Generator().manual_seed(seed)
+
+    def draw_turn():
+        n = int(min(max(round(256 * math.exp(float(torch.randn(1, generator=g, dtype=torch.float64)))), 16), 2048))
+        reply = int(torch.randint(32, 257, (1,), generator=g))
+        user = f"user-{int(torch.randint(0, personas, (1,), generator=g))}"
+        return user, torch.randint(6, cfg.vocab_size, (n,), generator=g).tolist(), reply
+
+    for _ in range(4):                                   # warm-up turns (prefill, decode, write paths)
+        srv.submit(*draw_turn())
+    srv.run()
+    out = []
+    for lam in rates:
+        t, arrivals = 0.0, []
+        while True:
+            t += float(torch.empty(1).exponential_(lam, generator=g))
+            if t > duration_s:
+                break
+            arrivals.append((t, *draw_turn()))
+        srv.stats.clear()
+        start = time.perf_counter()
+        live, done = [], []
+        i = 0
+        while i < len(arrivals) or live:
+            now = time.perf_counter() - start
+            while i < len(arrivals) and arrivals[i][0] <= now:
+                at, user, prompt, reply = arrivals[i]
+                live.append((at, srv.submit(user, prompt, reply)))
+                i += 1
+            if srv.idle():
+                time.sleep(max(0.0, min(arrivals[i][0] - now, 0.05)) if i < len(arrivals) else 0.0)
+                continue
+            srv.step()
+            now = time.perf_counter() - start
+            still = []
+            for at, turn in live:
+                (done if turn.done else still).append((at, turn) if not turn.done else (now - at, turn))
+            live = still
+        wall = time.perf_counter() - start
+        lat = np.array([x for x, _ in done]) if done else np.zeros(1)
+        st = srv.stats
+        out.append({
+            "rate_req_s": lam, "turns": len(done), "wall_s": wall,
+            "decode_tok_s": st["decode_tokens"] / wall, "write_tok_s": st["write_tokens"] / wall,
+            "prefill_tok_s": st["prefill_tokens"] / wall,
+            "latency_s": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
+                          "mean": float(lat.mean())},
+            "mean_decode_batch": st["decode_tokens"] / max(st["decode_steps"], 1),
+            "busy_s": {"prefill": st["prefill_s"], "decode": st["decode_s"], "write": st["write_s"]},
+        })
+        print(json.dumps(out[-1]), file=sys.stderr, flush=True)
+    return {"workload": f"continuous-batching serve sweep (BASELINE config 5) on the {config} model, 1 GPU",
+            "personas": personas, "max_batch": max_batch, "arrivals": "Poisson", "duration_s": duration_s,
+            "prompts": "lognormal, median 256, sigma 1.0, clipped to [16, 2048]",
+            "replies": "uniform in [32, 256] tokens, forced length (greedy, stop ids masked)",
+            "writes": "every completed turn: chunk-TTT write + surprise gate + elastic pull", "points": out}
+
+
 # ----------------------------------------------------------------------------- arms
 def reference_arm(args, world, rank):
     if rank != 0:
@@ -512,6 +587,12 @@ def ours_arm(args, world, rank, local):
     if args.only_decode:          # profiling case: the config-3 decode + write workload alone
         if rank == 0:
             print(json.dumps(decode_workload(device, rank, lib, DEC)), flush=True)
+        return 0
+    if args.serve_sweep:          # BASELINE config 5 (minutes per model): one JSON object
+        if rank == 0:
+            rates = [float(x) for x in args.serve_rates.split(",")]
+            print(json.dumps(serve_sweep(device, lib, args.serve_config, rates, args.serve_seconds,
+                                         personas=args.serve_personas)), flush=True)
         return 0
     st = make_states(device, seed=1234 + rank)
     B, T = CFG["states"], CFG["tokens"]
@@ -665,6 +746,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode + write workloads (configs 3, 4)")
     ap.add_argument("--no-1p58b", action="store_true", help="skip the 1.58B (config 4) decode + write workload")
+    ap.add_argument("--serve-sweep", action="store_true", help="run only the config-5 serve sweep (1 GPU)")
+    ap.add_argument("--serve-config", default="151M", choices=("151M", "1P58B"))
+    ap.add_argument("--serve-rates", default="1,2,4,8,16,32,64", help="arrival rates, req/s")
+    ap.add_argument("--serve-seconds", type=float, default=20.0, help="arrival window per rate")
+    ap.add_argument("--serve-personas", type=int, default=256)
     ap.add_argument("--only-decode", action="store_true",
                     help="profiling: run only the config-3 decode + write workload (one JSON object, 1 GPU)")
     ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")

@@ -164,7 +164,9 @@ int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int chunk_begin,
  *                masters;  UTTT_DTYPE_BF16: w_up = packed [W_up | W_gate]
  *                (S, d, 2h) BF16 read copy (inference_read_weights, :648-668),
  *                w_gate unused, w_down (S, h, d) BF16.
- *   state_index  int32 (B): row b reads state state_index[b] (NULL: state b).
+ *   state_index  int32 (B): row b reads state state_index[b] (NULL: state b);
+ *                with T == 1 and BF16 copies a negative entry marks a padding
+ *                row of a packed batch: no weights are read and its output is x.
  *   ln_*         FP32 (d,) LayerNorm affine, as the reference applies it.
  *   out          (B, T, d) in out_dtype.
  * T == 1 with BF16 copies runs the decode GEMV; otherwise 64-token tiles on

@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
     if (tid == 0) set_status(p.status, UTTT_ERR_INVALID);   // a bad row -> state map entry: touch nothing
     return;
   }
+  if (p.state_index && p.state_index[b] < 0) return;       // a padding row of a readout: no weights read
 
   if (tid == 0) {
     for (int i = 0; i < NSLOT; ++i) {

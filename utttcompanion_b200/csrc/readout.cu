@@ -64,6 +64,17 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y, j0 = blockIdx.x * GT;
   const int state = state_index ? state_index[b] : b;
+  if (state < 0) {   // a padding row of a packed batch: no weights are read, out = x
+    if (blockIdx.x == 0 && done != nullptr)
+      for (int i = tid; i < d; i += GTHREADS) {
+        const float xv = __bfloat162float(x[(size_t)b * d + i]);
+        if (out_bf16)
+          reinterpret_cast<__nv_bfloat16*>(out)[(size_t)b * d + i] = __float2bfloat16(xv);
+        else
+          reinterpret_cast<float*>(out)[(size_t)b * d + i] = xv;
+      }
+    return;
+  }
   for (int i = tid; i < d / 8; i += GTHREADS) {
     float f[8];
     bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + (size_t)b * d) + i), f);

@@ -25,6 +25,7 @@ from __future__ import annotations
 import collections
 import hashlib
 import math
+import time
 from dataclasses import dataclass, field
 from typing import Deque, Dict, List, Optional
 
@@ -170,8 +171,21 @@ class ServingEngine:
 
     def __init__(self, engine: UtttB200, capacity: int, max_batch: int, surprise_threshold: float = 0.25,
                  elastic_anchor_lambda: float = 0.02, max_weight_drift_ratio: Optional[float] = 0.35,
-                 online_ttt: bool = True):
+                 online_ttt: bool = True, stop_free: bool = False, write_batch: int = 8,
+                 write_wait_s: float = 0.05):
+        """``stop_free``: replies run to their ``max_new_tokens`` (role ids and EOS are masked
+        from the greedy pick, as the reference's graph-vs-eager test does), e.g. for
+        forced-length load tests; otherwise stream_generate's stop rules apply.
+        Finished turns are written together: once ``write_batch`` are waiting, the oldest has
+        waited ``write_wait_s`` seconds, or nothing is left to decode (a one-persona write
+        keeps only h/128 CTAs busy; a batch fills the GPU)."""
         self.engine = engine
+        self.stop_free = stop_free
+        self.write_batch = max(1, write_batch)
+        self.write_wait_s = write_wait_s
+        self._write_queue: List[Turn] = []
+        self._pending_writes: List[Turn] = []
+        self._write_since = 0.0
         self.arena = PersonaArena(engine, capacity)
         self.max_batch = max_batch
         self.surprise_threshold = surprise_threshold
@@ -179,8 +193,9 @@ class ServingEngine:
         self.max_weight_drift_ratio = max_weight_drift_ratio
         self.online_ttt = online_ttt
         # padding rows of the packed graph decode the padding persona at position 0
-        self.graph = DecodeGraph(engine, max_batch, self.arena.read_packed, self.arena.read_down, stop_free=False,
+        self.graph = DecodeGraph(engine, max_batch, self.arena.read_packed, self.arena.read_down, stop_free=stop_free,
                                  pad_slot=self.arena.pad_slot)
+        self.stats = collections.Counter()      # seconds and tokens of prefill / decode / write
         self.waiting: Deque[Turn] = collections.deque()
         self.active: List[Optional[Turn]] = [None] * max_batch
         self.finished: List[Turn] = []
@@ -200,7 +215,7 @@ class ServingEngine:
         return t
 
     def idle(self) -> bool:
-        return not self.waiting and all(a is None for a in self.active)
+        return not self.waiting and not self._write_queue and all(a is None for a in self.active)
 
     def run(self, max_steps: int = 1_000_000) -> List[Turn]:
         steps = 0
@@ -231,10 +246,13 @@ class ServingEngine:
             self.arena.pinned.add(t.slot)
             self.in_flight_users.add(t.user_id)
             ids = torch.tensor(t.prompt_ids, dtype=torch.long)
+            t0 = time.perf_counter()
             logits = e.prefill(ids, t.slot, self.arena.read_packed, self.arena.read_down, t.slot)
-            tok, _ = e.greedy(logits.unsqueeze(0), stop_free=False)
+            tok, _ = e.greedy(logits.unsqueeze(0), stop_free=self.stop_free)
             t.pos = len(t.prompt_ids)
             t.next_token = int(tok.item())
+            self.stats["prefill_s"] += time.perf_counter() - t0
+            self.stats["prefill_tokens"] += len(t.prompt_ids)
             self.active[row] = t
             self._accept(row, t)
         self.waiting.extendleft(reversed(deferred))
@@ -242,11 +260,12 @@ class ServingEngine:
     def _accept(self, row: int, t: Turn) -> None:
         """Apply stream_generate's stop rules to the token just picked (model/uttt_model.py:1036-1050)."""
         tok = t.next_token
-        if tok in (USER_ID, ASSISTANT_ID):
+        if tok in (USER_ID, ASSISTANT_ID) and not self.stop_free:
             t.decoded = True
         else:
             t.reply.append(tok)
-            if (t.eos_token_id is not None and tok == t.eos_token_id) or len(t.reply) >= t.max_new_tokens:
+            if (not self.stop_free and t.eos_token_id is not None and tok == t.eos_token_id) or \
+                    len(t.reply) >= t.max_new_tokens:
                 t.decoded = True
         if t.decoded:
             self.active[row] = None
@@ -254,25 +273,41 @@ class ServingEngine:
             self._pending_writes.append(t)
 
     def step(self) -> None:
-        self._pending_writes: List[Turn] = []
+        self._pending_writes = []
         self._admit()
         rows = [(i, t) for i, t in enumerate(self.active) if t is not None]
         if rows:
             B = self.max_batch
-            tokens = torch.zeros(B, dtype=torch.int32)
-            pos = torch.zeros(B, dtype=torch.int32)
-            slots = torch.full((B,), self.arena.pad_slot, dtype=torch.int32)
+            # rows: token, position, KV slot, fast-weight state (-1: padding row, no weights read)
+            host = torch.zeros(4, B, dtype=torch.int32)
+            host[2].fill_(self.arena.pad_slot)
+            host[3].fill_(-1)
             for i, t in rows:
-                tokens[i], pos[i], slots[i] = t.next_token, t.pos, t.slot
-            ids, _ = self.graph.step(tokens.to(self.engine.device), pos.to(self.engine.device),
-                                     slots.to(self.engine.device), slots.to(self.engine.device))
+                host[0, i], host[1, i], host[2, i], host[3, i] = t.next_token, t.pos, t.slot, t.slot
+            t0 = time.perf_counter()
+            dev = host.to(self.engine.device)
+            ids, _ = self.graph.step(dev[0], dev[1], dev[2], dev[3])
             host_ids = ids.cpu().tolist()
+            self.stats["decode_s"] += time.perf_counter() - t0
+            self.stats["decode_steps"] += 1
+            self.stats["decode_tokens"] += len(rows)
             for i, t in rows:
                 t.pos += 1
                 t.next_token = int(host_ids[i])
                 self._accept(i, t)
         if self._pending_writes:
-            self._write(self._pending_writes)
+            if not self._write_queue:
+                self._write_since = time.perf_counter()
+            self._write_queue.extend(self._pending_writes)
+        q = self._write_queue
+        if q and (len(q) >= self.write_batch or all(a is None for a in self.active)
+                  or time.perf_counter() - self._write_since >= self.write_wait_s):
+            self._write_queue = []
+            t0 = time.perf_counter()
+            self._write(q)
+            self.stats["write_s"] += time.perf_counter() - t0
+            self.stats["write_batches"] += 1
+            self.stats["write_tokens"] += sum(len(t.prompt_ids) + len(t.reply) for t in q)
 
     def _write(self, turns: List[Turn]) -> None:
         """Step 2 + 3 of a turn for every finished turn at once (personalizer.py:480-551)."""
