@@ -192,9 +192,16 @@ class ServingEngine:
         self.elastic_anchor_lambda = elastic_anchor_lambda
         self.max_weight_drift_ratio = max_weight_drift_ratio
         self.online_ttt = online_ttt
-        # padding rows of the packed graph decode the padding persona at position 0
-        self.graph = DecodeGraph(engine, max_batch, self.arena.read_packed, self.arena.read_down, stop_free=stop_free,
-                                 pad_slot=self.arena.pad_slot)
+        # one captured packed step per batch bucket (1, 2, 4, ... max_batch): a step runs the smallest
+        # bucket that holds the live turns; padding rows use the padding slot and read no weights
+        sizes, b = [], 1
+        while b < max_batch:
+            sizes.append(b)
+            b *= 2
+        sizes.append(max_batch)
+        self.graphs = {n: DecodeGraph(engine, n, self.arena.read_packed, self.arena.read_down, stop_free=stop_free,
+                                      pad_slot=self.arena.pad_slot) for n in reversed(sizes)}
+        self.graph = self.graphs[max_batch]
         self.stats = collections.Counter()      # seconds and tokens of prefill / decode / write
         self.waiting: Deque[Turn] = collections.deque()
         self.active: List[Optional[Turn]] = [None] * max_batch
@@ -277,23 +284,23 @@ class ServingEngine:
         self._admit()
         rows = [(i, t) for i, t in enumerate(self.active) if t is not None]
         if rows:
-            B = self.max_batch
-            # rows: token, position, KV slot, fast-weight state (-1: padding row, no weights read)
+            B = min(n for n in self.graphs if n >= len(rows))
+            # packed rows 0..len(rows)-1: token, position, KV slot, fast-weight state (-1: padding row)
             host = torch.zeros(4, B, dtype=torch.int32)
             host[2].fill_(self.arena.pad_slot)
             host[3].fill_(-1)
-            for i, t in rows:
-                host[0, i], host[1, i], host[2, i], host[3, i] = t.next_token, t.pos, t.slot, t.slot
+            for r, (i, t) in enumerate(rows):
+                host[0, r], host[1, r], host[2, r], host[3, r] = t.next_token, t.pos, t.slot, t.slot
             t0 = time.perf_counter()
             dev = host.to(self.engine.device)
-            ids, _ = self.graph.step(dev[0], dev[1], dev[2], dev[3])
+            ids, _ = self.graphs[B].step(dev[0], dev[1], dev[2], dev[3])
             host_ids = ids.cpu().tolist()
             self.stats["decode_s"] += time.perf_counter() - t0
             self.stats["decode_steps"] += 1
             self.stats["decode_tokens"] += len(rows)
-            for i, t in rows:
+            for r, (i, t) in enumerate(rows):
                 t.pos += 1
-                t.next_token = int(host_ids[i])
+                t.next_token = int(host_ids[r])
                 self._accept(i, t)
         if self._pending_writes:
             if not self._write_queue:
