@@ -432,7 +432,7 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
 
 # ----------------------------------------------------------------------------- serve sweep (config 5)
 def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=64, seed=0, write_batch=32,
-                write_wait_s=0.2):
+                write_wait_s=0.2, async_writes=False):
     """continuous batching of persona turns on one GPU.  Turns arrive as
     a Poisson process at each rate; each picks a user uniformly among ``personas``, a prompt
     of lognormal length (median 256, sigma 1.0, clipped to [16, 2048]) with uniform ids and a
@@ -447,7 +447,8 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
     eng = UtttB200(sd, cfg, device=device, max_personas=personas + 1, max_positions=2048 + 256 + 64)
     del sd
     srv = ServingEngine(eng, capacity=personas, max_batch=max_batch, surprise_threshold=cfg.surprise_threshold,
-                        stop_free=True, write_batch=write_batch, write_wait_s=write_wait_s)
+                        stop_free=True, write_batch=write_batch, write_wait_s=write_wait_s,
+                        async_writes=async_writes)
     g = torch.Generator().manual_seed(seed)
 
     def draw_turn():
@@ -497,11 +498,16 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
                           "mean": float(lat.mean())},
             "mean_decode_batch": st["decode_tokens"] / max(st["decode_steps"], 1),
             "busy_s": {"prefill": st["prefill_s"], "decode": st["decode_s"], "write": st["write_s"]},
+            "write_batches": st["write_batches"],
+            "decode_ms_per_step": 1e3 * st["decode_s"] / max(st["decode_steps"], 1),
+            "write_ms_per_turn": 1e3 * st["write_s"] / max(len(done), 1),
+            "prefill_ms_per_turn": 1e3 * st["prefill_s"] / max(len(done), 1),
         })
         print(json.dumps(out[-1]), file=sys.stderr, flush=True)
     return {"workload": f"continuous-batching serve sweep (BASELINE config 5) on the {config} model, 1 GPU",
             "personas": personas, "max_batch": max_batch, "arrivals": "Poisson", "duration_s": duration_s,
             "write_batch": write_batch, "write_wait_s": write_wait_s,
+            "writes_overlap_decode": async_writes,
             "prompts": "lognormal, median 256, sigma 1.0, clipped to [16, 2048]",
             "replies": "uniform in [32, 256] tokens, forced length (greedy, stop ids masked)",
             "writes": "every completed turn: chunk-TTT write + surprise gate + elastic pull", "points": out}
@@ -595,6 +601,7 @@ def ours_arm(args, world, rank, local):
             rates = [float(x) for x in args.serve_rates.split(",")]
             print(json.dumps(serve_sweep(device, lib, args.serve_config, rates, args.serve_seconds,
                                          personas=args.serve_personas, write_batch=args.serve_write_batch,
+                                         async_writes=args.serve_async_writes,
                                          write_wait_s=args.serve_write_wait)), flush=True)
         return 0
     st = make_states(device, seed=1234 + rank)
@@ -756,6 +763,8 @@ def main():
     ap.add_argument("--serve-personas", type=int, default=256)
     ap.add_argument("--serve-write-batch", type=int, default=32, help="finished turns written together")
     ap.add_argument("--serve-write-wait", type=float, default=0.2, help="longest wait of a finished turn, s")
+    ap.add_argument("--serve-async-writes", action="store_true",
+                    help="write on a side stream from a worker thread, overlapping decode")
     ap.add_argument("--only-decode", action="store_true",
                     help="profiling: run only the config-3 decode + write workload (one JSON object, 1 GPU)")
     ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")

@@ -40,7 +40,8 @@ def _sequential(sd, cfg, turns, max_new, lam, ratio, threshold):
     return states, replies, margins
 
 
-def test_serving_matches_sequential_turns_and_spills_lru():
+@pytest.mark.parametrize("async_writes", [False, True])
+def test_serving_matches_sequential_turns_and_spills_lru(async_writes):
     cfg = _cfg()
     sd = reference_init_state_dict(cfg, seed=11)
     gen = torch.Generator().manual_seed(5)
@@ -50,9 +51,10 @@ def test_serving_matches_sequential_turns_and_spills_lru():
     lam, ratio, thr, max_new = 0.02, 0.35, 0.0, 10
     eng = UtttB200(sd, cfg, max_personas=4)
     srv = ServingEngine(eng, capacity=3, max_batch=3, surprise_threshold=thr, elastic_anchor_lambda=lam,
-                        max_weight_drift_ratio=ratio)
+                        max_weight_drift_ratio=ratio, async_writes=async_writes)
     handles = [srv.submit(u, p, max_new) for u, p in turns]
     srv.run()
+    srv.close()
     torch.cuda.synchronize()
     assert all(h.result is not None for h in handles)
     states, replies, margins = _sequential(sd, cfg, turns, max_new, lam, ratio, thr)

@@ -5,9 +5,11 @@
 // k/v written in place into the persona's KV ring at slot pos % W, then
 // attention over the min(pos+1, W) valid slots.  The ring holds exactly the
 // keys the reference's trimmed cache holds (the last W positions), so the
-// softmax runs over the same set.  One CTA per (row, kv head); the n_rep query
-// heads of the group share every K/V load; warps split the slots, lanes split
-// the head dimension, online softmax per warp, merged through shared memory.
+// softmax runs over the same set.  One cluster per (row, kv head): its S CTAs
+// split the ring's slots (S grows while the batch alone would leave SMs idle);
+// the n_rep query heads of the group share every K/V load.  Each CTA's softmax
+// partial (max, sum, unnormalised output) is merged with the others' in
+// distributed shared memory, in rank order.
 //
 // Prefill / chunk (T new tokens per row): RoPE into a contiguous per-row KV
 // window buffer that starts with up to W-1 history positions, then causal
@@ -18,8 +20,12 @@
 // RoPE tables are the reference's FP32 cos/sin (RotaryEmbedding._build_cache,
 // :910-933); like apply_rope on BF16 activations (:946-958) every product and
 // the sum are rounded to BF16.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "host_util.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace uttt {
 namespace {
@@ -40,29 +46,37 @@ constexpr int MAX_HD = 128;
 constexpr int MAX_REP = 8;
 constexpr int MAX_W = 1024;
 
-__host__ __device__ constexpr size_t dec_smem_floats(int hd, int rep, int w) {
-  return (size_t)rep * (hd + w + DEC_THREADS / 32 + (DEC_THREADS / 32) * hd);
+// ring slots per CTA, padded to 4 floats so the partial outputs after them stay 16-byte aligned
+__host__ __device__ constexpr int dec_span_pad(int span) { return (span + 3) & ~3; }
+
+__host__ __device__ constexpr size_t dec_smem_floats(int hd, int rep, int span) {
+  return (size_t)rep * (hd + dec_span_pad(span) + DEC_THREADS / 32 + (DEC_THREADS / 32) * hd) + (size_t)rep * (hd + 2);
 }
 
-// One CTA per (row, kv group), REP query heads per group.  Scores: every
-// thread owns one ring slot and reads its whole K row with 16-byte loads (all
-// slots' loads in flight at once); softmax over the slots in shared memory;
-// output: HD/8 threads cover one V row with 16-byte loads, so a pass reads
-// 256*8/HD rows; every query head of the group accumulates from the same V
-// load, the rows of a warp are combined by shuffles and the warps through
-// shared memory.  Shared memory (dynamic): q [REP][HD], p [REP][W],
-// reductions [REP][8], partial outputs [8][REP][HD].
+// grid (B, kv groups, S), cluster (1, 1, S); CTA k of a cluster takes ring
+// slots [k*W/S, (k+1)*W/S), REP query heads per group.  Scores: every thread
+// owns one ring slot and reads its whole K row with 16-byte loads (all slots'
+// loads in flight at once); softmax over the slots in shared memory; output:
+// HD/8 threads cover one V row with 16-byte loads, so a pass reads 256*8/HD
+// rows; every query head of the group accumulates from the same V load, the
+// rows of a warp are combined by shuffles and the warps through shared memory.
+// Shared memory (dynamic): q [REP][HD], p [REP][span padded to 4], reductions [REP][8],
+// partial outputs [8][REP][HD], the CTA's merged partial [REP][HD] + max and
+// sum [REP][2] (read by the cluster).
 template <int HD, int REP>
 __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
     const __nv_bfloat16* __restrict__ qkv, int qkv_ld, const int* __restrict__ pos, const int* __restrict__ slot,
     __nv_bfloat16* __restrict__ kring, __nv_bfloat16* __restrict__ vring, int n_kv, int W,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float scale, __nv_bfloat16* __restrict__ out,
     int out_ld) {
+  const int S = gridDim.z, span = W / S, s_lo = blockIdx.z * span, sp = dec_span_pad(span);
   extern __shared__ float dsm[];
   float* qs = dsm;                                    // [REP][HD]
-  float* ps = qs + REP * HD;                          // [REP][W]
-  float* red = ps + (size_t)REP * W;                  // [REP][8]
+  float* ps = qs + REP * HD;                          // [REP][sp]
+  float* red = ps + (size_t)REP * sp;                 // [REP][8]
   float* part = red + REP * (DEC_THREADS / 32);       // [8][REP][HD]
+  float* cacc = part + (DEC_THREADS / 32) * REP * HD; // [REP][HD]
+  float* cml = cacc + REP * HD;                       // [REP][2]: max, sum
   const int b = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_heads = n_kv * REP;
   const int p = pos[b];
@@ -78,20 +92,22 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
   const __nv_bfloat16* krow = row + (size_t)n_heads * HD + (size_t)g * HD;
   const __nv_bfloat16* vrow = row + (size_t)(n_heads + n_kv) * HD + (size_t)g * HD;
   const int ws = p % W;
-  for (int e = tid; e < HD; e += DEC_THREADS) {
-    kring[ring_base + (size_t)ws * HD + e] = __float2bfloat16(rope_elem(krow, e, HD, cr, sr));
-    vring[ring_base + (size_t)ws * HD + e] = vrow[e];
-  }
+  if (ws >= s_lo && ws < s_lo + span)   // the new slot is read by the CTA that owns it
+    for (int e = tid; e < HD; e += DEC_THREADS) {
+      kring[ring_base + (size_t)ws * HD + e] = __float2bfloat16(rope_elem(krow, e, HD, cr, sr));
+      vring[ring_base + (size_t)ws * HD + e] = vrow[e];
+    }
   __syncthreads();
   const int nvalid = p + 1 < W ? p + 1 : W;
+  const int s_hi = min(s_lo + span, nvalid);   // may be empty (s_hi <= s_lo): the partial is then zero
 
   // ---- scores: one slot per thread
   float mloc[REP];
 #pragma unroll
   for (int r = 0; r < REP; ++r) mloc[r] = -INFINITY;
-  for (int s0 = 0; s0 < nvalid; s0 += DEC_THREADS) {
+  for (int s0 = s_lo; s0 < s_hi; s0 += DEC_THREADS) {
     const int s = s0 + tid;
-    if (s < nvalid) {
+    if (s < s_hi) {
       const uint4* kp = reinterpret_cast<const uint4*>(kring + ring_base + (size_t)s * HD);
       uint4 kv[HD / 8];
 #pragma unroll
@@ -112,7 +128,7 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
 #pragma unroll
       for (int r = 0; r < REP; ++r) {
         const float sc = dot[r] * scale;
-        ps[(size_t)r * W + s] = sc;
+        ps[(size_t)r * sp + (s - s_lo)] = sc;
         mloc[r] = fmaxf(mloc[r], sc);
       }
     }
@@ -134,11 +150,11 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
     lsum[r] = 0.f;
   }
   __syncthreads();
-  for (int s = tid; s < nvalid; s += DEC_THREADS) {
+  for (int s = s_lo + tid; s < s_hi; s += DEC_THREADS) {
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
-      const float e = __expf(ps[(size_t)r * W + s] - mx[r]);
-      ps[(size_t)r * W + s] = e;
+      const float e = __expf(ps[(size_t)r * sp + (s - s_lo)] - mx[r]);
+      ps[(size_t)r * sp + (s - s_lo)] = e;
       lsum[r] += e;
     }
   }
@@ -157,13 +173,13 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[r][i] = 0.f;
 #pragma unroll 2
-  for (int s = rsub; s < nvalid; s += RPI) {
+  for (int s = s_lo + rsub; s < s_hi; s += RPI) {
     const uint4 v4 = *reinterpret_cast<const uint4*>(vring + ring_base + (size_t)s * HD + e8);
     const float f[8] = {bf16_lo(v4.x), bf16_hi(v4.x), bf16_lo(v4.y), bf16_hi(v4.y),
                         bf16_lo(v4.z), bf16_hi(v4.z), bf16_lo(v4.w), bf16_hi(v4.w)};
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
-      const float pr = ps[(size_t)r * W + s];
+      const float pr = ps[(size_t)r * sp + (s - s_lo)];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[r][i] = fmaf(pr, f[i], acc[r][i]);
     }
@@ -191,8 +207,40 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
       a += part[((size_t)w * REP + r) * HD + ee];
       l += red[r * 8 + w];
     }
-    out[(size_t)b * out_ld + (size_t)(g * REP + r) * HD + ee] = __float2bfloat16(a / l);
+    if (S == 1)
+      out[(size_t)b * out_ld + (size_t)(g * REP + r) * HD + ee] = __float2bfloat16(a / l);
+    else
+      cacc[i] = a;
   }
+  if (S == 1) return;
+  if (tid == 0) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float l = 0.f;
+      for (int w = 0; w < DEC_THREADS / 32; ++w) l += red[r * 8 + w];
+      cml[2 * r] = mx[r];
+      cml[2 * r + 1] = l;
+    }
+  }
+  // ---- merge the cluster's partials: CTA k writes output elements k, k + S*256, ...
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  for (int i = blockIdx.z * DEC_THREADS + tid; i < REP * HD; i += S * DEC_THREADS) {
+    const int r = i / HD;
+    float M = -INFINITY;
+    for (int k = 0; k < S; ++k) M = fmaxf(M, cl.map_shared_rank(cml, k)[2 * r]);
+    float num = 0.f, den = 0.f;
+    for (int k = 0; k < S; ++k) {
+      const float* ml = cl.map_shared_rank(cml, k);
+      const float m = ml[2 * r];
+      if (m == -INFINITY) continue;   // a CTA whose slots are all beyond the valid ones
+      const float sc = __expf(m - M);
+      num += sc * cl.map_shared_rank(cacc, k)[i];
+      den += sc * ml[2 * r + 1];
+    }
+    out[(size_t)b * out_ld + (size_t)(g * REP) * HD + i] = __float2bfloat16(num / den);
+  }
+  cl.sync();   // no CTA leaves while another still reads its partial
 }
 
 template <int HD, int REP>
@@ -205,8 +253,24 @@ int launch_attn_decode(int B, int n_kv, int W, const __nv_bfloat16* qkv, int qkv
                                               (int)(dec_smem_floats(HD, REP, MAX_W) * sizeof(float)))));
     attr = true;
   }
-  attn_decode_kernel<HD, REP><<<dim3(B, n_kv), DEC_THREADS, dec_smem_floats(HD, REP, W) * sizeof(float), st>>>(
-      qkv, qkv_ld, pos, slot, kring, vring, n_kv, W, cos_t, sin_t, scale, out, out_ld);
+  // split the ring over a cluster while the batch leaves SMs idle (at least 16 slots per CTA)
+  int S = 1;
+  while (S < 8 && (long long)B * n_kv * S < 2LL * num_sms() && W % (2 * S) == 0 && W / (2 * S) >= 16) S *= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(B, n_kv, S);
+  cfg.blockDim = dim3(DEC_THREADS);
+  cfg.dynamicSmemBytes = dec_smem_floats(HD, REP, W / S) * sizeof(float);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = S;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, REP>, qkv, qkv_ld, pos, slot, kring, vring, n_kv, W, cos_t,
+                         sin_t, scale, out, out_ld) != cudaSuccess)
+    return launch_status();
   return launch_status();
 }
 

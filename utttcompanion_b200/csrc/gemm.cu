@@ -12,8 +12,12 @@
 // projection (residual add, RMSNorm, sigmoid gates) and writes BF16.
 #include <string.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "host_util.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace uttt {
 namespace {
@@ -119,10 +123,13 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
-// Row-wise finishing of a projection: up to 6 column segments per row, one CTA
-// per row (4 independent loads per thread in flight).  The FP32 accumulator
-// row is zeroed after use, so the next projection can accumulate into it
-// without a memset.
+// Row-wise finishing of a projection: up to 6 column segments per row.  A row
+// is striped over a cluster of CF CTAs (grid (M, CF); CF grows while the rows
+// alone would leave SMs idle, so a decode batch of one row still spreads over
+// 8 SMs), 4 independent loads per thread in flight; a row statistic (the
+// RMSNorm sums of squares) is summed over the cluster's CTAs in distributed
+// shared memory, in rank order.  The FP32 accumulator row is zeroed after use,
+// so the next projection can accumulate into it without a memset.
 // ---------------------------------------------------------------------------
 constexpr int F_THREADS = 256;
 constexpr int F_UNROLL = 4;
@@ -165,27 +172,47 @@ __device__ __forceinline__ float seg_value(const UtttSegment& sg, float v, int r
   }
 }
 
+// A row statistic summed over the CTAs of the row's cluster (slot si of each CTA's cred).
+__device__ __forceinline__ float cluster_row_sum(float v, float* cred, int si, int CF) {
+  if (CF == 1) return v;
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) cred[si] = v;
+  cl.sync();
+  float s = 0.f;
+  for (int k = 0; k < CF; ++k) s += cl.map_shared_rank(cred, k)[si];
+  return s;
+}
+
+__device__ __forceinline__ void row_sync(int CF) {
+  if (CF == 1)
+    __syncthreads();
+  else
+    cg::this_cluster().sync();
+}
+
 __global__ void __launch_bounds__(F_THREADS) finish_kernel(float* __restrict__ y, int N, int nseg,
                                                            const __grid_constant__ SegPack sp, float eps) {
   __shared__ float red[F_THREADS / 32];
-  const int r = blockIdx.x, tid = threadIdx.x;
+  __shared__ float cred[6];
+  const int CF = gridDim.y, r = blockIdx.x, tid = threadIdx.x;
+  const int first = blockIdx.y * F_THREADS + tid, stride = CF * F_THREADS;   // this CTA's stripe of the row
   float* yrow = y + (size_t)r * N;
   for (int si = 0; si < nseg; ++si) {
     const UtttSegment& sg = sp.s[si];
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(sg.out) + (size_t)r * sg.out_ld;
     float* outf = reinterpret_cast<float*>(sg.out) + (size_t)r * sg.out_ld;
     if (sg.op == UTTT_SEG_NORM) {
-      // rms_norm of a BF16 row an earlier segment of this row has just written
-      __syncthreads();
+      // rms_norm of a BF16 row an earlier segment of this row has just written (every CTA of the cluster)
+      row_sync(CF);
       const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(sg.aux) + (size_t)r * sg.aux_ld;
       const float* gamma = reinterpret_cast<const float*>(sg.aux2);
       float ss = 0.f;
-      for (int i = tid; i < sg.len; i += F_THREADS) {
+      for (int i = first; i < sg.len; i += stride) {
         const float v = __bfloat162float(src[i]);
         ss += v * v;
       }
-      const float rinv = rsqrtf(fblock_sum(ss, red) / (float)sg.len + eps);
-      for (int i = tid; i < sg.len; i += F_THREADS) {
+      const float rinv = rsqrtf(cluster_row_sum(fblock_sum(ss, red), cred, si, CF) / (float)sg.len + eps);
+      for (int i = first; i < sg.len; i += stride) {
         float v = __bfloat162float(src[i]) * rinv;
         if (gamma) v *= bf16r(gamma[i]);
         if (sg.out_f32)
@@ -199,22 +226,22 @@ __global__ void __launch_bounds__(F_THREADS) finish_kernel(float* __restrict__ y
     float rinv = 1.f;
     if (sg.op == UTTT_SEG_RMSNORM) {
       float ss = 0.f;
-      for (int i = tid; i < sg.len; i += F_THREADS) {
+      for (int i = first; i < sg.len; i += stride) {
         const float v = bf16r(ys[i]);
         ss += v * v;
       }
-      rinv = rsqrtf(fblock_sum(ss, red) / (float)sg.len + eps);
+      rinv = rsqrtf(cluster_row_sum(fblock_sum(ss, red), cred, si, CF) / (float)sg.len + eps);
     }
-    for (int i0 = tid; i0 < sg.len; i0 += F_THREADS * F_UNROLL) {
+    for (int i0 = first; i0 < sg.len; i0 += stride * F_UNROLL) {
       float v[F_UNROLL];
 #pragma unroll
       for (int u = 0; u < F_UNROLL; ++u) {
-        const int i = i0 + u * F_THREADS;
+        const int i = i0 + u * stride;
         v[u] = i < sg.len ? ys[i] : 0.f;
       }
 #pragma unroll
       for (int u = 0; u < F_UNROLL; ++u) {
-        const int i = i0 + u * F_THREADS;
+        const int i = i0 + u * stride;
         if (i < sg.len) {
           const float o = seg_value(sg, v[u], r, i, rinv);
           if (sg.out_f32)
@@ -225,8 +252,9 @@ __global__ void __launch_bounds__(F_THREADS) finish_kernel(float* __restrict__ y
       }
     }
   }
-  __syncthreads();   // every segment has read this row before it is cleared
-  for (int i = tid; i < N; i += F_THREADS) yrow[i] = 0.f;   // leave the accumulator zero for the next call
+  // every segment of every CTA has read this row (and its partial sums) before it is cleared
+  row_sync(CF);
+  for (int i = first; i < N; i += stride) yrow[i] = 0.f;   // leave the accumulator zero for the next call
 }
 
 }  // namespace
@@ -298,9 +326,22 @@ extern "C" int uttt_linear(int M, int N, int K, const void* x, const void* w, in
   SegPack sp;
   memset(&sp, 0, sizeof(sp));
   for (int i = 0; i < nseg; ++i) sp.s[i] = segs[i];
+  int CF = 1;   // CTAs per row (a cluster): spread narrow batches over the SMs
+  while (CF < 8 && (long long)M * CF < 2LL * num_sms() && N > CF * F_THREADS * F_UNROLL) CF *= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M, CF);
+  cfg.blockDim = dim3(F_THREADS);
+  cfg.stream = st;
+  cudaLaunchAttribute attr1[1];
+  attr1[0].id = cudaLaunchAttributeClusterDimension;
+  attr1[0].val.clusterDim.x = 1;
+  attr1[0].val.clusterDim.y = CF;
+  attr1[0].val.clusterDim.z = 1;
+  cfg.attrs = attr1;
+  cfg.numAttrs = 1;
   {
     ProfScope ps(UTTT_PROF_FINISH, st);
-    finish_kernel<<<M, F_THREADS, 0, st>>>(y, N, nseg, sp, eps);
+    if (cudaLaunchKernelEx(&cfg, finish_kernel, y, N, nseg, sp, eps) != cudaSuccess) return launch_status();
   }
   return launch_status();
 }

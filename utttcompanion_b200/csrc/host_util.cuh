@@ -24,6 +24,20 @@ inline int cuda_status(cudaError_t e) {
 // Check the launch that was just issued.
 inline int launch_status() { return cuda_status(cudaGetLastError()); }
 
+// SMs of the current device (cached per device ordinal).
+inline int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
 #define UTTT_TRY(expr)              \
   do {                              \
     int _s = (expr);                \

@@ -6,16 +6,25 @@
 // state, so the kernel is bound by HBM: every weight byte is read exactly
 // once with 16-byte coalesced loads straight into registers.
 //
-// grid = (ceil(h / 128) hidden tiles, B states), 8 warps.  A CTA computes u, g
-// for its 128 hidden units (one warp instruction covers a row of both: lanes
-// 0-15 read u, lanes 16-31 read g; the warps split K = d), h = silu(g) * u,
-// then the partial z = h W_down[tile, :] (the warps split the tile's rows),
-// reduced in shared memory and added into z (FP32) with one red.add per
-// column.  The last CTA of a state to finish (device-scope counter) applies
-// the LayerNorm and the residual.  u, g, silu(g), h and z are rounded to BF16
-// where the reference's autocast rounds them.
+// grid = (ceil(h / 128) hidden tiles, B states, KS splits), 8 warps.  A CTA
+// computes u, g for its 128 hidden units over its K-slice of d rows (one warp
+// instruction covers a row of both: lanes 0-15 read u, lanes 16-31 read g; the
+// warps split the slice), h = silu(g) * u, then the partial z = h W_down[tile, :]
+// over its slice of d columns (the warps split the tile's rows), reduced in
+// shared memory and added into z (FP32) with one red.add per column.  With
+// KS > 1 the KS CTAs of a tile form one thread-block cluster: their partial u, g
+// meet in distributed shared memory, summed in rank order by every CTA, so all
+// of them hold the same h.  KS grows when B * tiles would leave SMs idle (one
+// persona of the 1.58B model has 54 tiles on 148 SMs): each CTA then streams
+// 1/KS of the tile's bytes.  The last CTA of a state to finish (device-scope
+// counter) applies the LayerNorm and the residual.  u, g, silu(g), h and z are
+// rounded to BF16 where the reference's autocast rounds them.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "host_util.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace uttt {
 namespace {
@@ -58,14 +67,17 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   __shared__ __align__(16) float xs[MD];
   __shared__ __align__(16) float part[8][ZG];
   __shared__ float ug[2 * GT];
+  __shared__ __align__(16) float ugp[2 * GT];   // this CTA's partial u, g (read by its cluster)
   __shared__ float hs[GT];
   __shared__ float red[GTHREADS / 32];
   __shared__ int last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.y, j0 = blockIdx.x * GT;
+  const int KS = gridDim.z, ks = blockIdx.z;
+  const int kper = d / KS, kb = ks * kper, ke = kb + kper;   // this CTA's rows of W_up/W_gate, columns of W_down
   const int state = state_index ? state_index[b] : b;
-  if (state < 0) {   // a padding row of a packed batch: no weights are read, out = x
-    if (blockIdx.x == 0 && done != nullptr)
+  if (state < 0) {   // a padding row of a packed batch: no weights are read, out = x (whole clusters leave)
+    if (blockIdx.x == 0 && ks == 0 && done != nullptr)
       for (int i = tid; i < d; i += GTHREADS) {
         const float xv = __bfloat162float(x[(size_t)b * d + i]);
         if (out_bf16)
@@ -91,7 +103,7 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (j0 + c8 < h) {
 #pragma unroll 8
-      for (int k = warp; k < d; k += 8) {
+      for (int k = kb + warp; k < ke; k += 8) {
         float f[8];
         bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(col + (size_t)k * ld)), f);
         const float xv = xs[k];
@@ -108,7 +120,19 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) s += part[w][tid];
+    if (KS == 1) {
+      ug[tid] = round_bf16(s);
+    } else {
+      ugp[tid] = s;
+    }
+  }
+  if (KS > 1) {
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();                                   // every partial of the cluster is in place
+    float s = 0.f;
+    for (int r = 0; r < KS; ++r) s += cl.map_shared_rank(ugp, r)[tid];
     ug[tid] = round_bf16(s);
+    cl.sync();                                   // no CTA leaves while another still reads its partial
   }
   __syncthreads();
   if (tid < GT) {
@@ -121,8 +145,8 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   // ---- partial z: warp w takes the tile's rows 16w..16w+15, lane 8 columns of a 256-column chunk
   const __nv_bfloat16* drow = wd + (size_t)state * h * d + (size_t)j0 * d;
   float* zrow = zacc + (size_t)b * d;
-  for (int c0 = 0; c0 < d; c0 += ZG) {
-    const int ncol = min(ZG, d - c0);
+  for (int c0 = kb; c0 < ke; c0 += ZG) {
+    const int ncol = min(ZG, ke - c0);
     float acc[2][8];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc)
@@ -168,7 +192,7 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   if (done == nullptr) return;
   __threadfence();
   __syncthreads();
-  if (tid == 0) last = atomicAdd(done + b, 1u) == gridDim.x - 1;
+  if (tid == 0) last = atomicAdd(done + b, 1u) == gridDim.x * gridDim.z - 1;
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -264,13 +288,30 @@ int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __n
                           const __nv_bfloat16* wd, const int* state_index, const float* ln_w, const float* ln_b,
                           float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st) {
   if (d % 128 != 0 || d > MAXD || h % 8 != 0) return UTTT_ERR_UNSUPPORTED;
-  const dim3 grid((h + GT - 1) / GT, B);
+  const int tiles = (h + GT - 1) / GT;
+  // split K over a cluster until the launch covers two CTAs per SM (d / KS stays a
+  // multiple of 16 columns, so the 16-byte W_down loads keep their alignment)
+  int KS = 1;
+  while (KS < 8 && (long long)tiles * B * KS < 2LL * num_sms() && d % (16 * KS * 2) == 0) KS *= 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, B, KS);
+  cfg.blockDim = dim3(GTHREADS);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = KS;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (d <= 1024)   // small states: 4 CTAs per SM keep a short launch in one wave
-    readout_decode_kernel<1024, 4><<<grid, GTHREADS, 0, st>>>(x, wp, wd, state_index, d, h, ln_w, ln_b, eps, zacc,
-                                                              done, out, out_bf16);
+    e = cudaLaunchKernelEx(&cfg, readout_decode_kernel<1024, 4>, x, wp, wd, state_index, d, h, ln_w, ln_b, eps,
+                           zacc, done, out, out_bf16);
   else
-    readout_decode_kernel<MAXD, 3><<<grid, GTHREADS, 0, st>>>(x, wp, wd, state_index, d, h, ln_w, ln_b, eps, zacc,
-                                                              done, out, out_bf16);
+    e = cudaLaunchKernelEx(&cfg, readout_decode_kernel<MAXD, 3>, x, wp, wd, state_index, d, h, ln_w, ln_b, eps,
+                           zacc, done, out, out_bf16);
+  if (e != cudaSuccess) return UTTT_ERR_CUDA;
   return launch_status();
 }
 

@@ -19,21 +19,23 @@ import torch
 from . import _lib
 
 _ws_lock = threading.Lock()
-_workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+_workspaces: Dict[Tuple[int, int, int], torch.Tensor] = {}
 # Every buffer ever handed out stays allocated: a captured CUDA graph keeps the
 # raw pointers of the workspaces it was recorded with, so a buffer outgrown by
 # a later, larger call must not return to the allocator while a graph could
 # still replay into it.
-_retired: Dict[Tuple[int, int], list] = {}
+_retired: Dict[Tuple[int, int, int], list] = {}
 
 
 def workspace(nbytes: int, device: torch.device, slot: int = 0) -> torch.Tensor:
-    """A cached, zero-initialised device workspace of at least ``nbytes`` (per device and slot).
+    """A cached, zero-initialised device workspace of at least ``nbytes`` (per device, slot and
+    current stream, so work queued on different streams never shares scratch).
 
     Growing a slot allocates a new buffer (at least twice the old size) and keeps
     the old one alive for the life of the process, so pointers captured by CUDA
     graphs stay valid."""
-    key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
+    dev = device.index if device.index is not None else torch.cuda.current_device()
+    key = (dev, slot, torch.cuda.current_stream(dev).cuda_stream)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
