@@ -131,6 +131,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
 // wait until at most N committed bulk groups are still reading their shared-memory source
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() {

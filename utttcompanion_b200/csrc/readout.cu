@@ -16,7 +16,10 @@
 // meet in distributed shared memory, summed in rank order by every CTA, so all
 // of them hold the same h.  KS grows when B * tiles would leave SMs idle (one
 // persona of the 1.58B model has 54 tiles on 148 SMs): each CTA then streams
-// 1/KS of the tile's bytes.  The last CTA of a state to finish (device-scope
+// 1/KS of the tile's bytes.  KS is the largest split whose clusters all fit
+// on the GPU at once (the occupancy API counts them; 8-CTA clusters of this
+// kernel fit 48 at a time, so one 1.58B persona uses 4-CTA clusters and a single
+// wave).  The last CTA of a state to finish (device-scope
 // counter) applies the LayerNorm and the residual.  u, g, silu(g), h and z are
 // rounded to BF16 where the reference's autocast rounds them.
 #include <cooperative_groups.h>
@@ -289,14 +292,42 @@ int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __n
                           float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st) {
   if (d % 128 != 0 || d > MAXD || h % 8 != 0) return UTTT_ERR_UNSUPPORTED;
   const int tiles = (h + GT - 1) / GT;
-  // split K over a cluster until the launch covers two CTAs per SM (d / KS stays a
-  // multiple of 16 columns, so the 16-byte W_down loads keep their alignment)
-  int KS = 1;
-  while (KS < 8 && (long long)tiles * B * KS < 2LL * num_sms() && d % (16 * KS * 2) == 0) KS *= 2;
+  const bool small = d <= 1024;
+  const void* fn = small ? (const void*)readout_decode_kernel<1024, 4> : (const void*)readout_decode_kernel<MAXD, 3>;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles, B, KS);
   cfg.blockDim = dim3(GTHREADS);
   cfg.stream = st;
+  // The largest K split (a cluster of KS CTAs per tile, d / KS a multiple of 16 columns so the
+  // 16-byte W_down loads stay aligned) whose B * tiles clusters are all resident at once; a
+  // batch too large for any split to fit in one wave runs unsplit.
+  static int ncl_cache[16][2][4];   // resident clusters of 2, 4, 8 CTAs per (device, variant); 0: unknown
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 15;
+  int KS = 1;
+  for (int k = 8, ki = 3; k >= 2; k >>= 1, --ki) {
+    if (d % (16 * k) != 0) continue;
+    int& ncl = ncl_cache[dev][small][ki];
+    if (ncl == 0) {
+      cudaLaunchAttribute ca;
+      ca.id = cudaLaunchAttributeClusterDimension;
+      ca.val.clusterDim.x = 1;
+      ca.val.clusterDim.y = 1;
+      ca.val.clusterDim.z = k;
+      cfg.gridDim = dim3(1, 1, k);
+      cfg.attrs = &ca;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&ncl, fn, &cfg) != cudaSuccess || ncl <= 0) {
+        cudaGetLastError();
+        ncl = -1;
+      }
+    }
+    if (ncl > 0 && (long long)tiles * B <= ncl) {
+      KS = k;
+      break;
+    }
+  }
+  cfg.gridDim = dim3(tiles, B, KS);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
