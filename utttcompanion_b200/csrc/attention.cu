@@ -14,8 +14,9 @@
 // Prefill / chunk (T new tokens per row): RoPE into a contiguous per-row KV
 // window buffer that starts with up to W-1 history positions, then causal
 // sliding-window attention (query at absolute position p sees keys in
-// (p - W, p]).  64 queries per CTA, two threads per query (each half of the
-// head dimension), 64-key tiles staged in shared memory.
+// (p - W, p]) on the tensor cores for head dims 64 and 128 (attn_prefill_tc_kernel);
+// other head dims use a CUDA-core kernel (64 queries per CTA, two threads per
+// query, 64-key tiles staged in shared memory).
 //
 // RoPE tables are the reference's FP32 cos/sin (RotaryEmbedding._build_cache,
 // :910-933); like apply_rope on BF16 activations (:946-958) every product and
@@ -384,6 +385,244 @@ __global__ void __launch_bounds__(PF_THREADS) attn_prefill_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill / chunk attention on the tensor cores (head dim 64 or 128).
+//
+// One CTA per (query block, kv group, row): the REP query heads of the group
+// and QB = 128 / REP queries stack into the 128 rows of the MMA (row i: query
+// i / REP, head i % REP), so every K/V tile is read once for the whole group.
+// The keys the block needs ([first query - W + 1, last query]) stream through
+// shared memory by TMA in 64-key tiles.  Two passes over the tiles:
+//   pass 1: S = Q K^T (TMEM) -> exact row max m and sum l of exp(s - m);
+//   pass 2: S again -> P = exp(s - m) / l -> O += P V (TMEM);
+// so O never needs the rescaling of an online softmax.  P enters the MMA as two
+// BF16 tiles, P_hi = bf16(P) and P_lo = bf16(P - P_hi), accumulated into the
+// same O: about 16 significant bits, as the reference's FP32 softmax feeds its
+// P.V product (an FP32 P would need the lower-rate TF32 kind and FP32 V tiles).  Warp 0 issues the TMA
+// loads, warp 1 the MMAs, warps 2-5 own one row each (TMEM lane = row).
+// ---------------------------------------------------------------------------
+constexpr int TP_THREADS = 192;
+constexpr int TP_NS = 3;   // K/V tiles in flight
+
+template <int HD>
+struct TpLayout {
+  static constexpr int QB = HD / 64;            // 64-column blocks of a head vector
+  static constexpr int Q_BYTES = 128 * HD * 2;  // Q: [128 rows][HD], K-major SW128, per 64-column block 16 KB
+  static constexpr int KT_BYTES = 64 * HD * 2;  // one K (or V) tile: [64 keys][HD], per block 8 KB
+  static constexpr int SLOT = 2 * KT_BYTES;     // K then V
+  static constexpr int P_BYTES = 128 * 64 * 2;  // P_hi or P_lo: [128 rows][64 keys], K-major SW128
+  static constexpr int SMEM = 1024 + Q_BYTES + TP_NS * SLOT + 4 * P_BYTES;   // 2 buffers x (P_hi, P_lo)
+};
+
+template <int HD>
+__global__ void __launch_bounds__(TP_THREADS, 1) attn_prefill_tc_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    const __nv_bfloat16* __restrict__ q, int T, int hist, int L, int n_heads, int n_kv, int rep, int W, float scale,
+    __nv_bfloat16* __restrict__ out) {
+  using LY = TpLayout<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t kv_full[TP_NS], kv_empty[TP_NS], s_full[2], s_empty[2], p_full[2], p_empty[2], q_ready,
+      o_done;
+  __shared__ uint32_t tmem_slot;
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sQ = base;
+  uint8_t* sKV = sQ + LY::Q_BYTES;
+  uint8_t* sP = sKV + TP_NS * LY::SLOT;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qb = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int QBK = 128 / rep;                       // queries per block
+  const int lo = max(0, hist + qb * QBK - (W - 1));
+  const int hi = hist + min(T, (qb + 1) * QBK) - 1;
+  const int ntiles = (hi - lo) / 64 + 1;
+  const int row0 = (b * n_kv + g) * L;             // first KV-buffer row of this (row, group)
+
+  if (tid == 0) {
+    for (int i = 0; i < TP_NS; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(&q_ready, 128);
+    mbar_init(&o_done, 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 128;       // S: 2 x 64 columns, O: HD columns
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      // pass 1: K of tiles 0..n-1; pass 2: K and V of tiles 0..n-1 (slot = sequence % TP_NS)
+      for (int it = 0; it < 2 * ntiles; ++it) {
+        const int s = it % TP_NS, j = it < ntiles ? it : it - ntiles;
+        const bool with_v = it >= ntiles;
+        mbar_wait(&kv_empty[s], ((it / TP_NS) & 1) ^ 1, nullptr);
+        uint8_t* dst = sKV + s * LY::SLOT;
+        mbar_arrive_expect_tx(&kv_full[s], (uint32_t)(with_v ? 2 : 1) * LY::KT_BYTES);
+#pragma unroll
+        for (int h = 0; h < LY::QB; ++h) tma_load_2d(dst + h * 8192, &tmK, &kv_full[s], h * 64, row0 + lo + j * 64);
+        if (with_v)
+#pragma unroll
+          for (int h = 0; h < LY::QB; ++h)
+            tma_load_2d(dst + LY::KT_BYTES + h * 8192, &tmV, &kv_full[s], h * 64, row0 + lo + j * 64);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16(128, 64, false, false);   // A = Q K-major, B = K K-major
+      const uint32_t id_o = idesc_bf16(128, HD, false, true);    // A = P K-major, B = V MN-major
+      const uint32_t qa = smem_u32(sQ);
+      mbar_wait(&q_ready, 0, nullptr);
+      tc_fence_after();
+      auto issue_s = [&](int it) {                 // S tile of sequence it into TMEM buffer it & 1
+        const int s = it % TP_NS, sb = it & 1;
+        mbar_wait(&kv_full[s], (it / TP_NS) & 1, nullptr);
+        mbar_wait(&s_empty[sb], ((it >> 1) & 1) ^ 1, nullptr);
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sKV + s * LY::SLOT);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          mma_bf16(tS + sb * 64, sdesc_sw128(qa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                   sdesc_sw128(ka + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024), id_s, k > 0 ? 1u : 0u);
+        mma_commit(&s_full[sb]);
+      };
+      for (int it = 0; it < ntiles; ++it) {        // pass 1
+        issue_s(it);
+        mma_commit(&kv_empty[it % TP_NS]);
+      }
+      issue_s(ntiles);                             // pass 2: S of tile j + 1 goes out before P V of tile j
+      for (int j = 0; j < ntiles; ++j) {
+        if (j + 1 < ntiles) issue_s(ntiles + j + 1);
+        const int it = ntiles + j, s = it % TP_NS, pb = j & 1;
+        mbar_wait(&p_full[pb], (j >> 1) & 1, nullptr);
+        tc_fence_after();
+        const uint32_t va = smem_u32(sKV + s * LY::SLOT + LY::KT_BYTES), pa = smem_u32(sP + pb * 2 * LY::P_BYTES);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // P_hi V
+          mma_bf16(tO, sdesc_sw128(pa + k * 32, 16, 1024), sdesc_sw128(va + k * 2048, 8192, 1024), id_o,
+                   (j > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // + P_lo V
+          mma_bf16(tO, sdesc_sw128(pa + LY::P_BYTES + k * 32, 16, 1024), sdesc_sw128(va + k * 2048, 8192, 1024),
+                   id_o, 1u);
+        mma_commit(&p_empty[pb]);
+        mma_commit(&kv_empty[s]);
+      }
+      mma_commit(&o_done);
+    }
+  } else {
+    // ---- one row per thread: row i = query i / rep, head i % rep of the group
+    const int i = (warp & 3) * 32 + lane;
+    const int tq = i / rep, r = i - tq * rep, t = qb * QBK + tq;
+    const bool valid = i < rep * QBK && t < T;
+    const int kpos = hist + t;                     // this query's index in the KV buffer
+    const size_t qrow = ((size_t)b * T + t) * n_heads + (size_t)g * rep + r;
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(q + qrow * HD);
+#pragma unroll
+      for (int c = 0; c < HD / 8; ++c) {
+        const uint4 v = valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(sQ + (c >> 3) * 16384 + sw128_offset(i, (c & 7) * 16)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&q_ready);
+    }
+    const uint32_t trow = (uint32_t)((warp & 3) * 32);
+    float m = -INFINITY, l = 0.f;
+    for (int it = 0; it < 2 * ntiles; ++it) {
+      const int j = it < ntiles ? it : it - ntiles, sb = it & 1;
+      const int kt = lo + j * 64;
+      mbar_wait(&s_full[sb], (it >> 1) & 1, nullptr);
+      tc_fence_after();
+      float sv[64];
+#pragma unroll
+      for (int c = 0; c < 64; c += 16) tmem_ld16(tmem_addr(tS + sb * 64, trow, c), *reinterpret_cast<float(*)[16]>(&sv[c]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      // key kt + c is visible to this query when it is in (kpos - W, kpos]
+      const int cmax = valid ? min(63, kpos - kt) : -1;        // keys past kpos are masked
+      const int cmin = valid ? max(0, kpos - W + 1 - kt) : 64;  // keys at or before kpos - W are masked
+      if (it < ntiles) {
+        float mt = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c >= cmin && c <= cmax) mt = fmaxf(mt, sv[c] * scale);
+        if (mt > -INFINITY) {
+          const float mn = fmaxf(m, mt);
+          float sum = 0.f;
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c >= cmin && c <= cmax) sum += __expf(sv[c] * scale - mn);
+          l = (m > -INFINITY ? l * __expf(m - mn) : 0.f) + sum;
+          m = mn;
+        }
+      } else {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const int pb = j & 1;
+        mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1, nullptr);
+        uint8_t* phi = sP + pb * 2 * LY::P_BYTES;
+        uint8_t* plo = phi + LY::P_BYTES;
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          float pv[8], lo8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int cc = c + e;
+            pv[e] = (cc >= cmin && cc <= cmax) ? __expf(sv[cc] * scale - m) * inv : 0.f;
+            lo8[e] = pv[e] - __bfloat162float(__float2bfloat16(pv[e]));
+          }
+          uint4 pk, pl;
+          pk.x = pack_bf16x2(pv[0], pv[1]);
+          pk.y = pack_bf16x2(pv[2], pv[3]);
+          pk.z = pack_bf16x2(pv[4], pv[5]);
+          pk.w = pack_bf16x2(pv[6], pv[7]);
+          pl.x = pack_bf16x2(lo8[0], lo8[1]);
+          pl.y = pack_bf16x2(lo8[2], lo8[3]);
+          pl.z = pack_bf16x2(lo8[4], lo8[5]);
+          pl.w = pack_bf16x2(lo8[6], lo8[7]);
+          *reinterpret_cast<uint4*>(phi + sw128_offset(i, c * 2)) = pk;
+          *reinterpret_cast<uint4*>(plo + sw128_offset(i, c * 2)) = pl;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&p_full[pb]);
+      }
+    }
+    // ---- O (TMEM) -> BF16 rows of out
+    mbar_wait(&o_done, 0, nullptr);
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < HD; c += 16) {
+      float ov[16];
+      tmem_ld16(tmem_addr(tO, trow, c), ov);
+      tmem_wait_ld();
+      if (valid) {
+        uint4 a, bq;
+        a.x = pack_bf16x2(ov[0], ov[1]);   a.y = pack_bf16x2(ov[2], ov[3]);
+        a.z = pack_bf16x2(ov[4], ov[5]);   a.w = pack_bf16x2(ov[6], ov[7]);
+        bq.x = pack_bf16x2(ov[8], ov[9]);  bq.y = pack_bf16x2(ov[10], ov[11]);
+        bq.z = pack_bf16x2(ov[12], ov[13]); bq.w = pack_bf16x2(ov[14], ov[15]);
+        uint4* dst = reinterpret_cast<uint4*>(out + qrow * HD + c);
+        dst[0] = a;
+        dst[1] = bq;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
 // Copy the last min(W, L) positions of a KV window buffer into the ring slots
 // of the persona: position p -> slot p % W.
 __global__ void ring_fill_kernel(const __nv_bfloat16* __restrict__ kbuf, const __nv_bfloat16* __restrict__ vbuf,
@@ -444,8 +683,36 @@ extern "C" int uttt_attn_prefill(int B, int T, int start_pos, int hist, int n_he
                                              hist, L, rope_cos, rope_sin, (__nv_bfloat16*)q_scratch,
                                              (__nv_bfloat16*)k_buf, (__nv_bfloat16*)v_buf);
   UTTT_TRY(launch_status());
-  const dim3 grid((T + PF_Q - 1) / PF_Q, n_heads, B);
   const float scale = 1.f / sqrtf((float)hd);
+  const int rep = n_heads / n_kv;
+  if ((hd == 64 || hd == 128) && rep <= 8) {
+    // tensor-core path: K / V window buffers as 2-D [B * n_kv * L rows][hd] maps, 64 x 64 boxes
+    CUtensorMap tmK, tmV;
+    const uint64_t dims[2] = {(uint64_t)hd, (uint64_t)B * n_kv * L}, str[1] = {(uint64_t)hd * 2};
+    const uint32_t box[2] = {64, 64};
+    UTTT_TRY(make_tmap_bf16(&tmK, k_buf, 2, dims, str, box));
+    UTTT_TRY(make_tmap_bf16(&tmV, v_buf, 2, dims, str, box));
+    const int qbk = 128 / rep;
+    const dim3 tgrid((T + qbk - 1) / qbk, n_kv, B);
+#define UTTT_TP(HDV)                                                                                            \
+  do {                                                                                                          \
+    static bool attr_set = false;                                                                               \
+    if (!attr_set) {                                                                                            \
+      UTTT_TRY(cuda_status(cudaFuncSetAttribute(attn_prefill_tc_kernel<HDV>,                                    \
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, TpLayout<HDV>::SMEM))); \
+      attr_set = true;                                                                                          \
+    }                                                                                                           \
+    attn_prefill_tc_kernel<HDV><<<tgrid, TP_THREADS, TpLayout<HDV>::SMEM, st>>>(                                \
+        tmK, tmV, (const __nv_bfloat16*)q_scratch, T, hist, L, n_heads, n_kv, rep, W, scale, (__nv_bfloat16*)out); \
+  } while (0)
+    if (hd == 64)
+      UTTT_TP(64);
+    else
+      UTTT_TP(128);
+#undef UTTT_TP
+    return launch_status();
+  }
+  const dim3 grid((T + PF_Q - 1) / PF_Q, n_heads, B);
 #define UTTT_PF(HDV)                                                                                          \
   attn_prefill_kernel<HDV><<<grid, PF_THREADS, 0, st>>>((const __nv_bfloat16*)q_scratch,                       \
                                                        (const __nv_bfloat16*)k_buf, (const __nv_bfloat16*)v_buf, \
