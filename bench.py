@@ -513,6 +513,62 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             "writes": "every completed turn: chunk-TTT write + surprise gate + elastic pull", "points": out}
 
 
+def micro_case(device, kind, batch, tokens, hist, iters=30):
+    """Kernel profiling cases at the 1.58B layer shape (one JSON object; not a bench line).
+
+    ``readout``: the decode readout (GEMV + fused LayerNorm, d=2560, h=6912) of ``batch``
+    rows, each on its own BF16 read copy; 24 copies (2.5 GB) cycle so every call streams
+    its weights from HBM.  ``attn``: the prefill / chunk attention (20 query heads over 5 KV
+    heads of dim 128, window 512) of ``batch`` rows x ``tokens`` new tokens after ``hist``
+    history positions (RoPE kernel included)."""
+    from utttcompanion_b200 import _lib
+    from utttcompanion_b200.fastweight import _stream
+    lib = _lib.load()
+    g = torch.Generator(device=device).manual_seed(0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if kind == "readout":
+        from utttcompanion_b200.readout import fast_readout
+        d, h, S = 2560, 6912, 24
+        packed = (torch.randn(S, d, 2 * h, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        down = (torch.randn(S, h, d, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        lw, lb = torch.ones(d, device=device), torch.zeros(d, device=device)
+        x = torch.randn(batch, 1, d, device=device, generator=g).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        idx = [((torch.arange(batch, device=device) + i * batch) % S).to(torch.int32) for i in range(iters + 3)]
+        call = lambda i: fast_readout(x, packed, None, down, lw, lb, state_index=idx[i], packed=True,  # noqa: E731
+                                      ln_prepared=True, out=out)
+        nbytes = batch * 3 * d * h * 2
+    else:
+        hd, nh, nkv, W = 128, 20, 5, 512
+        L = hist + tokens
+        qkv_dim = (nh + 2 * nkv) * hd
+        qkv = torch.randn(batch * tokens, qkv_dim, device=device, generator=g).to(torch.bfloat16)
+        from utttcompanion_b200.model import rope_tables
+        cos, sin = (t.to(device).contiguous() for t in rope_tables(hd, hist + tokens + 8, 10000.0))
+        qs = torch.empty(batch * tokens, nh, hd, dtype=torch.bfloat16, device=device)
+        kb = torch.randn(batch, nkv, L, hd, device=device, generator=g).to(torch.bfloat16)
+        vb = torch.randn_like(kb)
+        out = torch.empty(batch * tokens, nh, hd, dtype=torch.bfloat16, device=device)
+        st = _stream(device)
+
+        def call(i):
+            _lib.check(lib.uttt_attn_prefill(batch, tokens, hist, hist, nh, nkv, hd, W, qkv.data_ptr(), qkv_dim,
+                                             cos.data_ptr(), sin.data_ptr(), qs.data_ptr(), kb.data_ptr(),
+                                             vb.data_ptr(), out.data_ptr(), st), "uttt_attn_prefill")
+        nbytes = batch * nkv * L * hd * 2 * 2
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(iters):
+        call(3 + i)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / iters * 1e3
+    return {"micro": kind, "batch": batch, "tokens": tokens, "hist": hist, "us_per_call": us,
+            "bytes_per_call": nbytes, "gb_s": nbytes / us / 1e3, "iters": iters}
+
+
 # ----------------------------------------------------------------------------- arms
 def reference_arm(args, world, rank):
     if rank != 0:
@@ -592,6 +648,11 @@ def ours_arm(args, world, rank, local):
         return float(t.item())
 
     lib = _lib.load()
+    if args.micro:                # kernel profiling cases (1 GPU)
+        if rank == 0:
+            print(json.dumps(micro_case(device, args.micro, args.micro_batch, args.micro_tokens, args.micro_hist,
+                                        iters=args.steps)), flush=True)
+        return 0
     if args.only_decode:          # profiling case: the config-3 decode + write workload alone
         if rank == 0:
             print(json.dumps(decode_workload(device, rank, lib, DEC)), flush=True)
@@ -767,6 +828,11 @@ def main():
                     help="write on a side stream from a worker thread, overlapping decode")
     ap.add_argument("--only-decode", action="store_true",
                     help="profiling: run only the config-3 decode + write workload (one JSON object, 1 GPU)")
+    ap.add_argument("--micro", choices=("readout", "attn"), default=None,
+                    help="profiling case: one kernel at the 1.58B layer shape")
+    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--micro-tokens", type=int, default=64)
+    ap.add_argument("--micro-hist", type=int, default=0)
     ap.add_argument("--states", type=int, default=None, help="override states per GPU (profiling cases)")
     ap.add_argument("--tokens", type=int, default=None, help="override tokens per state (profiling cases)")
     args = ap.parse_args()
