@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_decode_kernel(
   float* cml = cacc + REP * HD;                       // [REP][2]: max, sum
   const int b = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_heads = n_kv * REP;
+  pdl_wait();
+  pdl_trigger();
   const int p = pos[b];
   const int sl = slot[b];
   const __nv_bfloat16* row = qkv + (size_t)b * qkv_ld;
@@ -262,13 +264,14 @@ int launch_attn_decode(int B, int n_kv, int W, const __nv_bfloat16* qkv, int qkv
   cfg.blockDim = dim3(DEC_THREADS);
   cfg.dynamicSmemBytes = dec_smem_floats(HD, REP, W / S) * sizeof(float);
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 1;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = S;
+  at[1] = pdl_attribute();
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, REP>, qkv, qkv_ld, pos, slot, kring, vring, n_kv, W, cos_t,
                          sin_t, scale, out, out_ld) != cudaSuccess)
     return launch_status();

@@ -31,6 +31,15 @@ __device__ __forceinline__ void set_status(int* status, int code) {
 }
 
 // ----------------------------------------------------------------------------
+// programmatic dependent launch
+// ----------------------------------------------------------------------------
+// pdl_wait: returns once every grid this launch depends on has completed and its
+// writes are visible (at once for a launch without the programmatic attribute).
+// pdl_trigger: lets the next launch in the stream start its prologue now.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ----------------------------------------------------------------------------
 // shared-memory addresses, fences
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

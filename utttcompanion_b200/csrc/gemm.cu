@@ -67,7 +67,17 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
     if (lane == 0) {
       tma_prefetch_desc(&tmW);
       tma_prefetch_desc(&tmX);
-      for (int kb = kb0, it = 0; kb < kb1; ++kb, ++it) {
+      // the weights do not depend on earlier launches: the first stages' W tiles are
+      // requested before waiting for the previous kernel (which wrote X)
+      const int npre = min(G_STAGES, kb1 - kb0);
+      for (int it = 0; it < npre; ++it) {
+        mbar_arrive_expect_tx(&full[it], (uint32_t)stage_bytes);
+        tma_load_2d(base + it * stage_bytes, &tmW, &full[it], (kb0 + it) * 64, n0);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int it = 0; it < npre; ++it) tma_load_2d(base + it * stage_bytes + 16384, &tmX, &full[it], (kb0 + it) * 64, m0);
+      for (int kb = kb0 + npre, it = npre; kb < kb1; ++kb, ++it) {
         const int s = it % G_STAGES;
         mbar_wait(&empty[s], ((it / G_STAGES) & 1) ^ 1, p.status);
         uint8_t* st = base + s * stage_bytes;
@@ -93,7 +103,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) gemm_kernel(const __grid_constan
       mma_commit(&done);
     }
   } else {
-    // epilogue: lane = output feature, TMEM columns = tokens
+    // epilogue: lane = output feature, TMEM columns = tokens (Y32 was last written by an earlier launch)
+    pdl_wait();
     mbar_wait(&done, 0, p.status);
     tc_fence_after();
     const int q = warp & 3;
@@ -196,6 +207,8 @@ __global__ void __launch_bounds__(F_THREADS) finish_kernel(float* __restrict__ y
   __shared__ float cred[6];
   const int CF = gridDim.y, r = blockIdx.x, tid = threadIdx.x;
   const int first = blockIdx.y * F_THREADS + tid, stride = CF * F_THREADS;   // this CTA's stripe of the row
+  pdl_wait();
+  pdl_trigger();
   float* yrow = y + (size_t)r * N;
   for (int si = 0; si < nseg; ++si) {
     const UtttSegment& sg = sp.s[si];
@@ -320,7 +333,15 @@ extern "C" int uttt_linear(int M, int N, int K, const void* x, const void* w, in
   }
   {
     ProfScope ps(UTTT_PROF_GEMM, st);
-    gemm_kernel<<<dim3(ntiles, mtiles, splits), G_THREADS, smem, st>>>(tmW, tmX, p);
+    cudaLaunchConfig_t gc = {};
+    gc.gridDim = dim3(ntiles, mtiles, splits);
+    gc.blockDim = dim3(G_THREADS);
+    gc.dynamicSmemBytes = smem;
+    gc.stream = st;
+    cudaLaunchAttribute ga[1] = {pdl_attribute()};
+    gc.attrs = ga;
+    gc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&gc, gemm_kernel, tmW, tmX, p) != cudaSuccess) return launch_status();
   }
   UTTT_TRY(launch_status());
   SegPack sp;
@@ -332,13 +353,14 @@ extern "C" int uttt_linear(int M, int N, int K, const void* x, const void* w, in
   cfg.gridDim = dim3(M, CF);
   cfg.blockDim = dim3(F_THREADS);
   cfg.stream = st;
-  cudaLaunchAttribute attr1[1];
+  cudaLaunchAttribute attr1[2];
   attr1[0].id = cudaLaunchAttributeClusterDimension;
   attr1[0].val.clusterDim.x = 1;
   attr1[0].val.clusterDim.y = CF;
   attr1[0].val.clusterDim.z = 1;
+  attr1[1] = pdl_attribute();
   cfg.attrs = attr1;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   {
     ProfScope ps(UTTT_PROF_FINISH, st);
     if (cudaLaunchKernelEx(&cfg, finish_kernel, y, N, nseg, sp, eps) != cudaSuccess) return launch_status();

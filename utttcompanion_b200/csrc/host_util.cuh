@@ -24,6 +24,15 @@ inline int cuda_status(cudaError_t e) {
 // Check the launch that was just issued.
 inline int launch_status() { return cuda_status(cudaGetLastError()); }
 
+// Launch attribute: the kernel may start while the previous kernel of the stream
+// runs; it calls pdl_wait() before touching anything an earlier launch wrote.
+inline cudaLaunchAttribute pdl_attribute() {
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = 1;
+  return a;
+}
+
 // SMs of the current device (cached per device ordinal).
 inline int num_sms() {
   static int cached[64] = {0};

@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   const int b = blockIdx.y, j0 = blockIdx.x * GT;
   const int KS = gridDim.z, ks = blockIdx.z;
   const int kper = d / KS, kb = ks * kper, ke = kb + kper;   // this CTA's rows of W_up/W_gate, columns of W_down
+  pdl_wait();      // launched after the accumulator memset: returns at once
+  pdl_trigger();   // the projection after the readout may start its weight prefetch
   const int state = state_index ? state_index[b] : b;
   if (state < 0) {   // a padding row of a packed batch: no weights are read, out = x (whole clusters leave)
     if (blockIdx.x == 0 && ks == 0 && done != nullptr)
