@@ -24,6 +24,7 @@ by a barrier + synchronize on every rank and the max over ranks is used.
 from __future__ import annotations
 
 import argparse
+import collections
 import json
 import math
 import os
@@ -432,33 +433,47 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
 
 # ----------------------------------------------------------------------------- serve sweep (config 5)
 def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=64, seed=0, write_batch=32,
-                write_wait_s=0.2, async_writes=False):
-    """continuous batching of persona turns on one GPU.  Turns arrive as
-    a Poisson process at each rate; each picks a user uniformly among ``personas``, a prompt
-    of lognormal length (median 256, sigma 1.0, clipped to [16, 2048]) with uniform ids and a
-    forced reply length uniform in [32, 256] (greedy); every completed turn is written into its
-    user's state (chunk-TTT write, surprise gate, elastic pull).  Reports generated and written
-    tokens per second and the arrival -> result latency of every turn."""
+                write_wait_s=0.2, async_writes=False, world=1, rank=0):
+    """continuous batching of persona turns, personas partitioned by user id.
+
+    Turns arrive as a Poisson process at each rate; each picks a user uniformly among
+    ``personas``, a prompt of lognormal length (median 256, sigma 1.0, clipped to [16, 2048])
+    with uniform ids and a forced reply length uniform in [32, 256] (greedy); every completed
+    turn is written into its user's state (chunk-TTT write, surprise gate, elastic pull).
+    Every rank draws the same schedule and serves the turns of the users ``PersonaRouter``
+    maps to it (no collective on the data path); the ranks start each rate together and rank 0
+    gathers the latencies.  Reports whole-job generated / written tokens per second over the
+    slowest rank's wall time and the arrival -> result latency of every turn.  Returns the
+    result on rank 0, None elsewhere."""
     from utttcompanion_b200 import workloads as wl
     from utttcompanion_b200.model import UtttB200
-    from utttcompanion_b200.serving import ServingEngine
+    from utttcompanion_b200.serving import PersonaRouter, ServingEngine
     cfg = {"151M": wl.CONFIG_151M, "1P58B": wl.CONFIG_1P58B}[config]
+    router = PersonaRouter(world)
+    mine = [u for u in (f"user-{i}" for i in range(personas)) if router.rank_of(u) == rank]
     sd = wl.random_state_dict(cfg, seed=seed, device=device)
-    eng = UtttB200(sd, cfg, device=device, max_personas=personas + 1, max_positions=2048 + 256 + 64)
+    eng = UtttB200(sd, cfg, device=device, max_personas=len(mine) + 1, max_positions=2048 + 256 + 64)
     del sd
-    srv = ServingEngine(eng, capacity=personas, max_batch=max_batch, surprise_threshold=cfg.surprise_threshold,
+    srv = ServingEngine(eng, capacity=max(len(mine), 1), max_batch=max_batch, surprise_threshold=cfg.surprise_threshold,
                         stop_free=True, write_batch=write_batch, write_wait_s=write_wait_s,
                         async_writes=async_writes)
     g = torch.Generator().manual_seed(seed)
 
-    def draw_turn():
-        n = int(min(max(round(256 * math.exp(float(torch.randn(1, generator=g, dtype=torch.float64)))), 16), 2048))
-        reply = int(torch.randint(32, 257, (1,), generator=g))
-        user = f"user-{int(torch.randint(0, personas, (1,), generator=g))}"
-        return user, torch.randint(6, cfg.vocab_size, (n,), generator=g).tolist(), reply
+    def draw_turn(gen=g):
+        n = int(min(max(round(256 * math.exp(float(torch.randn(1, generator=gen, dtype=torch.float64)))), 16), 2048))
+        reply = int(torch.randint(32, 257, (1,), generator=gen))
+        user = f"user-{int(torch.randint(0, personas, (1,), generator=gen))}"
+        return user, torch.randint(6, cfg.vocab_size, (n,), generator=gen).tolist(), reply
 
-    for _ in range(4):                                   # warm-up turns (prefill, decode, write paths)
-        srv.submit(*draw_turn())
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    gw = torch.Generator().manual_seed(seed + 1 + rank)   # warm-up turns of this rank's users; the
+    for k in range(4):                                     # shared schedule generator stays in step
+        _, ids, rl = draw_turn(gw)
+        srv.submit(mine[k % len(mine)], ids, rl)
     srv.run()
     out = []
     for lam in rates:
@@ -468,7 +483,9 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             if t > duration_s:
                 break
             arrivals.append((t, *draw_turn()))
+        arrivals = [a for a in arrivals if router.rank_of(a[1]) == rank]
         srv.stats.clear()
+        barrier()
         start = time.perf_counter()
         live, done = [], []
         i = 0
@@ -488,25 +505,44 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
                 (done if turn.done else still).append((at, turn) if not turn.done else (now - at, turn))
             live = still
         wall = time.perf_counter() - start
-        lat = np.array([x for x, _ in done]) if done else np.zeros(1)
-        st = srv.stats
+        st = dict(srv.stats)
+        part = {"wall": wall, "lat": [x for x, _ in done], "stats": st}
+        if world > 1:
+            import torch.distributed as dist
+            parts = [None] * world
+            dist.all_gather_object(parts, part)
+        else:
+            parts = [part]
+        if rank != 0:
+            continue
+        wall = max(pp["wall"] for pp in parts)
+        lat = np.array([x for pp in parts for x in pp["lat"]]) if any(pp["lat"] for pp in parts) else np.zeros(1)
+        tot = collections.Counter()
+        for pp in parts:
+            tot.update(pp["stats"])
+        nturns = sum(len(pp["lat"]) for pp in parts)
         out.append({
-            "rate_req_s": lam, "turns": len(done), "wall_s": wall,
-            "decode_tok_s": st["decode_tokens"] / wall, "write_tok_s": st["write_tokens"] / wall,
-            "prefill_tok_s": st["prefill_tokens"] / wall,
+            "rate_req_s": lam, "turns": nturns, "wall_s": wall,
+            "decode_tok_s": tot["decode_tokens"] / wall, "write_tok_s": tot["write_tokens"] / wall,
+            "prefill_tok_s": tot["prefill_tokens"] / wall,
             "latency_s": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
                           "mean": float(lat.mean())},
-            "mean_decode_batch": st["decode_tokens"] / max(st["decode_steps"], 1),
-            "busy_s": {"prefill": st["prefill_s"], "decode": st["decode_s"], "write": st["write_s"]},
-            "write_batches": st["write_batches"],
-            "decode_ms_per_step": 1e3 * st["decode_s"] / max(st["decode_steps"], 1),
-            "write_ms_per_turn": 1e3 * st["write_s"] / max(len(done), 1),
-            "prefill_ms_per_turn": 1e3 * st["prefill_s"] / max(len(done), 1),
+            "mean_decode_batch": tot["decode_tokens"] / max(tot["decode_steps"], 1),
+            "busy_s": {"prefill": tot["prefill_s"], "decode": tot["decode_s"], "write": tot["write_s"]},
+            "write_batches": tot["write_batches"],
+            "decode_ms_per_step": 1e3 * tot["decode_s"] / max(tot["decode_steps"], 1),
+            "write_ms_per_turn": 1e3 * tot["write_s"] / max(nturns, 1),
+            "prefill_ms_per_turn": 1e3 * tot["prefill_s"] / max(nturns, 1),
+            "turns_per_rank": [len(pp["lat"]) for pp in parts],
         })
         print(json.dumps(out[-1]), file=sys.stderr, flush=True)
-    return {"workload": f"continuous-batching serve sweep (BASELINE config 5) on the {config} model, 1 GPU",
-            "personas": personas, "max_batch": max_batch, "arrivals": "Poisson", "duration_s": duration_s,
-            "write_batch": write_batch, "write_wait_s": write_wait_s,
+    srv.close()
+    if rank != 0:
+        return None
+    return {"workload": f"continuous-batching serve sweep (BASELINE config 5) on the {config} model, "
+                        f"{world} GPU(s), personas partitioned by user id",
+            "n_gpus": world, "personas": personas, "max_batch": max_batch, "arrivals": "Poisson",
+            "duration_s": duration_s, "write_batch": write_batch, "write_wait_s": write_wait_s,
             "writes_overlap_decode": async_writes,
             "prompts": "lognormal, median 256, sigma 1.0, clipped to [16, 2048]",
             "replies": "uniform in [32, 256] tokens, forced length (greedy, stop ids masked)",
@@ -657,13 +693,18 @@ def ours_arm(args, world, rank, local):
         if rank == 0:
             print(json.dumps(decode_workload(device, rank, lib, DEC)), flush=True)
         return 0
-    if args.serve_sweep:          # BASELINE config 5 (minutes per model): one JSON object
+    if args.serve_sweep:          # BASELINE config 5 (minutes per model): one JSON object from rank 0
+        rates = [float(x) for x in args.serve_rates.split(",")]
+        res = serve_sweep(device, lib, args.serve_config, rates, args.serve_seconds,
+                          personas=args.serve_personas, write_batch=args.serve_write_batch,
+                          async_writes=args.serve_async_writes, write_wait_s=args.serve_write_wait,
+                          world=world, rank=rank)
         if rank == 0:
-            rates = [float(x) for x in args.serve_rates.split(",")]
-            print(json.dumps(serve_sweep(device, lib, args.serve_config, rates, args.serve_seconds,
-                                         personas=args.serve_personas, write_batch=args.serve_write_batch,
-                                         async_writes=args.serve_async_writes,
-                                         write_wait_s=args.serve_write_wait)), flush=True)
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
         return 0
     st = make_states(device, seed=1234 + rank)
     B, T = CFG["states"], CFG["tokens"]
