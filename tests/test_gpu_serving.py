@@ -75,3 +75,32 @@ def test_serving_matches_sequential_turns_and_spills_lru(async_writes):
             assert rel_l2(got, getattr(st, n).cpu().numpy()) < 1e-3, (uid, n)
     alice = [h for h in handles if h.user_id == "alice"]
     assert alice[1].result["step"] > alice[0].result["step"] > 0
+
+
+def test_arena_persona_files_round_trip_through_a_fresh_engine(tmp_path):
+    """A persona written by one serving engine in the reference's file format is
+    restored bit-exactly by another engine's arena and resumes there."""
+    cfg = _cfg()
+    sd = reference_init_state_dict(cfg, seed=11)
+    gen = torch.Generator().manual_seed(9)
+    eng = UtttB200(sd, cfg, max_personas=3)
+    srv = ServingEngine(eng, capacity=2, max_batch=2, surprise_threshold=0.0)
+    t = srv.submit("alice", torch.randint(6, cfg.vocab_size, (40,), generator=gen).tolist(), 8)
+    srv.run()
+    assert t.result["step"] > 0
+    path = srv.arena.save_user("alice", tmp_path)
+    assert path.name == "alice_state.pt" and (tmp_path / "alice.pt").exists()
+    saved = srv.arena.export_user("alice")
+
+    eng2 = UtttB200(sd, cfg, max_personas=3)
+    srv2 = ServingEngine(eng2, capacity=2, max_batch=2, surprise_threshold=0.0)
+    assert srv2.arena.load_user("alice", tmp_path)
+    assert not srv2.arena.load_user("bob", tmp_path)
+    srv2.arena.acquire("alice")
+    got = srv2.arena.export_user("alice")
+    for n in ("w_up", "w_gate", "w_down", "s_up", "s_gate", "s_down"):
+        assert torch.equal(got[n], saved[n]), n
+    assert got["step"] == saved["step"]
+    t2 = srv2.submit("alice", torch.randint(6, cfg.vocab_size, (30,), generator=gen).tolist(), 8)
+    srv2.run()
+    assert t2.result["step"] > saved["step"]

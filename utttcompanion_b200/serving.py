@@ -156,6 +156,36 @@ class PersonaArena:
             return self.export_slot(self.slot_of_user[user_id])
         return self.host[user_id]
 
+    def save_user(self, user_id: str, directory, base_signature: Optional[str] = None,
+                  base_fingerprint: Optional[str] = None, drift_metrics: Optional[dict] = None):
+        """Write ``user_id``'s persona (resident or spilled) as a reference persona file,
+        ``{directory}/{user_id}_state.pt`` plus the ``{user_id}.pt`` alias
+        (``DualTrackCheckpointManager._save_state_to_disk``, engine/checkpoint_manager.py:530-563)."""
+        from . import persona_store
+        payload = persona_store.make_payload(user_id, self.export_user(user_id), base_signature, base_fingerprint,
+                                             drift_metrics)
+        return persona_store.write_persona_file(directory, payload)
+
+    def load_user(self, user_id: str, directory, base_fingerprint: Optional[str] = None) -> bool:
+        """Stage ``user_id``'s persona file, if there is one, so the user's next turn resumes
+        from it (validated first; engine/checkpoint_manager.py:335-373).  A resident persona
+        is overwritten in place unless a turn of it is in flight."""
+        from . import persona_store
+        path = persona_store.find_persona_file(directory, user_id)
+        if path is None:
+            return False
+        cfg = self.engine.cfg
+        state, _ = persona_store.read_persona_file(path, user_id, cfg.d_model, cfg.d_ff_fast, base_fingerprint)
+        if user_id in self.slot_of_user:
+            s = self.slot_of_user[user_id]
+            if s in self.pinned:
+                raise ValueError(f"persona {user_id!r} has a turn in flight")
+            self.import_slot(s, state)
+            self.refresh([s])
+        else:
+            self.host[user_id] = state
+        return True
+
 
 @dataclass
 class Turn:
