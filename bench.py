@@ -375,7 +375,8 @@ def decode_workload(device, rank, lib, spec):
 def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     """The 1.58B decode with every persona's hidden units split over all ranks
     (NCCL all-reduce of the readout's z per layer): the same personas, prompts
-    and tokens on every rank; eager packed steps; max-over-ranks step time."""
+    and tokens on every rank; the packed step with its 34 all-reduces captured in
+    one CUDA graph (eager steps if the capture is refused); max-over-ranks step time."""
     import torch.distributed as dist
     from utttcompanion_b200 import workloads as wl
     from utttcompanion_b200.hsplit import HiddenSplit
@@ -405,13 +406,32 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
         tokens, _ = eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))
         pos += 1
     torch.cuda.synchronize()
+    from utttcompanion_b200.model import DecodeGraph
+    graph, mode = None, "graph"
+    try:
+        graph = DecodeGraph(eng, P, packed, down, stop_free=True)
+    except RuntimeError as exc:          # capture of the collectives refused: time eager steps
+        graph, mode = None, f"eager ({str(exc).splitlines()[0][:120]})"
+        torch.cuda.synchronize()
+
+    def one_step(tokens, pos):
+        if graph is not None:
+            return graph.step(tokens, pos)[0]
+        return eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))[0]
+
+    for _ in range(3):
+        tokens = one_step(tokens, pos)
+        pos += 1
+    torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        tokens, _ = eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))
+        tokens = one_step(tokens, pos)
         pos += 1
     e1.record()
+    torch.cuda.synchronize()
+    del graph                            # a graph holding NCCL calls goes before the process group
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / steps], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -422,7 +442,7 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     del packed, down, eng
     return {
         "workload": f"1.58B packed greedy decode, every persona's fast-weight hidden units split over {world} GPUs "
-                    "(NCCL all-reduce of the readout z per layer), eager steps",
+                    f"(NCCL all-reduce of the readout z per layer), {mode} steps",
         "personas": P, "prompts": spec["prompt_desc"],
         "prompt_tokens": {"min": min(lens), "max": max(lens), "mean": float(np.mean(lens))},
         "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,
