@@ -348,3 +348,55 @@ def test_decode_graph_survives_workspace_growth():
         t_e, _ = eng.greedy(lg)
         p_e = p_e + 1
     assert all(float(j[0]) == 7.0 for j in junk)   # the graph wrote into none of them
+
+
+def test_151m_shape_decode_and_write_against_oracle():
+    """BASELINE config 3's model shape (d=768, 12 layers, 12 query heads over 4 KV heads of
+    dim 64, window 512, h=2048, V=32000; reference seed-0 init): a 96-token prompt, 8
+    teacher-forced decode steps at batch 1 (the cluster-split readout, attention and
+    projection finish) and a masked write of prompt + reply (2 chunks x 12 layers).
+
+    At this depth BF16 rounding alone moves the reference's logits by ~5e-2 (its BF16
+    path against its own FP32 path), more than the fixed 2e-2 bound the small models
+    use.  So each step's bound is calibrated by the oracle: the largest |BF16 - FP32|
+    of the oracle's logits at that step, times 1.5 (never below 2e-2)."""
+    from utttcompanion_b200.workloads import CONFIG_151M
+    cfg = CONFIG_151M
+    sd = reference_init_state_dict(cfg, seed=0)
+    eng = UtttB200(sd, cfg, max_personas=1)
+    ocfg = om.ModelConfig(**{k: v for k, v in cfg.to_dict().items() if k in om.ModelConfig.__dataclass_fields__})
+    oracle = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "bf16",
+                            *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
+    gen = torch.Generator().manual_seed(3)
+    prompt = torch.randint(6, cfg.vocab_size, (96,), generator=gen)
+    ost = oracle.state_for_forward(1, update=True)
+    n_steps = 8
+    oid, omargins, olog = oracle.generate_greedy(prompt.numpy(), ost, n_steps)
+    o32 = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "f32",
+                         *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
+    olog32 = o32.teacher_forced_logits(prompt.numpy(), oid, o32.state_for_forward(1, update=True))
+    st = eng.init_fast_state(1)
+    tf = eng.teacher_forced_logits(prompt, oid, st)
+    torch.cuda.synchronize()
+    for step in range(n_steps):
+        ours = tf[step].float().cpu().numpy()
+        noise = float(np.max(np.abs(np.asarray(olog[step], np.float64) - olog32[step])))
+        bound = max(LOGIT_TOL, 1.5 * noise)
+        err = float(np.max(np.abs(ours - olog[step])))
+        assert err <= bound, (step, err, noise)
+        if int(np.argmax(_mask(ours, oracle.active_limit))) != oid[step]:
+            assert omargins[step] <= 2 * bound, (step, omargins[step])
+    turn = prompt.tolist() + oid
+    C = cfg.chunk_size
+    padded = ((len(turn) + C - 1) // C) * C
+    inter = np.array(turn + [0] * (padded - len(turn)))
+    mask = np.array([1.0] * len(turn) + [0.0] * (padded - len(turn)), np.float32)
+    on, oms, opl, _ = oracle.test_time_update(inter[None], ost, mask[None])
+    new, ms, pl = eng.test_time_update(torch.tensor(inter), st, torch.tensor(mask))
+    torch.cuda.synchronize()
+    assert new.step == on.step == (padded // C) * cfg.n_layers
+    for n in ("w_up", "w_gate", "w_down"):
+        got, ref, base = getattr(new, n).cpu().numpy(), getattr(on, n), getattr(ost, n)
+        assert rel_l2(got, ref) < 5e-3, (n, rel_l2(got, ref))
+        assert rel_l2(got - base, ref - base) < 3e-2, (n, rel_l2(got - base, ref - base))
+    np.testing.assert_allclose(pl, opl, rtol=1e-2)
