@@ -490,6 +490,13 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             import torch.distributed as dist
             dist.barrier()
 
+    # bytes a decode step must move: every live persona's BF16 read copies in every layer, and the
+    # shared slow weights (projections + LM head) once per step
+    fast_tok = cfg.n_layers * 3.0 * cfg.d_model * cfg.d_ff_fast * 2.0
+    slow_step = float(sum(x.numel() * x.element_size() for lay in eng.layers for x in (lay.wqkv, lay.wo, lay.w_q,
+                                                                                           lay.w_o)))
+    slow_step += eng.lm_head.numel() * eng.lm_head.element_size()
+    hbm_peak = peaks()[0]
     gw = torch.Generator().manual_seed(seed + 1 + rank)   # warm-up turns of this rank's users; the
     for k in range(4):                                     # shared schedule generator stays in step
         _, ids, rl = draw_turn(gw)
@@ -555,6 +562,12 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             "prefill_ms_per_turn": 1e3 * tot["prefill_s"] / max(nturns, 1),
             "turns_per_rank": [len(pp["lat"]) for pp in parts],
         })
+        # decode HBM rate per GPU: the bytes its steps had to move over its busy decode time (host
+        # scheduling included), averaged over ranks
+        rates_gbs = [(pp["stats"].get("decode_tokens", 0) * fast_tok + pp["stats"].get("decode_steps", 0) * slow_step)
+                     / max(pp["stats"].get("decode_s", 0.0), 1e-9) / 1e9 for pp in parts]
+        out[-1]["decode_hbm_gbs_per_gpu"] = float(np.mean(rates_gbs))
+        out[-1]["decode_hbm_frac"] = float(np.mean(rates_gbs)) / hbm_peak
         print(json.dumps(out[-1]), file=sys.stderr, flush=True)
     srv.close()
     if rank != 0:

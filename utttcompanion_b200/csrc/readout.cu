@@ -16,10 +16,10 @@
 // meet in distributed shared memory, summed in rank order by every CTA, so all
 // of them hold the same h.  KS grows when B * tiles would leave SMs idle (one
 // persona of the 1.58B model has 54 tiles on 148 SMs): each CTA then streams
-// 1/KS of the tile's bytes.  KS is the largest split whose clusters all fit
-// on the GPU at once (the occupancy API counts them; 8-CTA clusters of this
-// kernel fit 48 at a time, so one 1.58B persona uses 4-CTA clusters and a single
-// wave).  The last CTA of a state to finish (device-scope
+// 1/KS of the tile's bytes.  KS (2..8, not only powers of two) is the largest
+// split whose clusters all fit on the GPU at once (the occupancy API counts
+// them; 8-CTA clusters of this kernel fit 48 at a time, so one 1.58B persona's
+// 54 tiles use smaller clusters in a single wave).  The last CTA of a state to finish (device-scope
 // counter) applies the LayerNorm and the residual.  u, g, silu(g), h and z are
 // rounded to BF16 where the reference's autocast rounds them.
 #include <cooperative_groups.h>
@@ -299,17 +299,17 @@ int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __n
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(GTHREADS);
   cfg.stream = st;
-  // The largest K split (a cluster of KS CTAs per tile, d / KS a multiple of 16 columns so the
-  // 16-byte W_down loads stay aligned) whose B * tiles clusters are all resident at once; a
-  // batch too large for any split to fit in one wave runs unsplit.
-  static int ncl_cache[16][2][4];   // resident clusters of 2, 4, 8 CTAs per (device, variant); 0: unknown
+  // The largest K split, 2..8 (a cluster of KS CTAs per tile, d / KS a multiple of 16 columns
+  // so the 16-byte W_down loads stay aligned), whose B * tiles clusters are all resident at
+  // once; a batch too large for any split to fit in one wave runs unsplit.
+  static int ncl_cache[16][2][9];   // resident clusters of k CTAs per (device, variant); 0: unknown
   int dev = 0;
   cudaGetDevice(&dev);
   dev &= 15;
   int KS = 1;
-  for (int k = 8, ki = 3; k >= 2; k >>= 1, --ki) {
+  for (int k = 8; k >= 2; --k) {
     if (d % (16 * k) != 0) continue;
-    int& ncl = ncl_cache[dev][small][ki];
+    int& ncl = ncl_cache[dev][small][k];
     if (ncl == 0) {
       cudaLaunchAttribute ca;
       ca.id = cudaLaunchAttributeClusterDimension;
