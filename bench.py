@@ -348,6 +348,12 @@ def decode_workload(device, rank, lib, spec):
     write_ms = e0.elapsed_time(e1)
     del new
     valid = float(mask.sum())
+    # bytes the write must move: per row-chunk (a persona's 64-token chunk with a valid token) and
+    # layer, FP32 W and S read + written (48 d h) and the chunk-start BF16 read copy read by the
+    # readout (6 d h); per row-chunk once, the read-copy rebuild (FP32 read, BF16 written: 18 d h)
+    row_chunks = sum((len(t) + 63) // 64 for t in turns)
+    dh = float(cfg.d_model) * cfg.d_ff_fast
+    write_bytes = row_chunks * (cfg.n_layers * 54.0 * dh + 18.0 * dh)
     return {
         "workload": f"packed multi-persona greedy decode + per-turn chunk-TTT write ({spec['label']})",
         "model": f"uTTT d={cfg.d_model}, {cfg.n_layers} layers, {cfg.n_heads}/{cfg.n_kv_heads} heads, "
@@ -360,6 +366,8 @@ def decode_workload(device, rank, lib, spec):
                                  "achieved": step_bytes / (dec_ms / 1e3) / 1e9, "unit": "GB/s"},
         "prefill_s_total": prefill_s,
         "write_tok_s": valid / (write_ms / 1e3), "write_padded_tok_s": P * Tpad / (write_ms / 1e3),
+        "write_roofline": {"bound": "hbm", "bytes": write_bytes, "row_chunks": row_chunks,
+                           "achieved": write_bytes / (write_ms / 1e3) / 1e9, "unit": "GB/s"},
         "write_ms": write_ms, "mean_surprise": float(np.mean(surprises)),
         "write_config": {"momentum": cfg.momentum_beta, "clip": cfg.max_inner_grad_norm,
                          "inner_lr": cfg.base_inner_lr},
@@ -879,7 +887,7 @@ def ours_arm(args, world, rank, local):
             "clocks": clk,
         }
         for key, dec in extra.items():
-            for rkey in ("readout_roofline", "decode_step_roofline"):
+            for rkey in ("readout_roofline", "decode_step_roofline", "write_roofline"):
                 if rkey in dec:
                     dec[rkey]["peak"] = hbm
                     dec[rkey]["frac"] = dec[rkey]["achieved"] / hbm
