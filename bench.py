@@ -339,7 +339,9 @@ def decode_workload(device, rank, lib, spec):
         mask[p, :len(t)] = 1.0
     st = FastState(w_up, w_gate, w_down, torch.zeros_like(w_up), torch.zeros_like(w_gate), torch.zeros_like(w_down),
                    eng.ln_w.clone(), eng.ln_b.clone())
-    eng.test_time_update_batch(inter[:, :64], st, mask[:, :64])      # warm-up (workspaces); st is not modified
+    # warm-up on two chunks of every row (workspaces and temporaries at the full row count are
+    # allocated before the timed region); st is not modified
+    eng.test_time_update_batch(inter[:, :128], st, mask[:, :128])
     torch.cuda.synchronize()
     e0.record()
     new, surprises, _ = eng.test_time_update_batch(inter, st, mask)
