@@ -65,7 +65,8 @@ class ModelConfig:
         return asdict(self)
 
 
-# BASELINE.json configs (dims as SURVEY.md section 8 computes them)
+# Model shapes of the benchmark configurations: the tiny CPU-runnable model, the 151M-class decoder and
+# the 1.58B decoder (the dims of the reference's configs/5090_max_config.yaml, with C = 64)
 CONFIG_TINY = ModelConfig(vocab_size=8000, d_model=256, n_layers=4, n_heads=4, n_kv_heads=4, d_ff_fast=688,
                           sliding_window_size=128, chunk_size=64)
 CONFIG_151M = ModelConfig(vocab_size=32000, d_model=768, n_layers=12, n_heads=12, n_kv_heads=4, d_ff_fast=2048,
