@@ -593,7 +593,9 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
 
 
 def micro_case(device, kind, batch, tokens, hist, iters=30):
-    """Kernel profiling cases at the 1.58B layer shape (one JSON object; not a bench line).
+    """Kernel profiling cases at the 1.58B shape (one JSON object; not a bench line).
+
+    ``decode``: one packed decode step of ``batch`` personas through all 34 layers (CUDA graph).
 
     ``readout``: the decode readout (GEMV + fused LayerNorm, d=2560, h=6912) of ``batch``
     rows, each on its own BF16 read copy; 24 copies (2.5 GB) cycle so every call streams
@@ -605,7 +607,29 @@ def micro_case(device, kind, batch, tokens, hist, iters=30):
     lib = _lib.load()
     g = torch.Generator(device=device).manual_seed(0)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if kind == "readout":
+    if kind == "decode":
+        # one packed 1.58B decode step of `batch` personas (each its own perturbed read copies),
+        # replayed from its CUDA graph; bytes = every persona's read copies in every layer + the
+        # slow weights once + each persona's KV window
+        from utttcompanion_b200 import workloads as wl
+        from utttcompanion_b200.model import DecodeGraph, UtttB200
+        cfg = wl.CONFIG_1P58B
+        sd = wl.random_state_dict(cfg, seed=0, device=device)
+        eng = UtttB200(sd, cfg, device=device, max_personas=batch, max_positions=1024)
+        w0 = (sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"], sd["fast_weight_pool.w_down_init"])
+        del sd
+        packed, down = eng.read_copies(*wl.perturbed_persona_states(*w0, batch, 1e-3, seed=1, device=device))
+        graph = DecodeGraph(eng, batch, packed, down, stop_free=True)
+        tok = torch.full((batch,), 7, dtype=torch.int32, device=device)
+        pos = torch.full((batch,), 600, dtype=torch.int32, device=device)
+
+        def call(i):
+            graph.step(tok, pos)
+        slow = sum(x.numel() * x.element_size() for lay in eng.layers for x in (lay.wqkv, lay.wo, lay.w_q, lay.w_o))
+        slow += eng.lm_head.numel() * eng.lm_head.element_size()
+        kv = batch * cfg.n_layers * cfg.sliding_window_size * cfg.n_kv_heads * cfg.head_dim * 2 * 2
+        nbytes = batch * cfg.n_layers * 3 * cfg.d_model * cfg.d_ff_fast * 2 + slow + kv
+    elif kind == "readout":
         from utttcompanion_b200.readout import fast_readout
         d, h, S = 2560, 6912, 24
         packed = (torch.randn(S, d, 2 * h, device=device, generator=g) * 0.02).to(torch.bfloat16)
@@ -929,7 +953,7 @@ def main():
                     help="write on a side stream from a worker thread, overlapping decode")
     ap.add_argument("--only-decode", action="store_true",
                     help="profiling: run only the config-3 decode + write workload (one JSON object, 1 GPU)")
-    ap.add_argument("--micro", choices=("readout", "attn"), default=None,
+    ap.add_argument("--micro", choices=("readout", "attn", "decode"), default=None,
                     help="profiling case: one kernel at the 1.58B layer shape")
     ap.add_argument("--micro-batch", type=int, default=1)
     ap.add_argument("--micro-tokens", type=int, default=64)
