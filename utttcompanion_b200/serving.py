@@ -463,7 +463,8 @@ class ServingEngine:
             outcomes.append((t, s, per_layer[r], gate))
         # every commit and read-copy refresh has landed before a turn is done: the user's next
         # turn (admitted as soon as this one is done) decodes with the written state
-        torch.cuda.current_stream(self.engine.device).synchronize()
+        if self.engine.device.type == "cuda":
+            torch.cuda.current_stream(self.engine.device).synchronize()
         for t, s, pl, gate in outcomes:
             self._finish(t, s, pl, gate)
 
