@@ -865,14 +865,14 @@ def ours_arm(args, world, rank, local):
             torch.cuda.empty_cache()
             if world > 1:
                 dec_ms = max_over_ranks(dec["decode_ms_per_step"])
-                e2e_ms = max_over_ranks(spec["personas"] / dec["decode_e2e_tok_s"] * 1e3)
+                dec_e2e_ms = max_over_ranks(spec["personas"] / dec["decode_e2e_tok_s"] * 1e3)
                 write_ms = max_over_ranks(dec["write_ms"])
                 valid = sum_over_ranks(dec["write_tok_s"] * dec["write_ms"] / 1e3)
                 padded = sum_over_ranks(dec["write_padded_tok_s"] * dec["write_ms"] / 1e3)
                 total = spec["personas"] * world
                 dec.update({"personas_per_gpu": spec["personas"], "personas": total, "n_gpus": world,
                             "decode_tok_s": total / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
-                            "decode_e2e_tok_s": total / (e2e_ms / 1e3), "write_ms": write_ms,
+                            "decode_e2e_tok_s": total / (dec_e2e_ms / 1e3), "write_ms": write_ms,
                             "write_tok_s": valid / (write_ms / 1e3), "write_padded_tok_s": padded / (write_ms / 1e3),
                             "partition": "personas by user id, no collective; step times max over ranks"})
             extra[spec["key"]] = dec
