@@ -248,7 +248,7 @@ int uttt_linear(int M, int N, int K, const void* x, const void* w, int nseg, con
  *   k_ring, v_ring  BF16 (slots, n_kv, W, hd) of one layer
  *   rope_cos/sin    FP32 (positions, hd) tables (RotaryEmbedding, :899-943)
  *   out    BF16 rows (B, out_ld), heads concatenated.
- * hd in {32, 64, 128}, n_heads / n_kv <= 8.
+ * hd in {32, 64, 128}, n_heads / n_kv <= 8, W <= 1024.
  */
 int uttt_attn_decode(int B, int n_heads, int n_kv, int hd, int W, const void* qkv, int qkv_ld, const int* pos,
                      const int* slot, void* k_ring, void* v_ring, const float* rope_cos, const float* rope_sin,
@@ -261,7 +261,10 @@ int uttt_attn_decode(int B, int n_heads, int n_kv, int hd, int W, const void* qk
  *                 hist.. (RoPE'd k, v) and reads all of them.
  *   q_scratch     BF16 (B, T, n_heads, hd) scratch for the RoPE'd queries.
  *   out           BF16 (B, T, n_heads*hd).
- * Query at absolute position p attends keys in (p - W, p].
+ * Query at absolute position p attends keys in (p - W, p].  Head dims 64 and
+ * 128 with n_heads / n_kv <= 8 run on the tensor cores (softmax statistics and
+ * the P.V product keep FP32-level precision); head dim 32 on the CUDA cores.
+ * Requires hist <= start_pos and hist <= W - 1.
  */
 int uttt_attn_prefill(int B, int T, int start_pos, int hist, int n_heads, int n_kv, int hd, int W, const void* qkv,
                       int qkv_ld, const float* rope_cos, const float* rope_sin, void* q_scratch, void* k_buf,
