@@ -90,6 +90,11 @@ struct ChunkParams {
   int ld_ug;
   const int* state_index;
   int n_states;        // > 0: state_index entries must be below it (checked on the device)
+  // bwd d-split (gridDim.z CTAs of a cluster share one hidden tile of one state): the
+  // partial dH / next-chunk U', G' of every CTA, [b][tile][rank][3][128 rows][64 tokens]
+  // FP32, and per (b, tile) two arrival counters (zero before the launch)
+  float* xch;
+  unsigned* xflag;
 };
 
 template <typename WT>
@@ -633,10 +638,63 @@ constexpr int WTILE = HT * QW * 4;        // 16 KB: one staged FP32 tile
 constexpr int NF = 5;                     // FP32 W_down quarter tiles in flight (phase-1 ring)
 constexpr int ZSLOT = 32 * 1024;          // one BF16 [128 d][128 hidden] A tile of the next chunk's Z'
 
+// d-split exchange: the producers of every CTA of a (tile, state) cluster store
+// their partial values (NP parts of one hidden row x 32 token columns) into parts
+// part0.. of their rank's slot, count themselves in on counter `flag_i`, wait
+// (bounded) until every rank has, and replace the values with the sum over ranks
+// in rank order, so all ranks hold the same bits.  A wait that runs out records
+// UTTT_ERR_TIMEOUT and uses what it has.
+template <int NP>
+__device__ __forceinline__ void dsplit_exchange(float (&v)[NP][32], const ChunkParams& p, int part0, int flag_i,
+                                                int row, int c0) {
+  const int KS = gridDim.z, rank = blockIdx.z;
+  const size_t cell = ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * KS;   // [b][tile][rank]
+  auto at = [&](int r, int part) { return p.xch + (((cell + r) * 3 + part) * HT + row) * CT + c0; };
+#pragma unroll
+  for (int k = 0; k < NP; ++k) {
+    float* mine = at(rank, part0 + k);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      *reinterpret_cast<float4*>(mine + i) = make_float4(v[k][i], v[k][i + 1], v[k][i + 2], v[k][i + 3]);
+  }
+  __threadfence();
+  named_bar(1, NPROD);
+  unsigned* flag = p.xflag + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 2 + flag_i;
+  if (threadIdx.x == 0) {
+    atomicAdd(flag, 1u);
+    uint32_t polls = 0;
+    while (*reinterpret_cast<volatile unsigned*>(flag) < (unsigned)KS) {
+      if (++polls > (1u << 22) || status_set(p.status)) {
+        set_status(p.status, UTTT_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  named_bar(1, NPROD);
+  __threadfence();
+#pragma unroll
+  for (int k = 0; k < NP; ++k) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[k][i] = 0.f;
+    for (int r = 0; r < KS; ++r) {
+      const float* src = at(r, part0 + k);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(src + i));
+        v[k][i] += x.x;
+        v[k][i + 1] += x.y;
+        v[k][i + 2] += x.z;
+        v[k][i + 3] += x.w;
+      }
+    }
+  }
+}
+
 // kFuse: also run the NEXT chunk's forward (U', G', H', partial Z') from the
 // weight tiles this kernel just updated, so the separate forward pass over
 // the FP32 masters disappears for every chunk but the first of a call.
-template <bool kMomentum, bool kFuse>
+template <bool kMomentum, bool kFuse, bool kSplit>
 __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const __grid_constant__ CUtensorMap tmDZ,
                                                                 const __grid_constant__ WMaps wm,
@@ -669,8 +727,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     return;
   }
   const int h0 = t * HT;
-  const int nkb = p.d / 64;
-  const int nch = p.d / 128;
+  const int nch_all = p.d / 128;
+  // d-split: the gridDim.z CTAs of a cluster share this (tile, state); rank ksr owns the 128-wide
+  // d chunks [j0, j0 + nch).  Loop counters below are local to that range (barrier phases);
+  // global d coordinates add j0 (chunks), kb0 (64-wide k-blocks) or q0 (32-wide quarters).
+  const int KS = kSplit ? (int)gridDim.z : 1, ksr = kSplit ? (int)blockIdx.z : 0;   // kSplit: a compile-time choice
+  const int nch = kSplit ? nch_all / KS : nch_all, j0 = kSplit ? ksr * nch : 0;
+  const int nkb = kSplit ? 2 * nch : p.d / 64, kb0 = 2 * j0;
+  const int q0 = 4 * j0;
 
   if (tid == 0) {
     for (int i = 0; i < NSLOT; ++i) {
@@ -744,22 +808,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   // (lanes are consecutive hidden rows, so S_up / S_gate accesses coalesce).
   constexpr int bytesA = 2 * WTILE, nbufA = 3;
   constexpr int bytesB = WTILE, nbufB = 4;
-  const int nq = p.d / QW;
+  const int nq = kSplit ? 4 * nch : p.d / QW;   // this rank's 32-wide quarters (local counter)
   const bool fuse = kFuse && update;
   // the next chunk's forward reads the (possibly unchanged) tiles as well
   const bool stage = (update && !skip) || fuse;
-  auto load_a = [&](int qi) {
+  auto load_a = [&](int qi) {            // qi: local quarter
     const int buf = qi % nbufA;
     uint8_t* B0 = slots + buf * bytesA;
     mbar_arrive_expect_tx(&wfullA[buf], 2 * WTILE);
-    tma_load_3d(B0, &wm.up, &wfullA[buf], h0, qi * QW, sb);
-    tma_load_3d(B0 + WTILE, &wm.gate, &wfullA[buf], h0, qi * QW, sb);
+    tma_load_3d(B0, &wm.up, &wfullA[buf], h0, (q0 + qi) * QW, sb);
+    tma_load_3d(B0 + WTILE, &wm.gate, &wfullA[buf], h0, (q0 + qi) * QW, sb);
   };
   auto load_b = [&](int qi) {
     const int buf = qi % nbufB;
     uint8_t* B0 = slots + buf * bytesB;
     mbar_arrive_expect_tx(&wfullB[buf], WTILE);
-    tma_load_3d(B0, &wm.down, &wfullB[buf], qi * QW, h0, sb);
+    tma_load_3d(B0, &wm.down, &wfullB[buf], (q0 + qi) * QW, h0, sb);
   };
   // momentum of this state: s_* (d, h) for up / gate, (h, d) for down
   const size_t s_off = (size_t)sb * p.d * p.h;
@@ -824,6 +888,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       tmem_ld16(tmem_addr(tDH, q * 32, c0), *reinterpret_cast<float(*)[16]>(&dh[0]));
       tmem_ld16(tmem_addr(tDH, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&dh[16]));
       tmem_wait_ld();
+      if constexpr (kSplit) dsplit_exchange(*reinterpret_cast<float(*)[1][32]>(&dh), p, 0, 0, row, c0);   // dH over all of d
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         float du[8], dg[8], hv[8];
@@ -865,7 +930,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       // this quarter's momentum (issued before the waits so its latency overlaps them)
       const bool s_io = update && !skip && row_ok;
       float su[16], sg[16];
-      const size_t so = s_off + (size_t)(qi * QW + cq) * p.h + h0 + row;
+      const size_t so = s_off + (size_t)((q0 + qi) * QW + cq) * p.h + h0 + row;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         su[e] = (kMomentum && s_io) ? p.s_up[so + (size_t)e * p.h] : 0.f;
@@ -945,31 +1010,63 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       const int c0 = half * 32;
       float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
       float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
+      if constexpr (!kSplit) {
 #pragma unroll 1
-      for (int c16 = 0; c16 < 32; c16 += 16) {
-        float u[16], g[16];
-        tmem_ld16(tmem_addr(tUN, q * 32, c0 + c16), u);
-        tmem_ld16(tmem_addr(tGN, q * 32, c0 + c16), g);
-        tmem_wait_ld();
+        for (int c16 = 0; c16 < 32; c16 += 16) {
+          float u[16], g[16];
+          tmem_ld16(tmem_addr(tUN, q * 32, c0 + c16), u);
+          tmem_ld16(tmem_addr(tGN, q * 32, c0 + c16), g);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          us[(size_t)(c0 + c16 + i) * p.hp] = u[i];
-          gs[(size_t)(c0 + c16 + i) * p.hp] = g[i];
+          for (int i = 0; i < 16; ++i) {
+            us[(size_t)(c0 + c16 + i) * p.hp] = u[i];
+            gs[(size_t)(c0 + c16 + i) * p.hp] = g[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 16; i += 8) {
+            uint4 pk;
+            float hv[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float gg2 = g[i + e];
+              hv[e] = (c0 + c16 + i + e < p.Cc_next) ? gg2 * sigmoidf_(gg2) * u[i + e] : 0.f;
+            }
+            pk.x = pack_bf16x2(hv[0], hv[1]);
+            pk.y = pack_bf16x2(hv[2], hv[3]);
+            pk.z = pack_bf16x2(hv[4], hv[5]);
+            pk.w = pack_bf16x2(hv[6], hv[7]);
+            *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + c16 + i) * 2)) = pk;
+          }
+        }
+      } else {
+        float ug[2][32];                                 // U', G' of this thread's row, 32 token columns
+        tmem_ld16(tmem_addr(tUN, q * 32, c0), *reinterpret_cast<float(*)[16]>(&ug[0][0]));
+        tmem_ld16(tmem_addr(tUN, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&ug[0][16]));
+        tmem_ld16(tmem_addr(tGN, q * 32, c0), *reinterpret_cast<float(*)[16]>(&ug[1][0]));
+        tmem_ld16(tmem_addr(tGN, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&ug[1][16]));
+        tmem_wait_ld();
+        dsplit_exchange(ug, p, 1, 1, row, c0);   // U', G' over all of d
+        if (ksr == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            us[(size_t)(c0 + i) * p.hp] = ug[0][i];
+            gs[(size_t)(c0 + i) * p.hp] = ug[1][i];
+          }
         }
 #pragma unroll
-        for (int i = 0; i < 16; i += 8) {
+        for (int i = 0; i < 32; i += 8) {
           uint4 pk;
           float hv[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float gg2 = g[i + e];
-            hv[e] = (c0 + c16 + i + e < p.Cc_next) ? gg2 * sigmoidf_(gg2) * u[i + e] : 0.f;
+            const float gg2 = ug[1][i + e];
+            hv[e] = (c0 + i + e < p.Cc_next) ? gg2 * sigmoidf_(gg2) * ug[0][i + e] : 0.f;
           }
           pk.x = pack_bf16x2(hv[0], hv[1]);
           pk.y = pack_bf16x2(hv[2], hv[3]);
           pk.z = pack_bf16x2(hv[4], hv[5]);
           pk.w = pack_bf16x2(hv[6], hv[7]);
-          *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + c16 + i) * 2)) = pk;
+          *reinterpret_cast<uint4*>(sH + sw128_offset(row, (c0 + i) * 2)) = pk;
         }
       }
       fence_proxy_async_smem();
@@ -1001,7 +1098,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       fence_proxy_async_smem();
       named_bar(2 + half, 128);
       if (zissuer) {
-        tma_reduce_add_2d(&wm.zacc, zstage, mt * 128, b * CT + half * 32);
+        tma_reduce_add_2d(&wm.zacc, zstage, (j0 + mt) * 128, b * CT + half * 32);   // mt: local d tile
         bulk_commit();
       }
     };
@@ -1031,7 +1128,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       const int buf = qi % nbufB;
       // this thread's 16 momentum values of S_down row h0 + row (64 contiguous bytes)
       const bool sd_io = update && !skip && row_ok;
-      const size_t sdo = s_off + (size_t)(h0 + row) * p.d + qi * QW + cq;
+      const size_t sdo = s_off + (size_t)(h0 + row) * p.d + (q0 + qi) * QW + cq;
       float4 sdv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
@@ -1101,8 +1198,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         mbar_wait(&qdoneA[buf], (qi / nbufA) & 1, p.status);
         uint8_t* B0 = slots + buf * bytesA;
         if (!skip) {
-          tma_store_3d(&wm.up, B0, h0, qi * QW, sb);
-          tma_store_3d(&wm.gate, B0 + WTILE, h0, qi * QW, sb);
+          tma_store_3d(&wm.up, B0, h0, (q0 + qi) * QW, sb);
+          tma_store_3d(&wm.gate, B0 + WTILE, h0, (q0 + qi) * QW, sb);
           bulk_commit();
         }
         if (qi + nbufA < nq) {
@@ -1117,7 +1214,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         mbar_wait(&qdoneB[buf], (qi / nbufB) & 1, p.status);
         uint8_t* B0 = slots + buf * bytesB;
         if (!skip) {
-          tma_store_3d(&wm.down, B0, qi * QW, h0, sb);
+          tma_store_3d(&wm.down, B0, (q0 + qi) * QW, h0, sb);
           bulk_commit();
         }
         if (qi + nbufB < nq) {
@@ -1138,26 +1235,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
             const int qi = 2 * kb + hq, fs = qi % NF;
             mbar_wait(&fempty[fs], ((qi / NF) & 1) ^ 1, p.status);
             mbar_arrive_expect_tx(&ffull[fs], WTILE);
-            tma_load_3d(fring1 + fs * WTILE, &wm.down, &ffull[fs], qi * QW, h0, sb);
+            tma_load_3d(fring1 + fs * WTILE, &wm.down, &ffull[fs], (q0 + qi) * QW, h0, sb);
           }
         }
         const int s = it % NSLOT;
         mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full[s], 8192);
-        tma_load_2d(slots + s * BWD_SLOT + 16384, &tmDZ, &full[s], kb * 64, b * CT);
+        tma_load_2d(slots + s * BWD_SLOT + 16384, &tmDZ, &full[s], (kb0 + kb) * 64, b * CT);
       }
       // loop A, in the MMA warp's order of use: K slice 0, then per d chunk j
       // the next chunk's K tile 2j, K slice j+1, K tile 2j+1
       auto kslice = [&](int j) {   // MN-major B of gradW_up / gradW_gate, 128 d
         mbar_wait(&empty3, (j & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full3, 16384);
-        tma_load_3d(slots3, &tmK, &full3, j * 128, p.tok0, b);
-        tma_load_3d(slots3 + 8192, &tmK, &full3, j * 128 + 64, p.tok0, b);
+        tma_load_3d(slots3, &tmK, &full3, (j0 + j) * 128, p.tok0, b);
+        tma_load_3d(slots3 + 8192, &tmK, &full3, (j0 + j) * 128 + 64, p.tok0, b);
       };
       auto knext = [&](int kbi) {  // the next chunk's K tile of 64 d
         if (kbi > 0) mbar_wait(&ug_free, (kbi - 1) & 1, p.status);
         mbar_arrive_expect_tx(&kfull, 8192);
-        tma_load_3d(sKN, &tmK, &kfull, kbi * 64, p.tok0_next, b);
+        tma_load_3d(sKN, &tmK, &kfull, (kb0 + kbi) * 64, p.tok0_next, b);
       };
       const bool fuse = kFuse && update;
       kslice(0);
@@ -1171,8 +1268,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         const int jj = nch + j;
         mbar_wait(&empty3, (jj & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full3, 16384);
-        tma_load_2d(slots3 + 16384, &tmDZ, &full3, j * 128, b * CT);
-        tma_load_2d(slots3 + 24576, &tmDZ, &full3, j * 128 + 64, b * CT);
+        tma_load_2d(slots3 + 16384, &tmDZ, &full3, (j0 + j) * 128, b * CT);
+        tma_load_2d(slots3 + 24576, &tmDZ, &full3, (j0 + j) * 128 + 64, b * CT);
       }
     }
   } else {  // MMA warp
@@ -1285,6 +1382,21 @@ size_t bwd_smem() { return 1024 + NSLOT * BWD_SLOT + 32768 + 3 * 16384 + 2 * 163
 
 using namespace uttt;
 
+namespace uttt {
+namespace {
+// Batches of at most this many rows may split d over 2-CTA clusters in the bwd kernel.
+constexpr int DSPLIT_MAX_B = 4;
+size_t dsplit_xch_bytes(int B, int h) {
+  const size_t tiles = ((size_t)h + HT - 1) / HT;
+  return ws_round((size_t)B * tiles * 2 * 3 * HT * CT * sizeof(float));
+}
+size_t dsplit_flag_bytes(int B, int h) {
+  const size_t tiles = ((size_t)h + HT - 1) / HT;
+  return ws_round((size_t)B * tiles * 2 * sizeof(unsigned));
+}
+}  // namespace
+}  // namespace uttt
+
 extern "C" size_t uttt_chunk_write_workspace(int B, int C, int d, int h) {
   if (B <= 0 || d <= 0 || h <= 0) return 0;
   (void)C;
@@ -1294,6 +1406,7 @@ extern "C" size_t uttt_chunk_write_workspace(int B, int C, int d, int h) {
   bytes += 2 * ws_round((size_t)B * CT * hp * sizeof(float));  // u_save, g_save
   bytes += ws_round((size_t)B * CT * d * 2);                   // dz
   bytes += ws_round((size_t)B * sizeof(float));                 // norm2
+  if (B <= DSPLIT_MAX_B) bytes += dsplit_xch_bytes(B, h) + dsplit_flag_bytes(B, h);   // d-split exchange
   return bytes;
 }
 
@@ -1350,6 +1463,21 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   p.state_index = state_rows;
   p.n_states = n_states;
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
+  // d-split of the bwd kernel: with few rows, 54 hidden tiles per 1.58B state leave SMs idle or
+  // end on a thin last wave; two CTAs per (tile, state), each streaming half of d, finish in
+  // fewer waves.  Used when it saves waves and the caller's workspace holds the exchange area.
+  const int ntiles = (h + HT - 1) / HT;
+  int KS = 1;
+  if (B <= DSPLIT_MAX_B && (d / 128) % 2 == 0) {
+    const long long n = (long long)ntiles * B, sms = num_sms();
+    const long long w1 = (n + sms - 1) / sms, w2 = (2 * n + sms - 1) / sms;
+    const size_t xb = dsplit_xch_bytes(B, h), fb = dsplit_flag_bytes(B, h);
+    if (w2 < 2 * w1 && ws.used + xb + fb <= ws.cap) {
+      p.xch = ws.take<float>(xb / sizeof(float));
+      p.xflag = ws.take<unsigned>(fb / sizeof(unsigned));
+      KS = 2;
+    }
+  }
 
   CUtensorMap tmK, tmDZ;
   {
@@ -1384,18 +1512,38 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   if (!attr_done) {
     UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false, false>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true, false>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<false, true>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_bwd_kernel<true, true>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
+    const void* bwd_kernels[8] = {
+        (const void*)chunk_bwd_kernel<false, false, false>, (const void*)chunk_bwd_kernel<true, false, false>,
+        (const void*)chunk_bwd_kernel<false, true, false>,  (const void*)chunk_bwd_kernel<true, true, false>,
+        (const void*)chunk_bwd_kernel<false, false, true>,  (const void*)chunk_bwd_kernel<true, false, true>,
+        (const void*)chunk_bwd_kernel<false, true, true>,   (const void*)chunk_bwd_kernel<true, true, true>};
+    for (const void* fn : bwd_kernels)
+      UTTT_TRY(cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
     attr_done = true;
   }
   UTTT_TRY(cuda_status(cudaMemsetAsync(p.zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
   const dim3 grid((h + HT - 1) / HT, B);
+  // bwd launch: grid (tiles, rows, KS); with KS > 1 the KS CTAs of a (tile, row) form one
+  // cluster (co-scheduled, so their exchange waits always end) and the exchange counters
+  // start from zero
+  auto launch_bwd = [&](void (*kernel)(const CUtensorMap, const CUtensorMap, const WMaps, const ChunkParams, int),
+                        int update) -> int {
+    if (KS > 1)
+      UTTT_TRY(cuda_status(cudaMemsetAsync(p.xflag, 0, dsplit_flag_bytes(B, h), st)));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ntiles, B, KS);
+    cfg.blockDim = dim3(BWD_THREADS);
+    cfg.dynamicSmemBytes = bwd_smem();
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = KS;
+    cfg.attrs = at;
+    cfg.numAttrs = KS > 1 ? 1 : 0;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmK, tmDZ, wmaps, p, update));
+  };
   // The forward of every chunk but the first runs inside the previous chunk's
   // backward kernel (kFuse), from the weight tiles it has just updated.
   for (int ci = 0; ci < n_chunks; ++ci) {
@@ -1421,9 +1569,9 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     if (max_grad_norm > 0.f) {
       ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
       if (momentum_beta != 0.f)
-        chunk_bwd_kernel<true, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+        UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<true, false, true> : chunk_bwd_kernel<true, false, false>, 0));
       else
-        chunk_bwd_kernel<false, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 0);
+        UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<false, false, true> : chunk_bwd_kernel<false, false, false>, 0));
       UTTT_TRY(launch_status());
       // hidden split: the clip norm runs over every rank's gradient slices
       if (partial_sum && partial_sum(p.norm2, (size_t)B, partial_sum_ctx, stream) != 0) return UTTT_ERR_CUDA;
@@ -1433,14 +1581,14 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
       if (momentum_beta != 0.f) {
         if (fuse)
-          chunk_bwd_kernel<true, true><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<true, true, true> : chunk_bwd_kernel<true, true, false>, 1));
         else
-          chunk_bwd_kernel<true, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<true, false, true> : chunk_bwd_kernel<true, false, false>, 1));
       } else {
         if (fuse)
-          chunk_bwd_kernel<false, true><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<false, true, true> : chunk_bwd_kernel<false, true, false>, 1));
         else
-          chunk_bwd_kernel<false, false><<<grid, BWD_THREADS, bwd_smem(), st>>>(tmK, tmDZ, wmaps, p, 1);
+          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<false, false, true> : chunk_bwd_kernel<false, false, false>, 1));
       }
     }
     UTTT_TRY(launch_status());
