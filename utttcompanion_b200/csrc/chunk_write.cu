@@ -95,6 +95,7 @@ struct ChunkParams {
   // FP32, and per (b, tile) two arrival counters (zero before the launch)
   float* xch;
   unsigned* xflag;
+  int dsplit;          // fwd kernel d-split (its kSplit variant): CTAs per (tile, row), folded into blockIdx.x
 };
 
 template <typename WT>
@@ -166,7 +167,60 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* raw) {
 // ============================================================================
 // fwd: U, G, H and the partial Z of one 128-row hidden tile
 // ============================================================================
-template <typename WT>
+// d-split exchange: the producers of every CTA of a (tile, state) cluster store
+// their partial values (NP parts of one hidden row x 32 token columns) into parts
+// part0.. of their rank's slot, count themselves in on counter `flag_i`, wait
+// (bounded) until every rank has, and replace the values with the sum over ranks
+// in rank order, so all ranks hold the same bits.  A wait that runs out records
+// UTTT_ERR_TIMEOUT and uses what it has.
+// `pair` indexes the (tile, row) whose KS ranks exchange; their slots are [pair][rank][3][128][64].
+template <int NP>
+__device__ __forceinline__ void dsplit_exchange(float (&v)[NP][32], const ChunkParams& p, size_t pair, int KS,
+                                                int rank, int part0, int flag_i, int row, int c0) {
+  const size_t cell = pair * KS;
+  auto at = [&](int r, int part) { return p.xch + (((cell + r) * 3 + part) * HT + row) * CT + c0; };
+#pragma unroll
+  for (int k = 0; k < NP; ++k) {
+    float* mine = at(rank, part0 + k);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      *reinterpret_cast<float4*>(mine + i) = make_float4(v[k][i], v[k][i + 1], v[k][i + 2], v[k][i + 3]);
+  }
+  __threadfence();
+  named_bar(1, NPROD);
+  unsigned* flag = p.xflag + pair * 2 + flag_i;
+  if (threadIdx.x == 0) {
+    atomicAdd(flag, 1u);
+    uint32_t polls = 0;
+    while (*reinterpret_cast<volatile unsigned*>(flag) < (unsigned)KS) {
+      if (++polls > (1u << 22) || status_set(p.status)) {
+        set_status(p.status, UTTT_ERR_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  named_bar(1, NPROD);
+  __threadfence();
+#pragma unroll
+  for (int k = 0; k < NP; ++k) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[k][i] = 0.f;
+    for (int r = 0; r < KS; ++r) {
+      const float* src = at(r, part0 + k);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(src + i));
+        v[k][i] += x.x;
+        v[k][i + 1] += x.y;
+        v[k][i + 2] += x.z;
+        v[k][i + 3] += x.w;
+      }
+    }
+  }
+}
+
+template <typename WT, bool kSplit>
 __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const ChunkParams p) {
   using Q = Quad<WT>;
@@ -179,14 +233,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // one chunk (t = hidden tile, b = state) or, in tiles mode, every 64-token tile of a readout
   // (x = token tile, fastest, so the CTAs that share a hidden tile's weights run together)
-  const int t = p.tiles ? blockIdx.y : blockIdx.x, b = p.tiles ? blockIdx.z : blockIdx.y;
-  const int tok0 = p.tiles ? blockIdx.x * CT : p.tok0;
+  // kSplit: the p.dsplit CTAs of a cluster (consecutive blockIdx.x) share one (tile, row) and each
+  // reduces U, G over its share of d (exchanged before H) and forms Z for its share of d's columns
+  const int KS = kSplit ? p.dsplit : 1;
+  const int xb = kSplit ? (int)blockIdx.x / KS : (int)blockIdx.x, ksr = kSplit ? (int)blockIdx.x % KS : 0;
+  const int t = p.tiles ? blockIdx.y : xb, b = p.tiles ? blockIdx.z : blockIdx.y;
+  const int tok0 = p.tiles ? xb * CT : p.tok0;
   const int Cc = p.tiles ? min(CT, p.T - tok0) : p.Cc;
   const int zr = p.z_rows ? p.z_rows : CT;
   const size_t zrow0 = (size_t)b * zr + (p.tiles ? tok0 : 0);   // this tile's first zacc row
   const int h0 = t * HT;
-  const int nkb = p.d / 64;
-  const int nmt = p.d / 128;
+  const int nkb = kSplit ? p.d / 64 / KS : p.d / 64, kb0 = ksr * nkb;     // local k-blocks of U, G
+  const int nmt = kSplit ? p.d / 128 / KS : p.d / 128, mt0 = ksr * nmt;   // local d tiles of Z
   if (p.state_index && p.n_states > 0 && (unsigned)p.state_index[b] >= (unsigned)p.n_states) {
     if (tid == 0) set_status(p.status, UTTT_ERR_INVALID);   // a bad row -> state map entry: touch nothing
     return;
@@ -231,7 +289,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         const int idx = tid + j * NPROD;  // 0..2047
         const int kr = idx >> 5, c4 = (idx & 31) * 4;
         const int col = h0 + c4;
-        const size_t off = (size_t)(kb * 64 + kr) * p.ld_ug + col;
+        const size_t off = (size_t)((kb0 + kb) * 64 + kr) * p.ld_ug + col;
         if (col < p.h) {
           fu[j] = Q::load(wu + off);
           fg[j] = Q::load(wg + off);
@@ -265,7 +323,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       tmem_ld16(tmem_addr(tG, q * 32, c0), *reinterpret_cast<float(*)[16]>(&g[0]));
       tmem_ld16(tmem_addr(tG, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&g[16]));
       tmem_wait_ld();
-      if (p.u_save) {
+      if constexpr (kSplit) {   // U, G over all of d (exchange counter 0, zeroed before the launch)
+        float ug[2][32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          ug[0][i] = u[i];
+          ug[1][i] = g[i];
+        }
+        const int ntile = p.tiles ? (int)gridDim.y : (int)gridDim.x / KS;
+        dsplit_exchange(ug, p, (size_t)b * ntile + t, KS, ksr, 1, 0, row, c0);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          u[i] = ug[0][i];
+          g[i] = ug[1][i];
+        }
+      }
+      if (p.u_save && ksr == 0) {
         float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
         float* gs = p.g_save + (size_t)b * CT * p.hp + h0 + row;
 #pragma unroll
@@ -307,7 +380,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         const int idx = tid + j * NPROD;  // 0..4095
         const int hh = idx >> 5, c4 = (idx & 31) * 4;
         typename Q::V f = Q::zero();
-        if (h0 + hh < p.h) f = Q::load(wd + (size_t)(h0 + hh) * p.d + mt * 128 + c4);
+        if (h0 + hh < p.h) f = Q::load(wd + (size_t)(h0 + hh) * p.d + (mt0 + mt) * 128 + c4);
         *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = Q::pack(f);
       }
       fence_proxy_async_smem();
@@ -326,7 +399,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&zfree[zb]);
-        float* za = p.zacc + zrow0 * p.d + pm * 128 + row;
+        float* za = p.zacc + zrow0 * p.d + (mt0 + pm) * 128 + row;
         for (int i = 0; i < 32; ++i)
           if (c0 + i < Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
       }
@@ -341,7 +414,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
       tmem_wait_ld();
-      float* za = p.zacc + zrow0 * p.d + pm * 128 + row;
+      float* za = p.zacc + zrow0 * p.d + (mt0 + pm) * 128 + row;
       for (int i = 0; i < 32; ++i)
         if (c0 + i < Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
     }
@@ -353,7 +426,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
         const int s = it % NSLOT;
         mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full[s], 8192);
-        tma_load_3d(slots + s * SLOT_BYTES + 32768, &tmK, &full[s], kb * 64, tok0, b);
+        tma_load_3d(slots + s * SLOT_BYTES + 32768, &tmK, &full[s], (kb0 + kb) * 64, tok0, b);
       }
       for (int mt = 0; mt < nmt; ++mt, ++it) {
         const int s = it % NSLOT;
@@ -638,59 +711,6 @@ constexpr int WTILE = HT * QW * 4;        // 16 KB: one staged FP32 tile
 constexpr int NF = 5;                     // FP32 W_down quarter tiles in flight (phase-1 ring)
 constexpr int ZSLOT = 32 * 1024;          // one BF16 [128 d][128 hidden] A tile of the next chunk's Z'
 
-// d-split exchange: the producers of every CTA of a (tile, state) cluster store
-// their partial values (NP parts of one hidden row x 32 token columns) into parts
-// part0.. of their rank's slot, count themselves in on counter `flag_i`, wait
-// (bounded) until every rank has, and replace the values with the sum over ranks
-// in rank order, so all ranks hold the same bits.  A wait that runs out records
-// UTTT_ERR_TIMEOUT and uses what it has.
-template <int NP>
-__device__ __forceinline__ void dsplit_exchange(float (&v)[NP][32], const ChunkParams& p, int part0, int flag_i,
-                                                int row, int c0) {
-  const int KS = gridDim.z, rank = blockIdx.z;
-  const size_t cell = ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * KS;   // [b][tile][rank]
-  auto at = [&](int r, int part) { return p.xch + (((cell + r) * 3 + part) * HT + row) * CT + c0; };
-#pragma unroll
-  for (int k = 0; k < NP; ++k) {
-    float* mine = at(rank, part0 + k);
-#pragma unroll
-    for (int i = 0; i < 32; i += 4)
-      *reinterpret_cast<float4*>(mine + i) = make_float4(v[k][i], v[k][i + 1], v[k][i + 2], v[k][i + 3]);
-  }
-  __threadfence();
-  named_bar(1, NPROD);
-  unsigned* flag = p.xflag + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 2 + flag_i;
-  if (threadIdx.x == 0) {
-    atomicAdd(flag, 1u);
-    uint32_t polls = 0;
-    while (*reinterpret_cast<volatile unsigned*>(flag) < (unsigned)KS) {
-      if (++polls > (1u << 22) || status_set(p.status)) {
-        set_status(p.status, UTTT_ERR_TIMEOUT);
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  named_bar(1, NPROD);
-  __threadfence();
-#pragma unroll
-  for (int k = 0; k < NP; ++k) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[k][i] = 0.f;
-    for (int r = 0; r < KS; ++r) {
-      const float* src = at(r, part0 + k);
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 x = __ldcg(reinterpret_cast<const float4*>(src + i));
-        v[k][i] += x.x;
-        v[k][i + 1] += x.y;
-        v[k][i + 2] += x.z;
-        v[k][i + 3] += x.w;
-      }
-    }
-  }
-}
-
 // kFuse: also run the NEXT chunk's forward (U', G', H', partial Z') from the
 // weight tiles this kernel just updated, so the separate forward pass over
 // the FP32 masters disappears for every chunk but the first of a call.
@@ -888,7 +908,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       tmem_ld16(tmem_addr(tDH, q * 32, c0), *reinterpret_cast<float(*)[16]>(&dh[0]));
       tmem_ld16(tmem_addr(tDH, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&dh[16]));
       tmem_wait_ld();
-      if constexpr (kSplit) dsplit_exchange(*reinterpret_cast<float(*)[1][32]>(&dh), p, 0, 0, row, c0);   // dH over all of d
+      if constexpr (kSplit)   // dH over all of d
+        dsplit_exchange(*reinterpret_cast<float(*)[1][32]>(&dh), p, (size_t)b * gridDim.x + t, KS, ksr, 0, 0, row, c0);
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         float du[8], dg[8], hv[8];
@@ -1045,7 +1066,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         tmem_ld16(tmem_addr(tGN, q * 32, c0), *reinterpret_cast<float(*)[16]>(&ug[1][0]));
         tmem_ld16(tmem_addr(tGN, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&ug[1][16]));
         tmem_wait_ld();
-        dsplit_exchange(ug, p, 1, 1, row, c0);   // U', G' over all of d
+        dsplit_exchange(ug, p, (size_t)b * gridDim.x + t, KS, ksr, 1, 1, row, c0);   // U', G' over all of d
         if (ksr == 0) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -1394,6 +1415,44 @@ size_t dsplit_flag_bytes(int B, int h) {
   const size_t tiles = ((size_t)h + HT - 1) / HT;
   return ws_round((size_t)B * tiles * 2 * sizeof(unsigned));
 }
+// 2 when splitting d over 2-CTA clusters saves waves for n one-CTA-per-SM work items
+int dsplit_factor(long long n) {
+  const long long sms = num_sms();
+  const long long w1 = (n + sms - 1) / sms, w2 = (2 * n + sms - 1) / sms;
+  return w2 < 2 * w1 ? 2 : 1;
+}
+// The fwd kernel on `grid` (one CTA per (tile, row)); with KS > 1 its KS-CTA split variant on
+// (grid.x * KS, grid.y, grid.z), each cluster one (tile, row), exchange counters zeroed first.
+template <typename WT>
+int launch_fwd(const CUtensorMap& tm, ChunkParams p, dim3 grid, int KS, size_t flag_bytes, cudaStream_t st) {
+  if (KS <= 1) {
+    chunk_fwd_kernel<WT, false><<<grid, NTHREADS, fwd_smem(), st>>>(tm, p);
+    return launch_status();
+  }
+  p.dsplit = KS;
+  UTTT_TRY(cuda_status(cudaMemsetAsync(p.xflag, 0, flag_bytes, st)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid.x * KS, grid.y, grid.z);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = fwd_smem();
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = KS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, chunk_fwd_kernel<WT, true>, tm, p));
+}
+int set_fwd_attributes() {
+  const void* fns[4] = {(const void*)chunk_fwd_kernel<float, false>, (const void*)chunk_fwd_kernel<float, true>,
+                        (const void*)chunk_fwd_kernel<__nv_bfloat16, false>,
+                        (const void*)chunk_fwd_kernel<__nv_bfloat16, true>};
+  for (const void* fn : fns)
+    UTTT_TRY(cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+  return UTTT_OK;
+}
 }  // namespace
 }  // namespace uttt
 
@@ -1469,10 +1528,8 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   const int ntiles = (h + HT - 1) / HT;
   int KS = 1;
   if (B <= DSPLIT_MAX_B && (d / 128) % 2 == 0) {
-    const long long n = (long long)ntiles * B, sms = num_sms();
-    const long long w1 = (n + sms - 1) / sms, w2 = (2 * n + sms - 1) / sms;
     const size_t xb = dsplit_xch_bytes(B, h), fb = dsplit_flag_bytes(B, h);
-    if (w2 < 2 * w1 && ws.used + xb + fb <= ws.cap) {
+    if (dsplit_factor((long long)ntiles * B) == 2 && ws.used + xb + fb <= ws.cap) {
       p.xch = ws.take<float>(xb / sizeof(float));
       p.xflag = ws.take<unsigned>(fb / sizeof(unsigned));
       KS = 2;
@@ -1510,8 +1567,7 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   }
   static bool attr_done = false;
   if (!attr_done) {
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    UTTT_TRY(set_fwd_attributes());
     const void* bwd_kernels[8] = {
         (const void*)chunk_bwd_kernel<false, false, false>, (const void*)chunk_bwd_kernel<true, false, false>,
         (const void*)chunk_bwd_kernel<false, true, false>,  (const void*)chunk_bwd_kernel<true, true, false>,
@@ -1555,7 +1611,7 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     p.Cc_next = fuse ? ((T - p.tok0_next) < C ? (T - p.tok0_next) : C) : 0;
     if (ci == 0) {
       ProfScope ps(UTTT_PROF_CHUNK_FWD, st);
-      chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmK, p);
+      UTTT_TRY(launch_fwd<float>(tmK, p, grid, KS, dsplit_flag_bytes(B, h), st));
     }
     UTTT_TRY(launch_status());
     // hidden split: this chunk's Z is the sum of every rank's partial Z
@@ -1625,8 +1681,7 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
                                  1, st);
   static bool attr_done = false;
   if (!attr_done) {
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    UTTT_TRY(set_fwd_attributes());
     attr_done = true;
   }
   ChunkParams p;
@@ -1651,9 +1706,7 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
     uint32_t box[3] = {64, 64, 1};
     UTTT_TRY(make_tmap_bf16(&tmX, x, 3, dims, str, box));
   }
-  chunk_fwd_kernel<__nv_bfloat16><<<dim3((T + CT - 1) / CT, (h + HT - 1) / HT, B), NTHREADS, fwd_smem(), st>>>(tmX,
-                                                                                                           p);
-  return launch_status();
+  return launch_fwd<__nv_bfloat16>(tmX, p, dim3((T + CT - 1) / CT, (h + HT - 1) / HT, B), 1, 0, st);
 }
 
 extern "C" int uttt_readout_finish(int B, int d, const float* z, const void* x, const float* ln_weight,
@@ -1669,8 +1722,10 @@ extern "C" int uttt_readout_finish(int B, int d, const float* z, const void* x, 
 
 extern "C" size_t uttt_fast_readout_workspace(int B, int T, int d, int h) {
   if (B <= 0 || T <= 0 || d <= 0 || h <= 0) return 0;
-  (void)h;
-  return 256 + ws_round((size_t)B * (T > CT ? T : CT) * d * sizeof(float));
+  size_t bytes = 256 + ws_round((size_t)B * (T > CT ? T : CT) * d * sizeof(float));
+  // one token tile of a few rows: room for the d-split exchange of the tensor-core readout
+  if (T > 1 && T <= CT && B <= DSPLIT_MAX_B) bytes += dsplit_xch_bytes(B, h) + dsplit_flag_bytes(B, h);
+  return bytes;
 }
 
 extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, const void* w_up,
@@ -1704,10 +1759,7 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
   UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * T * d * sizeof(float), st)));
   static bool attr_done = false;
   if (!attr_done) {
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<float>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(chunk_fwd_kernel<__nv_bfloat16>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fwd_smem())));
+    UTTT_TRY(set_fwd_attributes());
     attr_done = true;
   }
   ChunkParams p;
@@ -1742,12 +1794,24 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
     UTTT_TRY(make_tmap_bf16(&tmX, x, 3, dims, str, box));
   }
   const dim3 grid((T + CT - 1) / CT, (h + HT - 1) / HT, B);
+  // one token tile of a few rows (the write path's per-layer readout of a chunk): split d over
+  // 2-CTA clusters when that saves waves and the workspace holds the exchange area
+  int KS = 1;
+  const size_t fbytes = dsplit_flag_bytes(B, h);
+  if (T > 1 && T <= CT && B <= DSPLIT_MAX_B && (d / 128) % 2 == 0 && dsplit_factor((long long)grid.y * B) == 2) {
+    const size_t xb = dsplit_xch_bytes(B, h);
+    if (ws.used + xb + fbytes <= ws.cap) {
+      p.xch = ws.take<float>(xb / sizeof(float));
+      p.xflag = ws.take<unsigned>(fbytes / sizeof(unsigned));
+      KS = 2;
+    }
+  }
   {
     ProfScope ps(UTTT_PROF_READOUT, st);
     if (w_dtype == UTTT_DTYPE_BF16)
-      chunk_fwd_kernel<__nv_bfloat16><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
+      UTTT_TRY(launch_fwd<__nv_bfloat16>(tmX, p, grid, KS, fbytes, st));
     else
-      chunk_fwd_kernel<float><<<grid, NTHREADS, fwd_smem(), st>>>(tmX, p);
+      UTTT_TRY(launch_fwd<float>(tmX, p, grid, KS, fbytes, st));
   }
   UTTT_TRY(launch_status());
   {
