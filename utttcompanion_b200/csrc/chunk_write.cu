@@ -869,7 +869,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
             const int idx = tid + j * NPROD;  // 0..1023 : 128 rows x 8 float4
             f[j] = *reinterpret_cast<const float4*>(src + sw128_offset(idx >> 3, (idx & 7) * 16));
           }
-          mbar_arrive(&fempty[fs]);
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j) f[j] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -883,6 +882,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
           pk.y = pack_bf16x2(f[j].z, f[j].w);
           *reinterpret_cast<uint2*>(sA + sw128_offset(hh, (hq * QW + c4) * 2)) = pk;
         }
+        // the ring tile is released only once its values are used: an arrive right after the
+        // shared loads let the TMA refill overwrite a tile before a delayed load had read it
+        if (!skip) mbar_arrive(&fempty[(2 * kb + hq) % NF]);
       }
       fence_proxy_async_smem();
       mbar_arrive(&full[s]);
