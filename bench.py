@@ -31,6 +31,7 @@ import os
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import numpy as np
@@ -65,18 +66,63 @@ def traffic_record():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU while the timed region runs:
+    read through NVML every 20 ms by a background thread (the device found by its PCI bus id), or,
+    without NVML, from an nvidia-smi loop every 200 ms.  Read-only: no setting is changed."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h): reported name -> mask
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4))
+    PERIOD_S = 0.02
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
         self.path = None
+        self.nv = None
+        self.thread = None
+
+    def _nvml_start(self) -> bool:
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                pr = torch.cuda.get_device_properties(self.idx)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nv, self.handle, self.reasons_fn = pynvml, handle, reasons
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+            self.samples, self.bits = [], 0
+            self.halt = threading.Event()
+            self._sample()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+            return True
+        except Exception:
+            self.nv = None
+            return False
+
+    def _sample(self):
+        try:
+            self.samples.append(float(self.nv.nvmlDeviceGetClockInfo(self.handle, self.nv.NVML_CLOCK_SM)))
+            self.bits |= int(self.reasons_fn(self.handle))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self.halt.wait(self.PERIOD_S):
+            self._sample()
 
     def start(self):
+        if self._nvml_start():
+            return
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -88,6 +134,19 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.nv is not None:
+            self.halt.set()
+            self.thread.join(timeout=5)
+            self._sample()
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
+            if not self.samples:
+                return None
+            return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(nm for nm, bit in self.REASON_BITS if self.bits & bit),
+                    "samples": len(self.samples), "source": f"NVML every {int(self.PERIOD_S * 1000)} ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -115,7 +174,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi every 200 ms"}
 
 
 def dist_env():
