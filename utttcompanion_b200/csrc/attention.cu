@@ -250,12 +250,11 @@ template <int HD, int REP>
 int launch_attn_decode(int B, int n_kv, int W, const __nv_bfloat16* qkv, int qkv_ld, const int* pos, const int* slot,
                        __nv_bfloat16* kring, __nv_bfloat16* vring, const float* cos_t, const float* sin_t, float scale,
                        __nv_bfloat16* out, int out_ld, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(attn_decode_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)(dec_smem_floats(HD, REP, MAX_W) * sizeof(float)))));
-    attr = true;
-  }
+  static DeviceOnce attr;
+  UTTT_TRY(run_once_per_device(attr, [] {
+    return cuda_status(cudaFuncSetAttribute(attn_decode_kernel<HD, REP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)(dec_smem_floats(HD, REP, MAX_W) * sizeof(float))));
+  }));
   // split the ring over a cluster while the batch leaves SMs idle (at least 16 slots per CTA)
   int S = 1;
   while (S < 8 && (long long)B * n_kv * S < 2LL * num_sms() && W % (2 * S) == 0 && W / (2 * S) >= 16) S *= 2;
@@ -699,12 +698,11 @@ extern "C" int uttt_attn_prefill(int B, int T, int start_pos, int hist, int n_he
     const dim3 tgrid((T + qbk - 1) / qbk, n_kv, B);
 #define UTTT_TP(HDV)                                                                                            \
   do {                                                                                                          \
-    static bool attr_set = false;                                                                               \
-    if (!attr_set) {                                                                                            \
-      UTTT_TRY(cuda_status(cudaFuncSetAttribute(attn_prefill_tc_kernel<HDV>,                                    \
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize, TpLayout<HDV>::SMEM))); \
-      attr_set = true;                                                                                          \
-    }                                                                                                           \
+    static DeviceOnce attr_set;                                                                                 \
+    UTTT_TRY(run_once_per_device(attr_set, [] {                                                                 \
+      return cuda_status(cudaFuncSetAttribute(attn_prefill_tc_kernel<HDV>,                                      \
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, TpLayout<HDV>::SMEM)); \
+    }));                                                                                                        \
     attn_prefill_tc_kernel<HDV><<<tgrid, TP_THREADS, TpLayout<HDV>::SMEM, st>>>(                                \
         tmK, tmV, (const __nv_bfloat16*)q_scratch, T, hist, L, n_heads, n_kv, rep, W, scale, (__nv_bfloat16*)out); \
   } while (0)

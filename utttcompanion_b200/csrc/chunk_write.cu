@@ -1567,8 +1567,8 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
     uint32_t box_z[2] = {128, 32};
     UTTT_TRY(make_tmap_f32(&wmaps.zacc, p.zacc, 2, dims_z, str_z, box_z, false));
   }
-  static bool attr_done = false;
-  if (!attr_done) {
+  static DeviceOnce attr_done;
+  UTTT_TRY(run_once_per_device(attr_done, [] {
     UTTT_TRY(set_fwd_attributes());
     const void* bwd_kernels[8] = {
         (const void*)chunk_bwd_kernel<false, false, false>, (const void*)chunk_bwd_kernel<true, false, false>,
@@ -1577,8 +1577,8 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
         (const void*)chunk_bwd_kernel<false, true, true>,   (const void*)chunk_bwd_kernel<true, true, true>};
     for (const void* fn : bwd_kernels)
       UTTT_TRY(cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
-    attr_done = true;
-  }
+    return (int)UTTT_OK;
+  }));
   UTTT_TRY(cuda_status(cudaMemsetAsync(p.zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
   const dim3 grid((h + HT - 1) / HT, B);
   // bwd launch: grid (tiles, rows, KS); with KS > 1 the KS CTAs of a (tile, row) form one
@@ -1681,11 +1681,8 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
     return launch_readout_decode(B, d, h, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_packed,
                                  (const __nv_bfloat16*)w_down, state_index, nullptr, nullptr, 1.f, z, nullptr, nullptr,
                                  1, st);
-  static bool attr_done = false;
-  if (!attr_done) {
-    UTTT_TRY(set_fwd_attributes());
-    attr_done = true;
-  }
+  static DeviceOnce attr_done;
+  UTTT_TRY(run_once_per_device(attr_done, [] { return set_fwd_attributes(); }));
   ChunkParams p;
   memset(&p, 0, sizeof(p));
   p.B = B; p.T = T; p.C = CT; p.d = d; p.h = h; p.hp = (h + 127) / 128 * 128;
@@ -1759,11 +1756,8 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
                                  ob, st);
   }
   UTTT_TRY(cuda_status(cudaMemsetAsync(zacc, 0, (size_t)B * T * d * sizeof(float), st)));
-  static bool attr_done = false;
-  if (!attr_done) {
-    UTTT_TRY(set_fwd_attributes());
-    attr_done = true;
-  }
+  static DeviceOnce attr_done;
+  UTTT_TRY(run_once_per_device(attr_done, [] { return set_fwd_attributes(); }));
   ChunkParams p;
   memset(&p, 0, sizeof(p));
   p.B = B; p.T = T; p.C = CT; p.d = d; p.h = h; p.hp = (h + 127) / 128 * 128;

@@ -325,12 +325,11 @@ extern "C" int uttt_linear(int M, int N, int K, const void* x, const void* w, in
     UTTT_TRY(make_tmap_bf16(&tmX, x, 2, dims, str, box));
   }
   const size_t smem = 1024 + (size_t)G_STAGES * (16384 + TN * 128);
-  static bool attr = false;
-  if (!attr) {
-    UTTT_TRY(cuda_status(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)(1024 + G_STAGES * (16384 + 256 * 128)))));
-    attr = true;
-  }
+  static DeviceOnce attr;
+  UTTT_TRY(run_once_per_device(attr, [] {
+    return cuda_status(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)(1024 + G_STAGES * (16384 + 256 * 128))));
+  }));
   {
     ProfScope ps(UTTT_PROF_GEMM, st);
     cudaLaunchConfig_t gc = {};

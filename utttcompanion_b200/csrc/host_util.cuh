@@ -9,6 +9,9 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/uttt_b200.h"
 
 namespace uttt {
@@ -19,6 +22,28 @@ inline int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return UTTT_OK;
   last_cuda_error_ref() = (int)e;
   return UTTT_ERR_CUDA;
+}
+
+// A launcher's set-up step (a kernel's dynamic shared-memory limit, which belongs to
+// the device it is set on) run once per device by whichever thread launches there
+// first; its status is kept and returned to every later caller on that device.
+struct DeviceOnce {
+  std::mutex mu;
+  std::atomic<int> done[64];   // 0: not run yet; otherwise the step's status + 1
+};
+template <class F>
+inline int run_once_per_device(DeviceOnce& once, F&& step) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return UTTT_ERR_CUDA;
+  int s = once.done[dev].load(std::memory_order_acquire);
+  if (s) return s - 1;
+  std::lock_guard<std::mutex> g(once.mu);
+  s = once.done[dev].load(std::memory_order_relaxed);
+  if (!s) {
+    s = step() + 1;
+    once.done[dev].store(s, std::memory_order_release);
+  }
+  return s - 1;
 }
 
 // Check the launch that was just issued.
