@@ -11,7 +11,9 @@ scripted position, so the test checks the scheduler itself:
   caps it;
 - LRU spill of the persona arena and the deferral of a turn that finds every
   slot pinned;
-- batched writes (``write_batch``) and the result fields of each turn.
+- batched writes (``write_batch``) and the result fields of each turn;
+- the streaming event sequence of ``stream_interact_and_evolve``
+  (``engine/personalizer.py:369-583``): token events, then ``ttt_status``.
 """
 
 import torch
@@ -133,3 +135,34 @@ def test_writes_are_batched(monkeypatch):
     srv.run()
     assert all(t.done for t in turns)
     assert [n for n, _ in eng.writes] == [3, 3]
+
+
+def test_streaming_turn_events(monkeypatch):
+    # the event sequence of stream_interact_and_evolve: one token event per reply token as it is
+    # decoded (EOS included, as the reference yields it), then ttt_status with the result
+    eng, srv = _server(monkeypatch, capacity=4, max_batch=4, stops={23: EOS_ID})
+    other = srv.submit("b", [7] * 30, max_new_tokens=6)          # advances with the stream
+    gen = srv.stream_interact_and_evolve("a", [7] * 20, max_new_tokens=10)
+    events = []
+    try:
+        while True:
+            events.append(next(gen))
+    except StopIteration as stop:
+        result = stop.value
+    assert [e["type"] for e in events] == ["token"] * 4 + ["ttt_status"]
+    assert [e["token_id"] for e in events[:4]] == [30, 31, 32, EOS_ID]
+    assert events[-1]["result"] is result and result["reply_ids"] == [30, 31, 32, EOS_ID]
+    assert result["gate_triggered"] and result["user_id"] == "a"
+    srv.run()
+    assert other.done and len(other.result["reply_ids"]) == 6
+    # callbacks of submitted turns see the same sequence
+    seen = []
+    t = srv.submit("c", [7] * 5, max_new_tokens=3, on_event=seen.append)
+    srv.run()
+    assert [e["type"] for e in seen] == ["token"] * 3 + ["ttt_status"] and seen[-1]["result"] is t.result
+    for bad in (0, 2.0, "3"):
+        try:
+            srv.submit("d", [7], max_new_tokens=bad)
+        except ValueError:
+            continue
+        raise AssertionError(bad)

@@ -29,7 +29,7 @@ import queue
 import threading
 import time
 from dataclasses import dataclass, field
-from typing import Deque, Dict, List, Optional
+from typing import Any, Callable, Deque, Dict, Generator, List, Optional
 
 import torch
 
@@ -200,6 +200,10 @@ class Turn:
     decoded: bool = False
     done: bool = False
     result: Optional[dict] = None
+    # called with {"type": "token", "token_id": id} for every reply token as it is accepted, then
+    # once with {"type": "ttt_status", "result": result} when the turn is done (on the thread that
+    # finished it: the worker thread with async writes)
+    on_event: Optional[Callable[[dict], None]] = None
 
 
 class ServingEngine:
@@ -266,10 +270,12 @@ class ServingEngine:
 
     # ------------------------------------------------------------------ API
     def submit(self, user_id: str, prompt_ids: List[int], max_new_tokens: int = 128,
-               eos_token_id: Optional[int] = EOS_ID) -> Turn:
+               eos_token_id: Optional[int] = EOS_ID, on_event: Optional[Callable[[dict], None]] = None) -> Turn:
         if not prompt_ids:
             raise ValueError("empty prompt")
-        t = Turn(str(user_id), list(prompt_ids), max_new_tokens, eos_token_id)
+        if type(max_new_tokens) is not int or max_new_tokens < 1:
+            raise ValueError("max_new_tokens must be a positive integer")
+        t = Turn(str(user_id), list(prompt_ids), max_new_tokens, eos_token_id, on_event=on_event)
         self.waiting.append(t)
         return t
 
@@ -326,6 +332,25 @@ class ServingEngine:
             self.step()
         return t.result
 
+    def stream_interact_and_evolve(self, user_id: str, prompt_ids: List[int],
+                                   max_new_tokens: int = 128) -> Generator[Dict[str, Any], None, dict]:
+        """Streaming one-turn API, the event sequence of
+        ``uTTTPersonalizer.stream_interact_and_evolve`` (``engine/personalizer.py:369-583``):
+        ``{"type": "token", ...}`` for each reply token as it is decoded, then, once the
+        test-time update and the stability guard have run, ``{"type": "ttt_status",
+        "result": ...}``; the generator returns the result.  Token events carry token ids
+        (``token_id``); the reference's ``content`` strings come from its tokenizer.  This
+        generator drives the engine itself, so other submitted turns advance with it."""
+        events: Deque[dict] = collections.deque()
+        t = self.submit(user_id, prompt_ids, max_new_tokens, on_event=events.append)
+        while True:
+            while events:
+                ev = events.popleft()
+                yield ev
+                if ev["type"] == "ttt_status":
+                    return t.result
+            self.step()
+
     # ------------------------------------------------------------------ scheduler
     def _admit(self) -> None:
         e = self.engine
@@ -363,6 +388,8 @@ class ServingEngine:
             t.decoded = True
         else:
             t.reply.append(tok)
+            if t.on_event is not None:
+                t.on_event({"type": "token", "token_id": tok})
             if (not self.stop_free and t.eos_token_id is not None and tok == t.eos_token_id) or \
                     len(t.reply) >= t.max_new_tokens:
                 t.decoded = True
@@ -472,6 +499,8 @@ class ServingEngine:
         drift = self.pool.compute_drift(self.arena.state([t.slot]))
         with self._lock:
             self._finish_locked(t, surprise, per_layer, gate, drift)
+        if t.on_event is not None:
+            t.on_event({"type": "ttt_status", "result": t.result})
 
     def _finish_locked(self, t: Turn, surprise, per_layer, gate, drift) -> None:
         t.result = {
