@@ -589,7 +589,12 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             now = time.perf_counter() - start
             while i < len(arrivals) and arrivals[i][0] <= now:
                 at, user, prompt, reply = arrivals[i]
-                live.append((at, srv.submit(user, prompt, reply)))
+                rec = {}
+
+                def on_event(ev, rec=rec):      # time to first token: the prefill's greedy pick
+                    if ev["type"] == "token" and "first" not in rec:
+                        rec["first"] = time.perf_counter() - start
+                live.append((at, srv.submit(user, prompt, reply, on_event=on_event), rec))
                 i += 1
             if srv.idle():
                 time.sleep(max(0.0, min(arrivals[i][0] - now, 0.05)) if i < len(arrivals) else 0.0)
@@ -597,12 +602,15 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             srv.step()
             now = time.perf_counter() - start
             still = []
-            for at, turn in live:
-                (done if turn.done else still).append((at, turn) if not turn.done else (now - at, turn))
+            for at, turn, rec in live:
+                if turn.done:
+                    done.append((now - at, rec.get("first", now) - at))
+                else:
+                    still.append((at, turn, rec))
             live = still
         wall = time.perf_counter() - start
         st = dict(srv.stats)
-        part = {"wall": wall, "lat": [x for x, _ in done], "stats": st}
+        part = {"wall": wall, "lat": [x for x, _ in done], "ttft": [y for _, y in done], "stats": st}
         if world > 1:
             import torch.distributed as dist
             parts = [None] * world
@@ -613,6 +621,7 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             continue
         wall = max(pp["wall"] for pp in parts)
         lat = np.array([x for pp in parts for x in pp["lat"]]) if any(pp["lat"] for pp in parts) else np.zeros(1)
+        ttft = np.array([x for pp in parts for x in pp["ttft"]]) if any(pp["ttft"] for pp in parts) else np.zeros(1)
         tot = collections.Counter()
         for pp in parts:
             tot.update(pp["stats"])
@@ -623,6 +632,7 @@ def serve_sweep(device, lib, config, rates, duration_s, personas=256, max_batch=
             "prefill_tok_s": tot["prefill_tokens"] / wall,
             "latency_s": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
                           "mean": float(lat.mean())},
+            "first_token_s": {"p50": float(np.percentile(ttft, 50)), "p99": float(np.percentile(ttft, 99))},
             "mean_decode_batch": tot["decode_tokens"] / max(tot["decode_steps"], 1),
             "busy_s": {"prefill": tot["prefill_s"], "decode": tot["decode_s"], "write": tot["write_s"]},
             "write_batches": tot["write_batches"],
