@@ -75,6 +75,17 @@ int uttt_profile_read(float* total_ms, int* launches);
 int uttt_selftest_gemm(int mode, int M, int N, int K, const void* a, const void* b, float* d, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* Bounded-wait self-test: launches one CTA that waits, with the kernels' own
+ * bounded-wait code, on an event that never happens (kind 0: an mbarrier phase
+ * with no arrival; kind 1: a d-split exchange counter that nothing increments)
+ * for at most max_polls polls (1 .. 2^20).  The wait expires, records
+ * UTTT_ERR_TIMEOUT in the workspace status word (read it with
+ * uttt_read_status) and sets the int at byte 260 of the workspace to 1 when the
+ * kernel returns.  workspace_bytes >= 512.  No counterpart in the reference;
+ * it shows that an expired device wait reaches the caller as an error while the
+ * context stays usable. */
+int uttt_selftest_wait(int kind, unsigned max_polls, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- chunk-wise TTT write ---------------------------------------------- */
 /* Host hook of a hidden-dimension split: replaces `count` FP32 values at
  * device address `data` by their sum over every rank of the split (an
@@ -141,8 +152,11 @@ int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_c
  * array's device address (cudaGetSymbolAddress), so make that first call
  * before any stream capture.  All calls share the array: calls that overlap
  * on the GPU race and must be ordered by the caller.  The array's status word
- * is cleared at the start of each call, so an expired device wait is not
- * reported through uttt_read_status for this variant.
+ * is cleared at the start of each call; read it after the call (and before the
+ * next one) with uttt_chunk_write_noalloc_status.  The array's device address
+ * is cached per device and per CUDA context: after cudaDeviceReset (or any
+ * re-creation of the primary context) the next call looks it up again, so
+ * that call too must come before any stream capture.
  */
 #define UTTT_NOALLOC_SCRATCH_BYTES (8u << 20)
 int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q,
@@ -151,6 +165,13 @@ int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int chunk_begin,
                              const float* ln_weight, const float* ln_bias, float momentum_beta,
                              float max_grad_norm, int normalize_by_dim, float eps, void* out, int out_dtype,
                              float* token_loss, float* clip_scale, void* stream);
+/* Status word of the allocation-free write's static scratch on the current
+ * device: synchronises `stream`, returns UTTT_OK if every bounded device wait of
+ * the last uttt_chunk_write_noalloc call ended, UTTT_ERR_TIMEOUT if one expired
+ * (that call's state may then be wrong), or UTTT_ERR_CUDA if the word could not
+ * be read; reset != 0 clears the word.  Allocates nothing.  No counterpart in
+ * the reference. */
+int uttt_chunk_write_noalloc_status(int reset, void* stream);
 
 /* ---- fast-weight readout ------------------------------------------------ */
 /*

@@ -71,6 +71,8 @@ def test_noalloc_chunk_write_matches_workspace_entry_point_twice():
                    "uttt_chunk_write_noalloc")
         torch.cuda.synchronize()
         assert lib.uttt_read_status(ws.data_ptr(), 1, stream) == 0
+        # every bounded device wait of the allocation-free call ended (its status word is 0)
+        assert lib.uttt_chunk_write_noalloc_status(0, stream) == 0, call
         for n in names:
             got, want = na[n].cpu().numpy(), ref[n].cpu().numpy()
             assert np.isfinite(got).all(), (call, n)

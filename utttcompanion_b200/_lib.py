@@ -45,11 +45,13 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_profile_enable": (i32, [i32]),
     "uttt_profile_read": (i32, [vp, vp]),
     "uttt_selftest_gemm": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, sz, vp]),
+    "uttt_selftest_wait": (i32, [i32, C.c_uint, vp, sz, vp]),
     "uttt_chunk_write_workspace": (sz, [i32, i32, i32, i32]),
     "uttt_chunk_write": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, i32, vp, vp, vp, vp, sz, vp]),
     "uttt_chunk_write_noalloc": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp]),
+    "uttt_chunk_write_noalloc_status": (i32, [i32, vp]),
     "uttt_fast_readout_workspace": (sz, [i32, i32, i32, i32]),
     "uttt_fast_readout": (i32, [i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, f32, vp, i32, vp, sz, vp]),
     "uttt_fast_readout_partial": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]),

@@ -191,14 +191,7 @@ __device__ __forceinline__ void dsplit_exchange(float (&v)[NP][32], const ChunkP
   unsigned* flag = p.xflag + pair * 2 + flag_i;
   if (threadIdx.x == 0) {
     atomicAdd(flag, 1u);
-    uint32_t polls = 0;
-    while (*reinterpret_cast<volatile unsigned*>(flag) < (unsigned)KS) {
-      if (++polls > (1u << 22) || status_set(p.status)) {
-        set_status(p.status, UTTT_ERR_TIMEOUT);
-        break;
-      }
-      __nanosleep(64);
-    }
+    counter_wait(flag, (unsigned)KS, p.status, kMaxCounterPolls);
   }
   named_bar(1, NPROD);
   __threadfence();

@@ -25,19 +25,24 @@ __device__ __align__(256) static unsigned char g_noalloc_scratch[UTTT_NOALLOC_SC
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_addr[kMaxDevices] = {};
+unsigned long long g_ctx[kMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on the current device.  In host code the
-// symbol itself is only a host-side stand-in, so the address is looked up once
-// per device (with that device current) and cached.
+// symbol itself is only a host-side stand-in, so the address is looked up with
+// the device current and cached per device, together with the id of the CUDA
+// context it belongs to: a context re-created after cudaDeviceReset reloads the
+// module, and the next call then looks the address up again.
 int scratch_address(void** out) {
   int dev = 0;
   UTTT_TRY(cuda_status(cudaGetDevice(&dev)));
   if (dev < 0 || dev >= kMaxDevices) return UTTT_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> g(g_mu);
-  if (!g_addr[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!g_addr[dev] || ctx == 0 || ctx != g_ctx[dev]) {
     void* p = nullptr;
     UTTT_TRY(cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch)));
     g_addr[dev] = p;
+    g_ctx[dev] = current_context_id();
   }
   *out = g_addr[dev];
   return UTTT_OK;
@@ -66,4 +71,17 @@ extern "C" int uttt_chunk_write_noalloc(int B, int T, int C, int d, int h, int c
                           s_up, s_gate, s_down, ln_weight, ln_bias, momentum_beta, max_grad_norm, normalize_by_dim,
                           eps, out, out_dtype, token_loss, clip_scale, B, nullptr, nullptr, nullptr, scratch, (size_t)UTTT_NOALLOC_SCRATCH_BYTES,
                           stream);
+}
+
+// Reads the scratch's status word on the current device (see the header).
+extern "C" int uttt_chunk_write_noalloc_status(int reset, void* stream) {
+  using namespace uttt;
+  void* scratch = nullptr;
+  UTTT_TRY(scratch_address(&scratch));
+  cudaStream_t st = (cudaStream_t)stream;
+  int word = 0;
+  UTTT_TRY(cuda_status(cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, st)));
+  if (reset) UTTT_TRY(cuda_status(cudaMemsetAsync(scratch, 0, sizeof(int), st)));
+  UTTT_TRY(cuda_status(cudaStreamSynchronize(st)));
+  return word;
 }

@@ -90,19 +90,41 @@ __device__ __forceinline__ bool status_set(const int* status) {
   return status && *reinterpret_cast<const volatile int*>(status) != 0;
 }
 
-// Returns false (and records UTTT_ERR_TIMEOUT) if the phase never completed.
-// Once any wait in the grid has expired, every later wait returns at once, so
-// a lost arrival ends the whole launch quickly instead of timing out per CTA.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// Returns false (and records UTTT_ERR_TIMEOUT) if the phase never completed
+// within max_polls polls.  Once any wait in the grid has expired, every later
+// wait returns at once, so a lost arrival ends the whole launch quickly instead
+// of timing out per CTA.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* status, uint32_t max_polls) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   if (status_set(status)) return false;
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 1023u) == 1023u && status_set(status)) return false;
   }
   set_status(status, UTTT_ERR_TIMEOUT);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  return mbar_wait_limit(bar, parity, status, kMaxPolls);
+}
+
+// Bounded wait of one thread until the global counter `flag` (written by other
+// CTAs with atomics) reaches `target`.  Returns false and records
+// UTTT_ERR_TIMEOUT after max_polls polls, or at once once the launch's status
+// word holds an error.
+constexpr uint32_t kMaxCounterPolls = 1u << 22;
+__device__ __forceinline__ bool counter_wait(const unsigned* flag, unsigned target, int* status,
+                                             uint32_t max_polls) {
+  uint32_t polls = 0;
+  while (*reinterpret_cast<const volatile unsigned*>(flag) < target) {
+    if (++polls > max_polls || status_set(status)) {
+      set_status(status, UTTT_ERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 // ----------------------------------------------------------------------------

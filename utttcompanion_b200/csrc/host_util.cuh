@@ -24,26 +24,30 @@ inline int cuda_status(cudaError_t e) {
   return UTTT_ERR_CUDA;
 }
 
+// Unique id of the calling thread's current CUDA context (cuCtxGetId through the
+// runtime's driver entry point), or 0 if there is none or it cannot be read.  A
+// context re-created after cudaDeviceReset gets a new id.
+unsigned long long current_context_id();
+
 // A launcher's set-up step (a kernel's dynamic shared-memory limit, which belongs to
-// the device it is set on) run once per device by whichever thread launches there
-// first; its status is kept and returned to every later caller on that device.
+// the context it is set in) run once per device and context by whichever thread
+// launches there first.  Only a successful run is remembered: a failed step is
+// retried by the next caller, and a new context (after cudaDeviceReset) runs it again.
 struct DeviceOnce {
   std::mutex mu;
-  std::atomic<int> done[64];   // 0: not run yet; otherwise the step's status + 1
+  std::atomic<unsigned long long> ctx[64];   // context id of the last successful run, 0: none
 };
 template <class F>
 inline int run_once_per_device(DeviceOnce& once, F&& step) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return UTTT_ERR_CUDA;
-  int s = once.done[dev].load(std::memory_order_acquire);
-  if (s) return s - 1;
+  const unsigned long long id = current_context_id();
+  if (id != 0 && once.ctx[dev].load(std::memory_order_acquire) == id) return UTTT_OK;
   std::lock_guard<std::mutex> g(once.mu);
-  s = once.done[dev].load(std::memory_order_relaxed);
-  if (!s) {
-    s = step() + 1;
-    once.done[dev].store(s, std::memory_order_release);
-  }
-  return s - 1;
+  if (id != 0 && once.ctx[dev].load(std::memory_order_relaxed) == id) return UTTT_OK;
+  const int s = step();
+  if (s == UTTT_OK) once.ctx[dev].store(current_context_id(), std::memory_order_release);
+  return s;
 }
 
 // Check the launch that was just issued.

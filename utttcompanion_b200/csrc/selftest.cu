@@ -144,3 +144,46 @@ extern "C" int uttt_selftest_gemm(int mode, int M, int N, int K, const void* a, 
       tmA, tmB, (const float*)a, mode, M, N, K, d, ws_status(workspace));
   return launch_status();
 }
+
+// ----------------------------------------------------------------------------
+// Bounded-wait self-test: one CTA runs the kernels' own bounded waits on an
+// event that never happens (an mbarrier phase nothing arrives on, or a d-split
+// exchange counter nothing increments), with a short caller-given poll limit.
+// The wait expires, records UTTT_ERR_TIMEOUT in the workspace status word and
+// the kernel returns; no copy or MMA is in flight, so the context stays usable.
+// ----------------------------------------------------------------------------
+namespace uttt {
+namespace {
+__global__ void __launch_bounds__(32) selftest_wait_kernel(int kind, uint32_t max_polls, unsigned* counter,
+                                                           int* returned, int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbarrier_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    if (kind == 0)
+      mbar_wait_limit(&bar, 0, status, max_polls);      // phase 0 never completes: no arrival
+    else
+      counter_wait(counter, 1u, status, max_polls);    // the counter stays 0
+    *returned = 1;
+  }
+}
+}  // namespace
+}  // namespace uttt
+
+extern "C" int uttt_selftest_wait(int kind, unsigned max_polls, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  using namespace uttt;
+  UTTT_REQUIRE(workspace && workspace_bytes >= 512, UTTT_ERR_WORKSPACE);
+  UTTT_REQUIRE(kind == 0 || kind == 1, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(max_polls >= 1 && max_polls <= (1u << 20), UTTT_ERR_INVALID);
+  uint8_t* ws = (uint8_t*)workspace;
+  unsigned* counter = (unsigned*)(ws + 256);
+  int* returned = (int*)(ws + 260);
+  cudaStream_t st = (cudaStream_t)stream;
+  UTTT_TRY(cuda_status(cudaMemsetAsync(ws + 256, 0, 8, st)));
+  selftest_wait_kernel<<<1, 32, 0, st>>>(kind, max_polls, counter, returned, ws_status(workspace));
+  return launch_status();
+}
