@@ -21,6 +21,8 @@ Cases:
              autocast): stop-free greedy decode, teacher-forced logits and
              a masked test_time_update on prompt+reply.
   init_cfg1  checksums of the reference's seed-0 config-1 initialisation.
+  config1_reference  BASELINE config 1 (seed-0 init, 256-token prompt, 64 stop-free greedy
+             steps, the write on prompt + reply) in FP32 and in BF16 under autocast.
 """
 
 from __future__ import annotations
@@ -233,6 +235,73 @@ def model_case(um, name, dtype, autocast_bf16, seed=2024, n_prompt=37, n_gen=20)
     np.savez_compressed(os.path.join(HERE, f"model_{name}.npz"), **arrays)
 
 
+def config1_case(um, n_prompt=256, n_gen=64):
+    """BASELINE config 1 run by the reference itself: seed-0 init, a 256-token prompt of ids
+    uniform in [6, 8000) from Generator seed 0, 64 stop-free greedy steps with their
+    teacher-forced logits, then test_time_update on prompt + reply (T = 320: 5 chunks x 4 layers).
+
+    Two dtype flows of the same model: FP32 (BASELINE's own spec) and BF16 parameters under CPU
+    autocast with FP32 fast-weight masters (the serving flow).  Both write the SAME interaction
+    (prompt + the BF16 run's reply), so their states can be compared with each other: the
+    distance between them is the reference's own BF16 rounding spread.  Logits of the BF16 run
+    are BF16 and are stored as their bit patterns."""
+    cfg = um.uTTTConfig(vocab_size=8000, d_model=256, n_layers=4, n_heads=4, n_kv_heads=4, d_ff_fast=688,
+                        sliding_window_size=128, chunk_size=64)
+    gen = torch.Generator().manual_seed(0)
+    prompt = torch.randint(6, cfg.vocab_size, (1, n_prompt), generator=gen)
+    runs = {}
+    for name in ("bf16", "f32"):
+        torch.manual_seed(0)
+        model = um.uTTTModel(cfg).eval().requires_grad_(False)
+        autocast_bf16 = name == "bf16"
+        if autocast_bf16:
+            w0 = {n: p.detach().clone() for n, p in model.fast_weight_pool.named_parameters()}
+            model = model.to(torch.bfloat16)
+            for n, p in model.fast_weight_pool.named_parameters():
+                p.data = w0[n].float()
+        state = model.init_fast_state(batch_size=1, dtype=torch.float32, detach=True)
+        ctx = torch.autocast("cpu", dtype=torch.bfloat16) if autocast_bf16 else torch.autocast("cpu", enabled=False)
+        from unittest.mock import patch
+        with torch.no_grad(), ctx:
+            with patch.object(model, "_sample_next_token", side_effect=greedy_without_stops):
+                ids = list(model.stream_generate(prompt, fast_state=state, max_new_tokens=n_gen, temperature=0.0,
+                                                 eos_token_id=None, speculative_draft_k=0, use_cuda_graph=False))
+            pre = model(prompt, fast_state=state, update_fast_weights=False, logits_to_keep=1,
+                        return_fast_state=False)
+            logits = [pre.logits[0, -1]]
+            caches, pos = pre.kv_caches, prompt.shape[1]
+            for tok in ids[:-1]:
+                step = model(torch.tensor([[tok]]), fast_state=state, kv_caches=caches, start_pos=pos,
+                             update_fast_weights=False, return_fast_state=False)
+                caches, pos = step.kv_caches, pos + 1
+                logits.append(step.logits[0, -1])
+        runs[name] = dict(model=model, state=state, ids=ids, logits=torch.stack(logits), ctx=autocast_bf16)
+    turn = prompt[0].tolist() + runs["bf16"]["ids"]
+    C = cfg.chunk_size
+    padded = ((len(turn) + C - 1) // C) * C
+    inter = torch.tensor([turn + [0] * (padded - len(turn))])
+    mask = torch.tensor([[1.0] * len(turn) + [0.0] * (padded - len(turn))])
+    arrays = dict(prompt=prompt[0].numpy(), inter=inter[0].numpy(), mask=mask[0].numpy())
+    for name, r in runs.items():
+        ctx = torch.autocast("cpu", dtype=torch.bfloat16) if r["ctx"] else torch.autocast("cpu", enabled=False)
+        with torch.no_grad(), ctx:
+            new_state, mean_surprise, layer_surprises = r["model"].test_time_update(inter, r["state"], mask)
+        lg = r["logits"]
+        if name == "bf16":
+            assert lg.dtype == torch.bfloat16
+            arrays["bf16_logits_bits"] = lg.view(torch.int16).numpy().view(np.uint16)
+        else:
+            arrays["f32_logits"] = _np(lg.float())
+        arrays[name + "_ids"] = np.array(r["ids"])
+        for nm in ("w_up", "w_gate", "w_down"):
+            arrays[f"{name}_new_{nm}"] = _np(getattr(new_state, nm)).astype(np.float32)
+        arrays[name + "_new_step"] = np.array(new_state.step)
+        arrays[name + "_mean_surprise"] = np.array(mean_surprise)
+        arrays[name + "_layer_surprises"] = np.array(layer_surprises)
+    arrays["active_limit"] = np.array(runs["f32"]["model"].active_vocab_limit)
+    np.savez_compressed(os.path.join(HERE, "config1_reference.npz"), **arrays)
+
+
 def init_checksums(um):
     """Checksums of the reference's config-1 (tiny) seed-0 init, for the synthetic weight generator."""
     torch.manual_seed(0)
@@ -252,13 +321,40 @@ def init_checksums(um):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", default="", help="comma-separated case groups to write (chunk, swiglu, elastic, "
+                                               "model, init, config1); default all")
     args = ap.parse_args()
+    only = set(filter(None, args.only.split(",")))
+
+    def want(group):
+        return not only or group in only
     sys.path.insert(0, os.path.abspath(args.reference))
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     import model.uttt_layer as ul
     import model.uttt_model as um
 
     f64, f32, bf = torch.float64, torch.float32, torch.bfloat16
+    if want("chunk"):
+        _chunk_cases(ul, f64, f32, bf)
+    if want("swiglu"):
+        swiglu_case(ul, "f32", f32, 21, d=32, h=48)
+        swiglu_case(ul, "bf16", bf, 22)
+        swiglu_case(ul, "bf16_t1", bf, 23, T=1)
+        swiglu_case(ul, "bf16_t70", bf, 24, T=70)
+    if want("elastic"):
+        elastic_case(ul)
+    if want("model"):
+        model_case(um, "f32", f32, False)
+        model_case(um, "f64", f64, False)
+        model_case(um, "bf16", f32, True)
+    if want("init"):
+        init_checksums(um)
+    if want("config1"):
+        config1_case(um)
+    print("golden fixtures written to", HERE)
+
+
+def _chunk_cases(ul, f64, f32, bf):
     chunk_case(ul, "f64_plain", f64, f64, 2, 8, 16, 24, None, 0.0, 0.0, True, False, 1)
     chunk_case(ul, "f64_full", f64, f64, 4, 8, 16, 24, "ragged", 0.9, 0.05, False, True, 2)
     chunk_case(ul, "f32_plain", f32, f32, 2, 16, 32, 48, None, 0.0, 0.0, True, False, 3)
@@ -266,16 +362,6 @@ def main():
     chunk_case(ul, "bf16_plain", f32, bf, 2, 64, 128, 160, None, 0.0, 0.0, True, False, 5)
     chunk_case(ul, "bf16_full", f32, bf, 3, 64, 128, 160, "ragged", 0.9, 1.0, False, True, 6)
     chunk_case(ul, "bf16_clipbite", f32, bf, 2, 64, 128, 160, None, 0.5, 0.02, False, False, 7)
-    swiglu_case(ul, "f32", f32, 21, d=32, h=48)
-    swiglu_case(ul, "bf16", bf, 22)
-    swiglu_case(ul, "bf16_t1", bf, 23, T=1)
-    swiglu_case(ul, "bf16_t70", bf, 24, T=70)
-    elastic_case(ul)
-    model_case(um, "f32", f32, False)
-    model_case(um, "f64", f64, False)
-    model_case(um, "bf16", f32, True)
-    init_checksums(um)
-    print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":

@@ -1,12 +1,22 @@
 """GPU parity of the B200 model engine (decode + chunk-first TTT write).
 
-Bounds (north star): logits |diff| <= 2e-2 (+ one BF16 ULP of the value);
-greedy ids identical wherever the reference's top-1/top-2 margin exceeds
-twice the logits bound (a near-tie below that may legitimately flip between
-two BF16 implementations, as the reference itself saw between its graph and
-eager decoders); updated FP32 state rel-L2 <= 5e-3 and the written delta
-W'-W rel-L2 <= 3e-2 against the reference's BF16-autocast path (whose own
-BF16 rounding of every gradient accounts for the gap).
+Bounds, against the reference's BF16 path (its own outputs where a fixture exists, else the
+oracle's BF16 emulation of it):
+  logits   |diff| <= 2e-2 absolute (north star).  Where the reference's own BF16 rounding moves
+           its logits by more than that (its BF16 path against its FP32 path, teacher-forced
+           along the same ids, measured by the pinned oracle in the test), the step's bound is
+           1.5x that spread instead.
+  greedy   every step compared, teacher-forced along the reference's ids; an id may differ only
+           where the reference's top-1 / top-2 margin is within twice the step's logits bound
+           (a near-tie, which flips between any two BF16 implementations: the reference's own
+           BF16 and FP32 paths disagree at step 0 of config 1).  Free-running decode equals the
+           reference up to its first flip, which must be such a near-tie.
+  state    updated FP32 masters rel-L2 <= 1e-3 (north star).  For W_down, which one turn moves
+           by a large fraction of its norm (std 0.1/sqrt(h) at init), the reference's own
+           BF16-vs-FP32 spread of the written state is larger than 1e-3; its bound is then 1.5x
+           that spread (the reference's two fixture runs where they exist, else the oracle's).
+  update   W' - W rel-L2 <= 3e-2 (the reference rounds every gradient to BF16).
+Every measured figure is recorded in the session's parity report.
 """
 
 import os
@@ -15,8 +25,9 @@ import numpy as np
 import pytest
 import torch
 
+from conftest import record
 from oracle import model as om
-from oracle.numerics import rel_l2
+from oracle.numerics import from_bf16_bits, rel_l2
 from utttcompanion_b200.model import FastState, UtttB200
 from utttcompanion_b200.workloads import CONFIG_TINY, ModelConfig, reference_init_state_dict
 
@@ -24,63 +35,15 @@ from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
 LOGIT_TOL = 2e-2
+STATE_TOL = 1e-3
+SPREAD_FACTOR = 1.5
+NAMES = ("w_up", "w_gate", "w_down")
 
 
 def load(name):
     out = dict(np.load(os.path.join(GOLDEN, name + ".npz")))
     out.update(np.load(os.path.join(GOLDEN, "model_shared.npz")))
     return out
-
-
-def logits_close(got, ref):
-    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
-    return np.abs(got - ref) <= LOGIT_TOL + np.abs(ref) / 128
-
-
-def masked_margin(logits, limit):
-    w = np.asarray(logits, np.float64).copy()
-    w[:6] = -np.inf
-    w[limit:] = -np.inf
-    top = np.sort(w)[-2:]
-    return float(top[1] - top[0]), int(np.argmax(w))
-
-
-def small_engine(g):
-    cfg = ModelConfig.from_dict(eval(str(g["cfg_json"])))
-    sd = {k[3:]: torch.tensor(g[k]) for k in g if k.startswith("W::")}
-    eng = UtttB200(sd, cfg, max_personas=2)
-    st = eng.init_fast_state(1)
-    st.w_up, st.w_gate, st.w_down = (torch.tensor(g["state_" + n]).cuda().contiguous()
-                                     for n in ("w_up", "w_gate", "w_down"))
-    return eng, cfg, st
-
-
-def test_small_model_matches_reference_bf16_path():
-    g = load("model_bf16")
-    eng, cfg, st = small_engine(g)
-    prompt = torch.tensor(g["prompt"])
-    ids = [int(x) for x in g["ids"]]
-    tf = eng.teacher_forced_logits(prompt, ids, st)
-    torch.cuda.synchronize()
-    for step, (ours, ref) in enumerate(zip(tf, g["logits"])):
-        ok = logits_close(ours.cpu().numpy(), ref)
-        assert ok.all(), (step, float(np.max(np.abs(ours.cpu().numpy() - ref))))
-        margin, ref_id = masked_margin(ref, int(g["active_limit"]))
-        got_id = int(np.argmax(_mask(ours.cpu().numpy(), int(g["active_limit"]))))
-        if margin > 2 * LOGIT_TOL:
-            assert got_id == ref_id, (step, margin)
-    new, mean_s, per_layer = eng.test_time_update(torch.tensor(g["inter"]), st, torch.tensor(g["mask"]))
-    torch.cuda.synchronize()
-    assert new.step == int(g["new_step"])
-    for n in ("w_up", "w_gate", "w_down"):
-        got = getattr(new, n).cpu().numpy()
-        assert rel_l2(got, g["new_" + n]) < 5e-3, n
-        assert rel_l2(got - g["state_" + n], g["new_" + n] - g["state_" + n]) < 3e-2, (
-            n, rel_l2(got - g["state_" + n], g["new_" + n] - g["state_" + n]))
-    for n in ("s_up", "s_down"):
-        assert rel_l2(getattr(new, n).cpu().numpy(), g["new_" + n]) < 3e-2, n
-    assert abs(mean_s - float(g["mean_surprise"])) < 1e-2 * abs(float(g["mean_surprise"]))
-    np.testing.assert_allclose(per_layer, g["layer_surprises"], rtol=1e-2)
 
 
 def _mask(logits, limit):
@@ -90,61 +53,162 @@ def _mask(logits, limit):
     return w
 
 
-def test_small_model_free_running_greedy_matches_reference_until_a_near_tie():
+def masked_margin(logits, limit):
+    w = _mask(logits, limit)
+    top = np.sort(w)[-2:]
+    return float(top[1] - top[0]), int(np.argmax(w))
+
+
+def oracle_pair(weights, cfg, cos, sin):
+    ocfg = om.ModelConfig(**{k: v for k, v in cfg.items() if k in om.ModelConfig.__dataclass_fields__})
+    return (om.OracleModel(weights, ocfg, "bf16", cos, sin), om.OracleModel(weights, ocfg, "f32", cos, sin))
+
+
+def _with_state(model, w):
+    st = model.state_for_forward(1, update=True)
+    if w is not None:
+        st.w_up, st.w_gate, st.w_down = (np.asarray(x, np.float32).copy() for x in w)
+    return st
+
+
+def logit_spread(o16, o32, prompt, ids, w=None):
+    """Per-step max |BF16 - FP32| of the oracle's logits, teacher-forced along ``ids``: the
+    reference's own BF16 rounding noise at each step."""
+    a = o16.teacher_forced_logits(prompt, ids, _with_state(o16, w))
+    b = o32.teacher_forced_logits(prompt, ids, _with_state(o32, w))
+    return [float(np.max(np.abs(np.asarray(x, np.float64) - y))) for x, y in zip(a, b)], a
+
+
+def state_spread(o16, o32, inter, mask, w=None):
+    """rel-L2 between the oracle's BF16 and FP32 writes of the same interaction."""
+    n16, *_ = o16.test_time_update(inter[None], _with_state(o16, w), mask[None])
+    n32, *_ = o32.test_time_update(inter[None], _with_state(o32, w), mask[None])
+    return {n: rel_l2(getattr(n16, n), getattr(n32, n)) for n in NAMES}, n16
+
+
+def check_logits(name, ours, ref, spread, ids, limit):
+    """Teacher-forced logits along the reference's ``ids``: every step within its bound, every
+    greedy flip at a near-tie.  Returns (steps compared, flips)."""
+    errs, bounds, flips = [], [], []
+    for step, (o, r) in enumerate(zip(ours, ref)):
+        o = np.asarray(o, np.float64)
+        bound = max(LOGIT_TOL, SPREAD_FACTOR * spread[step])
+        err = float(np.max(np.abs(o - r)))
+        errs.append(err)
+        bounds.append(bound)
+        assert err <= bound, (name, step, err, spread[step])
+        if int(np.argmax(_mask(o, limit))) != ids[step]:
+            margin, _ = masked_margin(r, limit)
+            flips.append(step)
+            assert margin <= 2 * bound, (name, step, margin)
+    record(name, steps_compared=len(errs), max_abs_logit_diff=max(errs), steps_over_2e2=sum(e > LOGIT_TOL for e in errs),
+           max_bound=max(bounds), flips=flips)
+    return len(errs), flips
+
+
+def check_free_running(name, got, ref_ids, ref_logits, spread, limit):
+    """Free-running greedy ids equal the reference's up to the first flip, which must be a near-tie."""
+    first = None
+    for step, (a, b) in enumerate(zip(got, ref_ids)):
+        if a != b:
+            first = step
+            margin, _ = masked_margin(ref_logits[step], limit)
+            bound = max(LOGIT_TOL, SPREAD_FACTOR * spread[step])
+            assert margin <= 2 * bound, (name, step, margin)
+            break
+    assert len(got) == len(ref_ids)
+    record(name, free_running_equal_steps=len(ref_ids) if first is None else first)
+    return first
+
+
+def check_state(name, new, ref, base, spread, extra=None):
+    for n in NAMES:
+        got = getattr(new, n).cpu().numpy()
+        bound = max(STATE_TOL, SPREAD_FACTOR * spread[n])
+        r = rel_l2(got, ref[n])
+        u = rel_l2(got - base[n], ref[n] - base[n])
+        record(name, **{f"{n}_state": r, f"{n}_state_bound": bound, f"{n}_update": u,
+                        f"{n}_bf16_fp32_spread": spread[n]})
+        assert r <= bound, (name, n, r, bound)
+        assert u <= 3e-2, (name, n, u)
+        if extra is not None:
+            r32 = rel_l2(got, extra[n])
+            record(name, **{f"{n}_state_vs_fp32": r32})
+            assert r32 <= bound, (name, n, "vs FP32", r32, bound)
+
+
+def small_engine(g):
+    cfg = ModelConfig.from_dict(eval(str(g["cfg_json"])))
+    sd = {k[3:]: torch.tensor(g[k]) for k in g if k.startswith("W::")}
+    eng = UtttB200(sd, cfg, max_personas=2)
+    st = eng.init_fast_state(1)
+    st.w_up, st.w_gate, st.w_down = (torch.tensor(g["state_" + n]).cuda().contiguous() for n in NAMES)
+    return eng, cfg, st
+
+
+def test_small_model_matches_reference_bf16_path():
+    """The reference's own small model (fixture written by the reference under BF16 autocast):
+    20 teacher-forced steps and the masked write of prompt + reply."""
     g = load("model_bf16")
     eng, cfg, st = small_engine(g)
+    weights = {k[3:]: g[k] for k in g if k.startswith("W::")}
+    o16, o32 = oracle_pair(weights, eval(str(g["cfg_json"])), g["rope_cos"], g["rope_sin"])
+    w0 = [g["state_" + n] for n in NAMES]
     ids = [int(x) for x in g["ids"]]
-    got, margins, _ = eng.generate_greedy(torch.tensor(g["prompt"]), st, len(ids))
-    for step, (a, b) in enumerate(zip(got, ids)):
-        if a != b:
-            margin, _ = masked_margin(g["logits"][step], int(g["active_limit"]))
-            assert margin <= 2 * LOGIT_TOL, (step, margin)
-            break
+    limit = int(g["active_limit"])
+    spread, _ = logit_spread(o16, o32, g["prompt"], ids, w0)
+    tf = eng.teacher_forced_logits(torch.tensor(g["prompt"]), ids, st)
+    torch.cuda.synchronize()
+    n, _ = check_logits("small_model_bf16", [t.cpu().numpy() for t in tf], g["logits"], spread, ids, limit)
+    assert n == len(ids)
+    got, _, _ = eng.generate_greedy(torch.tensor(g["prompt"]), st, len(ids))
+    check_free_running("small_model_bf16", got, ids, g["logits"], spread, limit)
+    new, mean_s, per_layer = eng.test_time_update(torch.tensor(g["inter"]), st, torch.tensor(g["mask"]))
+    torch.cuda.synchronize()
+    assert new.step == int(g["new_step"])
+    sspread, _ = state_spread(o16, o32, g["inter"], g["mask"], w0)
+    check_state("small_model_bf16", new, {n: g["new_" + n] for n in NAMES}, {n: g["state_" + n] for n in NAMES},
+                sspread)
+    for n in ("s_up", "s_down"):
+        assert rel_l2(getattr(new, n).cpu().numpy(), g["new_" + n]) < 3e-2, n
+    assert abs(mean_s - float(g["mean_surprise"])) < 1e-2 * abs(float(g["mean_surprise"]))
+    np.testing.assert_allclose(per_layer, g["layer_surprises"], rtol=1e-2)
 
 
-def test_config1_tiny_model_against_oracle():
-    """BASELINE config 1 (reference seed-0 init): 256-token prompt, 64 greedy
-    steps (teacher-forced on the oracle's ids) and a masked write on
-    prompt + reply (5 chunks x 4 layers)."""
+def test_config1_against_the_reference_bf16_and_fp32_runs():
+    """BASELINE config 1 as the reference itself ran it (fixture ``config1_reference``): seed-0
+    init, a 256-token prompt, all 64 greedy steps compared teacher-forced along the reference's
+    BF16 ids and free-running, then the masked write of prompt + reply (5 chunks x 4 layers)
+    against the reference's BF16 run and against its FP32 run (BASELINE's own dtype)."""
+    g = dict(np.load(os.path.join(GOLDEN, "config1_reference.npz")))
     cfg = CONFIG_TINY
     sd = reference_init_state_dict(cfg, seed=0)
     eng = UtttB200(sd, cfg, max_personas=1)
-    ocfg = om.ModelConfig(**{k: v for k, v in cfg.to_dict().items() if k in om.ModelConfig.__dataclass_fields__})
-    oracle = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "bf16",
-                            *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
-    gen = torch.Generator().manual_seed(0)
-    prompt = torch.randint(6, cfg.vocab_size, (256,), generator=gen)
-    ost = oracle.state_for_forward(1, update=True)
-    n_steps = 64
-    oid, omargins, olog = oracle.generate_greedy(prompt.numpy(), ost, n_steps)
+    o16, o32 = oracle_pair({k: v.numpy() for k, v in sd.items()}, cfg.to_dict(),
+                           *[t.cpu().numpy() for t in (eng.rope_cos, eng.rope_sin)])
+    prompt = g["prompt"]
+    ids = [int(x) for x in g["bf16_ids"]]
+    ref_logits = from_bf16_bits(g["bf16_logits_bits"])
+    limit = int(g["active_limit"])
+    assert len(ids) == 64
+    spread, _ = logit_spread(o16, o32, prompt, ids)
     st = eng.init_fast_state(1)
-    tf = eng.teacher_forced_logits(prompt, oid, st)
+    tf = eng.teacher_forced_logits(torch.tensor(prompt), ids, st)
     torch.cuda.synchronize()
-    flips = 0
-    for step in range(n_steps):
-        ours = tf[step].cpu().numpy()
-        ok = logits_close(ours, olog[step])
-        assert ok.all(), (step, float(np.max(np.abs(ours - olog[step]))))
-        got = int(np.argmax(_mask(ours, oracle.active_limit)))
-        if got != oid[step]:
-            flips += 1
-            assert omargins[step] <= 2 * LOGIT_TOL, (step, omargins[step])
-    # write on prompt + reply padded to a multiple of 64 with a mask (personalizer.py:483-501)
-    turn = prompt.tolist() + oid
-    C = cfg.chunk_size
-    padded = ((len(turn) + C - 1) // C) * C
-    inter = np.array(turn + [0] * (padded - len(turn)))
-    mask = np.array([1.0] * len(turn) + [0.0] * (padded - len(turn)), np.float32)
-    on, oms, opl, _ = oracle.test_time_update(inter[None], ost, mask[None])
-    new, ms, pl = eng.test_time_update(torch.tensor(inter), st, torch.tensor(mask))
+    n, _ = check_logits("config1", [t.cpu().numpy() for t in tf], ref_logits, spread, ids, limit)
+    assert n >= 64
+    got, _, _ = eng.generate_greedy(torch.tensor(prompt), st, 64)
+    check_free_running("config1", got, ids, ref_logits, spread, limit)
+    new, ms, pl = eng.test_time_update(torch.tensor(g["inter"]), st, torch.tensor(g["mask"]))
     torch.cuda.synchronize()
-    assert new.step == on.step == 5 * cfg.n_layers
-    for n in ("w_up", "w_gate", "w_down"):
-        got, ref, base = getattr(new, n).cpu().numpy(), getattr(on, n), getattr(ost, n)
-        # W_down starts at std 0.1/sqrt(h) and one turn moves a large part of it
-        assert rel_l2(got, ref) < 5e-3, (n, rel_l2(got, ref))
-        assert rel_l2(got - base, ref - base) < 3e-2, (n, rel_l2(got - base, ref - base))
-    np.testing.assert_allclose(pl, opl, rtol=1e-2)
+    assert new.step == int(g["bf16_new_step"]) == 5 * cfg.n_layers
+    ref16 = {n: g["bf16_new_" + n] for n in NAMES}
+    ref32 = {n: g["f32_new_" + n] for n in NAMES}
+    own_spread = {n: rel_l2(ref16[n], ref32[n]) for n in NAMES}   # the reference's BF16 vs its FP32
+    base = {n: getattr(eng.init_fast_state(1), n).cpu().numpy() for n in NAMES}
+    check_state("config1", new, ref16, base, own_spread, extra=ref32)
+    assert abs(ms - float(g["bf16_mean_surprise"])) < 1e-2 * abs(float(g["bf16_mean_surprise"]))
+    np.testing.assert_allclose(pl, g["bf16_layer_surprises"], rtol=1e-2)
 
 
 def test_packed_multi_persona_decode_equals_per_persona_decode():
@@ -265,6 +329,36 @@ def test_decode_graph_replay_equals_eager_steps():
         p_e = p_e + 1
 
 
+def _oracle_model_case(name, cfg, sd, eng, prompt, n_steps):
+    """Teacher-forced decode along the oracle's own greedy ids, free-running decode, and the
+    masked write of prompt + reply, against the oracle's BF16 path with bounds calibrated by its
+    BF16-vs-FP32 spread."""
+    o16, o32 = oracle_pair({k: v.numpy() for k, v in sd.items()}, cfg.to_dict(),
+                           *[t.cpu().numpy() for t in (eng.rope_cos, eng.rope_sin)])
+    oid, _, olog = o16.generate_greedy(prompt.numpy(), o16.state_for_forward(1, update=True), n_steps)
+    spread, _ = logit_spread(o16, o32, prompt.numpy(), oid)
+    st = eng.init_fast_state(1)
+    tf = eng.teacher_forced_logits(prompt, oid, st)
+    torch.cuda.synchronize()
+    n, _ = check_logits(name, [t.float().cpu().numpy() for t in tf], olog, spread, oid, o16.active_limit)
+    assert n == n_steps
+    got, _, _ = eng.generate_greedy(prompt, st, n_steps)
+    check_free_running(name, got, oid, olog, spread, o16.active_limit)
+    turn = prompt.tolist() + oid
+    C = cfg.chunk_size
+    padded = ((len(turn) + C - 1) // C) * C
+    inter = np.array(turn + [0] * (padded - len(turn)))
+    mask = np.array([1.0] * len(turn) + [0.0] * (padded - len(turn)), np.float32)
+    sspread, on = state_spread(o16, o32, inter, mask)
+    _, _, opl, _ = o16.test_time_update(inter[None], o16.state_for_forward(1, update=True), mask[None])
+    new, _, pl = eng.test_time_update(torch.tensor(inter), st, torch.tensor(mask))
+    torch.cuda.synchronize()
+    assert new.step == on.step == (padded // C) * cfg.n_layers
+    base = {n: getattr(eng.init_fast_state(1), n).cpu().numpy() for n in NAMES}
+    check_state(name, new, {n: getattr(on, n) for n in NAMES}, base, sspread)
+    np.testing.assert_allclose(pl, opl, rtol=1e-2)
+
+
 def test_head_dim_128_gqa4_model_against_oracle():
     """The 1.58B configuration's attention shape (head dim 128, 4 query heads per
     KV head) at a small width: a prompt longer than the window, teacher-forced
@@ -274,34 +368,8 @@ def test_head_dim_128_gqa4_model_against_oracle():
     assert cfg.head_dim == 128
     sd = reference_init_state_dict(cfg, seed=3)
     eng = UtttB200(sd, cfg, max_personas=1)
-    ocfg = om.ModelConfig(**{k: v for k, v in cfg.to_dict().items() if k in om.ModelConfig.__dataclass_fields__})
-    oracle = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "bf16",
-                            *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
     gen = torch.Generator().manual_seed(5)
-    prompt = torch.randint(6, cfg.vocab_size, (80,), generator=gen)
-    ost = oracle.state_for_forward(1, update=True)
-    n_steps = 24
-    oid, omargins, olog = oracle.generate_greedy(prompt.numpy(), ost, n_steps)
-    st = eng.init_fast_state(1)
-    tf = eng.teacher_forced_logits(prompt, oid, st)
-    torch.cuda.synchronize()
-    for step in range(n_steps):
-        ours = tf[step].cpu().numpy()
-        assert logits_close(ours, olog[step]).all(), (step, float(np.max(np.abs(ours - olog[step]))))
-        if int(np.argmax(_mask(ours, oracle.active_limit))) != oid[step]:
-            assert omargins[step] <= 2 * LOGIT_TOL, (step, omargins[step])
-    turn = prompt.tolist() + oid
-    padded = ((len(turn) + 63) // 64) * 64
-    inter = np.array(turn + [0] * (padded - len(turn)))
-    mask = np.array([1.0] * len(turn) + [0.0] * (padded - len(turn)), np.float32)
-    on, _, opl, _ = oracle.test_time_update(inter[None], ost, mask[None])
-    new, _, pl = eng.test_time_update(torch.tensor(inter), st, torch.tensor(mask))
-    torch.cuda.synchronize()
-    for n in ("w_up", "w_gate", "w_down"):
-        got, ref, base = getattr(new, n).cpu().numpy(), getattr(on, n), getattr(ost, n)
-        assert rel_l2(got, ref) < 5e-3, (n, rel_l2(got, ref))
-        assert rel_l2(got - base, ref - base) < 3e-2, (n, rel_l2(got - base, ref - base))
-    np.testing.assert_allclose(pl, opl, rtol=1e-2)
+    _oracle_model_case("head_dim_128", cfg, sd, eng, torch.randint(6, cfg.vocab_size, (80,), generator=gen), 64)
 
 
 def test_decode_graph_survives_workspace_growth():
@@ -352,51 +420,14 @@ def test_decode_graph_survives_workspace_growth():
 
 def test_151m_shape_decode_and_write_against_oracle():
     """BASELINE config 3's model shape (d=768, 12 layers, 12 query heads over 4 KV heads of
-    dim 64, window 512, h=2048, V=32000; reference seed-0 init): a 96-token prompt, 8
-    teacher-forced decode steps at batch 1 (the cluster-split readout, attention and
-    projection finish) and a masked write of prompt + reply (2 chunks x 12 layers).
-
-    At this depth BF16 rounding alone moves the reference's logits by ~5e-2 (its BF16
-    path against its own FP32 path), more than the fixed 2e-2 bound the small models
-    use.  So each step's bound is calibrated by the oracle: the largest |BF16 - FP32|
-    of the oracle's logits at that step, times 1.5 (never below 2e-2)."""
+    dim 64, window 512, h=2048, V=32000; reference seed-0 init): a 96-token prompt, 16
+    teacher-forced and free-running decode steps at batch 1 (the cluster-split readout,
+    attention and projection finish) and a masked write of prompt + reply (2 chunks x 12
+    layers).  At this depth BF16 rounding alone moves the reference's logits by ~5e-2 against
+    its own FP32 path, so the calibrated logits bound applies at most steps."""
     from utttcompanion_b200.workloads import CONFIG_151M
     cfg = CONFIG_151M
     sd = reference_init_state_dict(cfg, seed=0)
     eng = UtttB200(sd, cfg, max_personas=1)
-    ocfg = om.ModelConfig(**{k: v for k, v in cfg.to_dict().items() if k in om.ModelConfig.__dataclass_fields__})
-    oracle = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "bf16",
-                            *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
     gen = torch.Generator().manual_seed(3)
-    prompt = torch.randint(6, cfg.vocab_size, (96,), generator=gen)
-    ost = oracle.state_for_forward(1, update=True)
-    n_steps = 8
-    oid, omargins, olog = oracle.generate_greedy(prompt.numpy(), ost, n_steps)
-    o32 = om.OracleModel({k: v.numpy() for k, v in sd.items()}, ocfg, "f32",
-                         *[t.numpy() for t in (eng.rope_cos.cpu(), eng.rope_sin.cpu())])
-    olog32 = o32.teacher_forced_logits(prompt.numpy(), oid, o32.state_for_forward(1, update=True))
-    st = eng.init_fast_state(1)
-    tf = eng.teacher_forced_logits(prompt, oid, st)
-    torch.cuda.synchronize()
-    for step in range(n_steps):
-        ours = tf[step].float().cpu().numpy()
-        noise = float(np.max(np.abs(np.asarray(olog[step], np.float64) - olog32[step])))
-        bound = max(LOGIT_TOL, 1.5 * noise)
-        err = float(np.max(np.abs(ours - olog[step])))
-        assert err <= bound, (step, err, noise)
-        if int(np.argmax(_mask(ours, oracle.active_limit))) != oid[step]:
-            assert omargins[step] <= 2 * bound, (step, omargins[step])
-    turn = prompt.tolist() + oid
-    C = cfg.chunk_size
-    padded = ((len(turn) + C - 1) // C) * C
-    inter = np.array(turn + [0] * (padded - len(turn)))
-    mask = np.array([1.0] * len(turn) + [0.0] * (padded - len(turn)), np.float32)
-    on, oms, opl, _ = oracle.test_time_update(inter[None], ost, mask[None])
-    new, ms, pl = eng.test_time_update(torch.tensor(inter), st, torch.tensor(mask))
-    torch.cuda.synchronize()
-    assert new.step == on.step == (padded // C) * cfg.n_layers
-    for n in ("w_up", "w_gate", "w_down"):
-        got, ref, base = getattr(new, n).cpu().numpy(), getattr(on, n), getattr(ost, n)
-        assert rel_l2(got, ref) < 5e-3, (n, rel_l2(got, ref))
-        assert rel_l2(got - base, ref - base) < 3e-2, (n, rel_l2(got - base, ref - base))
-    np.testing.assert_allclose(pl, opl, rtol=1e-2)
+    _oracle_model_case("config3_shape", cfg, sd, eng, torch.randint(6, cfg.vocab_size, (96,), generator=gen), 16)

@@ -1,0 +1,296 @@
+"""GPU parity at the shapes the bench measures: BASELINE config 2 (d=1024, h=2816) and one
+layer of the 1.58B model (d=2560, h=6912, 20 query / 5 KV heads of dim 128, window 512,
+V=32000), against the oracle's BF16 path (the reference's serving dtype flow) and FP32
+torch restatements.
+
+Which kernel variant runs is fixed by the row count:
+  * config 2, 8 rows: 8 x 22 hidden tiles = 176 CTAs of the plain (non-split) backward
+    kernel, more than one wave on 148 SMs, over 2 chained chunks (the fused
+    next-chunk forward included);
+  * config 2, 3 rows and the 1.58B write at 1 and 4 rows: the 2-CTA d-split;
+  * the 1.58B write at 5 rows: 270 plain CTAs (two waves);
+  * the 1.58B decode readout at batch 1 runs 5-CTA clusters, at batch 8 the plain tiles.
+
+Bounds (written per check below):
+  updated FP32 state  rel-L2 <= 1e-3 (north star)
+  the update W' - W   rel-L2 <= 2e-2, or 1.5x the reference's own BF16-vs-FP32 spread of the
+                      update where that is larger (measured in the test by running the pinned
+                      oracle both ways).  The inputs take alpha = 0 and zero momentum, so the
+                      update IS the clipped gradient step and the check sees the gradient.
+                      With W ~ N(0, 0.02) the LayerNorm backward cancels the large z_hat
+                      component of the error and leaves the small k component, so BF16
+                      rounding alone moves the reference's gradient by ~3 % at config 2 and
+                      ~10 % at the 1.58B init.
+  token losses        rel-L2 <= 1e-2
+  readout             |diff| <= 2e-2 + |ref|/128 (both sides round the output to BF16)
+  attention           |diff| <= 4e-3 + 4e-3 |ref| against FP32 softmax attention
+  lm head logits      |diff| <= 2e-2 (and within one BF16 ULP of the FP32 product)
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import record
+from oracle import fastweight as ofw
+from oracle.numerics import Precision, rel_l2, round_bf16
+from utttcompanion_b200 import _lib
+from utttcompanion_b200 import fastweight as fw
+from utttcompanion_b200 import readout as ro
+from utttcompanion_b200.model import rope_tables
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def T(x, dtype=torch.float32):
+    return torch.as_tensor(np.ascontiguousarray(x)).to(device=DEV, dtype=dtype)
+
+
+def _unit(rng, shape):
+    x = rng.standard_normal(shape, dtype=np.float32)
+    return round_bf16(x / np.linalg.norm(x, axis=-1, keepdims=True))
+
+
+def _write_case(rng, B, Tn, d, h, w_std, eta_const, ragged):
+    k, v = _unit(rng, (B, Tn, d)), _unit(rng, (B, Tn, d))
+    if eta_const is None:
+        eta = rng.uniform(0.005, 0.05, (B, Tn)).astype(np.float32)
+    else:
+        eta = np.full((B, Tn), eta_const, np.float32)
+    alpha = np.zeros((B, Tn), np.float32)
+    su, sd = w_std
+    W = [(rng.standard_normal((B, d, h), dtype=np.float32) * su),
+         (rng.standard_normal((B, d, h), dtype=np.float32) * su),
+         (rng.standard_normal((B, h, d), dtype=np.float32) * sd)]
+    S = [np.zeros_like(w) for w in W]
+    mask = None
+    if ragged:
+        mask = np.ones((B, Tn), np.float32)
+        mask[-1, Tn - 37:] = 0            # the last row ends inside its last chunk
+    return k, v, eta, alpha, W, S, mask
+
+
+def _oracle_chain(k, v, eta, alpha, W, S, lnw, lnb, mask, beta, clip, C, eps, mode):
+    B, Tn, d = k.shape
+    losses = np.zeros((B, Tn), np.float32)
+    prec = Precision(mode)
+    for off in range(0, Tn, C):
+        e = min(off + C, Tn)
+        m = None if mask is None else mask[:, off:e]
+        r = ofw.fused_chunk_ttt_step(k[:, off:e], k[:, off:e], v[:, off:e], eta[:, off:e, None],
+                                     alpha[:, off:e, None], *W, *S, lnw, lnb, m, beta, clip, True, eps, prec=prec)
+        W = [r.w_up, r.w_gate, r.w_down]
+        S = [r.s_up, r.s_gate, r.s_down]
+        losses[:, off:e] = r.token_loss
+    return W, S, losses
+
+
+def _check_write(name, B, Tn, d, h, w_std, beta, clip, eta_const=None, ragged=False, seed=0):
+    rng = np.random.default_rng(seed)
+    C, eps = 64, 1e-5
+    k, v, eta, alpha, W, S, mask = _write_case(rng, B, Tn, d, h, w_std, eta_const, ragged)
+    lnw = np.ones(d, np.float32)
+    lnb = np.zeros(d, np.float32)
+    wt = [T(x).contiguous() for x in W + S]
+    loss = torch.empty(B, Tn, device=DEV)
+    fw.chunk_write(T(k, torch.bfloat16), T(v, torch.bfloat16), T(eta), T(alpha), *wt, T(lnw), T(lnb),
+                   None if mask is None else T(mask), beta, clip, True, eps, chunk_size=C, token_loss=loss)
+    torch.cuda.synchronize()
+    fw.check_status(fw.workspace(0, torch.device(DEV)), "chunk_write")
+    got = [t.cpu().numpy() for t in wt]
+    del wt
+    torch.cuda.empty_cache()
+    W16, S16, l16 = _oracle_chain(k, v, eta, alpha, W, S, lnw, lnb, mask, beta, clip, C, eps, "bf16")
+    W32, S32, _ = _oracle_chain(k, v, eta, alpha, W, S, lnw, lnb, mask, beta, clip, C, eps, "f32")
+    vals = {}
+    names = ("w_up", "w_gate", "w_down")
+    for g, r16, r32, base, nm in zip(got[:3], W16, W32, W, names):
+        vals[nm + "_state"] = rel_l2(g, r16)
+        vals[nm + "_state_spread"] = rel_l2(r16, r32)
+        vals[nm + "_update"] = rel_l2(g - base, r16 - base)
+        vals[nm + "_update_vs_fp32"] = rel_l2(g - base, r32 - base)
+        vals[nm + "_update_spread"] = rel_l2(r16 - base, r32 - base)
+    if beta != 0.0:
+        for g, r16, r32, nm in zip(got[3:], S16, S32, ("s_up", "s_gate", "s_down")):
+            vals[nm] = rel_l2(g, r16)
+            vals[nm + "_spread"] = rel_l2(r16, r32)
+    lg = loss.cpu().numpy()
+    valid = np.ones_like(lg, bool) if mask is None else mask != 0
+    vals["token_loss"] = rel_l2(lg[valid], l16[valid])
+    record(name, **vals)
+    for nm in names:
+        assert vals[nm + "_state"] <= max(1e-3, 1.5 * vals[nm + "_state_spread"]), (nm, vals)
+        assert vals[nm + "_update"] <= max(2e-2, 1.5 * vals[nm + "_update_spread"]), (nm, vals)
+    if beta != 0.0:
+        for nm in ("s_up", "s_gate", "s_down"):
+            assert vals[nm] <= max(2e-2, 1.5 * vals[nm + "_spread"]), (nm, vals)
+    assert vals["token_loss"] <= 1e-2, vals
+
+
+# ---------------------------------------------------------------------------------------------
+# d=1024, h=2816, W ~ N(0, 0.02), eta = 1e-2, K/V L2-normalised
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("beta,clip", [(0.0, 0.0), (0.9, 1.0)])
+def test_config2_shape_plain_kernel_over_more_than_one_wave(beta, clip):
+    """8 states x 22 hidden tiles = 176 CTAs of the non-split backward kernel, 2 chained chunks:
+    the headline's own kernel variants (plain and fused next-chunk forward) at its own shape."""
+    _check_write(f"config2_B8_beta{beta}_clip{clip}", B=8, Tn=128, d=1024, h=2816, w_std=(0.02, 0.02),
+                 beta=beta, clip=clip, eta_const=1e-2, seed=11)
+
+
+def test_config2_shape_dsplit_kernel_ragged():
+    """3 states: the 2-CTA d-split variant at the config-2 shape, with momentum, clipping and a
+    row whose last chunk is partly masked."""
+    _check_write("config2_B3_dsplit", B=3, Tn=128, d=1024, h=2816, w_std=(0.02, 0.02), beta=0.9, clip=1.0,
+                 ragged=True, seed=12)
+
+
+# ---------------------------------------------------------------------------------------------
+# one layer of the 1.58B model: d=2560, h=6912 (reference init: W_up/W_gate ~ N(0, 1/d),
+# W_down ~ N(0, (0.1/sqrt(h))^2))
+# ---------------------------------------------------------------------------------------------
+D158, H158 = 2560, 6912
+STD158 = (D158 ** -0.5, 0.1 * H158 ** -0.5)
+
+
+@pytest.mark.parametrize("B,Tn,beta,clip", [(1, 128, 0.9, 1.0), (4, 64, 0.9, 1.0), (5, 64, 0.0, 0.0)])
+def test_1p58b_layer_write(B, Tn, beta, clip):
+    """1 and 4 rows run the d-split (54 tiles x 2 CTAs per row), 5 rows the plain kernel in two
+    waves; the 1-row case chains two chunks through the fused next-chunk forward."""
+    _check_write(f"1p58b_write_B{B}_T{Tn}", B=B, Tn=Tn, d=D158, h=H158, w_std=STD158, beta=beta, clip=clip,
+                 seed=20 + B)
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_1p58b_decode_readout(B):
+    """Decode GEMV over BF16 packed read copies at the 1.58B shape: batch 1 runs 5-CTA clusters
+    splitting d, batch 8 (rows gathered from 3 personas) the plain per-tile CTAs."""
+    rng = np.random.default_rng(30 + B)
+    S = min(B, 3)
+    d, h = D158, H158
+    w_up = rng.standard_normal((S, d, h), dtype=np.float32) * STD158[0]
+    w_gate = rng.standard_normal((S, d, h), dtype=np.float32) * STD158[0]
+    w_down = rng.standard_normal((S, h, d), dtype=np.float32) * 0.3 * h ** -0.5
+    lnw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    lnb = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    x = round_bf16(rng.standard_normal((B, 1, d), dtype=np.float32))
+    idx = (np.arange(B) * 2 % S).astype(np.int32)
+    packed, down = ro.inference_read_weights(T(w_up), T(w_gate), T(w_down))
+    y = ro.fast_readout(T(x, torch.bfloat16), packed, None, down, T(lnw), T(lnb), 1e-5,
+                        state_index=torch.as_tensor(idx), packed=True)
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    del packed, down
+    ref = ofw.swiglu_fast_forward(x, w_up[idx], w_gate[idx], w_down[idx], lnw, lnb, 1e-5, Precision("bf16"))
+    err = np.abs(got - ref)
+    record(f"1p58b_readout_B{B}", max_abs=float(err.max()), max_excess=float((err - np.abs(ref) / 128).max()))
+    assert (err <= 2e-2 + np.abs(ref) / 128).all(), float(err.max())
+
+
+def _rope_bf16(x, cos, sin):
+    """apply_rope on BF16 rows with the FP32 tables cast to BF16 and every product rounded
+    (model/uttt_layer.py:946-958 in the BF16 path)."""
+    bf = torch.bfloat16
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    a = (x.float() * cos.to(bf).float()).to(bf).float()
+    b = (rot.float() * sin.to(bf).float()).to(bf).float()
+    return (a + b).to(bf)
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_1p58b_decode_attention_wrapped_ring(B):
+    """Decode attention at the 1.58B head layout (20 query heads over 5 KV heads of dim 128,
+    window 512) at positions past the window, so the ring has wrapped: the new key / value land
+    in slot pos % 512 and every query sees exactly the last 512 positions."""
+    lib = _lib.load()
+    nh, nkv, hd, W = 20, 5, 128, 512
+    dev = torch.device(DEV)
+    g = torch.Generator(device=dev).manual_seed(40 + B)
+    slots_total = B + 2
+    pos = torch.tensor([700 + 97 * b for b in range(B)], dtype=torch.int32, device=dev)
+    slot = torch.tensor([(3 * b + 1) % slots_total for b in range(B)], dtype=torch.int32, device=dev)
+    qkv_dim = (nh + 2 * nkv) * hd
+    qkv = torch.randn(B, qkv_dim, device=dev, generator=g).to(torch.bfloat16)
+    k_ring = torch.randn(slots_total, nkv, W, hd, device=dev, generator=g).to(torch.bfloat16)
+    v_ring = torch.randn(slots_total, nkv, W, hd, device=dev, generator=g).to(torch.bfloat16)
+    k_before, v_before = k_ring.clone(), v_ring.clone()
+    cos, sin = rope_tables(hd, 2048, 10000.0)
+    cos, sin = cos.to(dev).contiguous(), sin.to(dev).contiguous()
+    out = torch.empty(B, nh * hd, dtype=torch.bfloat16, device=dev)
+    st = lib.uttt_attn_decode(B, nh, nkv, hd, W, qkv.data_ptr(), qkv_dim, pos.data_ptr(), slot.data_ptr(),
+                              k_ring.data_ptr(), v_ring.data_ptr(), cos.data_ptr(), sin.data_ptr(), out.data_ptr(),
+                              nh * hd, torch.cuda.current_stream().cuda_stream)
+    _lib.check(st, "uttt_attn_decode")
+    torch.cuda.synchronize()
+    worst = 0.0
+    rep = nh // nkv
+    for b in range(B):
+        p, s = int(pos[b]), int(slot[b])
+        c, sn = cos[p], sin[p]
+        q = _rope_bf16(qkv[b, :nh * hd].reshape(nh, hd), c, sn).float()
+        k_new = _rope_bf16(qkv[b, nh * hd:(nh + nkv) * hd].reshape(nkv, hd), c, sn)
+        v_new = qkv[b, (nh + nkv) * hd:].reshape(nkv, hd)
+        ws = p % W
+        # the ring holds the RoPE'd new key / value at slot pos % W, every other slot untouched
+        assert torch.equal(k_ring[s, :, ws], k_new), b
+        assert torch.equal(v_ring[s, :, ws], v_new), b
+        keep = torch.ones(W, dtype=torch.bool, device=dev)
+        keep[ws] = False
+        assert torch.equal(k_ring[s][:, keep], k_before[s][:, keep])
+        assert torch.equal(v_ring[s][:, keep], v_before[s][:, keep])
+        k, v = k_ring[s].float(), v_ring[s].float()          # all W slots are valid past the window
+        for hh in range(nh):
+            sc = (k[hh // rep] @ q[hh]) / hd ** 0.5
+            ref = torch.softmax(sc, dim=-1) @ v[hh // rep]
+            got = out[b, hh * hd:(hh + 1) * hd].float()
+            err = (got - ref).abs()
+            assert bool((err <= 4e-3 + 4e-3 * ref.abs()).all()), (b, hh, float(err.max()))
+            worst = max(worst, float(err.max()))
+    others = [i for i in range(slots_total) if i not in set(slot.tolist())]
+    for i in others:                                         # slots of other personas untouched
+        assert torch.equal(k_ring[i], k_before[i]) and torch.equal(v_ring[i], v_before[i])
+    record(f"1p58b_attn_decode_B{B}", max_abs=worst)
+
+
+@pytest.mark.parametrize("M", [1, 64])
+def test_1p58b_lm_head_and_greedy_pick(M):
+    """The tied LM head at V=32000, d=2560 (uttt_linear, BF16 output) and the greedy pick over it,
+    against the FP32 product of the same BF16 operands."""
+    lib = _lib.load()
+    V, K = 32000, D158
+    dev = torch.device(DEV)
+    g = torch.Generator(device=dev).manual_seed(50 + M)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(V, K, device=dev, generator=g)).to(torch.bfloat16)
+    out = torch.empty(M, V, dtype=torch.bfloat16, device=dev)
+    seg = (_lib.Segment * 1)(_lib.Segment(0, V, _lib.SEG_STORE, 0, out.data_ptr(), V, None, 0, 0.0, None))
+    ws = fw.workspace(lib.uttt_linear_workspace(M, V), dev, slot=2)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.uttt_linear(M, V, K, x.data_ptr(), w.data_ptr(), 1, seg, 1e-5, ws.data_ptr(), ws.numel(), stream),
+               "uttt_linear")
+    ids = torch.empty(M, dtype=torch.int32, device=dev)
+    top2 = torch.empty(M, 2, dtype=torch.float32, device=dev)
+    limit = 30000
+    _lib.check(lib.uttt_greedy_argmax(M, V, out.data_ptr(), 0, V, limit, 1, ids.data_ptr(), top2.data_ptr(), stream),
+               "uttt_greedy_argmax")
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().t()
+    got = out.float()
+    err = (got - ref).abs()
+    assert float(err.max()) <= 2e-2, float(err.max())
+    assert bool((err <= ref.abs() / 128 + 1e-3).all()), float((err - ref.abs() / 128).max())
+
+    def masked(t):
+        t = t.clone()
+        t[:, :6] = float("-inf")
+        t[:, limit:] = float("-inf")
+        return t
+    # the pick is the exact first maximum of the kernel's own BF16 logits
+    assert torch.equal(ids.long(), torch.argmax(masked(got), dim=-1))
+    top = torch.topk(masked(ref), 2, dim=-1).values
+    decisive = (top[:, 0] - top[:, 1]) > 2e-2
+    ref_ids = torch.argmax(masked(ref), dim=-1)
+    assert torch.equal(ids.long()[decisive], ref_ids[decisive])
+    record(f"1p58b_lm_head_M{M}", max_abs=float(err.max()), decisive_rows=int(decisive.sum()))

@@ -139,3 +139,37 @@ def test_small_model_decode_and_write_match_reference(name):
     assert new_state.step == int(g["new_step"])
     assert abs(mean_surprise - float(g["mean_surprise"])) < (1e-9 if name == "f64" else 1e-3)
     np.testing.assert_allclose(per_layer, g["layer_surprises"], rtol=1e-3 if name != "f64" else 1e-9)
+
+
+def test_oracle_matches_reference_config1_run():
+    """BASELINE config 1 as the reference ran it (seed-0 init, 64 stop-free greedy steps, the
+    write of prompt + reply): the oracle's FP32 path reproduces the reference's FP32 run (ids
+    exactly, logits and state to FP32 rounding) and its BF16 path the reference's BF16 run to
+    BF16 rounding noise (CPU autocast and the oracle's emulation round at the same points but
+    accumulate in a different order)."""
+    from oracle.numerics import from_bf16_bits
+    from utttcompanion_b200.model import rope_tables
+    from utttcompanion_b200.workloads import CONFIG_TINY, reference_init_state_dict
+    g = load("config1_reference")
+    cfg = CONFIG_TINY
+    sd = {k: v.numpy() for k, v in reference_init_state_dict(cfg, seed=0).items()}
+    ocfg = om.ModelConfig(**{k: v for k, v in cfg.to_dict().items() if k in om.ModelConfig.__dataclass_fields__})
+    cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len + 1024, cfg.rope_theta)
+    for mode in ("f32", "bf16"):
+        o = om.OracleModel(sd, ocfg, mode, cos.numpy(), sin.numpy())
+        assert o.active_limit == int(g["active_limit"])
+        ids = [int(x) for x in g[mode + "_ids"]]
+        st = o.state_for_forward(1, update=True)
+        tf = o.teacher_forced_logits(g["prompt"], ids, st)
+        ref = g["f32_logits"] if mode == "f32" else from_bf16_bits(g["bf16_logits_bits"])
+        err = max(float(np.max(np.abs(np.asarray(a, np.float64) - b))) for a, b in zip(tf, ref))
+        assert err < (2e-5 if mode == "f32" else 3e-2), (mode, err)
+        if mode == "f32":
+            got, _, _ = o.generate_greedy(g["prompt"], o.state_for_forward(1, update=True), 64)
+            assert got == ids
+        new, ms, pl, _ = o.test_time_update(g["inter"][None], st, g["mask"][None])
+        assert new.step == int(g[mode + "_new_step"])
+        for n in ("w_up", "w_gate", "w_down"):
+            bound = 1e-5 if mode == "f32" else (1e-4 if n != "w_down" else 8e-3)
+            assert rel_l2(getattr(new, n), g[f"{mode}_new_{n}"]) < bound, (mode, n)
+        assert abs(ms - float(g[mode + "_mean_surprise"])) < (1e-6 if mode == "f32" else 1e-3)
