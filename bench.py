@@ -236,40 +236,264 @@ def algorithmic_bytes(kind: int) -> float:
     return 0.0
 
 
-def cpu_baseline(max_seconds=20.0):
-    """The oracle port (numpy FP32, all host threads) on a bounded sample: chunk
-    steps of single config-2 states until ~max_seconds of CPU work."""
+# ----------------------------------------------------------------------------- the reference's own code
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def reference_modules():
+    """The reference's ``model`` package from ``baseline/_ref`` (an offline install of the unmodified
+    reference, which travels with the repository), or None when it is not installed."""
+    if not os.path.isdir(os.path.join(REF_DIR, "model")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import model.uttt_layer as ul
+    import model.uttt_model as um
+    return ul, um
+
+
+def use_all_host_threads() -> int:
+    """Give torch and numpy's BLAS every host core this process may run on, whatever
+    OMP_NUM_THREADS says (torchrun sets it to 1); returns the thread count."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    torch.set_num_threads(n)
+    return n
+
+
+def chunk_stepper(seed):
+    """One step = one 64-token chunk of one config-2 state on the host cores: the reference's own
+    ``fused_chunk_ttt_step`` (PyTorch FP32) from baseline/_ref, else the oracle port (numpy FP32).
+    Returns (step, kind, description)."""
+    d, h, C = CFG["d"], CFG["h"], CFG["chunk"]
+    mods = reference_modules()
+    if mods is not None:
+        ul, _ = mods
+        g = torch.Generator().manual_seed(seed)
+        W = [torch.randn(s, generator=g) * CFG["init_std"] for s in ((1, d, h), (1, d, h), (1, h, d))]
+        S = [torch.zeros_like(w) for w in W]
+        lnw, lnb = torch.ones(d), torch.zeros(d)
+
+        def unit():
+            x = torch.randn(1, C, d, generator=g)
+            return x / x.norm(dim=-1, keepdim=True)
+
+        def step():
+            k, v = unit(), unit()
+            eta = torch.full((1, C, 1), CFG["inner_lr"])
+            with torch.no_grad():
+                r = ul.fused_chunk_ttt_step(k, k, v, eta, torch.zeros_like(eta), *W, *S, lnw, lnb, None,
+                                            CFG["momentum"], CFG["clip"], True, CFG["eps"])
+            W[:], S[:] = list(r[1:4]), list(r[4:7])
+        return step, "reference", "the reference's own fused_chunk_ttt_step (PyTorch FP32, baseline/_ref)"
     from oracle import fastweight as ofw
     from oracle.numerics import Precision
-    rng = np.random.default_rng(0)
-    d, h, C = CFG["d"], CFG["h"], CFG["chunk"]
-    W = [rng.normal(0, CFG["init_std"], s).astype(np.float32) for s in ((1, d, h), (1, d, h), (1, h, d))]
-    S = [np.zeros_like(w) for w in W]
-    lnw, lnb = np.ones(d, np.float32), np.zeros(d, np.float32)
+    rng = np.random.default_rng(seed)
+    Wn = [rng.normal(0, CFG["init_std"], s).astype(np.float32) for s in ((1, d, h), (1, d, h), (1, h, d))]
+    Sn = [np.zeros_like(w) for w in Wn]
+    lnwn, lnbn = np.ones(d, np.float32), np.zeros(d, np.float32)
     prec = Precision("f32")
-    n, t0 = 0, time.perf_counter()
-    while True:
+
+    def step_port():
         k = rng.standard_normal((1, C, d)).astype(np.float32)
         k /= np.linalg.norm(k, axis=-1, keepdims=True)
         v = rng.standard_normal((1, C, d)).astype(np.float32)
         v /= np.linalg.norm(v, axis=-1, keepdims=True)
         eta = np.full((1, C, 1), CFG["inner_lr"], np.float32)
-        r = ofw.fused_chunk_ttt_step(k, k, v, eta, np.zeros_like(eta), *W, *S, lnw, lnb, None, CFG["momentum"],
+        r = ofw.fused_chunk_ttt_step(k, k, v, eta, np.zeros_like(eta), *Wn, *Sn, lnwn, lnbn, None, CFG["momentum"],
                                      CFG["clip"], True, CFG["eps"], prec=prec)
-        W, S = [r.w_up, r.w_gate, r.w_down], [r.s_up, r.s_gate, r.s_down]
+        Wn[:], Sn[:] = [r.w_up, r.w_gate, r.w_down], [r.s_up, r.s_gate, r.s_down]
+    return step_port, "port", "numpy FP32 restatement of fused_chunk_ttt_step (oracle port)"
+
+
+def cpu_baseline(max_seconds=20.0):
+    """The reference's chunk step on the host cores (all threads) on a bounded sample: chunk steps
+    of single config-2 states until ~max_seconds.  Returns (tok/s, steps, seconds, kind, desc, cores)."""
+    cores = use_all_host_threads()
+    step, kind, desc = chunk_stepper(0)
+    step()                                   # first call: allocations, thread pools
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
         n += 1
         el = time.perf_counter() - t0
         if el > max_seconds or n >= 400:
             break
-    return n * C / el, n, el
+    return n * CFG["chunk"] / el, n, el, kind, desc, cores
+
+
+def reference_model(um, cfg, device, dtype, seed=0):
+    """The reference's own ``uTTTModel`` of ``cfg``'s architecture holding the same random weights
+    as ``workloads.random_state_dict(cfg, seed)`` (built on the meta device and filled, so the 1.58B
+    model takes seconds); FP32, or ``dtype`` weights with the FP32 fast-weight pool as served."""
+    from utttcompanion_b200 import workloads as wl
+    fields = set(um.uTTTConfig.__dataclass_fields__)
+    rcfg = um.uTTTConfig(**{k: v for k, v in cfg.to_dict().items() if k in fields})
+    with torch.device("meta"):
+        m = um.uTTTModel(rcfg)
+    m = m.to_empty(device=device)
+    sd = wl.random_state_dict(cfg, seed=seed, device=device)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            src = sd.get(name)
+            if src is None:                   # parameters the serving path never reads
+                p.zero_()
+            else:
+                p.copy_(src.to(p.dtype))
+        for mod in m.modules():               # RoPE tables: rebuilt in FP32 as the module builds them
+            if hasattr(mod, "_build_cache") and "cos_cached" in mod._buffers:
+                mod._buffers.pop("cos_cached")
+                mod._buffers.pop("sin_cached")
+                mod._build_cache(rcfg.max_seq_len)
+    del sd
+    m = m.eval().requires_grad_(False)
+    if dtype != torch.float32:
+        pool = {n: p.detach().clone() for n, p in m.fast_weight_pool.named_parameters()}
+        m = m.to(dtype)
+        for n, p in m.fast_weight_pool.named_parameters():
+            p.data = pool[n]
+    return m
+
+
+def _stop_free_greedy(logits, **kwargs):
+    scores = logits.float().clone()
+    scores[:, :6] = -torch.inf
+    limit = kwargs.get("active_vocab_limit")
+    if limit is not None:
+        scores[:, limit:] = -torch.inf
+    return scores.argmax(dim=-1)
+
+
+def reference_turns(um, cfg, device, dtype, personas, prompt_len, new_tokens, repeats, graph=False, seed=0):
+    """Personas served one after another at batch 1 through the reference's own
+    ``stream_generate`` (greedy, forced length) and ``test_time_update`` (prompt + reply, padded to
+    64 with a mask), as its server does.  Decode tok/s counts the tokens after the first (the
+    prefill is timed apart); with ``graph`` the persona's second turn is timed, so the reference's
+    CUDA-graph capture is outside it.  Returns medians over ``repeats`` of per-persona figures."""
+    from unittest.mock import patch
+    m = reference_model(um, cfg, device, dtype, seed)
+    cuda = device.type == "cuda"
+    ctx = (lambda: torch.autocast("cuda", dtype=dtype)) if (cuda and dtype != torch.float32) else \
+        (lambda: torch.autocast(device.type, enabled=False))
+    g = torch.Generator().manual_seed(seed + 1)
+
+    def sync():
+        if cuda:
+            torch.cuda.synchronize(device)
+
+    dec, pre, wr = [], [], []
+    for rep in range(repeats + 1):
+        for _ in range(personas):
+            st = m.init_fast_state(batch_size=1, dtype=torch.float32, detach=True)
+            ids = torch.randint(6, cfg.vocab_size, (1, prompt_len), generator=g).to(device)
+            for turn in range(2 if graph else 1):
+                toks, stamps = [], []
+                sync()
+                t0 = time.perf_counter()
+                with torch.no_grad(), ctx(), patch.object(m, "_sample_next_token", side_effect=_stop_free_greedy):
+                    for t in m.stream_generate(ids, fast_state=st, max_new_tokens=new_tokens, temperature=0.0,
+                                               eos_token_id=None, speculative_draft_k=0, use_cuda_graph=graph):
+                        toks.append(t)
+                        stamps.append(time.perf_counter())
+            T = prompt_len + len(toks)
+            Tp = ((T + 63) // 64) * 64
+            inter = torch.tensor([ids[0].tolist() + toks + [0] * (Tp - T)], device=device)
+            mask = torch.tensor([[1.0] * T + [0.0] * (Tp - T)], device=device)
+            sync()
+            t2 = time.perf_counter()
+            with torch.no_grad(), ctx():
+                m.test_time_update(inter, st, mask)
+            sync()
+            t3 = time.perf_counter()
+            if rep == 0:
+                continue                      # warm-up round
+            pre.append(stamps[0] - t0)
+            dec.append((len(toks) - 1) / (stamps[-1] - stamps[0]))
+            wr.append(T / (t3 - t2))
+    m._cuda_graph_decoder = None
+    del m
+    if cuda:
+        torch.cuda.empty_cache()
+    return {"decode_tok_s_per_persona": float(np.median(dec)), "prefill_s": float(np.median(pre)),
+            "write_tok_s": float(np.median(wr)), "personas": personas, "prompt_tokens": prompt_len,
+            "decode_tokens": new_tokens, "repeats": repeats}
+
+
+def reference_model_baselines(device, spec, cfg):
+    """The reference's own serving path beside a decode sub-object: on the host cores (FP32, all
+    threads; a bounded sample) and on this B200 (BF16 autocast, batch 1, eager and with its
+    CUDAGraphDecoder).  None when baseline/_ref is absent."""
+    mods = reference_modules()
+    if mods is None:
+        return None
+    _, um = mods
+    out = {"source": "the reference's own uTTTModel.stream_generate + test_time_update from baseline/_ref, "
+                     "the same random weights as this sub-object's model"}
+    cores = use_all_host_threads()
+    cpu = torch.device("cpu")
+    if spec["config"] == "151M":
+        c = reference_turns(um, cfg, cpu, torch.float32, personas=2, prompt_len=128, new_tokens=16, repeats=3)
+        sample = "2 personas x (128-token prompt, 16 greedy tokens, one write of the turn), median of 3"
+    else:
+        c = reference_turns(um, cfg, cpu, torch.float32, personas=1, prompt_len=48, new_tokens=16, repeats=1)
+        sample = "1 persona x (48-token prompt, 16 greedy tokens, one write of the 64-token turn), once"
+    out["cpu"] = {**c, "cores": cores, "kind": "reference", "dtype": "f32", "sample": sample}
+    g_eager = reference_turns(um, cfg, device, torch.bfloat16, personas=1, prompt_len=512, new_tokens=64, repeats=1)
+    g_graph = reference_turns(um, cfg, device, torch.bfloat16, personas=1, prompt_len=512, new_tokens=64, repeats=1,
+                              graph=True)
+    out["gpu"] = {"eager": g_eager, "cuda_graph": {k: g_graph[k] for k in ("decode_tok_s_per_persona", "prefill_s")},
+                  "dtype": "bf16 autocast, FP32 fast-weight masters", "batch": 1,
+                  "sample": "1 persona: 512-token prompt, 64 greedy tokens (the reference's own published "
+                            "measurement shape), one write of the 576-token turn; eager and CUDA graph"}
+    return out
+
+
+def torch_reference_chunk_gpu(device, st, chunks=4):
+    """The reference's own fused_chunk_ttt_step (baseline/_ref) under BF16 autocast on this B200,
+    on the headline's 64 states: ``chunks`` sequential chunks after one warm-up chunk.  None when the
+    reference is not installed."""
+    mods = reference_modules()
+    if mods is None:
+        return None
+    ul, _ = mods
+    C = CFG["chunk"]
+    W = [st["w_up"].clone(), st["w_gate"].clone(), st["w_down"].clone()]
+    S = [torch.zeros_like(w) for w in W]
+    B = W[0].shape[0]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def chunk(i):
+        k = st["k"][:, i * C:(i + 1) * C]
+        v = st["v"][:, i * C:(i + 1) * C]
+        eta = st["eta"][:, i * C:(i + 1) * C, None]
+        alpha = st["alpha"][:, i * C:(i + 1) * C, None]
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            r = ul.fused_chunk_ttt_step(k, k, v, eta, alpha, *W, *S, st["ln_w"], st["ln_b"], None, CFG["momentum"],
+                                        CFG["clip"], True, CFG["eps"])
+        W[:], S[:] = list(r[1:4]), list(r[4:7])
+
+    chunk(0)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(1, chunks + 1):
+        chunk(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / chunks
+    del W, S
+    torch.cuda.empty_cache()
+    return {"value": B * C / (ms / 1e3), "unit": UNIT, "ms_per_chunk": ms, "chunks_timed": chunks,
+            "sample": f"{chunks} sequential chunks of the headline's {B} states (d={CFG['d']}, h={CFG['h']})",
+            "source": "the reference's own fused_chunk_ttt_step from baseline/_ref, BF16 autocast, FP32 masters",
+            "dtype": "bf16 autocast"}
 
 
 def host_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        return max([int(x.get("num_threads", 1)) for x in threadpool_info()] + [1])
-    except Exception:
-        return os.cpu_count() or 1
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
 
 
 # ----------------------------------------------------------------------------- decode + write (configs 3, 4)
@@ -291,13 +515,13 @@ DEC = dict(
     prompt_desc="uniform in [64, 1024]", prompt_max=1024, new_tokens=128, warmup_tokens=3, perturb_std=1e-3,
     init="reference")
 DEC4 = dict(
-    key="decode_1p58b", label="BASELINE config 4", config="1P58B", personas=64,
+    key="decode_1p58b", label="BASELINE config 4", config="1P58B", personas=64, batch1=True,
     prompts=_lognormal_prompts(512, 1.0, 32, 4096), prompt_desc="lognormal, median 512, sigma 1.0 (BASELINE gives "
     "no sigma), clipped to [32, 4096]", prompt_max=4096, new_tokens=256, warmup_tokens=3, perturb_std=1e-3,
     init="random")
 
 
-def decode_workload(device, rank, lib, spec):
+def decode_workload(device, rank, lib, spec, baselines=False):
     """Packed multi-persona greedy decode + per-turn chunk-TTT write.  ``spec``'s
     personas start from W_p = W_0 + N(0, perturb_std) with ragged prompts of
     uniform-random ids; they decode ``new_tokens`` greedy tokens as ONE packed
@@ -385,6 +609,7 @@ def decode_workload(device, rank, lib, spec):
     slow_bytes += eng.lm_head.numel() * eng.lm_head.element_size()
     kv_bytes = float(np.mean([sum(kp) for kp in kv_pos])) * cfg.n_kv_heads * cfg.head_dim * 2 * 2 * cfg.n_layers
     step_bytes = readout_bytes * cfg.n_layers + slow_bytes + kv_bytes
+    batch1 = decode_batch1(eng, packed, down, int(pos[0]), cfg) if spec.get("batch1") else None
     del graph, packed, down
     # one write per persona on prompt + reply (personalizer.py:483-512), batched over personas
     gen = torch.stack(generated, dim=1).cpu()                          # (P, new_tokens)
@@ -438,7 +663,52 @@ def decode_workload(device, rank, lib, spec):
         "decode_kernels_ms": {k: float(ms[i]) for i, k in enumerate(
             ["chunk_fwd", "chunk_ln", "chunk_norm", "chunk_bwd", "readout", "readout_ln", "gemm", "finish",
              "attn", "rowwise", "argmax"]) if cnt[i]},
+        **({"decode_batch1": batch1} if batch1 else {}),
+        **({"reference_baselines": reference_model_baselines(device, spec, cfg)} if baselines else {}),
     }
+
+
+def decode_batch1(eng, packed, down, pos0, cfg, steps=64):
+    """Batch-1 decode of one persona (the reference's only published serving measurement): the
+    captured packed step at batch 1, 64 tokens, device time per token; and the same loop reading
+    every token back to the host before the next step (``stream_generate``'s per-token ``.item()``)."""
+    from utttcompanion_b200.model import DecodeGraph
+    dev = eng.device
+    g1 = DecodeGraph(eng, 1, packed, down)
+    tok = torch.full((1,), 7, dtype=torch.int32, device=dev)
+    pos = torch.full((1,), pos0, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ids, _ = g1.step(tok, pos)
+        tok.copy_(ids)
+        pos += 1
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        ids, _ = g1.step(tok, pos)
+        tok.copy_(ids)
+        pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    host = torch.empty(1, dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ids, _ = g1.step(tok, pos)
+        host.copy_(ids, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        tok.fill_(int(host[0]))
+        pos += 1
+    e2e_s = (time.perf_counter() - t0) / steps
+    del g1
+    fast = cfg.n_layers * 3.0 * cfg.d_model * cfg.d_ff_fast * 2.0
+    slow = float(sum(x.numel() * x.element_size() for lay in eng.layers for x in (lay.wqkv, lay.wo, lay.w_q, lay.w_o)))
+    slow += eng.lm_head.numel() * eng.lm_head.element_size()
+    return {"tok_s": 1e3 / ms, "ms_per_token": ms, "e2e_tok_s": 1.0 / e2e_s, "steps": steps,
+            "hbm_gbs": (fast + slow) / (ms / 1e3) / 1e9,
+            "reference_published_rtx5090_tok_s": {"eager": 71.4, "cuda_graph": 123.1, "cuda_graph_packed": 127.4,
+                                                  "source": "docs/performance_20261029.md:12,19 (RTX 5090)"}}
 
 
 def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
@@ -461,6 +731,7 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     full = wl.perturbed_persona_states(*w0, P, spec["perturb_std"], seed=100, device=device)
     del w0
     local = hs.shard(*full)
+    keep = [w[:PARITY_ROWS].clone() for w in full]        # unsplit copies of the parity rows
     del full
     packed, down = eng.read_copies(*local)
     del local
@@ -469,12 +740,22 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     prompts = [torch.randint(6, cfg.vocab_size, (n,), generator=g) for n in lens]
     first = torch.stack([eng.prefill(prompts[p], p, packed, down, p) for p in range(P)])
     tokens, _ = eng.greedy(first)
+    tokens0 = tokens.clone()
     pos = torch.tensor(lens, dtype=torch.int32, device=device)
     slots = torch.arange(P, dtype=torch.int32, device=device)
-    for _ in range(3):
-        tokens, _ = eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))
+    step0 = None
+    for i in range(3):
+        lg = eng.decode_step(tokens, pos, slots, packed, down, slots)
+        if i == 0:
+            step0 = lg[:PARITY_ROWS].float().clone()
+        tokens, _ = eng.greedy(lg)
         pos += 1
     torch.cuda.synchronize()
+    parity = hsplit_parity(device, rank, hs, cfg, keep, prompts[:PARITY_ROWS], first[:PARITY_ROWS].float(),
+                           tokens0[:PARITY_ROWS], step0, torch.tensor(lens[:PARITY_ROWS], dtype=torch.int32,
+                                                                      device=device))
+    del keep
+    torch.cuda.empty_cache()
     from utttcompanion_b200.model import DecodeGraph
     graph, mode = None, "graph"
     try:
@@ -517,7 +798,80 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
         "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,
         "per_gpu_fast_weight_bytes_per_step": per_gpu,
         "per_gpu_hbm_gbs": per_gpu / (dec_ms / 1e3) / 1e9,
+        "parity": parity,
     }
+
+
+PARITY_ROWS = 8
+
+
+def hsplit_parity(device, rank, hs, cfg, full_rows, prompts, first_split, tokens0, step0_split, pos0):
+    """Correctness of the hidden split inside the bench run, against an unsplit engine on rank 0.
+
+    Decode: the split engine's prefill logits and its first packed decode step for the first
+    PARITY_ROWS personas, against an unsplit 1.58B engine on rank 0 fed the same prompts, tokens and
+    positions: max |logit difference| and whether every greedy id agrees.  Write: one chunk
+    (momentum 0.9, clip 1.0) of two personas at the 1.58B layer shape, each rank updating its hidden
+    slices with the partial Z and clip norms summed over the ranks; the slices gathered on rank 0
+    against the unsplit write of the same inputs (state and update rel-L2).  Every rank takes the
+    same collective steps."""
+    import torch.distributed as dist
+    from utttcompanion_b200 import fastweight as fw
+    from utttcompanion_b200.model import UtttB200
+    from utttcompanion_b200 import workloads as wl
+    out = {"rows": len(prompts)}
+    if rank == 0:
+        sd = wl.random_state_dict(cfg, seed=0, device=device)
+        ref = UtttB200(sd, cfg, device=device, max_personas=len(prompts), max_positions=4096 + 128)
+        del sd
+        rp, rd = ref.read_copies(*full_rows)
+        first = torch.stack([ref.prefill(prompts[p], p, rp, rd, p) for p in range(len(prompts))]).float()
+        slots = torch.arange(len(prompts), dtype=torch.int32, device=device)
+        step0 = ref.decode_step(tokens0, pos0, slots, rp, rd, slots).float()
+        d_pre = float((first - first_split).abs().max())
+        d_dec = float((step0 - step0_split).abs().max())
+        same = bool(torch.equal(first.argmax(-1), first_split.argmax(-1))
+                    and torch.equal(step0.argmax(-1), step0_split.argmax(-1)))
+        out.update(max_abs_logit_diff_prefill=d_pre, max_abs_logit_diff_decode=d_dec, greedy_equal=same,
+                   within_2e2=max(d_pre, d_dec) <= 2e-2)
+        del ref, rp, rd
+        torch.cuda.empty_cache()
+    # one split write of two personas' layer state against the unsplit write
+    B, d, h, C = 2, cfg.d_model, cfg.d_ff_fast, 64
+    g = torch.Generator(device=device).manual_seed(17)
+
+    def unit():
+        x = torch.randn(B, C, d, generator=g, device=device)
+        return (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16).contiguous()
+    k, v = unit(), unit()
+    eta = torch.rand(B, C, generator=g, device=device) * 0.04 + 0.005
+    alpha = torch.rand(B, C, generator=g, device=device) * 0.01
+    lnw, lnb = torch.ones(d, device=device), torch.zeros(d, device=device)
+    W = [w[:B].contiguous() for w in full_rows]
+    S = [torch.randn(w.shape, generator=g, device=device) * 1e-4 for w in W]
+    lo, hi = hs.bounds(h)
+    mine = [x.contiguous() for x in hs.shard(*W)] + [x.contiguous() for x in hs.shard(*S)]
+    fw.chunk_write(k, v, eta, alpha, *mine, lnw, lnb, None, 0.9, 1.0, True, 1e-5, chunk_size=C,
+                   partial_sum=hs.all_reduce)
+    parts = []
+    for t in mine[:3]:
+        bufs = [torch.empty_like(t) for _ in range(hs.world)]
+        dist.all_gather(bufs, t)
+        parts.append(bufs)
+    torch.cuda.synchronize()
+    if rank == 0:
+        got = [torch.cat(parts[0], dim=2), torch.cat(parts[1], dim=2), torch.cat(parts[2], dim=1)]
+        ref_state = [w.clone() for w in W] + [s.clone() for s in S]
+        fw.chunk_write(k, v, eta, alpha, *ref_state, lnw, lnb, None, 0.9, 1.0, True, 1e-5, chunk_size=C)
+        torch.cuda.synchronize()
+        rel = [float(torch.linalg.norm(a - b) / torch.linalg.norm(b)) for a, b in zip(got, ref_state[:3])]
+        upd = [float(torch.linalg.norm((a - w) - (b - w)) / torch.linalg.norm(b - w))
+               for a, b, w in zip(got, ref_state[:3], W)]
+        out.update(write_state_rel_l2=max(rel), write_update_rel_l2=max(upd),
+                   write_within_bounds=max(rel) <= 1e-3 and max(upd) <= 2e-2,
+                   write_case="one chunk, 2 personas, d=2560, h=6912 split over the ranks, momentum 0.9, clip 1.0")
+    del mine, parts, W, S
+    return out if rank == 0 else None
 
 
 # ----------------------------------------------------------------------------- serve sweep (config 5)
@@ -743,46 +1097,30 @@ def micro_case(device, kind, batch, tokens, hist, iters=30):
 
 # ----------------------------------------------------------------------------- arms
 def reference_arm(args, world, rank):
+    """The reference's own CPU implementation of the headline op on the host cores, rank 0 only:
+    each step one 64-token chunk of one config-2 state through its fused_chunk_ttt_step (PyTorch
+    FP32 from baseline/_ref; the oracle port when the reference is not installed), every host
+    thread in use whatever OMP_NUM_THREADS says."""
     if rank != 0:
         return 0
-    # each step: one chunk of one state through the oracle port (numpy FP32)
-    from oracle import fastweight as ofw
-    from oracle.numerics import Precision
-    rng = np.random.default_rng(1)
-    d, h, C = CFG["d"], CFG["h"], CFG["chunk"]
-    W = [rng.normal(0, CFG["init_std"], s).astype(np.float32) for s in ((1, d, h), (1, d, h), (1, h, d))]
-    S = [np.zeros_like(w) for w in W]
-    lnw, lnb = np.ones(d, np.float32), np.zeros(d, np.float32)
-    prec = Precision("f32")
-
-    def step():
-        nonlocal W, S
-        k = rng.standard_normal((1, C, d)).astype(np.float32)
-        k /= np.linalg.norm(k, axis=-1, keepdims=True)
-        v = rng.standard_normal((1, C, d)).astype(np.float32)
-        v /= np.linalg.norm(v, axis=-1, keepdims=True)
-        eta = np.full((1, C, 1), CFG["inner_lr"], np.float32)
-        r = ofw.fused_chunk_ttt_step(k, k, v, eta, np.zeros_like(eta), *W, *S, lnw, lnb, None, CFG["momentum"],
-                                     CFG["clip"], True, CFG["eps"], prec=prec)
-        W, S = [r.w_up, r.w_gate, r.w_down], [r.s_up, r.s_gate, r.s_down]
-
+    cores = use_all_host_threads()
+    step, kind, desc = chunk_stepper(1)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     el = time.perf_counter() - t0
+    C = CFG["chunk"]
     value = args.steps * C / el
-    cores = host_threads()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "chunk_ttt_write_isolated (BASELINE config 2)", **CFG,
                    "reference_sample": "one 64-token chunk of one state per step"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} chunk steps of one d=1024,h=2816 state (64 tokens each), "
-                                   "numpy FP32 restatement of fused_chunk_ttt_step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": f"{args.steps} chunk steps of one d=1024,h=2816 state (64 tokens each): {desc}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -917,6 +1255,10 @@ def ours_arm(args, world, rank, local):
     d2h = hl.numel() * hl.element_size()
     from utttcompanion_b200 import fastweight as fw
     fw.check_status(fw.workspace(0, device), "bench")
+    # the reference's own PyTorch op on this GPU, same states (rank 0 of a 1-GPU run)
+    torch_ref = None
+    if world == 1 and not args.no_cpu_baseline:
+        torch_ref = torch_reference_chunk_gpu(device, st)
 
     # decode + write workloads: at N = 1 configs 3 and 4; at N > 1 every rank serves its own
     # config-4 personas (64 per GPU below 4 GPUs, 256 in total from 4 GPUs up), then all
@@ -930,7 +1272,7 @@ def ours_arm(args, world, rank, local):
             spec4["personas"] = 64 if world < 4 else 256 // world
             specs.append(spec4)
         for spec in specs:
-            dec = decode_workload(device, rank, lib, spec)
+            dec = decode_workload(device, rank, lib, spec, baselines=world == 1 and not args.no_cpu_baseline)
             torch.cuda.empty_cache()
             if world > 1:
                 dec_ms = max_over_ranks(dec["decode_ms_per_step"])
@@ -990,10 +1332,12 @@ def ours_arm(args, world, rank, local):
                 dec["per_gpu_hbm_frac"] = dec["per_gpu_hbm_gbs"] / hbm
             line[key] = dec
         if world == 1 and not args.no_cpu_baseline:
-            v, n, el = cpu_baseline()
-            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": host_threads(), "kind": "port",
+            v, n, el, kind, desc, cores = cpu_baseline()
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": kind,
                                     "sample": f"{n} chunk steps of one config-2 state ({n * CFG['chunk']} tokens, "
-                                              f"{el:.1f} s), numpy FP32 restatement of fused_chunk_ttt_step"}
+                                              f"{el:.1f} s): {desc}"}
+        if torch_ref is not None:
+            line["torch_reference_gpu"] = torch_ref
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

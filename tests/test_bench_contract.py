@@ -30,7 +30,7 @@ def test_reference_arm_prints_one_contract_line():
     assert j["steps"] == 2 and j["warmup"] == 3           # warm-up is raised to the contract's minimum
     assert j["config"]["workload"].startswith("chunk_ttt_write_isolated")
     cb = j["cpu_baseline"]
-    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == j["value"] and cb["sample"]
+    assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["value"] == j["value"] and cb["sample"]
     assert j["e2e"] == {"value": j["value"], "unit": j["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 

@@ -25,7 +25,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import record
+from parity import LOGIT_TOL, NAMES, _mask, check_free_running, check_logits, check_state
 from oracle import model as om
 from oracle.numerics import from_bf16_bits, rel_l2
 from utttcompanion_b200.model import FastState, UtttB200
@@ -34,29 +34,12 @@ from utttcompanion_b200.workloads import CONFIG_TINY, ModelConfig, reference_ini
 from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
-LOGIT_TOL = 2e-2
-STATE_TOL = 1e-3
-SPREAD_FACTOR = 1.5
-NAMES = ("w_up", "w_gate", "w_down")
 
 
 def load(name):
     out = dict(np.load(os.path.join(GOLDEN, name + ".npz")))
     out.update(np.load(os.path.join(GOLDEN, "model_shared.npz")))
     return out
-
-
-def _mask(logits, limit):
-    w = np.asarray(logits, np.float64).copy()
-    w[:6] = -np.inf
-    w[limit:] = -np.inf
-    return w
-
-
-def masked_margin(logits, limit):
-    w = _mask(logits, limit)
-    top = np.sort(w)[-2:]
-    return float(top[1] - top[0]), int(np.argmax(w))
 
 
 def oracle_pair(weights, cfg, cos, sin):
@@ -84,57 +67,6 @@ def state_spread(o16, o32, inter, mask, w=None):
     n16, *_ = o16.test_time_update(inter[None], _with_state(o16, w), mask[None])
     n32, *_ = o32.test_time_update(inter[None], _with_state(o32, w), mask[None])
     return {n: rel_l2(getattr(n16, n), getattr(n32, n)) for n in NAMES}, n16
-
-
-def check_logits(name, ours, ref, spread, ids, limit):
-    """Teacher-forced logits along the reference's ``ids``: every step within its bound, every
-    greedy flip at a near-tie.  Returns (steps compared, flips)."""
-    errs, bounds, flips = [], [], []
-    for step, (o, r) in enumerate(zip(ours, ref)):
-        o = np.asarray(o, np.float64)
-        bound = max(LOGIT_TOL, SPREAD_FACTOR * spread[step])
-        err = float(np.max(np.abs(o - r)))
-        errs.append(err)
-        bounds.append(bound)
-        assert err <= bound, (name, step, err, spread[step])
-        if int(np.argmax(_mask(o, limit))) != ids[step]:
-            margin, _ = masked_margin(r, limit)
-            flips.append(step)
-            assert margin <= 2 * bound, (name, step, margin)
-    record(name, steps_compared=len(errs), max_abs_logit_diff=max(errs), steps_over_2e2=sum(e > LOGIT_TOL for e in errs),
-           max_bound=max(bounds), flips=flips)
-    return len(errs), flips
-
-
-def check_free_running(name, got, ref_ids, ref_logits, spread, limit):
-    """Free-running greedy ids equal the reference's up to the first flip, which must be a near-tie."""
-    first = None
-    for step, (a, b) in enumerate(zip(got, ref_ids)):
-        if a != b:
-            first = step
-            margin, _ = masked_margin(ref_logits[step], limit)
-            bound = max(LOGIT_TOL, SPREAD_FACTOR * spread[step])
-            assert margin <= 2 * bound, (name, step, margin)
-            break
-    assert len(got) == len(ref_ids)
-    record(name, free_running_equal_steps=len(ref_ids) if first is None else first)
-    return first
-
-
-def check_state(name, new, ref, base, spread, extra=None):
-    for n in NAMES:
-        got = getattr(new, n).cpu().numpy()
-        bound = max(STATE_TOL, SPREAD_FACTOR * spread[n])
-        r = rel_l2(got, ref[n])
-        u = rel_l2(got - base[n], ref[n] - base[n])
-        record(name, **{f"{n}_state": r, f"{n}_state_bound": bound, f"{n}_update": u,
-                        f"{n}_bf16_fp32_spread": spread[n]})
-        assert r <= bound, (name, n, r, bound)
-        assert u <= 3e-2, (name, n, u)
-        if extra is not None:
-            r32 = rel_l2(got, extra[n])
-            record(name, **{f"{n}_state_vs_fp32": r32})
-            assert r32 <= bound, (name, n, "vs FP32", r32, bound)
 
 
 def small_engine(g):

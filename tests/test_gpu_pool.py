@@ -73,7 +73,11 @@ def _close(got, ref, tol=1e-2):
     assert not bad.any(), (float(np.max(np.abs(got - ref))), int(bad.sum()))
 
 
-def test_slow_projections_and_q_proj_match_oracle():
+@pytest.mark.parametrize("param_dtype", [torch.float32, torch.bfloat16])
+def test_slow_projections_and_q_proj_match_oracle(param_dtype):
+    """Norm weights and gate biases as an FP32 model and as a BF16 model holds them: the BF16
+    case makes the drop-in convert them, and each converted operand must stay distinct (eta's
+    bias is not alpha's)."""
     rng = np.random.default_rng(0)
     d = 256
     x = round_bf16(rng.standard_normal((2, 7, d)))
@@ -81,10 +85,13 @@ def test_slow_projections_and_q_proj_match_oracle():
     w_eta, w_alpha = round_bf16(rng.normal(0, 0.05, (1, d))), round_bf16(rng.normal(0, 0.05, (1, d)))
     b_eta, b_alpha = np.array([0.1], np.float32), np.array([-1.386], np.float32)
     qn, kn = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32), (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    if param_dtype == torch.bfloat16:          # what the model holds after .to(bfloat16)
+        b_eta, b_alpha, qn, kn = (round_bf16(a) for a in (b_eta, b_alpha, qn, kn))
     q, k, v, eta, alpha = bp.fused_slow_projections(
         T(x, torch.bfloat16), T(w["w_q"], torch.bfloat16), T(w["w_k"], torch.bfloat16), T(w["w_v"], torch.bfloat16),
-        T(qn), T(kn), T(w_eta, torch.bfloat16), T(b_eta), T(w_alpha, torch.bfloat16), T(b_alpha), 0.015, 0.005, 1e-5)
-    qf = bp.fused_fast_q_proj(T(x, torch.bfloat16), T(w["w_q"], torch.bfloat16), T(qn), 1e-5)
+        T(qn, param_dtype), T(kn, param_dtype), T(w_eta, torch.bfloat16), T(b_eta, param_dtype),
+        T(w_alpha, torch.bfloat16), T(b_alpha, param_dtype), 0.015, 0.005, 1e-5)
+    qf = bp.fused_fast_q_proj(T(x, torch.bfloat16), T(w["w_q"], torch.bfloat16), T(qn, param_dtype), 1e-5)
     torch.cuda.synchronize()
     cfg = om.ModelConfig(d_model=d, n_layers=1, n_heads=4, n_kv_heads=4, base_inner_lr=0.015, base_weight_decay=0.005)
     weights = {"layers.0.uttt.w_q.weight": w["w_q"], "layers.0.uttt.w_k.weight": w["w_k"],

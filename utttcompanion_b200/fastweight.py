@@ -149,16 +149,18 @@ def _as_f32_2d(t: torch.Tensor, B: int, C: int) -> torch.Tensor:
     return t.reshape(B, C).to(torch.float32).contiguous()
 
 
-def fused_chunk_ttt_step(q, k, v, eta, alpha, w_up, w_gate, w_down, s_up, s_gate, s_down, ln_weight, ln_bias,
-                         token_mask, momentum_beta, max_inner_grad_norm, normalize_by_dim, eps,
-                         read_w_up=None, read_w_gate=None, read_w_down=None):
-    """Drop-in for ``fused_chunk_ttt_step`` (``model/uttt_layer.py:414-534``).
+def fused_chunk_ttt_step(q_chunk, k_chunk, v_chunk, eta_chunk, alpha_chunk, w_up, w_gate, w_down, s_up, s_gate,
+                         s_down, ln_weight, ln_bias, token_mask, momentum_beta, max_inner_grad_norm,
+                         normalize_by_dim, eps, read_w_up=None, read_w_gate=None, read_w_down=None):
+    """Drop-in for ``fused_chunk_ttt_step`` (``model/uttt_layer.py:414-534``), with its parameter
+    names (the reference's callers pass them by keyword, ``:732``).
 
     Returns ``(out, w_up', w_gate', w_down', s_up', s_gate', s_down', surprise)``
     as new tensors (the inputs are not modified), FP32 masters, ``out`` in
     q's dtype.  The surprise is the reference's batch-global mean of the
     unweighted per-token loss over valid tokens.
     """
+    q, k, v, eta, alpha = q_chunk, k_chunk, v_chunk, eta_chunk, alpha_chunk
     _require_cuda(q, k, v, w_up)
     B, C, d = k.shape
     if C > 64:

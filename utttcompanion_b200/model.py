@@ -256,6 +256,18 @@ class UtttB200:
     def prefill(self, ids: torch.Tensor, slot: int, read_packed: torch.Tensor, read_down: torch.Tensor,
                 state_index: int = 0) -> torch.Tensor:
         """Frozen forward of one persona's prompt; fills its KV ring; returns last-token logits (V,)."""
+        return self._lm_head(self._prefill_hidden(ids, slot, read_packed, read_down, state_index)[-1:])[0]
+
+    def prefill_logits(self, ids: torch.Tensor, slot: int, read_packed: torch.Tensor, read_down: torch.Tensor,
+                       state_index: int = 0, keep: int = 1) -> torch.Tensor:
+        """``prefill`` returning the logits of the last ``keep`` positions (0: every position),
+        (keep, V) FP32 of BF16 values (``uTTTModel.forward``'s ``logits_to_keep``)."""
+        x = self._prefill_hidden(ids, slot, read_packed, read_down, state_index)
+        return self._lm_head(x if keep <= 0 else x[-keep:].contiguous())
+
+    def _prefill_hidden(self, ids: torch.Tensor, slot: int, read_packed: torch.Tensor, read_down: torch.Tensor,
+                        state_index: int = 0) -> torch.Tensor:
+        """The prompt's final-normalised hidden rows (T, d) BF16; fills the persona's KV ring."""
         cfg = self.cfg
         ids = ids.reshape(-1)
         T = ids.numel()
@@ -286,7 +298,40 @@ class UtttB200:
             q = self._q_proj(lay, x2)
             r = self._readout(q.unsqueeze(0), read_packed, read_down, sidx)
             x = self._resid_linear(h, r.reshape(T, d), lay.w_o, self.layers[i + 1].attn_norm if i + 1 < L else self.norm)
-        return self._lm_head(x[-1:].contiguous())[0]
+        return x
+
+    # ------------------------------------------------------------------ KV rings <-> chronological caches
+    def export_kv(self, slot: int, end_pos: int) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+        """The persona's KV history as the reference's per-layer caches: (1, n_kv, L, hd) BF16 in
+        position order, L = min(end_pos, W), the keys RoPE'd (``SlidingWindowAttention.forward``,
+        model/uttt_layer.py:1080-1114; ``CUDAGraphDecoder.export_kv_caches``, engine/inference.py:295-302)."""
+        W = self.cfg.sliding_window_size
+        n = min(end_pos, W)
+        idx = torch.arange(end_pos - n, end_pos, device=self.device).remainder(W)
+        return [(k[slot:slot + 1].index_select(2, idx), v[slot:slot + 1].index_select(2, idx))
+                for k, v in zip(self.k_ring, self.v_ring)]
+
+    def import_kv(self, slot: int, caches, end_pos: int) -> None:
+        """Load the reference's chronological per-layer caches (positions end_pos - L .. end_pos - 1)
+        into the persona's rings at slot pos % W (``CUDAGraphDecoder.reset``, engine/inference.py:205-222)."""
+        W = self.cfg.sliding_window_size
+        if len(caches) != len(self.k_ring):
+            raise ValueError("one (key, value) cache per layer is required")
+        for (k, v), kr, vr in zip(caches, self.k_ring, self.v_ring):
+            n = k.shape[2]
+            if n > W or n > end_pos or k.shape != v.shape or k.shape[0] != 1:
+                raise ValueError("KV cache longer than the window or than its positions")
+            idx = torch.arange(end_pos - n, end_pos, device=self.device).remainder(W)
+            kr[slot].zero_()
+            vr[slot].zero_()
+            kr[slot].index_copy_(1, idx, k[0].to(device=self.device, dtype=torch.bfloat16))
+            vr[slot].index_copy_(1, idx, v[0].to(device=self.device, dtype=torch.bfloat16))
+
+    def use_state_ln(self, ln_weight: torch.Tensor, ln_bias: torch.Tensor) -> None:
+        """Make a persona state's readout LayerNorm affine the one the frozen path applies (in place,
+        so captured decode graphs see it), rounded as the BF16 path applies it (:253-257)."""
+        self.ln_w_act.copy_(ln_weight.to(torch.bfloat16).float())
+        self.ln_b_act.copy_(ln_bias.to(torch.bfloat16).float())
 
     def decode_step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: torch.Tensor, read_packed: torch.Tensor,
                     read_down: torch.Tensor, state_index: torch.Tensor) -> torch.Tensor:
@@ -369,14 +414,16 @@ class UtttB200:
         return new, surprises[0], per_layer[0]
 
     def test_time_update_batch(self, interaction_ids: torch.Tensor, fast_state: FastState,
-                               attention_mask: Optional[torch.Tensor] = None):
+                               attention_mask: Optional[torch.Tensor] = None, return_logits: bool = False):
         """The write of B personas at once: rows of ``interaction_ids`` (B, T) with
         masks; ``fast_state`` holds B stacked states.  Every chunk of every layer is
         one packed launch sequence over the rows still in the batch: a row leaves
         it once no valid token is left (its state is final, since a chunk without
         valid tokens keeps W and S exactly, model/uttt_layer.py:513-520), so a
         ragged batch costs what its rows' own lengths cost.
-        Returns (new stacked state, per-row mean surprise, per-row per-layer surprise).
+        Returns (new stacked state, per-row mean surprise, per-row per-layer surprise), and with
+        ``return_logits`` also the logits (B, T, V) FP32 of every position as the writing forward
+        reads them (every row then stays in the batch to its end, padding included).
         Per-row statistics follow the reference's single-persona definitions
         (model/uttt_model.py:598-607, 833-838)."""
         cfg = self.cfg
@@ -404,9 +451,10 @@ class UtttB200:
         alive = list(range(B))
         rows = torch.arange(B, dtype=torch.int32, device=dev)
         chunk_losses, counts = [], []
+        final = torch.empty(B, T, d, dtype=torch.bfloat16, device=dev) if return_logits else None
         for off in range(0, T, C):
             Cc = min(C, T - off)
-            keep_rows = [r for r in alive if last[r] >= off]
+            keep_rows = list(alive) if return_logits else [r for r in alive if last[r] >= off]
             if not keep_rows:
                 cur.step += L                      # the reference still steps through padded chunks
                 continue
@@ -464,7 +512,10 @@ class UtttB200:
                 if i + 1 < L:
                     x = self._resid_linear(hh, out.reshape(R, d), lay.w_o, self.layers[i + 1].attn_norm)
                 else:
-                    self._resid_linear(hh, out.reshape(R, d), lay.w_o)
+                    normed = self._resid_linear(hh, out.reshape(R, d), lay.w_o,
+                                                self.norm if final is not None else None)
+                    if final is not None:
+                        final[rows_l, off:off + Cc] = normed.reshape(Bc, Cc, d)
                 hidden = hh
             # ... then the L writes chain through the state as ONE call whose chunks are the
             # layers (row b's tokens: layer 0's chunk, layer 1's chunk, ...), so every write
@@ -502,6 +553,8 @@ class UtttB200:
         means = [sum(r) / max(len(r), 1) for r in per_layer]
         cur.last_surprise_loss = means[0] if B == 1 else float(sum(means) / B)
         cur.surprise_history = (list(fast_state.surprise_history) + (per_layer[0] if B == 1 else []))[-100:]
+        if final is not None:
+            return cur, means, per_layer, self._lm_head(final.reshape(B * T, d)).reshape(B, T, -1)
         return cur, means, per_layer
 
 

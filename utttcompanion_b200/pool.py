@@ -60,8 +60,11 @@ def fused_fast_q_proj(x, wq_w, q_norm_w, eps):
     d = wq_w.shape[0]
     xb = x.to(torch.bfloat16).reshape(-1, x.shape[-1]).contiguous()
     out = torch.empty(xb.shape[0], d, dtype=torch.bfloat16, device=x.device)
-    _linear_segments(xb, wq_w.to(torch.bfloat16).contiguous(),
-                     [_seg(0, d, _lib.SEG_RMSNORM, out, d, q_norm_w.to(torch.float32).contiguous())], eps)
+    # the segment holds only a raw pointer: the converted tensor must outlive the launch call,
+    # or the allocator may hand its memory to the next allocation before the kernel is queued
+    gamma = q_norm_w.to(torch.float32).contiguous()
+    _linear_segments(xb, wq_w.to(torch.bfloat16).contiguous(), [_seg(0, d, _lib.SEG_RMSNORM, out, d, gamma)], eps)
+    del gamma
     return out.reshape(*x.shape[:-1], d)
 
 
@@ -78,14 +81,18 @@ def fused_slow_projections(x, wq_w, wk_w, wv_w, q_norm_w, k_norm_w, w_eta_w, w_e
     v = torch.empty_like(q)
     eta = torch.empty(R, 1, dtype=torch.float32, device=x.device)
     alpha = torch.empty_like(eta)
-    f32 = lambda t: t.to(torch.float32).contiguous()  # noqa: E731
+    # Segments hold raw pointers, so every converted operand is kept alive (named) until the launch
+    # call has queued the kernel: a temporary freed earlier could be handed to the next conversion,
+    # and two segments would then read the same memory (eta would read alpha's bias).
+    gq, gk, b_eta, b_alpha = (t.to(torch.float32).contiguous() for t in (q_norm_w, k_norm_w, w_eta_b, w_alpha_b))
     _linear_segments(xb, w, [
-        _seg(0, d, _lib.SEG_RMSNORM, q, d, f32(q_norm_w)),
-        _seg(d, d, _lib.SEG_RMSNORM, k, d, f32(k_norm_w)),
+        _seg(0, d, _lib.SEG_RMSNORM, q, d, gq),
+        _seg(d, d, _lib.SEG_RMSNORM, k, d, gk),
         _seg(2 * d, d, _lib.SEG_RMSNORM, v, d),
-        _seg(3 * d, 1, _lib.SEG_SIGMOID, eta, 1, f32(w_eta_b), 0, base_inner_lr, out_f32=True),
-        _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, alpha, 1, f32(w_alpha_b), 0, base_weight_decay, out_f32=True),
+        _seg(3 * d, 1, _lib.SEG_SIGMOID, eta, 1, b_eta, 0, base_inner_lr, out_f32=True),
+        _seg(3 * d + 1, 1, _lib.SEG_SIGMOID, alpha, 1, b_alpha, 0, base_weight_decay, out_f32=True),
     ], eps)
+    del gq, gk, b_eta, b_alpha
     shp = x.shape[:-1]
     return (q.reshape(*shp, d), k.reshape(*shp, d), v.reshape(*shp, d),
             eta.to(torch.bfloat16).reshape(*shp, 1), alpha.to(torch.bfloat16).reshape(*shp, 1))

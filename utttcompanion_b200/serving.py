@@ -204,6 +204,10 @@ class Turn:
     # once with {"type": "ttt_status", "result": result} when the turn is done (on the thread that
     # finished it: the worker thread with async writes)
     on_event: Optional[Callable[[dict], None]] = None
+    # the ids the turn's write runs on, from (prompt ids, reply ids); None: prompt + reply.  A text
+    # front end passes the reference's re-tokenised "<|user|> ... <|assistant|> ..." turn
+    # (engine/personalizer.py:480-489) here.
+    write_ids: Optional[Callable[[List[int], List[int]], List[int]]] = None
 
 
 class ServingEngine:
@@ -270,12 +274,14 @@ class ServingEngine:
 
     # ------------------------------------------------------------------ API
     def submit(self, user_id: str, prompt_ids: List[int], max_new_tokens: int = 128,
-               eos_token_id: Optional[int] = EOS_ID, on_event: Optional[Callable[[dict], None]] = None) -> Turn:
+               eos_token_id: Optional[int] = EOS_ID, on_event: Optional[Callable[[dict], None]] = None,
+               write_ids: Optional[Callable[[List[int], List[int]], List[int]]] = None) -> Turn:
         if not prompt_ids:
             raise ValueError("empty prompt")
         if type(max_new_tokens) is not int or max_new_tokens < 1:
             raise ValueError("max_new_tokens must be a positive integer")
-        t = Turn(str(user_id), list(prompt_ids), max_new_tokens, eos_token_id, on_event=on_event)
+        t = Turn(str(user_id), list(prompt_ids), max_new_tokens, eos_token_id, on_event=on_event,
+                 write_ids=write_ids)
         self.waiting.append(t)
         return t
 
@@ -453,7 +459,10 @@ class ServingEngine:
             for t in turns:
                 self._finish(t, None, [], False)
             return
-        seqs = [t.prompt_ids + t.reply for t in turns]
+        seqs = [t.prompt_ids + t.reply if t.write_ids is None else list(t.write_ids(t.prompt_ids, t.reply))
+                for t in turns]
+        if any(not s for s in seqs):
+            raise ValueError("a turn's write sequence is empty")
         align = min(cfg.chunk_size, 64)
         Tpad = max(((len(s) + align - 1) // align) * align for s in seqs)
         ids = torch.full((len(turns), Tpad), PAD_ID, dtype=torch.long)
