@@ -1,12 +1,18 @@
 """Parity checks shared by the GPU tests: the north-star bounds, calibrated where the
 reference's own BF16 rounding exceeds them, with every measured figure recorded.
 
-  logits   |diff| <= 2e-2 absolute, or 1.5x the step's BF16-vs-FP32 spread of the reference
+  logits   |diff| <= 2e-2 absolute, or 2x the step's BF16-vs-FP32 spread of the reference
   greedy   teacher-forced along the reference's ids: a differing argmax only at a near-tie
            (top-1 / top-2 margin of the reference within twice the step's bound);
            free-running: equal up to the first flip, which must be such a near-tie
-  state    rel-L2 <= 1e-3, or 1.5x the reference's BF16-vs-FP32 spread of the written state
+  state    rel-L2 <= 1e-3, or 2x the reference's BF16-vs-FP32 spread of the written state
   update   W' - W rel-L2 <= 3e-2
+
+Why 2x the spread: the kernels are a second BF16 implementation of the same FP32 math, with
+their own accumulation order and fusion.  If each BF16 implementation sits within the spread
+of the FP32 result, the two can sit up to twice the spread apart (on opposite sides of it),
+so that is the distance at which ours is still as accurate as the reference's own BF16 path.
+The absolute floors (2e-2, 1e-3) are the north-star bounds themselves.
 """
 
 import numpy as np
@@ -16,7 +22,7 @@ from oracle.numerics import rel_l2
 
 LOGIT_TOL = 2e-2
 STATE_TOL = 1e-3
-SPREAD_FACTOR = 1.5
+SPREAD_FACTOR = 2.0
 NAMES = ("w_up", "w_gate", "w_down")
 
 

@@ -12,9 +12,9 @@ teacher-forced logits and the written state of prompt + reply.  Then:
     ``test_time_update`` run again;
   * ``uTTTModelB200.from_reference(model)`` runs the same calls on the B200 engine alone.
 
-Bounds (tests/parity.py): logits 2e-2, or 1.5x the reference's BF16-vs-FP32 spread at that
+Bounds (tests/parity.py): logits 2e-2, or 2x the reference's BF16-vs-FP32 spread at that
 step (the FP32 reference runs on the same GPU); greedy ids equal, or a near-tie flip; the
-written state 1e-3, or 1.5x the reference's own BF16-vs-FP32 spread of it.
+written state 1e-3, or 2x the reference's own BF16-vs-FP32 spread of it.
 """
 
 import os

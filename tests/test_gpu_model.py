@@ -5,7 +5,7 @@ oracle's BF16 emulation of it):
   logits   |diff| <= 2e-2 absolute (north star).  Where the reference's own BF16 rounding moves
            its logits by more than that (its BF16 path against its FP32 path, teacher-forced
            along the same ids, measured by the pinned oracle in the test), the step's bound is
-           1.5x that spread instead.
+           2x that spread instead.
   greedy   every step compared, teacher-forced along the reference's ids; an id may differ only
            where the reference's top-1 / top-2 margin is within twice the step's logits bound
            (a near-tie, which flips between any two BF16 implementations: the reference's own
@@ -13,7 +13,7 @@ oracle's BF16 emulation of it):
            reference up to its first flip, which must be such a near-tie.
   state    updated FP32 masters rel-L2 <= 1e-3 (north star).  For W_down, which one turn moves
            by a large fraction of its norm (std 0.1/sqrt(h) at init), the reference's own
-           BF16-vs-FP32 spread of the written state is larger than 1e-3; its bound is then 1.5x
+           BF16-vs-FP32 spread of the written state is larger than 1e-3; its bound is then 2x
            that spread (the reference's two fixture runs where they exist, else the oracle's).
   update   W' - W rel-L2 <= 3e-2 (the reference rounds every gradient to BF16).
 Every measured figure is recorded in the session's parity report.

@@ -13,7 +13,7 @@ Which kernel variant runs is fixed by the row count:
 
 Bounds (written per check below):
   updated FP32 state  rel-L2 <= 1e-3 (north star)
-  the update W' - W   rel-L2 <= 2e-2, or 1.5x the reference's own BF16-vs-FP32 spread of the
+  the update W' - W   rel-L2 <= 2e-2, or 2x the reference's own BF16-vs-FP32 spread of the
                       update where that is larger (measured in the test by running the pinned
                       oracle both ways).  The inputs take alpha = 0 and zero momentum, so the
                       update IS the clipped gradient step and the check sees the gradient.
@@ -120,11 +120,11 @@ def _check_write(name, B, Tn, d, h, w_std, beta, clip, eta_const=None, ragged=Fa
     vals["token_loss"] = rel_l2(lg[valid], l16[valid])
     record(name, **vals)
     for nm in names:
-        assert vals[nm + "_state"] <= max(1e-3, 1.5 * vals[nm + "_state_spread"]), (nm, vals)
-        assert vals[nm + "_update"] <= max(2e-2, 1.5 * vals[nm + "_update_spread"]), (nm, vals)
+        assert vals[nm + "_state"] <= max(1e-3, 2.0 * vals[nm + "_state_spread"]), (nm, vals)
+        assert vals[nm + "_update"] <= max(2e-2, 2.0 * vals[nm + "_update_spread"]), (nm, vals)
     if beta != 0.0:
         for nm in ("s_up", "s_gate", "s_down"):
-            assert vals[nm] <= max(2e-2, 1.5 * vals[nm + "_spread"]), (nm, vals)
+            assert vals[nm] <= max(2e-2, 2.0 * vals[nm + "_spread"]), (nm, vals)
     assert vals["token_loss"] <= 1e-2, vals
 
 
