@@ -312,6 +312,40 @@ int uttt_embed(int rows, int d, int V, const int* ids, const void* table, void* 
 int uttt_greedy_argmax(int rows, int V, const void* logits, int logits_f32, long long ld, int active_limit,
                        int stop_free, int* ids, float* top2, void* stream);
 
+/* ---- device-side scheduling of a packed decode batch ------------------------ */
+/*
+ * The continuous-batching engine keeps every row of its captured decode step in
+ * device arrays of B int32 entries: tokens (next input token), pos (its absolute
+ * position), slot (KV ring slot), state (fast-weight state index, -1: padding
+ * row), produced (reply tokens yielded), max_new (reply length limit), eos (id
+ * that ends the reply after being yielded, -1: none), status (UTTT_ROW_*), and
+ * ring (B, UTTT_ENGINE_RING): reply token n of row b at ring[b][n % RING].
+ *
+ * uttt_engine_step runs after a step's greedy pick `ids` (B entries) and applies
+ * stream_generate's stop rules (model/uttt_model.py:1036-1050) to every running
+ * row: USER / ASSISTANT ids (4, 5) end the reply unyielded; otherwise the id is
+ * yielded, and the reply ends at max_new tokens or after eos; stop_free != 0
+ * turns the stop ids off (forced-length replies).  A running row advances
+ * (tokens = id, pos += 1); a finished one becomes a padding row (slot =
+ * pad_slot, state = -1).  It replaces the host loop of stream_generate
+ * (:1020-1050) and of server/app.py's serialized worker: no host round trip
+ * between steps.
+ *
+ * uttt_engine_admit starts row `row` for a turn whose prefill's greedy pick is
+ * at device address first_id, at position pos0 with KV slot slot0 and state
+ * state0, and applies the same rule to that first token.
+ */
+#define UTTT_ENGINE_RING 8
+#define UTTT_ROW_IDLE 0
+#define UTTT_ROW_RUNNING 1
+#define UTTT_ROW_FINISHED 2
+int uttt_engine_step(int B, const int* ids, int* tokens, int* pos, int* slot, int* state, int* produced,
+                     const int* max_new, const int* eos, int* status, int* ring, int stop_free, int pad_slot,
+                     void* stream);
+int uttt_engine_admit(int row, const int* first_id, int pos0, int slot0, int state0, int max_new0, int eos0,
+                      int* tokens, int* pos, int* slot, int* state, int* produced, int* max_new, int* eos,
+                      int* status, int* ring, int stop_free, int pad_slot, void* stream);
+
 /* BF16 read copies of S FP32 states (SharedFastWeightPool.inference_read_weights,
  * model/uttt_layer.py:648-668): packed_up_gate (S, d, 2h) = [w_up | w_gate],
  * down (S, h, d) = w_down, round-to-nearest-even. */

@@ -3,7 +3,9 @@
 The GPU pieces are replaced by fakes: the model engine (prefill, greedy pick,
 batched write), the captured decode step and the read-copy refresh.  The fake
 decode emits token ``10 + pos % 50`` for every row, or a scripted stop id at a
-scripted position, so the test checks the scheduler itself:
+scripted position; the device rows are restated on the host (``engine_rules.HostTable``, the
+rule of ``uttt_engine_step`` that tests/test_gpu_engine.py checks on the GPU), so the test checks
+the scheduler itself:
 - admission and one turn in flight per user (``engine/personalizer.py``'s
   per-persona serialisation);
 - the reference's stop rules (``model/uttt_model.py:1036-1050``): EOS is
@@ -18,6 +20,7 @@ scripted position, so the test checks the scheduler itself:
 
 import torch
 
+from engine_rules import HostTable
 from utttcompanion_b200 import serving
 from utttcompanion_b200.model import ASSISTANT_ID, EOS_ID, FastState
 from utttcompanion_b200.workloads import ModelConfig
@@ -58,16 +61,22 @@ class FakeEngine:
 
 
 class FakeGraph:
-    def __init__(self, engine, batch, read_packed, read_down, stop_free=True, pad_slot=None):
-        self.engine, self.batch = engine, batch
+    """The captured step over the table's first ``batch`` rows: the fake decode's pick for each row,
+    then the rows' advance (``engine_rules.HostTable``, the device rule restated)."""
 
-    def step(self, tokens, pos, slots=None, state_index=None):
-        ids = torch.tensor([self.engine.token_at(int(p) + 1) for p in pos.tolist()], dtype=torch.int32)
+    def __init__(self, engine, batch, read_packed, read_down, stop_free=True, pad_slot=None, table=None):
+        self.engine, self.batch, self.table = engine, batch, table
+
+    def step(self):
+        ids = torch.tensor([self.engine.token_at(self.table.pos[b] + 1) for b in range(self.batch)],
+                           dtype=torch.int32)
+        self.table.advance(ids, self.batch)
         return ids, None
 
 
 def _server(monkeypatch, capacity, max_batch, stops=None, stop_free=False, write_batch=8):
     monkeypatch.setattr(serving, "DecodeGraph", FakeGraph)
+    monkeypatch.setattr(serving, "DecodeTable", HostTable)
     monkeypatch.setattr(serving.PersonaArena, "refresh", lambda self, slots: None)
     from utttcompanion_b200 import pool
     monkeypatch.setattr(pool.SharedFastWeightPoolB200, "apply_elastic_pull", lambda self, st, lam, ratio: st)

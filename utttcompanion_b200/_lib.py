@@ -27,6 +27,8 @@ UTTT_ERR_TIMEOUT = 4
 UTTT_ERR_WORKSPACE = 5
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+ENGINE_RING = 8
+ROW_IDLE, ROW_RUNNING, ROW_FINISHED = 0, 1, 2
 
 vp = C.c_void_p
 i32 = C.c_int
@@ -64,6 +66,8 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_rmsnorm": (i32, [i32, i32, vp, C.c_longlong, vp, f32, vp, C.c_longlong, vp]),
     "uttt_embed": (i32, [i32, i32, i32, vp, vp, vp, vp]),
     "uttt_greedy_argmax": (i32, [i32, i32, vp, i32, C.c_longlong, i32, i32, vp, vp, vp]),
+    "uttt_engine_step": (i32, [i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
+    "uttt_engine_admit": (i32, [i32, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, vp]),
     "uttt_pack_read_copies": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "uttt_apply_rope": (i32, [C.c_longlong, i32, i32, vp, vp, vp, vp, vp]),
     "uttt_guard_workspace": (sz, [i32]),

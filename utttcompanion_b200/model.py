@@ -558,6 +558,73 @@ class UtttB200:
         return cur, means, per_layer
 
 
+class DecodeTable:
+    """The rows of a packed decode batch, resident in device memory (the descriptor arrays of
+    ``uttt_engine_step`` / ``uttt_engine_admit``): next token, position, KV slot, fast-weight state,
+    reply length, limits, status and a ring of the last ``ENGINE_RING`` reply tokens per row.
+
+    The captured decode step advances the rows on the device after its greedy pick
+    (``advance``), so steps run back to back without the host.  The host starts a row with
+    ``admit`` (after the turn's prefill) and reads the rows back asynchronously with
+    ``snapshot`` / ``read``, one step behind, to stream tokens and retire finished turns.
+    Idle and finished rows are padding rows: KV slot ``pad_slot``, state -1."""
+
+    def __init__(self, device: torch.device, rows: int, pad_slot: int, stop_free: bool):
+        self.device = device
+        self.rows = rows
+        self.pad_slot = int(pad_slot)
+        self.stop_free = bool(stop_free)
+        i32 = dict(dtype=torch.int32, device=device)
+        self.tokens = torch.zeros(rows, **i32)
+        self.pos = torch.zeros(rows, **i32)
+        self.slots = torch.full((rows,), self.pad_slot, **i32)
+        self.state = torch.full((rows,), -1, **i32)
+        self.produced = torch.zeros(rows, **i32)
+        self.max_new = torch.ones(rows, **i32)
+        self.eos = torch.full((rows,), -1, **i32)
+        self.status = torch.full((rows,), _lib.ROW_IDLE, **i32)
+        self.ring = torch.zeros(rows, _lib.ENGINE_RING, **i32)
+        self.lib = _lib.load()
+        # two pinned host copies of (produced, status, ring), written alternately
+        self._host = [(torch.empty(rows, dtype=torch.int32).pin_memory(),
+                       torch.empty(rows, dtype=torch.int32).pin_memory(),
+                       torch.empty(rows, _lib.ENGINE_RING, dtype=torch.int32).pin_memory()) for _ in range(2)]
+        self._ready = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def _ptrs(self):
+        return (self.tokens.data_ptr(), self.pos.data_ptr(), self.slots.data_ptr(), self.state.data_ptr(),
+                self.produced.data_ptr(), self.max_new.data_ptr(), self.eos.data_ptr(), self.status.data_ptr(),
+                self.ring.data_ptr())
+
+    def advance(self, ids: torch.Tensor, n: int) -> None:
+        """Apply the stop rules to rows 0..n-1 after a step's greedy pick ``ids`` (device int32)."""
+        _lib.check(self.lib.uttt_engine_step(n, ids.data_ptr(), *self._ptrs(), int(self.stop_free), self.pad_slot,
+                                             _stream(self.device)), "uttt_engine_step")
+
+    def admit(self, row: int, first_id: torch.Tensor, pos: int, slot: int, state: int, max_new: int,
+              eos: Optional[int]) -> None:
+        """Start ``row`` for a turn whose prefill picked ``first_id`` (device int32, one element)."""
+        if not 0 <= row < self.rows:
+            raise ValueError("row outside the table")
+        _lib.check(self.lib.uttt_engine_admit(row, first_id.data_ptr(), int(pos), int(slot), int(state),
+                                              int(max_new), -1 if eos is None else int(eos), *self._ptrs(),
+                                              int(self.stop_free), self.pad_slot, _stream(self.device)),
+                   "uttt_engine_admit")
+
+    def snapshot(self, k: int) -> None:
+        """Queue copies of (produced, status, ring) into host buffer ``k`` (0 or 1) on the current stream."""
+        hp, hs, hr = self._host[k]
+        hp.copy_(self.produced, non_blocking=True)
+        hs.copy_(self.status, non_blocking=True)
+        hr.copy_(self.ring, non_blocking=True)
+        self._ready[k].record(torch.cuda.current_stream(self.device))
+
+    def read(self, k: int):
+        """Wait for snapshot ``k`` and return (produced, status, ring) as host tensors."""
+        self._ready[k].synchronize()
+        return self._host[k]
+
+
 class DecodeGraph:
     """A packed decode step (+ greedy pick) captured once in a CUDA graph.
 
@@ -570,19 +637,27 @@ class DecodeGraph:
     """
 
     def __init__(self, engine: "UtttB200", batch: int, read_packed: torch.Tensor, read_down: torch.Tensor,
-                 stop_free: bool = True, pad_slot: Optional[int] = None):
+                 stop_free: bool = True, pad_slot: Optional[int] = None, table: Optional["DecodeTable"] = None):
+        """``table``: the rows live in a device-resident ``DecodeTable`` (its first ``batch`` rows) and the
+        captured step ends with ``uttt_engine_step``, which advances them on the device: ``step()`` then
+        takes no inputs.  The table's rows must be idle (padding) while the graph is captured."""
         self.engine = engine
         dev = engine.device
         self.batch = batch
-        self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
-        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
-        if pad_slot is None:
-            if batch > min(engine.max_personas, read_packed.shape[0]):
-                raise ValueError("batch exceeds the persona slots; pass pad_slot")
-            self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
+        self.table = table
+        if table is not None:
+            self.tokens, self.pos = table.tokens[:batch], table.pos[:batch]
+            self.slots, self.sidx = table.slots[:batch], table.state[:batch]
         else:
-            self.slots = torch.full((batch,), pad_slot, dtype=torch.int32, device=dev)
-        self.sidx = self.slots.clone()
+            self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
+            self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+            if pad_slot is None:
+                if batch > min(engine.max_personas, read_packed.shape[0]):
+                    raise ValueError("batch exceeds the persona slots; pass pad_slot")
+                self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
+            else:
+                self.slots = torch.full((batch,), pad_slot, dtype=torch.int32, device=dev)
+            self.sidx = self.slots.clone()
         self.read_packed, self.read_down = read_packed, read_down
         self.stop_free = stop_free
         # warm up (workspaces, kernel attributes) on a side stream, then capture;
@@ -603,10 +678,16 @@ class DecodeGraph:
     def _body(self):
         lg = self.engine.decode_step(self.tokens, self.pos, self.slots, self.read_packed, self.read_down, self.sidx)
         ids, top2 = self.engine.greedy(lg, self.stop_free)
+        if self.table is not None:
+            self.table.advance(ids, self.batch)
         return lg, ids, top2
 
-    def step(self, tokens: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Tensor] = None,
-             state_index: Optional[torch.Tensor] = None):
+    def step(self, tokens: Optional[torch.Tensor] = None, pos: Optional[torch.Tensor] = None,
+             slots: Optional[torch.Tensor] = None, state_index: Optional[torch.Tensor] = None):
+        """Replay with new row inputs (or, with a ``table``, with the rows the device holds)."""
+        if self.table is not None:
+            self.graph.replay()
+            return self.ids, self.logits
         self.tokens.copy_(tokens, non_blocking=True)
         self.pos.copy_(pos, non_blocking=True)
         if slots is not None:

@@ -35,7 +35,7 @@ import torch
 
 from . import _lib
 from .fastweight import _stream, workspace
-from .model import ASSISTANT_ID, EOS_ID, PAD_ID, USER_ID, DecodeGraph, FastState, UtttB200
+from .model import EOS_ID, PAD_ID, DecodeGraph, DecodeTable, FastState, UtttB200
 
 
 class PersonaRouter:
@@ -195,8 +195,9 @@ class Turn:
     eos_token_id: Optional[int] = EOS_ID
     reply: List[int] = field(default_factory=list)
     slot: int = -1
-    pos: int = 0
-    next_token: int = 0
+    row: int = -1            # row of the packed decode batch while decoding
+    admit_seq: int = 0       # the first decode step that includes the turn
+    seen: int = 0            # reply tokens the host has taken from the device rows
     decoded: bool = False
     done: bool = False
     result: Optional[dict] = None
@@ -252,16 +253,23 @@ class ServingEngine:
         self.elastic_anchor_lambda = elastic_anchor_lambda
         self.max_weight_drift_ratio = max_weight_drift_ratio
         self.online_ttt = online_ttt
-        # one captured packed step per batch bucket (1, 2, 4, ... max_batch): a step runs the smallest
-        # bucket that holds the live turns; padding rows use the padding slot and read no weights
+        # The rows of the packed decode batch live on the device (DecodeTable): every captured step ends with
+        # the stop rules and the rows' advance (uttt_engine_step), so consecutive steps need nothing from the
+        # host.  One captured step per batch bucket (1, 2, 4, ... max_batch) over the table's first rows: a
+        # step runs the smallest bucket that holds every row in use; idle and finished rows are padding rows
+        # (padding slot, no fast-weight state) and read no weights.
+        self.table = DecodeTable(engine.device, max_batch, self.arena.pad_slot, stop_free)
         sizes, b = [], 1
         while b < max_batch:
             sizes.append(b)
             b *= 2
         sizes.append(max_batch)
         self.graphs = {n: DecodeGraph(engine, n, self.arena.read_packed, self.arena.read_down, stop_free=stop_free,
-                                      pad_slot=self.arena.pad_slot) for n in reversed(sizes)}
+                                      pad_slot=self.arena.pad_slot, table=self.table) for n in reversed(sizes)}
         self.graph = self.graphs[max_batch]
+        self._seq = 0                  # decode steps launched
+        self._snap_next = 0            # host buffer of the next snapshot
+        self._snap_pending = None      # (buffer, bucket, step) of the last launched step, not yet read back
         self.stats = collections.Counter()      # seconds and tokens of prefill / decode / write
         self.waiting: Deque[Turn] = collections.deque()
         self.active: List[Optional[Turn]] = [None] * max_batch
@@ -288,7 +296,8 @@ class ServingEngine:
     def idle(self) -> bool:
         with self._lock:
             busy = self._writes_in_flight
-        return not self.waiting and not self._write_queue and not busy and all(a is None for a in self.active)
+        return (not self.waiting and not self._write_queue and not busy and all(a is None for a in self.active)
+                and self._snap_pending is None)
 
     def close(self) -> None:
         """Stop the write worker (after the writes already queued)."""
@@ -379,55 +388,60 @@ class ServingEngine:
             t0 = time.perf_counter()
             logits = e.prefill(ids, t.slot, self.arena.read_packed, self.arena.read_down, t.slot)
             tok, _ = e.greedy(logits.unsqueeze(0), stop_free=self.stop_free)
-            t.pos = len(t.prompt_ids)
-            t.next_token = int(tok.item())
+            # the row starts on the device from the prefill's pick (no host round trip); the stop rules
+            # apply to that first token there too
+            self.table.admit(row, tok, len(t.prompt_ids), t.slot, t.slot, t.max_new_tokens, t.eos_token_id)
+            t.row, t.admit_seq, t.seen = row, self._seq, 0
             self.stats["prefill_s"] += time.perf_counter() - t0
             self.stats["prefill_tokens"] += len(t.prompt_ids)
             self.active[row] = t
-            self._accept(row, t)
         self.waiting.extendleft(reversed(deferred))
 
-    def _accept(self, row: int, t: Turn) -> None:
-        """Apply stream_generate's stop rules to the token just picked (model/uttt_model.py:1036-1050)."""
-        tok = t.next_token
-        if tok in (USER_ID, ASSISTANT_ID) and not self.stop_free:
-            t.decoded = True
-        else:
-            t.reply.append(tok)
-            if t.on_event is not None:
-                t.on_event({"type": "token", "token_id": tok})
-            if (not self.stop_free and t.eos_token_id is not None and tok == t.eos_token_id) or \
-                    len(t.reply) >= t.max_new_tokens:
+    def _harvest(self, buf: int, bucket: int, seq: int) -> None:
+        """Take the results of decode step ``seq`` (snapshot ``buf``): the reply tokens each turn yielded
+        since the last look, as token events, and the turns the device finished, which leave the batch
+        and queue their writes.  Turns admitted after that step are not in it."""
+        produced, status, ring = self.table.read(buf)
+        for r in range(min(bucket, len(self.active))):
+            t = self.active[r]
+            if t is None or t.admit_seq > seq:
+                continue
+            n = int(produced[r])
+            if n - t.seen > ring.shape[1]:
+                raise RuntimeError("decode rows advanced past the host's token ring")
+            for j in range(t.seen, n):
+                tok = int(ring[r, j % ring.shape[1]])
+                t.reply.append(tok)
+                if t.on_event is not None:
+                    t.on_event({"type": "token", "token_id": tok})
+            self.stats["decode_tokens"] += n - t.seen
+            t.seen = n
+            if int(status[r]) == _lib.ROW_FINISHED:
                 t.decoded = True
-        if t.decoded:
-            self.active[row] = None
-            self.finished.append(t)
-            self._pending_writes.append(t)
+                self.active[r] = None
+                self.finished.append(t)
+                self._pending_writes.append(t)
 
     def step(self) -> None:
+        """Admit waiting turns, launch one packed decode step, take the previous step's results back
+        (the GPU runs this step meanwhile), and write finished turns."""
         self._raise_write_error()
         self._pending_writes = []
         self._admit()
-        rows = [(i, t) for i, t in enumerate(self.active) if t is not None]
-        if rows:
-            B = min(n for n in self.graphs if n >= len(rows))
-            # packed rows 0..len(rows)-1: token, position, KV slot, fast-weight state (-1: padding row)
-            host = torch.zeros(4, B, dtype=torch.int32)
-            host[2].fill_(self.arena.pad_slot)
-            host[3].fill_(-1)
-            for r, (i, t) in enumerate(rows):
-                host[0, r], host[1, r], host[2, r], host[3, r] = t.next_token, t.pos, t.slot, t.slot
-            t0 = time.perf_counter()
-            dev = host.to(self.engine.device)
-            ids, _ = self.graphs[B].step(dev[0], dev[1], dev[2], dev[3])
-            host_ids = ids.cpu().tolist()
-            self.stats["decode_s"] += time.perf_counter() - t0
+        prev, self._snap_pending = self._snap_pending, None
+        t0 = time.perf_counter()
+        used = [r for r, t in enumerate(self.active) if t is not None]
+        if used:
+            bucket = min(n for n in self.graphs if n > max(used))
+            self.graphs[bucket].step()
+            buf, self._snap_next = self._snap_next, self._snap_next ^ 1
+            self.table.snapshot(buf)
+            self._snap_pending = (buf, bucket, self._seq)
+            self._seq += 1
             self.stats["decode_steps"] += 1
-            self.stats["decode_tokens"] += len(rows)
-            for r, (i, t) in enumerate(rows):
-                t.pos += 1
-                t.next_token = int(host_ids[r])
-                self._accept(i, t)
+        if prev is not None:
+            self._harvest(*prev)
+        self.stats["decode_s"] += time.perf_counter() - t0
         if self._pending_writes:
             if not self._write_queue:
                 self._write_since = time.perf_counter()
@@ -448,7 +462,7 @@ class ServingEngine:
                 t0 = time.perf_counter()
                 self._write(q)
                 self.stats["write_s"] += time.perf_counter() - t0
-        elif self.async_writes and not rows and self._writes_in_flight:
+        elif self.async_writes and not used and self._writes_in_flight:
             time.sleep(0.0005)           # nothing to decode (waiting turns wait for their users' writes)
 
     def _write(self, turns: List[Turn]) -> None:
