@@ -137,6 +137,29 @@ int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_c
                      void* partial_sum_ctx, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The same write with the stability guard of a persona turn folded into it
+ * (apply_elastic_pull, model/uttt_layer.py:773-832, and the sums of
+ * compute_drift, :834-874; engine/personalizer.py:524-552 applies them after
+ * the write): on the call's last chunk, every row b with final_rows[b] != 0
+ * (int32 device array, B entries) is pulled towards the shared W_0 right after
+ * its update, W <- W0 + (1 - anchor_lambda)(W - W0), inside the update kernel,
+ * and drift_sums[4b + m] (FP32 device, B x 4; zero it before the first call)
+ * receives ||W_m - W0_m||^2 of the pulled matrices m = up, gate, down.  The
+ * caller derives the drift clamp's scale from those sums (a second pass only
+ * when the clamp bites).  W0 is w_up0, w_gate0 (d, h) and w_down0 (h, d) FP32.
+ * q = k (the write's own readout is not produced), no clip-scale output, no
+ * hidden split; otherwise as uttt_chunk_write, with the same workspace.
+ */
+int uttt_chunk_write_guarded(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q,
+                             const void* k, const void* v, const float* eta, const float* alpha, const float* mask,
+                             float* w_up, float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
+                             const float* ln_weight, const float* ln_bias, float momentum_beta, float max_grad_norm,
+                             int normalize_by_dim, float eps, float* token_loss, int n_states, const int* state_rows,
+                             const float* w_up0, const float* w_gate0, const float* w_down0, float anchor_lambda,
+                             const int* final_rows, float* drift_sums, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/*
  * Allocation-free chunk write.  No counterpart in the reference.  (Rows map
  * to states one to one: n_states = B, state_rows = NULL.)
  *

@@ -146,3 +146,65 @@ def test_multi_chunk_sequence_matches_oracle(beta, clip, masked):
     lg = loss.cpu().numpy()
     valid = np.ones_like(lg, bool) if mask is None else mask != 0
     assert rel_l2(lg[valid], lr[valid]) < 1e-2
+
+
+@pytest.mark.parametrize("B,d,h,Tn", [(3, 256, 384, 150), (6, 256, 384, 64)])
+def test_guarded_write_equals_write_then_elastic_pull(B, d, h, Tn):
+    """uttt_chunk_write_guarded (the elastic pull inside each final row's last update, and the drift
+    sums of the pulled state) against uttt_chunk_write followed by the stand-alone guard pass
+    (uttt_elastic_pull, pinned to the reference's apply_elastic_pull by the elastic fixture) and
+    uttt_drift_sums: B = 3 runs the d-split kernels over 3 chained chunks, B = 6 the plain ones;
+    rows whose final flag is 0 are left unpulled.  Bounds: state rel-L2 <= 1e-6 (FP32 rounding of
+    one fused multiply-add), sums rel <= 1e-4 (atomic summation order)."""
+    from utttcompanion_b200 import _lib
+    rng = np.random.default_rng(B)
+
+    def unit(shape):
+        x = rng.standard_normal(shape)
+        return round_bf16(x / np.linalg.norm(x, axis=-1, keepdims=True))
+    k, v = unit((B, Tn, d)), unit((B, Tn, d))
+    eta = rng.uniform(0.005, 0.05, (B, Tn)).astype(np.float32)
+    alpha = rng.uniform(0.0, 0.01, (B, Tn)).astype(np.float32)
+    W0 = [rng.normal(0, d ** -0.5, (d, h)).astype(np.float32), rng.normal(0, d ** -0.5, (d, h)).astype(np.float32),
+          rng.normal(0, 0.1 * h ** -0.5, (h, d)).astype(np.float32)]
+    W = [(w[None] + rng.normal(0, 1e-2, (B,) + w.shape)).astype(np.float32) for w in W0]
+    S = [rng.normal(0, 1e-3, w.shape).astype(np.float32) for w in W]
+    lnw, lnb = np.ones(d, np.float32), np.zeros(d, np.float32)
+    final = np.array([1 if b % 3 != 1 else 0 for b in range(B)], np.int32)
+    lam = 0.02
+    a = [T(x).contiguous() for x in W + S]
+    g = [T(x).contiguous() for x in W + S]
+    w0 = [T(x).contiguous() for x in W0]
+    fw.chunk_write(T(k, torch.bfloat16), T(v, torch.bfloat16), T(eta), T(alpha), *a, T(lnw), T(lnb), None, 0.9, 1.0,
+                   True, 1e-5, chunk_size=64)
+    pulled = [x.clone() for x in a[:3]]
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    sel = [b for b in range(B) if final[b]]
+    for b in sel:                                           # the stand-alone guard pass on the final rows
+        one = [x[b:b + 1].contiguous() for x in pulled]
+        ws = fw.workspace(lib.uttt_guard_workspace(1), torch.device(DEV), slot=3)
+        _lib.check(lib.uttt_elastic_pull(1, d, h, *(x.data_ptr() for x in one), *(x.data_ptr() for x in w0), lam, 0.0,
+                                         ws.data_ptr(), ws.numel(), stream), "uttt_elastic_pull")
+        for x, o in zip(pulled, one):
+            x[b].copy_(o[0])
+    ref_sums = torch.zeros(4 * B + 4, device=DEV)
+    _lib.check(lib.uttt_drift_sums(B, d, h, *(x.data_ptr() for x in pulled), *(x.data_ptr() for x in w0),
+                                   ref_sums.data_ptr(), stream), "uttt_drift_sums")
+    sums = torch.zeros(B, 4, device=DEV)
+    fw.chunk_write(T(k, torch.bfloat16), T(v, torch.bfloat16), T(eta), T(alpha), *g, T(lnw), T(lnb), None, 0.9, 1.0,
+                   True, 1e-5, chunk_size=64, guard=(*w0, lam, T(final, torch.int32), sums))
+    torch.cuda.synchronize()
+    fw.check_status(fw.workspace(0, torch.device(DEV)), "chunk_write_guarded")
+    for got, want, nm in zip(g[:3], pulled, ("w_up", "w_gate", "w_down")):
+        err = rel_l2(got.cpu().numpy(), want.cpu().numpy())
+        assert err <= 1e-6, (nm, err)
+    for got, want in zip(g[3:], a[3:]):                     # momentum is not pulled
+        assert rel_l2(got.cpu().numpy(), want.cpu().numpy()) <= 1e-6
+    rs = ref_sums[:4 * B].reshape(B, 4).cpu().numpy()
+    gs = sums.cpu().numpy()
+    for b in range(B):
+        if final[b]:
+            assert np.allclose(gs[b, :3], rs[b, :3], rtol=1e-4), (b, gs[b], rs[b])
+        else:
+            assert (gs[b] == 0).all()

@@ -48,16 +48,23 @@ class FakeEngine:
         self.prefills.append((int(slot), len(ids)))
         return torch.tensor([float(len(ids))])       # carries the prompt length to greedy()
 
-    def greedy(self, logits, stop_free=True):
-        n = int(logits.reshape(-1)[0].item())
-        return torch.tensor([self.token_at(n)]), None
+    def prefill_batch(self, prompts, slots, packed, down, state_index):
+        for p, s_ in zip(prompts, slots):
+            self.prefills.append((int(s_), len(p)))
+        return torch.tensor([[float(len(p))] for p in prompts])   # each row carries its prompt length
 
-    def test_time_update_batch(self, ids, state, mask):
+    def greedy(self, logits, stop_free=True):
+        return torch.tensor([self.token_at(int(n)) for n in logits.reshape(-1).tolist()]), None
+
+    def test_time_update_batch(self, ids, state, mask, guard=None):
         self.writes.append((ids.shape[0], [int(m.sum()) for m in mask]))
         new = FastState(state.w_up + 1.0, state.w_gate, state.w_down, state.s_up, state.s_gate, state.s_down,
                         state.ln_weight, state.ln_bias)
         new.step = 2 * CFG.n_layers
-        return new, [1.0] * ids.shape[0], [[1.0] * CFG.n_layers for _ in range(ids.shape[0])]
+        out = (new, [1.0] * ids.shape[0], [[1.0] * CFG.n_layers for _ in range(ids.shape[0])])
+        if guard is not None:           # the pulled state's drift sums: 0.25 per matrix
+            out += (torch.full((ids.shape[0], 4), 0.25),)
+        return out
 
 
 class FakeGraph:
@@ -82,6 +89,7 @@ def _server(monkeypatch, capacity, max_batch, stops=None, stop_free=False, write
     monkeypatch.setattr(pool.SharedFastWeightPoolB200, "apply_elastic_pull", lambda self, st, lam, ratio: st)
     monkeypatch.setattr(pool.SharedFastWeightPoolB200, "compute_drift",
                         lambda self, st: {"drift_frobenius": 0.5, "drift_pct": 1.0})
+    monkeypatch.setattr(serving.ServingEngine, "_w0_sq", lambda self: [25.0, 25.0, 25.0])
     eng = FakeEngine(capacity + 1, stops)
     srv = serving.ServingEngine(eng, capacity=capacity, max_batch=max_batch, surprise_threshold=0.5,
                                 stop_free=stop_free, write_batch=write_batch, write_wait_s=1e9)
@@ -101,7 +109,9 @@ def test_stop_rules_and_results(monkeypatch):
     for t in (a, b, c):
         r = t.result
         assert r["gate_triggered"] and r["surprise_loss"] == 1.0 and r["step"] == 2 * CFG.n_layers
-        assert r["weight_drift_pct"] == 1.0 and r["user_id"] == t.user_id
+        # the drift report of a committed turn comes from the write's pulled sums (0.25 per matrix
+        # against ||W0_m||^2 = 25): 10 % of the anchor's norm, no drift pass
+        assert abs(r["weight_drift_pct"] - 10.0) < 1e-6 and r["user_id"] == t.user_id
     # the write saw prompt + reply of each turn
     assert sorted(n for _, lens in eng.writes for n in lens) == sorted([20 + 4, 40 + 4, 100 + 3])
 

@@ -51,6 +51,9 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_chunk_write_workspace": (sz, [i32, i32, i32, i32]),
     "uttt_chunk_write": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, i32, vp, vp, vp, vp, sz, vp]),
+    "uttt_chunk_write_guarded": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                       vp, vp, vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp, vp, f32, vp, vp, vp,
+                                       sz, vp]),
     "uttt_chunk_write_noalloc": (i32, [i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp, f32, f32, i32, f32, vp, i32, vp, vp, vp]),
     "uttt_chunk_write_noalloc_status": (i32, [i32, vp]),

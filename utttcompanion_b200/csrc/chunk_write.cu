@@ -96,6 +96,15 @@ struct ChunkParams {
   float* xch;
   unsigned* xflag;
   int dsplit;          // fwd kernel d-split (its kSplit variant): CTAs per (tile, row), folded into blockIdx.x
+  // stability guard in the last update of a row (uttt_chunk_write_guarded): on the call's last chunk,
+  // rows with g_final[b] != 0 get W <- W0 + g_keep (W - W0) (the elastic pull) right after their
+  // update, and sum ||W - W0||^2 of the pulled tiles per matrix into g_sums[4 b + m]
+  const float* g_w0_up;   // (d, h)
+  const float* g_w0_gate;
+  const float* g_w0_down; // (h, d)
+  const int* g_final;     // (B) or null: no guard
+  float* g_sums;          // (B, 4)
+  float g_keep;
 };
 
 template <typename WT>
@@ -941,6 +950,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     const int cq = half * 16;                        // this thread's 16 of the quarter's 32 columns
     const bool row_ok = h0 + row < p.h;
     float acc = 0.f;
+    // stability guard: this row's last update of the call (never a fused chunk: the call's last)
+    const bool guard = update && !skip && p.g_final != nullptr && p.g_final[b] != 0 &&
+                       p.chunk_index == p.n_chunks - 1 && !fuse;
+    float g_up = 0.f, g_gate = 0.f, g_down = 0.f;
     for (int qi = 0; qi < nq; ++qi) {
       const int j = qi >> 2, qq = qi & 3;
       // this quarter's momentum (issued before the waits so its latency overlaps them)
@@ -993,6 +1006,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
           for (int e = 0; e < 16; ++e) {
             p.s_up_out[so + (size_t)e * p.h] = su[e];
             p.s_gate_out[so + (size_t)e * p.h] = sg[e];
+          }
+        }
+        if (guard && row_ok) {          // elastic pull of the updated quarter (lanes: consecutive hidden rows)
+          const size_t go = (size_t)((q0 + qi) * QW + cq) * p.h + h0 + row;
+#pragma unroll 4
+          for (int e = 0; e < 16; ++e) {
+            const int o = (cq + e) * HT + row;
+            const float au = __ldg(p.g_w0_up + go + (size_t)e * p.h);
+            const float ag = __ldg(p.g_w0_gate + go + (size_t)e * p.h);
+            const float du = p.g_keep * (wu[o] - au), dg = p.g_keep * (wg[o] - ag);
+            wu[o] = au + du;
+            wg[o] = ag + dg;
+            g_up += du * du;
+            g_gate += dg * dg;
           }
         }
       }
@@ -1176,6 +1203,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
 #pragma unroll
         for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(p.s_down_out + sdo)[i] = sdv[i];
       }
+      if (guard && row_ok) {            // elastic pull of this row's 16 updated W_down values
+        const float4* a4 = reinterpret_cast<const float4*>(p.g_w0_down + (size_t)(h0 + row) * p.d + (q0 + qi) * QW + cq);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 a = __ldg(a4 + i);
+          const float dx = p.g_keep * (w4[i].x - a.x), dy = p.g_keep * (w4[i].y - a.y);
+          const float dz = p.g_keep * (w4[i].z - a.z), dw = p.g_keep * (w4[i].w - a.w);
+          w4[i] = make_float4(a.x + dx, a.y + dy, a.z + dz, a.w + dw);
+          *reinterpret_cast<float4*>(wd + sw128_offset(row, (cq + 4 * i) * 4)) = w4[i];
+          g_down += dx * dx + dy * dy + dz * dz + dw * dw;
+        }
+      }
       uint8_t* zA = (j & 1) ? sAU : slots + 4 * WTILE;  // Z' A tiles [128 d][128 hidden], MN-major
       if (fuse) {
         // this thread's 16 W'_down values of its hidden row -> BF16 A tile of d tile j
@@ -1202,6 +1241,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     if (!update) {
       acc = warp_sum(acc);
       if (lane == 0 && !skip) atomicAdd(p.norm2 + b, acc);
+    }
+    if (guard) {
+      g_up = warp_sum(g_up);
+      g_gate = warp_sum(g_gate);
+      g_down = warp_sum(g_down);
+      if (lane == 0) {
+        atomicAdd(p.g_sums + 4 * b + 0, g_up);
+        atomicAdd(p.g_sums + 4 * b + 1, g_gate);
+        atomicAdd(p.g_sums + 4 * b + 2, g_down);
+      }
     }
   } else if (warp == STORE_WARP) {
     // W' stores of loops A and B and the staging refills behind them, so the
@@ -1464,6 +1513,26 @@ extern "C" size_t uttt_chunk_write_workspace(int B, int C, int d, int h) {
   return bytes;
 }
 
+namespace uttt {
+namespace {
+struct GuardArgs {
+  const float* w0_up;
+  const float* w0_gate;
+  const float* w0_down;
+  float keep;
+  const int* final_rows;
+  float* sums;
+};
+int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q, const void* k,
+                     const void* v, const float* eta, const float* alpha, const float* mask, float* w_up,
+                     float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
+                     const float* ln_weight, const float* ln_bias, float momentum_beta, float max_grad_norm,
+                     int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss, float* clip_scale,
+                     int n_states, const int* state_rows, uttt_partial_sum_fn partial_sum, void* partial_sum_ctx,
+                     void* workspace, size_t workspace_bytes, void* stream, const GuardArgs* guard);
+}  // namespace
+}  // namespace uttt
+
 extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q,
                                 const void* k, const void* v, const float* eta, const float* alpha,
                                 const float* mask, float* w_up, float* w_gate, float* w_down, float* s_up,
@@ -1472,6 +1541,41 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
                                 void* out, int out_dtype, float* token_loss, float* clip_scale, int n_states,
                                 const int* state_rows, uttt_partial_sum_fn partial_sum, void* partial_sum_ctx,
                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return chunk_write_impl(B, T, C, d, h, chunk_begin, n_chunks, q, k, v, eta, alpha, mask, w_up, w_gate, w_down,
+                          s_up, s_gate, s_down, ln_weight, ln_bias, momentum_beta, max_grad_norm, normalize_by_dim,
+                          eps, out, out_dtype, token_loss, clip_scale, n_states, state_rows, partial_sum,
+                          partial_sum_ctx, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int uttt_chunk_write_guarded(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks,
+                                        const void* q, const void* k, const void* v, const float* eta,
+                                        const float* alpha, const float* mask, float* w_up, float* w_gate,
+                                        float* w_down, float* s_up, float* s_gate, float* s_down,
+                                        const float* ln_weight, const float* ln_bias, float momentum_beta,
+                                        float max_grad_norm, int normalize_by_dim, float eps, float* token_loss,
+                                        int n_states, const int* state_rows, const float* w_up0,
+                                        const float* w_gate0, const float* w_down0, float anchor_lambda,
+                                        const int* final_rows, float* drift_sums, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  UTTT_REQUIRE(w_up0 && w_gate0 && w_down0 && final_rows && drift_sums, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(anchor_lambda >= 0.f && anchor_lambda <= 1.f, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(((uintptr_t)w_down0 & 15u) == 0 && d % 4 == 0, UTTT_ERR_UNSUPPORTED);
+  const GuardArgs g{w_up0, w_gate0, w_down0, 1.f - anchor_lambda, final_rows, drift_sums};
+  return chunk_write_impl(B, T, C, d, h, chunk_begin, n_chunks, k, k, v, eta, alpha, mask, w_up, w_gate, w_down,
+                          s_up, s_gate, s_down, ln_weight, ln_bias, momentum_beta, max_grad_norm, normalize_by_dim,
+                          eps, nullptr, UTTT_DTYPE_F32, token_loss, nullptr, n_states, state_rows, nullptr, nullptr,
+                          workspace, workspace_bytes, stream, &g);
+}
+
+namespace uttt {
+namespace {
+int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q, const void* k,
+                     const void* v, const float* eta, const float* alpha, const float* mask, float* w_up,
+                     float* w_gate, float* w_down, float* s_up, float* s_gate, float* s_down,
+                     const float* ln_weight, const float* ln_bias, float momentum_beta, float max_grad_norm,
+                     int normalize_by_dim, float eps, void* out, int out_dtype, float* token_loss, float* clip_scale,
+                     int n_states, const int* state_rows, uttt_partial_sum_fn partial_sum, void* partial_sum_ctx,
+                     void* workspace, size_t workspace_bytes, void* stream, const GuardArgs* guard) {
   UTTT_REQUIRE(B > 0 && T > 0 && C > 0 && d > 0 && h > 0 && n_chunks >= 0 && chunk_begin >= 0, UTTT_ERR_INVALID);
   if (n_states <= 0) n_states = B;
   UTTT_REQUIRE(state_rows != nullptr || n_states == B, UTTT_ERR_INVALID);
@@ -1516,6 +1620,14 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   p.ss_ug = (long long)d * h; p.ss_d = (long long)h * d; p.ld_ug = h;
   p.state_index = state_rows;
   p.n_states = n_states;
+  if (guard) {
+    p.g_w0_up = guard->w0_up;
+    p.g_w0_gate = guard->w0_gate;
+    p.g_w0_down = guard->w0_down;
+    p.g_keep = guard->keep;
+    p.g_final = guard->final_rows;
+    p.g_sums = guard->sums;
+  }
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
   // d-split of the bwd kernel: with few rows, 54 hidden tiles per 1.58B state leave SMs idle or
   // end on a thin last wave; two CTAs per (tile, state), each streaming half of d, finish in
@@ -1649,6 +1761,8 @@ extern "C" int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_beg
   }
   return UTTT_OK;
 }
+}  // namespace
+}  // namespace uttt
 
 // ============================================================================
 // fast-weight readout entry point

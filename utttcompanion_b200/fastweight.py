@@ -77,7 +77,7 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
                 chunk_size: int = 64, chunk_begin: int = 0, n_chunks: Optional[int] = None,
                 out: Optional[torch.Tensor] = None, token_loss: Optional[torch.Tensor] = None,
                 clip_scale: Optional[torch.Tensor] = None, state_rows: Optional[torch.Tensor] = None,
-                partial_sum=None) -> None:
+                partial_sum=None, guard=None) -> None:
     """In-place multi-chunk write over ``(B, T, d)`` BF16 keys/values.
 
     Applies ``n_chunks`` consecutive chunk steps (``SharedFastWeightPool.chunk_step``
@@ -91,6 +91,10 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
     FP32 tensor ``t`` by its sum over the ranks (e.g. ``HiddenSplit.all_reduce``);
     it is called between launches for every chunk's partial Z and, with
     clipping, the squared gradient norms.
+    ``guard`` = (w_up0, w_gate0, w_down0, anchor_lambda, final_rows, drift_sums): the stability
+    guard folded into the write (``uttt_chunk_write_guarded``): on the last chunk, rows with
+    ``final_rows[b] != 0`` (int32 (B,)) are pulled towards W_0 right after their update and
+    ``drift_sums`` (FP32 (B, 4), zero on entry) receives each pulled matrix's ||W - W0||^2.
     """
     _require_cuda(k, v, eta, alpha, w_up, w_gate, w_down, s_up, s_gate, s_down, ln_weight, ln_bias, token_mask,
                   state_rows)
@@ -135,6 +139,23 @@ def chunk_write(k: torch.Tensor, v: torch.Tensor, eta: torch.Tensor, alpha: torc
                 traceback.print_exc()
                 return 1
         hook = _lib.PARTIAL_SUM_FN(_sum)
+    if guard is not None:
+        if partial_sum is not None or out is not None or clip_scale is not None:
+            raise ValueError("the guarded write takes no hidden split, readout or clip-scale output")
+        w0u, w0g, w0d, lam, final_rows, sums = guard
+        for t in (w0u, w0g, w0d, sums):
+            if t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError("W_0 and the drift sums must be contiguous FP32")
+        if final_rows.dtype != torch.int32 or final_rows.numel() != B or sums.numel() < 4 * B:
+            raise ValueError("final_rows must be int32 (B,) and drift_sums (B, 4)")
+        st = lib.uttt_chunk_write_guarded(
+            B, T, chunk_size, d, h, chunk_begin, n_chunks, _ptr(k), _ptr(k), _ptr(v), _ptr(eta), _ptr(alpha),
+            _ptr(token_mask), _ptr(w_up), _ptr(w_gate), _ptr(w_down), _ptr(s_up), _ptr(s_gate), _ptr(s_down),
+            _ptr(ln_weight), _ptr(ln_bias), float(momentum_beta), float(max_inner_grad_norm),
+            int(bool(normalize_by_dim)), float(eps), _ptr(token_loss), S, _ptr(state_rows), _ptr(w0u), _ptr(w0g),
+            _ptr(w0d), float(lam), _ptr(final_rows), _ptr(sums), ws.data_ptr(), ws.numel(), _stream(k.device))
+        _lib.check(st, "uttt_chunk_write_guarded")
+        return
     st = lib.uttt_chunk_write(
         B, T, chunk_size, d, h, chunk_begin, n_chunks, _ptr(k), _ptr(k), _ptr(v), _ptr(eta), _ptr(alpha),
         _ptr(token_mask), _ptr(w_up), _ptr(w_gate), _ptr(w_down), _ptr(s_up), _ptr(s_gate), _ptr(s_down),

@@ -300,6 +300,70 @@ class UtttB200:
             x = self._resid_linear(h, r.reshape(T, d), lay.w_o, self.layers[i + 1].attn_norm if i + 1 < L else self.norm)
         return x
 
+    def prefill_batch(self, prompts: Sequence[torch.Tensor], slots: Sequence[int], read_packed: torch.Tensor,
+                      read_down: torch.Tensor, state_index: Sequence[int]) -> torch.Tensor:
+        """Frozen forward of several personas' prompts of any lengths at once; fills each persona's KV
+        ring; returns the last-token logits (n, V) FP32 of BF16 values.
+
+        The prompts are packed one after another, each padded to a multiple of 64 tokens, so every
+        projection GEMM and the fast-weight readout (one 64-token tile per state row) run once per
+        layer for all of them; attention and the ring fill run per prompt on its own rows.  Padding
+        rows never reach a prompt's rows (causal attention, row-wise everything else)."""
+        cfg = self.cfg
+        n = len(prompts)
+        if n == 0 or len(slots) != n or len(state_index) != n:
+            raise ValueError("one slot and one state index per prompt")
+        lens = [int(p.numel()) for p in prompts]
+        if min(lens) < 1 or max(lens) + 1 >= self.n_pos:
+            raise ValueError("prompt empty or longer than the RoPE table")
+        d, hd, nh, nkv, W = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.sliding_window_size
+        dev = self.device
+        spans = [(T + 63) // 64 * 64 for T in lens]
+        offs = [0]
+        for sp in spans:
+            offs.append(offs[-1] + sp)
+        R = offs[-1]
+        ids = torch.zeros(R, dtype=torch.long)
+        tile_state = []
+        for p, T, o, sp, si in zip(prompts, lens, offs, spans, state_index):
+            ids[o:o + T] = p.reshape(-1).to(torch.long).cpu()
+            tile_state += [int(si)] * (sp // 64)
+        if int(ids.min()) < 0 or int(ids.max()) >= self.emb.shape[0]:
+            raise ValueError("token id outside the vocabulary")
+        h = self._embed(ids)
+        tiles = torch.tensor(tile_state, dtype=torch.int32, device=dev)
+        slot_t = [torch.tensor([int(s_)], dtype=torch.int32, device=dev) for s_ in slots]
+        qkv = torch.empty(R, self.qkv_dim, dtype=torch.bfloat16, device=dev)
+        qs = torch.empty(R, nh * hd, dtype=torch.bfloat16, device=dev)
+        kv_off = [0]
+        for T in lens:
+            kv_off.append(kv_off[-1] + nkv * T * hd)
+        kflat = torch.empty(kv_off[-1], dtype=torch.bfloat16, device=dev)
+        vflat = torch.empty_like(kflat)
+        att = torch.zeros(R, d, dtype=torch.bfloat16, device=dev)      # padding rows stay finite
+        esz = kflat.element_size()
+        x = self._rmsnorm(h, self.layers[0].attn_norm)
+        L = len(self.layers)
+        for i, lay in enumerate(self.layers):
+            self._linear(x, lay.wqkv, [_seg(0, self.qkv_dim, _lib.SEG_STORE, qkv, self.qkv_dim)])
+            for j, T in enumerate(lens):
+                o = offs[j]
+                kb = kflat.data_ptr() + kv_off[j] * esz
+                vb = vflat.data_ptr() + kv_off[j] * esz
+                _lib.check(self.lib.uttt_attn_prefill(1, T, 0, 0, nh, nkv, hd, W, qkv[o].data_ptr(), self.qkv_dim,
+                                                      self.rope_cos.data_ptr(), self.rope_sin.data_ptr(),
+                                                      qs[o].data_ptr(), kb, vb, att[o].data_ptr(), self._st()),
+                           "uttt_attn_prefill")
+                _lib.check(self.lib.uttt_kv_ring_fill(1, T, T, nkv, hd, W, kb, vb, slot_t[j].data_ptr(),
+                                                      self.k_ring[i].data_ptr(), self.v_ring[i].data_ptr(),
+                                                      self._st()), "uttt_kv_ring_fill")
+            x2 = self._resid_linear(h, att, lay.wo, lay.uttt_norm)
+            q = self._q_proj(lay, x2)
+            r = self._readout(q.reshape(R // 64, 64, d), read_packed, read_down, tiles)
+            x = self._resid_linear(h, r.reshape(R, d), lay.w_o, self.layers[i + 1].attn_norm if i + 1 < L else self.norm)
+        last = torch.tensor([o + T - 1 for o, T in zip(offs, lens)], dtype=torch.long, device=dev)
+        return self._lm_head(x.index_select(0, last).contiguous())
+
     # ------------------------------------------------------------------ KV rings <-> chronological caches
     def export_kv(self, slot: int, end_pos: int) -> List[Tuple[torch.Tensor, torch.Tensor]]:
         """The persona's KV history as the reference's per-layer caches: (1, n_kv, L, hd) BF16 in
@@ -414,7 +478,8 @@ class UtttB200:
         return new, surprises[0], per_layer[0]
 
     def test_time_update_batch(self, interaction_ids: torch.Tensor, fast_state: FastState,
-                               attention_mask: Optional[torch.Tensor] = None, return_logits: bool = False):
+                               attention_mask: Optional[torch.Tensor] = None, return_logits: bool = False,
+                               guard: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor, float]] = None):
         """The write of B personas at once: rows of ``interaction_ids`` (B, T) with
         masks; ``fast_state`` holds B stacked states.  Every chunk of every layer is
         one packed launch sequence over the rows still in the batch: a row leaves
@@ -425,7 +490,11 @@ class UtttB200:
         ``return_logits`` also the logits (B, T, V) FP32 of every position as the writing forward
         reads them (every row then stays in the batch to its end, padding included).
         Per-row statistics follow the reference's single-persona definitions
-        (model/uttt_model.py:598-607, 833-838)."""
+        (model/uttt_model.py:598-607, 833-838).
+        ``guard`` = (w_up0, w_gate0, w_down0, anchor_lambda): the elastic pull of the stability guard
+        (``apply_elastic_pull``, model/uttt_layer.py:773-832) runs inside each row's last update, and
+        the per-row sums ||W_m - W0_m||^2 of the pulled state (B, 4) FP32 come back as the last output.
+        A row whose turn is gated off is simply not committed, so the pull can always run."""
         cfg = self.cfg
         dev = self.device
         ids = interaction_ids.to(device=dev)
@@ -437,6 +506,8 @@ class UtttB200:
             raise ValueError("chunk_size > 64 is not supported by the B200 write kernels")
         if fast_state.w_up.shape[0] != B:
             raise ValueError(f"fast_state holds {fast_state.w_up.shape[0]} states for {B} rows")
+        if guard is not None and self.hsplit is not None:
+            raise ValueError("the guarded write needs whole (unsplit) states")
         cur = fast_state.clone()
         if attention_mask is None:
             mask_all, last = None, [T - 1] * B
@@ -452,6 +523,7 @@ class UtttB200:
         rows = torch.arange(B, dtype=torch.int32, device=dev)
         chunk_losses, counts = [], []
         final = torch.empty(B, T, d, dtype=torch.bfloat16, device=dev) if return_logits else None
+        drift = torch.zeros(B, 4, dtype=torch.float32, device=dev) if guard is not None else None
         for off in range(0, T, C):
             Cc = min(C, T - off)
             keep_rows = list(alive) if return_logits else [r for r in alive if last[r] >= off]
@@ -526,10 +598,20 @@ class UtttB200:
             Ar = ALPHA.reshape(L, Bc, Cc).permute(1, 0, 2).reshape(Bc, L * Cc).contiguous()
             Mr = None if m is None else m.repeat(1, L).contiguous()
             loss = torch.empty(Bc, L * Cc, dtype=torch.float32, device=dev)
+            g = None
+            if guard is not None:
+                # the rows whose last valid token is in this chunk take their final update here
+                fin = torch.tensor([1 if off <= last[r] < off + Cc else 0 for r in alive], dtype=torch.int32,
+                                   device=dev)
+                sums = torch.zeros(Bc, 4, dtype=torch.float32, device=dev)
+                g = (*guard, fin, sums)
             chunk_write(Kr, Vr, Er, Ar, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,
                         cur.ln_weight, cur.ln_bias, Mr, cfg.momentum_beta, float(cfg.max_inner_grad_norm or 0.0),
                         cfg.normalize_loss_by_dim, cfg.rms_norm_eps, chunk_size=Cc, token_loss=loss,
-                        state_rows=rows, partial_sum=None if self.hsplit is None else self.hsplit.all_reduce)
+                        state_rows=rows, partial_sum=None if self.hsplit is None else self.hsplit.all_reduce,
+                        guard=g)
+            if g is not None:
+                drift.index_add_(0, rows_l, sums)
             lz = loss.reshape(Bc, L, Cc)
             if m is None:
                 layer_loss = lz.mean(dim=2)                                        # (Bc, L)
@@ -553,9 +635,12 @@ class UtttB200:
         means = [sum(r) / max(len(r), 1) for r in per_layer]
         cur.last_surprise_loss = means[0] if B == 1 else float(sum(means) / B)
         cur.surprise_history = (list(fast_state.surprise_history) + (per_layer[0] if B == 1 else []))[-100:]
+        out = (cur, means, per_layer)
         if final is not None:
-            return cur, means, per_layer, self._lm_head(final.reshape(B * T, d)).reshape(B, T, -1)
-        return cur, means, per_layer
+            out += (self._lm_head(final.reshape(B * T, d)).reshape(B, T, -1),)
+        if drift is not None:
+            out += (drift,)
+        return out
 
 
 class DecodeTable:

@@ -217,8 +217,10 @@ class ServingEngine:
     def __init__(self, engine: UtttB200, capacity: int, max_batch: int, surprise_threshold: float = 0.25,
                  elastic_anchor_lambda: float = 0.02, max_weight_drift_ratio: Optional[float] = 0.35,
                  online_ttt: bool = True, stop_free: bool = False, write_batch: int = 8,
-                 write_wait_s: float = 0.05, async_writes: bool = False):
-        """``stop_free``: replies run to their ``max_new_tokens`` (role ids and EOS are masked
+                 write_wait_s: float = 0.05, async_writes: bool = False, prefill_budget: int = 16384):
+        """``prefill_budget``: turns admitted in one step are prefilled together (one batched prefill, the
+        prompts packed one after another) up to this many prompt tokens.
+        ``stop_free``: replies run to their ``max_new_tokens`` (role ids and EOS are masked
         from the greedy pick, as the reference's graph-vs-eager test does), e.g. for
         forced-length load tests; otherwise stream_generate's stop rules apply.
         Finished turns are written together: once ``write_batch`` are waiting, the oldest has
@@ -230,7 +232,9 @@ class ServingEngine:
         on the 151M serve sweep at 32 req/s it raised the mean latency from 0.72 s to
         3.1 s (writes between steps form fewer, larger batches)."""
         self.engine = engine
+        self._w0_norm2: Optional[List[float]] = None
         self.stop_free = stop_free
+        self.prefill_budget = max(1, int(prefill_budget))   # prompt tokens prefilled together per step
         self.write_batch = max(1, write_batch)
         self.write_wait_s = write_wait_s
         self._write_queue: List[Turn] = []
@@ -368,10 +372,19 @@ class ServingEngine:
 
     # ------------------------------------------------------------------ scheduler
     def _admit(self) -> None:
+        """Start waiting turns in free rows: one batched prefill of every admitted prompt (up to
+        ``prefill_budget`` prompt tokens per step, at least one turn), then each row starts on the device
+        from its prompt's greedy pick (no host round trip; the stop rules apply to that first token there
+        too)."""
         e = self.engine
         deferred: Deque[Turn] = collections.deque()
+        admitted: List[Turn] = []
+        tokens = 0
         while self.waiting and None in self.active:
             t = self.waiting.popleft()
+            if admitted and tokens + len(t.prompt_ids) > self.prefill_budget:
+                deferred.append(t)                          # the rest waits for the next step
+                break
             row = self.active.index(None)
             with self._lock:
                 if t.user_id in self.in_flight_users:      # its previous turn's write is still landing
@@ -384,18 +397,25 @@ class ServingEngine:
                     break
                 self.arena.pinned.add(t.slot)
                 self.in_flight_users.add(t.user_id)
-            ids = torch.tensor(t.prompt_ids, dtype=torch.long)
-            t0 = time.perf_counter()
-            logits = e.prefill(ids, t.slot, self.arena.read_packed, self.arena.read_down, t.slot)
-            tok, _ = e.greedy(logits.unsqueeze(0), stop_free=self.stop_free)
-            # the row starts on the device from the prefill's pick (no host round trip); the stop rules
-            # apply to that first token there too
-            self.table.admit(row, tok, len(t.prompt_ids), t.slot, t.slot, t.max_new_tokens, t.eos_token_id)
-            t.row, t.admit_seq, t.seen = row, self._seq, 0
-            self.stats["prefill_s"] += time.perf_counter() - t0
-            self.stats["prefill_tokens"] += len(t.prompt_ids)
+            t.row = row
             self.active[row] = t
+            admitted.append(t)
+            tokens += len(t.prompt_ids)
         self.waiting.extendleft(reversed(deferred))
+        if not admitted:
+            return
+        t0 = time.perf_counter()
+        logits = e.prefill_batch([torch.tensor(t.prompt_ids, dtype=torch.long) for t in admitted],
+                                 [t.slot for t in admitted], self.arena.read_packed, self.arena.read_down,
+                                 [t.slot for t in admitted])
+        picks, _ = e.greedy(logits, stop_free=self.stop_free)
+        for i, t in enumerate(admitted):
+            self.table.admit(t.row, picks[i:i + 1], len(t.prompt_ids), t.slot, t.slot, t.max_new_tokens,
+                             t.eos_token_id)
+            t.admit_seq, t.seen = self._seq, 0
+        self.stats["prefill_s"] += time.perf_counter() - t0
+        self.stats["prefill_tokens"] += tokens
+        self.stats["prefill_batches"] += 1
 
     def _harvest(self, buf: int, bucket: int, seq: int) -> None:
         """Take the results of decode step ``seq`` (snapshot ``buf``): the reply tokens each turn yielded
@@ -485,7 +505,15 @@ class ServingEngine:
             ids[r, :len(s)] = torch.tensor(s)
             mask[r, :len(s)] = 1.0
         state = self.arena.state(slots)
-        new, surprises, per_layer = self.engine.test_time_update_batch(ids, state, mask)
+        # the elastic pull runs inside each row's last update (model/uttt_layer.py:773-801) and the
+        # write returns the pulled state's ||W_m - W0_m||^2; a row whose turn is gated off is simply
+        # not committed, so the pull can run for every row
+        lam = max(float(self.elastic_anchor_lambda or 0.0), 0.0)
+        guard = (self.pool.w_up_init, self.pool.w_gate_init, self.pool.w_down_init, lam)
+        new, surprises, per_layer, sums = self.engine.test_time_update_batch(ids, state, mask, guard=guard)
+        sums = sums.double().cpu()
+        base = self._w0_sq()
+        ratio = self.max_weight_drift_ratio
         outcomes = []
         for r, t in enumerate(turns):
             s = surprises[r]
@@ -493,21 +521,26 @@ class ServingEngine:
                 raise ValueError("Test-time update returned a non-finite or negative surprise loss; "
                                  "persona was not changed")
             gate = s > self.surprise_threshold
+            meta = self.arena.meta[t.slot]
             if gate:
                 one = FastState(*(x[r:r + 1] for x in (new.w_up, new.w_gate, new.w_down, new.s_up, new.s_gate,
                                                       new.s_down)), new.ln_weight, new.ln_bias)
-                pulled = self.pool.apply_elastic_pull(one, self.elastic_anchor_lambda, self.max_weight_drift_ratio)
+                sq = [float(sums[r, m]) for m in range(3)]
+                scale = 1.0
+                if ratio is not None and ratio > 0.0:    # the drift clamp (:803-818): a pass only when it bites
+                    scale = min(ratio * math.sqrt(sum(base) + 1e-8) / math.sqrt(sum(sq) + 1e-8), 1.0)
+                    if scale < 1.0:
+                        one = self.pool.apply_elastic_pull(one, 0.0, ratio)
                 a = self.arena
-                for name, src in (("w_up", pulled.w_up), ("w_gate", pulled.w_gate), ("w_down", pulled.w_down),
-                                  ("s_up", pulled.s_up), ("s_gate", pulled.s_gate), ("s_down", pulled.s_down)):
+                for name, src in (("w_up", one.w_up), ("w_gate", one.w_gate), ("w_down", one.w_down),
+                                  ("s_up", one.s_up), ("s_gate", one.s_gate), ("s_down", one.s_down)):
                     getattr(a, name)[t.slot].copy_(src[0])
-                meta = a.meta[t.slot]
                 meta["step"] = int(meta.get("step", 0)) + new.step
                 meta["last_surprise_loss"] = s
                 meta["surprise_history"] = (meta.get("surprise_history", []) + per_layer[r])[-100:]
+                meta["drift"] = self._drift_report([q * scale * scale for q in sq], base)
                 a.refresh([t.slot])
             else:
-                meta = self.arena.meta[t.slot]
                 meta["last_surprise_loss"] = s
                 meta["surprise_history"] = (meta.get("surprise_history", []) + [s])[-100:]
             outcomes.append((t, s, per_layer[r], gate))
@@ -518,8 +551,38 @@ class ServingEngine:
         for t, s, pl, gate in outcomes:
             self._finish(t, s, pl, gate)
 
+    def _w0_sq(self) -> List[float]:
+        """||W0_m||^2 of the shared anchor, m = up, gate, down (computed once)."""
+        if self._w0_norm2 is None:
+            w0 = [w.unsqueeze(0).contiguous() for w in (self.pool.w_up_init, self.pool.w_gate_init,
+                                                          self.pool.w_down_init)]
+            d, h = w0[0].shape[1:]
+            out = torch.zeros(8, dtype=torch.float32, device=self.engine.device)
+            _lib.check(_lib.load().uttt_drift_sums(1, d, h, *(w.data_ptr() for w in w0),
+                                                   *(w.data_ptr() for w in w0), out.data_ptr(),
+                                                   _stream(self.engine.device)), "uttt_drift_sums")
+            self._w0_norm2 = [float(x) for x in out[4:7].double().cpu()]
+        return self._w0_norm2
+
+    @staticmethod
+    def _drift_report(sq: List[float], base: List[float]) -> Dict[str, float]:
+        """compute_drift's report (model/uttt_layer.py:834-874) from the per-matrix sums of squares."""
+        d_up, d_gate, d_down = (math.sqrt(max(q, 0.0)) for q in sq)
+        b_up, b_gate, b_down = (math.sqrt(q) for q in base)
+        total = math.sqrt(d_up ** 2 + d_gate ** 2 + d_down ** 2)
+        bn = math.sqrt(b_up ** 2 + b_gate ** 2 + b_down ** 2) + 1e-8
+        return {"drift_frobenius": total, "base_frobenius": bn, "drift_pct": total / bn * 100.0,
+                "w_up_drift": d_up, "w_gate_drift": d_gate, "w_down_drift": d_down,
+                "w_up_drift_pct": d_up / (b_up + 1e-8) * 100.0, "w_gate_drift_pct": d_gate / (b_gate + 1e-8) * 100.0,
+                "w_down_drift_pct": d_down / (b_down + 1e-8) * 100.0}
+
     def _finish(self, t: Turn, surprise, per_layer, gate) -> None:
-        drift = self.pool.compute_drift(self.arena.state([t.slot]))
+        meta = self.arena.meta[t.slot]
+        drift = meta.get("drift")
+        if drift is None:               # a persona this engine has not written: one drift pass
+            drift = self.pool.compute_drift(self.arena.state([t.slot]))
+            meta["drift"] = drift
+        drift = dict(drift, step=int(meta.get("step", 0)), last_surprise_loss=meta.get("last_surprise_loss", 0.0))
         with self._lock:
             self._finish_locked(t, surprise, per_layer, gate, drift)
         if t.on_event is not None:
