@@ -1255,7 +1255,7 @@ def ours_arm(args, world, rank, local):
                 bufs[i][n].copy_(host[n], non_blocking=True)
             ready[i].record(cps)
 
-    e2e_steps = max(2, min(args.steps, 5))
+    e2e_steps = max(2, args.steps)           # as many steps as the device-timed region
     barrier()
     torch.cuda.synchronize()
     e0.record()

@@ -370,7 +370,8 @@ def test_batched_ragged_prefill_equals_per_prompt_prefill():
     """UtttB200.prefill_batch over prompts of ragged lengths (1, 5, 64, 70, 130, 40: padded in-batch
     to 64-token spans, longer than the 32-slot window) gives each persona the logits and KV ring of
     its own prefill.  The packed GEMMs see more rows, so split-K and accumulation order differ:
-    logits within 1e-2 and equal greedy ids away from near-ties, rings within one BF16 ULP."""
+    logits within 1e-2 and equal greedy ids away from near-ties; layer 0's ring within one BF16 ULP,
+    deeper layers' rings within 2e-2 rel-L2 (their inputs carry that BF16 rounding)."""
     cfg = _tiny_cfg()
     sd = reference_init_state_dict(cfg, seed=12)
     P = 6
@@ -396,8 +397,13 @@ def test_batched_ragged_prefill_equals_per_prompt_prefill():
         top = np.sort(w1)[-2:]
         if top[1] - top[0] > 2e-2:
             assert int(np.argmax(w1)) == int(np.argmax(w2)), p
+    ring_rel = []
     for i in range(cfg.n_layers):
         for ra, rb in ((a.k_ring[i], b.k_ring[i]), (a.v_ring[i], b.v_ring[i])):
             x, y = ra.float(), rb.float()
-            assert bool(((x - y).abs() <= x.abs() / 128 + 1e-3).all()), i
-    record("prefill_batch", max_abs_logit_diff=worst)
+            if i == 0:      # layer 0's keys / values come straight from the embeddings: one BF16 ULP
+                assert bool(((x - y).abs() <= x.abs() / 128 + 1e-3).all()), i
+            rel = float(torch.linalg.norm(x - y) / torch.linalg.norm(x))
+            ring_rel.append(rel)
+            assert rel <= 2e-2, (i, rel)     # deeper layers carry the activations' BF16 rounding
+    record("prefill_batch", max_abs_logit_diff=worst, max_ring_rel_l2=max(ring_rel))

@@ -276,9 +276,65 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
   const int state = p.state_index ? p.state_index[b] : b;
   if (warp < 8) {
     // ------------------------------------------------------------ producers
+    // BF16 read copies need no conversion: every 16-byte chunk of a k-block / W_down tile goes
+    // straight into its swizzled operand slot by cp.async, kAhead ring items ahead of the one being
+    // handed to the tensor cores, so ~3 x 32 KB per CTA are in flight without registers (register
+    // loads kept ~32 KB in flight and left the BF16 readout at a third of HBM).  FP32 masters are
+    // converted by the producers as they arrive.
+    constexpr bool kAsync = sizeof(WT) == 2;
+    constexpr int kAhead = NSLOT - 1;
+    const int n_items = nkb + nmt;
+    int it = 0;
+    // ring item i: k-block i of U/G (i < nkb) or W_down tile i - nkb
+    auto issue = [&](int i) {
+      const int s = i % NSLOT;
+      mbar_wait(&empty[s], ((i / NSLOT) & 1) ^ 1, p.status);
+      uint8_t* base = slots + s * SLOT_BYTES;
+      if (i < nkb) {
+        // 64 rows (k) x 128 cols (hidden) of W_up and of W_gate: [64-col half][64 rows][128 B]
+        const __nv_bfloat16* wu = reinterpret_cast<const __nv_bfloat16*>(p.src_up) + (size_t)state * p.ss_ug;
+        const __nv_bfloat16* wg = reinterpret_cast<const __nv_bfloat16*>(p.src_gate) + (size_t)state * p.ss_ug;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int idx = tid + j * NPROD;  // 0..1023: 64 rows x 16 chunks of 8 columns
+          const int kr = idx >> 4, c8 = (idx & 15) * 8;
+          const int col = h0 + c8;
+          const bool ok = col < p.h;
+          const size_t off = (size_t)((kb0 + i) * 64 + kr) * p.ld_ug + (ok ? col : 0);
+          const uint32_t o = (c8 >> 6) * 8192 + sw128_offset(kr, (c8 & 63) * 2);
+          cp_async_16(base + o, wu + off, ok);
+          cp_async_16(base + 16384 + o, wg + off, ok);
+        }
+      } else {
+        // W_down rows of this hidden tile, d columns of tile mt: [dblk 2][hh 128][64 d]
+        const int mt = i - nkb;
+        const __nv_bfloat16* wd = reinterpret_cast<const __nv_bfloat16*>(p.src_down) + (size_t)state * p.ss_d;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int idx = tid + j * NPROD;  // 0..2047: 128 rows x 16 chunks of 8 columns
+          const int hh = idx >> 4, c8 = (idx & 15) * 8;
+          const bool ok = h0 + hh < p.h;
+          const size_t off = (size_t)(ok ? h0 + hh : h0) * p.d + (mt0 + mt) * 128 + c8;
+          cp_async_16(base + (c8 >> 6) * 16384 + sw128_offset(hh, (c8 & 63) * 2), wd + off, ok);
+        }
+      }
+    };
+    if constexpr (kAsync) {
+      for (int i = 0; i < kAhead; ++i) {
+        if (i < n_items) issue(i);
+        cp_async_commit();
+      }
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (kb + kAhead < n_items) issue(kb + kAhead);
+        cp_async_commit();
+        cp_async_wait<kAhead>();                        // this thread's copies of k-block kb have landed
+        fence_proxy_async_smem();
+        mbar_arrive(&full[kb % NSLOT]);
+      }
+      it = nkb;
+    } else {
     const WT* wu = reinterpret_cast<const WT*>(p.src_up) + (size_t)state * p.ss_ug;
     const WT* wg = reinterpret_cast<const WT*>(p.src_gate) + (size_t)state * p.ss_ug;
-    int it = 0;
     for (int kb = 0; kb < nkb; ++kb, ++it) {
       const int s = it % NSLOT;
       mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
@@ -312,6 +368,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       mbar_arrive(&full[s]);
     }
 
+    }
     // ------------------------------------------------------------ epilogue 1: H
     mbar_wait(&ug_done, 0, p.status);
     tc_fence_after();
@@ -371,43 +428,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
     }
 
     // ------------------------------------------------------------ W_down tiles + Z drain
-    const WT* wd = reinterpret_cast<const WT*>(p.src_down) + (size_t)state * p.ss_d;
-    for (int mt = 0; mt < nmt; ++mt, ++it) {
-      const int s = it % NSLOT;
-      mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
-      uint8_t* sA = slots + s * SLOT_BYTES;
-      // A (M = d slice of 128, K = 128 hidden rows), MN-major: [dblk 2][hh 128][64 d]
-#pragma unroll 4
-      for (int j = 0; j < 16; ++j) {
-        const int idx = tid + j * NPROD;  // 0..4095
-        const int hh = idx >> 5, c4 = (idx & 31) * 4;
-        typename Q::V f = Q::zero();
-        if (h0 + hh < p.h) f = Q::load(wd + (size_t)(h0 + hh) * p.d + (mt0 + mt) * 128 + c4);
-        *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = Q::pack(f);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&full[s]);
-
-      // drain the previous Z tile while the tensor cores work on this one
-      if (mt > 0) {
-        const int pm = mt - 1, zb = pm & 1;
-        mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
-        tc_fence_after();
-        const int q = warp & 3, half = warp >> 2;
-        const int row = q * 32 + lane, c0 = half * 32;
-        float z[32];
-        tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
-        tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&zfree[zb]);
-        float* za = p.zacc + zrow0 * p.d + (mt0 + pm) * 128 + row;
-        for (int i = 0; i < 32; ++i)
-          if (c0 + i < Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
-      }
-    }
-    {
-      const int pm = nmt - 1, zb = pm & 1;
+    // drains Z tile pm (TMEM rows = d, columns = tokens) into zacc; `release`: give the TMEM
+    // buffer back to the MMA warp (every tile but the last)
+    auto drain = [&](int pm, bool release) {
+      const int zb = pm & 1;
       mbar_wait(&zfull[zb], (pm >> 1) & 1, p.status);
       tc_fence_after();
       const int q = warp & 3, half = warp >> 2;
@@ -416,10 +440,45 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_fwd_kernel(const __grid_con
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0), *reinterpret_cast<float(*)[16]>(&z[0]));
       tmem_ld16(tmem_addr(tZ + zb * 64, q * 32, c0 + 16), *reinterpret_cast<float(*)[16]>(&z[16]));
       tmem_wait_ld();
+      if (release) {
+        tc_fence_before();
+        mbar_arrive(&zfree[zb]);
+      }
       float* za = p.zacc + zrow0 * p.d + (mt0 + pm) * 128 + row;
       for (int i = 0; i < 32; ++i)
         if (c0 + i < Cc) red_add_f32(za + (size_t)(c0 + i) * p.d, z[i]);
+    };
+    if constexpr (kAsync) {
+      for (int mt = 0; mt < nmt; ++mt) {
+        const int i = nkb + mt;
+        if (i + kAhead < n_items) issue(i + kAhead);
+        cp_async_commit();
+        cp_async_wait<kAhead>();                        // this thread's copies of item i have landed
+        fence_proxy_async_smem();
+        mbar_arrive(&full[i % NSLOT]);
+        if (mt > 0) drain(mt - 1, true);                // while the tensor cores work on tile mt
+      }
+    } else {
+      const WT* wd = reinterpret_cast<const WT*>(p.src_down) + (size_t)state * p.ss_d;
+      for (int mt = 0; mt < nmt; ++mt, ++it) {
+        const int s = it % NSLOT;
+        mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
+        uint8_t* sA = slots + s * SLOT_BYTES;
+        // A (M = d slice of 128, K = 128 hidden rows), MN-major: [dblk 2][hh 128][64 d]
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+          const int idx = tid + j * NPROD;  // 0..4095
+          const int hh = idx >> 5, c4 = (idx & 31) * 4;
+          typename Q::V f = Q::zero();
+          if (h0 + hh < p.h) f = Q::load(wd + (size_t)(h0 + hh) * p.d + (mt0 + mt) * 128 + c4);
+          *reinterpret_cast<uint2*>(sA + (c4 >> 6) * 16384 + sw128_offset(hh, (c4 & 63) * 2)) = Q::pack(f);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full[s]);
+        if (mt > 0) drain(mt - 1, true);                // drain the previous Z tile meanwhile
+      }
     }
+    drain(nmt - 1, false);
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
       tma_prefetch_desc(&tmK);
@@ -1780,6 +1839,8 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
                                          size_t workspace_bytes, void* stream) {
   UTTT_REQUIRE(B > 0 && T > 0 && d > 0 && h > 0 && x && w_packed && w_down && z && workspace, UTTT_ERR_INVALID);
   UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
+  // the tensor-core readout copies the BF16 read copies in 16-byte pieces
+  UTTT_REQUIRE((((uintptr_t)w_packed | (uintptr_t)w_down) & 15u) == 0, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(workspace_bytes >= 256, UTTT_ERR_WORKSPACE);
   cudaStream_t st = (cudaStream_t)stream;
   UTTT_TRY(cuda_status(cudaMemsetAsync(z, 0, (size_t)B * T * d * sizeof(float), st)));
@@ -1845,6 +1906,7 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
   UTTT_REQUIRE(out_dtype == UTTT_DTYPE_F32 || out_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
   UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && h % 8 == 0, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(eps > 0.f, UTTT_ERR_INVALID);
+  UTTT_REQUIRE(w_dtype == UTTT_DTYPE_F32 || (((uintptr_t)w_up | (uintptr_t)w_down) & 15u) == 0, UTTT_ERR_UNSUPPORTED);
   UTTT_REQUIRE(workspace_bytes >= uttt_fast_readout_workspace(B, T, d, h), UTTT_ERR_WORKSPACE);
   cudaStream_t st = (cudaStream_t)stream;
   WsCursor ws(workspace, workspace_bytes);

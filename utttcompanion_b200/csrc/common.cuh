@@ -171,6 +171,20 @@ __device__ __forceinline__ void bulk_wait_read() {
 // wait until all committed bulk groups have completed (writes visible)
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// 16-byte asynchronous copy global -> shared (no registers), zero-filled when !valid (then the
+// source is not read); completion is tracked per thread by commit / wait groups, and the data
+// must be made visible to the tensor cores with fence_proxy_async_smem() after the wait.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // named barrier over `count` threads (a multiple of 32), id 1..15
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
