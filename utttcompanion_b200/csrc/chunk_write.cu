@@ -105,7 +105,16 @@ struct ChunkParams {
   const int* g_final;     // (B) or null: no guard
   float* g_sums;          // (B, 4)
   float g_keep;
+  // clip-norm runs: the norm pass (update = 0) stores its epilogue-1 operands, the swizzled
+  // shared-memory images of dU, dG and H of every (row, tile), [b][tile][3][16 KB]; the update
+  // pass (update = 1) copies them back instead of reading W_down again for dH
+  uint8_t* ops;
+  // clip-norm runs: per row the chunk's Gram matrices K K^T and dZ dZ^T, [b][2][64][64] FP32 (zero
+  // before chunk_gram_kernel); with them the norm pass needs no weight-gradient tiles:
+  // ||K^T dU||^2 = <K K^T, dU^T dU> over the 64 x 64 token pairs, and likewise for dG and H^T dZ
+  float* gram;
 };
+constexpr int OPS_BYTES = 3 * 16384;   // one (row, tile) entry of ChunkParams::ops
 
 template <typename WT>
 struct Quad;
@@ -760,6 +769,63 @@ __global__ void __launch_bounds__(LN_THREADS) readout_ln_kernel(const float* __r
 // bwd: dH, dU, dG and the three weight gradients; NORM pass accumulates
 // ||grad||^2, UPDATE pass applies momentum / decay / clip in place.
 // ============================================================================
+// K K^T and dZ dZ^T of each row's chunk, summed over 128-wide slabs of d (grid (d / 128, B)).
+// Token rows past the chunk are zero.  Thread (ti, tj) owns the entries (ti + 16 a, tj + 16 c),
+// so a warp's 16-byte reads of the j rows fall in distinct banks of the padded rows.
+constexpr int GRAM_D = 128;
+__global__ void __launch_bounds__(256) chunk_gram_kernel(const ChunkParams p) {
+  __shared__ __align__(16) __nv_bfloat16 sm[2][CT][GRAM_D + 8];
+  const int tid = threadIdx.x, b = blockIdx.y, dd0 = blockIdx.x * GRAM_D;
+  for (int i = tid; i < CT * (GRAM_D / 8); i += 256) {
+    const int r = i / (GRAM_D / 8), c8 = (i % (GRAM_D / 8)) * 8;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), zv = kv;
+    if (r < p.Cc) {
+      kv = __ldg(reinterpret_cast<const uint4*>(p.k + ((size_t)b * p.T + p.tok0 + r) * p.d + dd0 + c8));
+      zv = __ldcg(reinterpret_cast<const uint4*>(p.dz + ((size_t)b * CT + r) * p.d + dd0 + c8));
+    }
+    *reinterpret_cast<uint4*>(&sm[0][r][c8]) = kv;
+    *reinterpret_cast<uint4*>(&sm[1][r][c8]) = zv;
+  }
+  __syncthreads();
+  const int ti = tid >> 4, tj = tid & 15;
+#pragma unroll 1
+  for (int m = 0; m < 2; ++m) {
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+#pragma unroll 1
+    for (int k8 = 0; k8 < GRAM_D; k8 += 8) {
+      uint4 xi[4], xj[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        xi[a] = *reinterpret_cast<const uint4*>(&sm[m][ti + 16 * a][k8]);
+        xj[a] = *reinterpret_cast<const uint4*>(&sm[m][tj + 16 * a][k8]);
+      }
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        float fi[4][2], fj[4][2];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const uint32_t vi = (&xi[a].x)[w], vj = (&xj[a].x)[w];
+          fi[a][0] = bf16_lo(vi); fi[a][1] = bf16_hi(vi);
+          fj[a][0] = bf16_lo(vj); fj[a][1] = bf16_hi(vj);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[a][c] += fi[a][0] * fj[c][0] + fi[a][1] * fj[c][1];
+      }
+    }
+    float* g = p.gram + ((size_t)b * 2 + m) * CT * CT;
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) red_add_f32(g + (ti + 16 * a) * CT + tj + 16 * c, acc[a][c]);
+  }
+}
+
 // FP32 tensor maps of the W masters for the TMA-staged update epilogue:
 // up/gate over (h, d, states) with 128 x 32 boxes, down over (d, h, states)
 // with 32 x 128 boxes (128-byte swizzle).
@@ -775,7 +841,10 @@ constexpr int ZSLOT = 32 * 1024;          // one BF16 [128 d][128 hidden] A tile
 // kFuse: also run the NEXT chunk's forward (U', G', H', partial Z') from the
 // weight tiles this kernel just updated, so the separate forward pass over
 // the FP32 masters disappears for every chunk but the first of a call.
-template <bool kMomentum, bool kFuse, bool kSplit>
+// kClip: a clip run (ChunkParams::ops and ::gram set): the norm pass (update = 0) takes the Gram
+// route and keeps its epilogue-1 operands, the update pass (update = 1) starts from them.  A
+// compile-time choice, so the unclipped kernels carry none of that code.
+template <bool kMomentum, bool kFuse, bool kSplit, bool kClip>
 __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_constant__ CUtensorMap tmK,
                                                                 const __grid_constant__ CUtensorMap tmDZ,
                                                                 const __grid_constant__ WMaps wm,
@@ -909,12 +978,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   // momentum of this state: s_* (d, h) for up / gate, (h, d) for down
   const size_t s_off = (size_t)sb * p.d * p.h;
 
+  // an update after a norm pass takes dU, dG, H from the norm pass: no phase 1, no W_down read for dH
+  const bool ops_in = kClip && update;
+  // a norm pass with the chunk's Gram matrices: no gradient tiles, the d-split's rank 0 sums for the pair
+  const bool gram = kClip && !update;
+  uint8_t* ops_at = kClip ? p.ops + ((size_t)b * gridDim.x + t) * OPS_BYTES : nullptr;
+
   if (warp < 8) {
     // ------------------------------------------------------------ W_down rows -> A (K-major)
     // Two FP32 quarter tiles (TMA; rows past h arrive as zeros) make one BF16
     // k-block of 64 d columns.
     int it = 0;
-    for (int kb = 0; kb < nkb; ++kb, ++it) {
+    for (int kb = 0; kb < (ops_in ? 0 : nkb); ++kb, ++it) {
       const int s = it % NSLOT;
       mbar_wait(&empty[s], ((it / NSLOT) & 1) ^ 1, p.status);
       uint8_t* sA = slots + s * BWD_SLOT;
@@ -954,7 +1029,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     // ------------------------------------------------------------ epilogue 1: dU, dG, H
     const int q = warp & 3, half = warp >> 2;
     const int row = q * 32 + lane;                   // hidden row within the tile
-    {
+    if (ops_in) {
+      // the norm pass's dU, dG, H tiles: 3072 16-byte pieces, 12 per thread, coalesced
+      const uint4* src = reinterpret_cast<const uint4*>(ops_at);
+      uint4* dst = reinterpret_cast<uint4*>(sDU);     // sDU, sDG, sHt are consecutive 16 KB tiles
+      uint4 v[12];
+#pragma unroll
+      for (int i = 0; i < 12; ++i) v[i] = __ldcg(src + tid + i * NPROD);
+#pragma unroll
+      for (int i = 0; i < 12; ++i) dst[tid + i * NPROD] = v[i];
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&ops_ready);
+    } else {
       const int c0 = half * 32;
       // the saved U / G of this thread's row are loaded while the dH MMAs finish
       const float* us = p.u_save + (size_t)b * CT * p.hp + h0 + row;
@@ -999,6 +1086,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         *reinterpret_cast<uint4*>(sDU + o) = a4;
         *reinterpret_cast<uint4*>(sDG + o) = b4;
         *reinterpret_cast<uint4*>(sHt + o) = c4;
+        if (kClip && !update && ksr == 0) {           // the norm pass keeps them for the update
+          *reinterpret_cast<uint4*>(ops_at + o) = a4;
+          *reinterpret_cast<uint4*>(ops_at + 16384 + o) = b4;
+          *reinterpret_cast<uint4*>(ops_at + 32768 + o) = c4;
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -1009,11 +1101,33 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     const int cq = half * 16;                        // this thread's 16 of the quarter's 32 columns
     const bool row_ok = h0 + row < p.h;
     float acc = 0.f;
+    if (gram && ksr == 0 && !skip) {
+      // TMEM lanes 0-63 of D1 hold dU^T dU, lanes 64-127 of D1 dG^T dG (columns 64-127) and of D2
+      // H^T H; each thread dots its 32 columns of its token row with the matching Gram row
+      mbar_wait(&gfull, 0, p.status);
+      tc_fence_after();
+      const int i = row & 63, cb = (row < 64 ? 0 : 64) + half * 32;
+      const float* gk = p.gram + (size_t)b * 2 * CT * CT + i * CT + half * 32;
+      const float* gz = gk + CT * CT;
+      float m1[32];
+      tmem_ld16(tmem_addr(tGU, q * 32, cb), *reinterpret_cast<float(*)[16]>(&m1[0]));
+      tmem_ld16(tmem_addr(tGU, q * 32, cb + 16), *reinterpret_cast<float(*)[16]>(&m1[16]));
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) acc += __ldcg(gk + e) * m1[e];
+      if (row >= 64) {
+        tmem_ld16(tmem_addr(tGG, q * 32, cb), *reinterpret_cast<float(*)[16]>(&m1[0]));
+        tmem_ld16(tmem_addr(tGG, q * 32, cb + 16), *reinterpret_cast<float(*)[16]>(&m1[16]));
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc += __ldcg(gz + e) * m1[e];
+      }
+    }
     // stability guard: this row's last update of the call (never a fused chunk: the call's last)
     const bool guard = update && !skip && p.g_final != nullptr && p.g_final[b] != 0 &&
                        p.chunk_index == p.n_chunks - 1 && !fuse;
     float g_up = 0.f, g_gate = 0.f, g_down = 0.f;
-    for (int qi = 0; qi < nq; ++qi) {
+    for (int qi = 0; qi < (gram ? 0 : nq); ++qi) {
       const int j = qi >> 2, qq = qi & 3;
       // this quarter's momentum (issued before the waits so its latency overlaps them)
       const bool s_io = update && !skip && row_ok;
@@ -1206,7 +1320,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     };
 
     // ------------------------------------------------------------ loop B: W_down
-    for (int qi = 0; qi < nq; ++qi) {
+    for (int qi = 0; qi < (gram ? 0 : nq); ++qi) {
       const int j = qi >> 2, qq = qi & 3, jj = nch + j;
       if (qq == 0) {
         mbar_wait(&gfull, jj & 1, p.status);
@@ -1353,7 +1467,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmDZ);
       int it = 0;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      for (int kb = 0; kb < (ops_in ? 0 : nkb); ++kb, ++it) {
         if (!skip) {
           for (int hq = 0; hq < 2; ++hq) {
             const int qi = 2 * kb + hq, fs = qi % NF;
@@ -1381,14 +1495,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         tma_load_3d(sKN, &tmK, &kfull, (kb0 + kbi) * 64, p.tok0_next, b);
       };
       const bool fuse = kFuse && update;
-      kslice(0);
-      for (int j = 0; j < nch; ++j) {
+      if (!gram) kslice(0);
+      for (int j = 0; j < (gram ? 0 : nch); ++j) {
         if (fuse) knext(2 * j);
         if (j + 1 < nch) kslice(j + 1);
         if (fuse) knext(2 * j + 1);
       }
       // loop B: dZ slices (MN-major B of gradW_down)
-      for (int j = 0; j < nch; ++j) {
+      for (int j = 0; j < (gram ? 0 : nch); ++j) {
         const int jj = nch + j;
         mbar_wait(&empty3, (jj & 1) ^ 1, p.status);
         mbar_arrive_expect_tx(&full3, 16384);
@@ -1400,7 +1514,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
     if (lane == 0) {
       const uint32_t id_dh = idesc_bf16(128, 64, false, false);
       int it = 0;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      for (int kb = 0; kb < (ops_in ? 0 : nkb); ++kb, ++it) {
         const int s = it % NSLOT;
         mbar_wait(&full[s], (it / NSLOT) & 1, p.status);
         tc_fence_after();
@@ -1411,7 +1525,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
                    (kb > 0 || ks > 0) ? 1u : 0u);
         mma_commit(&empty[s]);
       }
-      mma_commit(&dh_done);
+      if (ops_in)
+        mbar_arrive(&dh_done);                       // no dH MMAs: the phase-1 ring is free at once
+      else
+        mma_commit(&dh_done);
       mbar_wait(&ops_ready, 0, p.status);
       tc_fence_after();
       const uint32_t id_uw = idesc_bf16(128, 128, false, true);   // A = dU^T K-major, B = K MN-major
@@ -1419,6 +1536,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       const uint32_t du = smem_u32(sDU), dg = smem_u32(sDG), ht = smem_u32(sHt);
       const uint32_t id_ug = idesc_bf16(128, 64, false, false);   // next chunk: A = W'^T K-major, B = K' K-major
       const bool fuse = kFuse && update;
+      if (gram && ksr == 0 && !skip) {
+        // D1 = [dU^T; dG^T] [dU | dG], D2 = [dG^T; H^T] [dG | H]: M = N = 128 tokens in two 64-wide
+        // MN-major atoms 16 KB apart (sDU, sDG, sHt are consecutive), K = 128 hidden rows
+        const uint32_t id_g = idesc_bf16(128, 128, true, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t d1 = sdesc_sw128(du + ks * 2048, 16384, 1024);
+          const uint64_t d2 = sdesc_sw128(dg + ks * 2048, 16384, 1024);
+          mma_bf16(tGU, d1, d1, id_g, ks > 0 ? 1u : 0u);
+          mma_bf16(tGG, d2, d2, id_g, ks > 0 ? 1u : 0u);
+        }
+        mma_commit(&gfull);
+      }
       auto grad_ug = [&](int j) {                 // gradW_up^T, gradW_gate^T of d chunk j
         mbar_wait(&full3, j & 1, p.status);
         mbar_wait(&gfree, (j & 1) ^ 1, p.status);
@@ -1450,8 +1580,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       };
       // loop A: the gradient tiles of d chunk j+1 are issued as soon as the
       // producers have drained chunk j, ahead of the second U'/G' k-block
-      grad_ug(0);
-      for (int j = 0; j < nch; ++j) {
+      if (!gram) grad_ug(0);
+      for (int j = 0; j < (gram ? 0 : nch); ++j) {
         if (fuse) next_ug(2 * j);
         if (j + 1 < nch) grad_ug(j + 1);
         if (fuse) next_ug(2 * j + 1);
@@ -1476,7 +1606,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         mbar_wait(&h_ready, 0, p.status);
         tc_fence_after();
       }
-      for (int j = 0; j < nch; ++j) {
+      for (int j = 0; j < (gram ? 0 : nch); ++j) {
         const int jj = nch + j;
         mbar_wait(&full3, jj & 1, p.status);
         mbar_wait(&gfree, (jj & 1) ^ 1, p.status);
@@ -1500,6 +1630,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
 
 size_t fwd_smem() { return 1024 + NSLOT * SLOT_BYTES + 16384; }
 size_t bwd_smem() { return 1024 + NSLOT * BWD_SLOT + 32768 + 3 * 16384 + 2 * 16384 + 8192; }
+
+using BwdKernel = void (*)(const CUtensorMap, const CUtensorMap, const WMaps, const ChunkParams, int);
+// the backward variant for (momentum, fuse, d-split, clip run)
+BwdKernel bwd_kernel_table(bool mom, bool fuse, bool split, bool clip) {
+  static const BwdKernel k[16] = {
+      chunk_bwd_kernel<false, false, false, false>, chunk_bwd_kernel<true, false, false, false>,
+      chunk_bwd_kernel<false, true, false, false>,  chunk_bwd_kernel<true, true, false, false>,
+      chunk_bwd_kernel<false, false, true, false>,  chunk_bwd_kernel<true, false, true, false>,
+      chunk_bwd_kernel<false, true, true, false>,   chunk_bwd_kernel<true, true, true, false>,
+      chunk_bwd_kernel<false, false, false, true>,  chunk_bwd_kernel<true, false, false, true>,
+      chunk_bwd_kernel<false, true, false, true>,   chunk_bwd_kernel<true, true, false, true>,
+      chunk_bwd_kernel<false, false, true, true>,   chunk_bwd_kernel<true, false, true, true>,
+      chunk_bwd_kernel<false, true, true, true>,    chunk_bwd_kernel<true, true, true, true>};
+  return k[(mom ? 1 : 0) | (fuse ? 2 : 0) | (split ? 4 : 0) | (clip ? 8 : 0)];
+}
 
 }  // namespace
 }  // namespace uttt
@@ -1568,6 +1713,8 @@ extern "C" size_t uttt_chunk_write_workspace(int B, int C, int d, int h) {
   bytes += 2 * ws_round((size_t)B * CT * hp * sizeof(float));  // u_save, g_save
   bytes += ws_round((size_t)B * CT * d * 2);                   // dz
   bytes += ws_round((size_t)B * sizeof(float));                 // norm2
+  bytes += ws_round((size_t)B * ((h + HT - 1) / HT) * OPS_BYTES);   // clip runs: the norm pass's operands
+  bytes += ws_round((size_t)B * 2 * CT * CT * sizeof(float));       //            and the Gram matrices
   if (B <= DSPLIT_MAX_B) bytes += dsplit_xch_bytes(B, h) + dsplit_flag_bytes(B, h);   // d-split exchange
   return bytes;
 }
@@ -1687,6 +1834,10 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
     p.g_final = guard->final_rows;
     p.g_sums = guard->sums;
   }
+  if (max_grad_norm > 0.f) {
+    p.ops = ws.take<uint8_t>((size_t)B * ((h + HT - 1) / HT) * OPS_BYTES);
+    p.gram = ws.take<float>((size_t)B * 2 * CT * CT);
+  }
   if (!ws.ok()) return UTTT_ERR_WORKSPACE;
   // d-split of the bwd kernel: with few rows, 54 hidden tiles per 1.58B state leave SMs idle or
   // end on a thin last wave; two CTAs per (tile, state), each streaming half of d, finish in
@@ -1734,13 +1885,9 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
   static DeviceOnce attr_done;
   UTTT_TRY(run_once_per_device(attr_done, [] {
     UTTT_TRY(set_fwd_attributes());
-    const void* bwd_kernels[8] = {
-        (const void*)chunk_bwd_kernel<false, false, false>, (const void*)chunk_bwd_kernel<true, false, false>,
-        (const void*)chunk_bwd_kernel<false, true, false>,  (const void*)chunk_bwd_kernel<true, true, false>,
-        (const void*)chunk_bwd_kernel<false, false, true>,  (const void*)chunk_bwd_kernel<true, false, true>,
-        (const void*)chunk_bwd_kernel<false, true, true>,   (const void*)chunk_bwd_kernel<true, true, true>};
-    for (const void* fn : bwd_kernels)
-      UTTT_TRY(cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
+    for (int i = 0; i < 16; ++i)
+      UTTT_TRY(cuda_status(cudaFuncSetAttribute((const void*)bwd_kernel_table(i & 1, i & 2, i & 4, i & 8),
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bwd_smem())));
     return (int)UTTT_OK;
   }));
   UTTT_TRY(cuda_status(cudaMemsetAsync(p.zacc, 0, (size_t)B * CT * d * sizeof(float), st)));
@@ -1748,8 +1895,7 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
   // bwd launch: grid (tiles, rows, KS); with KS > 1 the KS CTAs of a (tile, row) form one
   // cluster (co-scheduled, so their exchange waits always end) and the exchange counters
   // start from zero
-  auto launch_bwd = [&](void (*kernel)(const CUtensorMap, const CUtensorMap, const WMaps, const ChunkParams, int),
-                        int update) -> int {
+  auto launch_bwd = [&](BwdKernel kernel, int update) -> int {
     if (KS > 1)
       UTTT_TRY(cuda_status(cudaMemsetAsync(p.xflag, 0, dsplit_flag_bytes(B, h), st)));
     cudaLaunchConfig_t cfg = {};
@@ -1790,10 +1936,10 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
     UTTT_TRY(launch_status());
     if (max_grad_norm > 0.f) {
       ProfScope ps(UTTT_PROF_CHUNK_NORM, st);
-      if (momentum_beta != 0.f)
-        UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<true, false, true> : chunk_bwd_kernel<true, false, false>, 0));
-      else
-        UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<false, false, true> : chunk_bwd_kernel<false, false, false>, 0));
+      UTTT_TRY(cuda_status(cudaMemsetAsync(p.gram, 0, (size_t)B * 2 * CT * CT * sizeof(float), st)));
+      chunk_gram_kernel<<<dim3(d / GRAM_D, B), 256, 0, st>>>(p);
+      UTTT_TRY(launch_status());
+      UTTT_TRY(launch_bwd(bwd_kernel_table(momentum_beta != 0.f, false, KS > 1, true), 0));
       UTTT_TRY(launch_status());
       // hidden split: the clip norm runs over every rank's gradient slices
       if (partial_sum && partial_sum(p.norm2, (size_t)B, partial_sum_ctx, stream) != 0) return UTTT_ERR_CUDA;
@@ -1801,17 +1947,7 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
-      if (momentum_beta != 0.f) {
-        if (fuse)
-          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<true, true, true> : chunk_bwd_kernel<true, true, false>, 1));
-        else
-          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<true, false, true> : chunk_bwd_kernel<true, false, false>, 1));
-      } else {
-        if (fuse)
-          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<false, true, true> : chunk_bwd_kernel<false, true, false>, 1));
-        else
-          UTTT_TRY(launch_bwd(KS > 1 ? chunk_bwd_kernel<false, false, true> : chunk_bwd_kernel<false, false, false>, 1));
-      }
+      UTTT_TRY(launch_bwd(bwd_kernel_table(momentum_beta != 0.f, fuse, KS > 1, max_grad_norm > 0.f), 1));
     }
     UTTT_TRY(launch_status());
     // hidden split: the next chunk's Z (computed by the fused kernel) from every rank's slices
