@@ -1048,7 +1048,10 @@ def micro_case(device, kind, batch, tokens, hist, iters=30):
     rows, each on its own BF16 read copy; 24 copies (2.5 GB) cycle so every call streams
     its weights from HBM.  ``attn``: the prefill / chunk attention (20 query heads over 5 KV
     heads of dim 128, window 512) of ``batch`` rows x ``tokens`` new tokens after ``hist``
-    history positions (RoPE kernel included)."""
+    history positions (RoPE kernel included).  ``write``: the chunk-TTT write of ``batch`` rows
+    (one state each) for ``tokens`` tokens at one 1.58B layer (momentum 0.9, clip 1.0, the model
+    write's settings), with the time of each kernel kind from live CUDA events; its bytes are
+    the update's 48·d·h per row and chunk."""
     from utttcompanion_b200 import _lib
     from utttcompanion_b200.fastweight import _stream
     lib = _lib.load()
@@ -1076,6 +1079,22 @@ def micro_case(device, kind, batch, tokens, hist, iters=30):
         slow += eng.lm_head.numel() * eng.lm_head.element_size()
         kv = batch * cfg.n_layers * cfg.sliding_window_size * cfg.n_kv_heads * cfg.head_dim * 2 * 2
         nbytes = batch * cfg.n_layers * 3 * cfg.d_model * cfg.d_ff_fast * 2 + slow + kv
+    elif kind == "write":
+        from utttcompanion_b200 import fastweight as fw
+        d, h, B, T = 2560, 6912, batch, tokens
+        W = [torch.randn(B, d, h, device=device, generator=g) * d ** -0.5,
+             torch.randn(B, d, h, device=device, generator=g) * d ** -0.5,
+             torch.randn(B, h, d, device=device, generator=g) * 0.1 * h ** -0.5]
+        S = [torch.zeros_like(w) for w in W]
+        k = torch.randn(B, T, d, device=device, generator=g)
+        k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        v = torch.randn(B, T, d, device=device, generator=g)
+        v = (v / v.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        eta, alpha = torch.full((B, T), 0.0075, device=device), torch.full((B, T), 0.001, device=device)
+        lw, lb = torch.ones(d, device=device), torch.zeros(d, device=device)
+        call = lambda i: fw.chunk_write(k, v, eta, alpha, *W, *S, lw, lb, None, 0.9, 1.0, True, 1e-5)  # noqa: E731
+        nbytes = B * ((T + 63) // 64) * 48 * d * h
+        iters = min(iters, 10)
     elif kind == "readout":
         from utttcompanion_b200.readout import fast_readout
         d, h, S = 2560, 6912, 24
@@ -1115,8 +1134,23 @@ def micro_case(device, kind, batch, tokens, hist, iters=30):
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) / iters * 1e3
-    return {"micro": kind, "batch": batch, "tokens": tokens, "hist": hist, "us_per_call": us,
-            "bytes_per_call": nbytes, "gb_s": nbytes / us / 1e3, "iters": iters}
+    out = {"micro": kind, "batch": batch, "tokens": tokens, "hist": hist, "us_per_call": us,
+           "bytes_per_call": nbytes, "gb_s": nbytes / us / 1e3, "iters": iters}
+    if kind == "write":
+        # per kernel kind, live CUDA events on the write's stream (one more pass of `iters` calls)
+        lib.uttt_profile_enable(1)
+        for i in range(iters):
+            call(i)
+        ms = np.zeros(16, np.float32)
+        cnt = np.zeros(16, np.int32)
+        lib.uttt_profile_read(ms.ctypes.data, cnt.ctypes.data)
+        lib.uttt_profile_enable(0)
+        kinds = {"forward": 0, "layernorm_backward": 1, "clip_norm": 2, "update": 3}
+        out["kernels_us_per_call"] = {n: float(ms[i]) * 1e3 / iters for n, i in kinds.items()}
+        upd = out["kernels_us_per_call"]["update"]
+        out["update_gb_s"] = nbytes / upd / 1e3
+        out["update_hbm_frac"] = out["update_gb_s"] / peaks()[0]
+    return out
 
 
 # ----------------------------------------------------------------------------- arms
@@ -1390,7 +1424,7 @@ def main():
                     help="write on a side stream from a worker thread, overlapping decode")
     ap.add_argument("--only-decode", action="store_true",
                     help="profiling: run only the config-3 decode + write workload (one JSON object, 1 GPU)")
-    ap.add_argument("--micro", choices=("readout", "attn", "decode"), default=None,
+    ap.add_argument("--micro", choices=("readout", "attn", "decode", "write"), default=None,
                     help="profiling case: one kernel at the 1.58B layer shape")
     ap.add_argument("--micro-batch", type=int, default=1)
     ap.add_argument("--micro-tokens", type=int, default=64)

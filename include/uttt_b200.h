@@ -126,6 +126,12 @@ typedef int (*uttt_partial_sum_fn)(float* data, size_t count, void* ctx, void* s
  *                  A hook that fails ends the call with UTTT_ERR_CUDA.
  *
  * Requires d % 128 == 0, 1 <= C <= 64.
+ *
+ * uttt_chunk_write_workspace: bytes of device scratch the call needs (the
+ * status word, partial Z, saved U / G, dZ and norms of a 64-token chunk; for
+ * clipped calls the norm pass's dU / dG / H tiles, 48 KB per row and 128
+ * hidden units, and two 64 x 64 Gram matrices per row; for B <= 16 the
+ * exchange area of the 2-CTA d-split).
  */
 size_t uttt_chunk_write_workspace(int B, int C, int d, int h);
 int uttt_chunk_write(int B, int T, int C, int d, int h, int chunk_begin, int n_chunks, const void* q, const void* k,

@@ -32,6 +32,7 @@ import pytest
 import torch
 
 from conftest import record
+from parity import SPREAD_FACTOR
 from oracle import fastweight as ofw
 from oracle.numerics import Precision, rel_l2, round_bf16
 from utttcompanion_b200 import _lib
@@ -154,10 +155,12 @@ D158, H158 = 2560, 6912
 STD158 = (D158 ** -0.5, 0.1 * H158 ** -0.5)
 
 
-@pytest.mark.parametrize("B,Tn,beta,clip", [(1, 128, 0.9, 1.0), (4, 64, 0.9, 1.0), (5, 64, 0.0, 0.0)])
+@pytest.mark.parametrize("B,Tn,beta,clip", [(1, 128, 0.9, 1.0), (4, 64, 0.9, 1.0), (5, 64, 0.0, 0.0),
+                                            (6, 64, 0.9, 1.0)])
 def test_1p58b_layer_write(B, Tn, beta, clip):
-    """1 and 4 rows run the d-split (54 tiles x 2 CTAs per row), 5 rows the plain kernel in two
-    waves; the 1-row case chains two chunks through the fused next-chunk forward."""
+    """1, 4 and 6 rows run the d-split (54 tiles x 2 CTAs per row; 6 rows in 5 half-size waves
+    instead of 3 full ones), 5 rows the plain kernel in two waves; the 1-row case chains two chunks
+    through the fused next-chunk forward."""
     _check_write(f"1p58b_write_B{B}_T{Tn}", B=B, Tn=Tn, d=D158, h=H158, w_std=STD158, beta=beta, clip=clip,
                  seed=20 + B)
 
@@ -186,6 +189,40 @@ def test_1p58b_decode_readout(B):
     err = np.abs(got - ref)
     record(f"1p58b_readout_B{B}", max_abs=float(err.max()), max_excess=float((err - np.abs(ref) / 128).max()))
     assert (err <= 2e-2 + np.abs(ref) / 128).all(), float(err.max())
+
+
+@pytest.mark.parametrize("B", [1, 6, 8])
+def test_1p58b_chunk_readout(B):
+    """Tensor-core readout of one 64-token tile per row over BF16 packed read copies at the 1.58B
+    shape (the per-layer readout of a write chunk): 1 and 6 rows split d over 2-CTA clusters,
+    8 rows run one CTA per (tile, row); operands copied by cp.async from copies of 3 personas.
+    Bound per token row: 2e-2 + |ref|/128, or twice the row's BF16-vs-FP32 spread of the oracle
+    where that is larger (the LayerNorm's 1/std amplifies the BF16 rounding of z at isolated
+    elements: the oracle's own spread reaches 0.05 here, while the kernel keeps z in FP32)."""
+    rng = np.random.default_rng(40 + B)
+    S = min(B, 3)
+    d, h = D158, H158
+    w_up = rng.standard_normal((S, d, h), dtype=np.float32) * STD158[0]
+    w_gate = rng.standard_normal((S, d, h), dtype=np.float32) * STD158[0]
+    w_down = rng.standard_normal((S, h, d), dtype=np.float32) * 0.3 * h ** -0.5
+    lnw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    lnb = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    x = round_bf16(rng.standard_normal((B, 64, d), dtype=np.float32))
+    idx = (np.arange(B) * 2 % S).astype(np.int32)
+    packed, down = ro.inference_read_weights(T(w_up), T(w_gate), T(w_down))
+    y = ro.fast_readout(T(x, torch.bfloat16), packed, None, down, T(lnw), T(lnb), 1e-5,
+                        state_index=torch.as_tensor(idx), packed=True)
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    del packed, down
+    ref = ofw.swiglu_fast_forward(x, w_up[idx], w_gate[idx], w_down[idx], lnw, lnb, 1e-5, Precision("bf16"))
+    r32 = ofw.swiglu_fast_forward(x, w_up[idx], w_gate[idx], w_down[idx], lnw, lnb, 1e-5, Precision("f32"))
+    spread = np.abs(ref - r32).max(axis=-1, keepdims=True)
+    err = np.abs(got - ref)
+    bound = np.maximum(2e-2 + np.abs(ref) / 128, SPREAD_FACTOR * spread)
+    record(f"1p58b_chunk_readout_B{B}", max_abs=float(err.max()), max_spread=float(spread.max()),
+           over_floor=int((err > 2e-2 + np.abs(ref) / 128).sum()))
+    assert (err <= bound).all(), (float(err.max()), float(spread.max()))
 
 
 def _rope_bf16(x, cos, sin):

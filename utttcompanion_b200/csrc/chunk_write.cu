@@ -1653,8 +1653,12 @@ using namespace uttt;
 
 namespace uttt {
 namespace {
-// Batches of at most this many rows may split d over 2-CTA clusters in the bwd kernel.
-constexpr int DSPLIT_MAX_B = 4;
+// Batches of at most this many rows may split d over 2-CTA clusters (the bwd kernel and the
+// one-tile forward); at the 1.58B shape (54 hidden tiles) that saves waves for 1, 3, 4, 6, 9, 11,
+// 12, 14 and 15 rows.  The workspace sizes include the exchange area up to this batch.
+constexpr int DSPLIT_MAX_B = 16;
+// the same for the tensor-core readout of one token tile (uttt_fast_readout)
+constexpr int READOUT_DSPLIT_MAX_B = 4;
 size_t dsplit_xch_bytes(int B, int h) {
   const size_t tiles = ((size_t)h + HT - 1) / HT;
   return ws_round((size_t)B * tiles * 2 * 3 * HT * CT * sizeof(float));
@@ -1895,11 +1899,11 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
   // bwd launch: grid (tiles, rows, KS); with KS > 1 the KS CTAs of a (tile, row) form one
   // cluster (co-scheduled, so their exchange waits always end) and the exchange counters
   // start from zero
-  auto launch_bwd = [&](BwdKernel kernel, int update) -> int {
-    if (KS > 1)
+  auto launch_bwd = [&](BwdKernel kernel, int update, int ks) -> int {
+    if (ks > 1)
       UTTT_TRY(cuda_status(cudaMemsetAsync(p.xflag, 0, dsplit_flag_bytes(B, h), st)));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ntiles, B, KS);
+    cfg.gridDim = dim3(ntiles, B, ks);
     cfg.blockDim = dim3(BWD_THREADS);
     cfg.dynamicSmemBytes = bwd_smem();
     cfg.stream = st;
@@ -1907,9 +1911,9 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
     at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = KS;
+    at[0].val.clusterDim.z = ks;
     cfg.attrs = at;
-    cfg.numAttrs = KS > 1 ? 1 : 0;
+    cfg.numAttrs = ks > 1 ? 1 : 0;
     return cuda_status(cudaLaunchKernelEx(&cfg, kernel, tmK, tmDZ, wmaps, p, update));
   };
   // The forward of every chunk but the first runs inside the previous chunk's
@@ -1939,7 +1943,9 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
       UTTT_TRY(cuda_status(cudaMemsetAsync(p.gram, 0, (size_t)B * 2 * CT * CT * sizeof(float), st)));
       chunk_gram_kernel<<<dim3(d / GRAM_D, B), 256, 0, st>>>(p);
       UTTT_TRY(launch_status());
-      UTTT_TRY(launch_bwd(bwd_kernel_table(momentum_beta != 0.f, false, KS > 1, true), 0));
+      // unsplit: the norm pass streams only W_down, and a pair's exchange of dH plus rank 0's Gram
+      // tail cost more than the halved stream saves (measured at 6 and 9 rows of the 1.58B shape)
+      UTTT_TRY(launch_bwd(bwd_kernel_table(momentum_beta != 0.f, false, false, true), 0, 1));
       UTTT_TRY(launch_status());
       // hidden split: the clip norm runs over every rank's gradient slices
       if (partial_sum && partial_sum(p.norm2, (size_t)B, partial_sum_ctx, stream) != 0) return UTTT_ERR_CUDA;
@@ -1947,7 +1953,7 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
     UTTT_TRY(launch_status());
     {
       ProfScope ps(UTTT_PROF_CHUNK_BWD, st);
-      UTTT_TRY(launch_bwd(bwd_kernel_table(momentum_beta != 0.f, fuse, KS > 1, max_grad_norm > 0.f), 1));
+      UTTT_TRY(launch_bwd(bwd_kernel_table(momentum_beta != 0.f, fuse, KS > 1, max_grad_norm > 0.f), 1, KS));
     }
     UTTT_TRY(launch_status());
     // hidden split: the next chunk's Z (computed by the fused kernel) from every rank's slices
@@ -2027,7 +2033,7 @@ extern "C" size_t uttt_fast_readout_workspace(int B, int T, int d, int h) {
   if (B <= 0 || T <= 0 || d <= 0 || h <= 0) return 0;
   size_t bytes = 256 + ws_round((size_t)B * (T > CT ? T : CT) * d * sizeof(float));
   // one token tile of a few rows: room for the d-split exchange of the tensor-core readout
-  if (T > 1 && T <= CT && B <= DSPLIT_MAX_B) bytes += dsplit_xch_bytes(B, h) + dsplit_flag_bytes(B, h);
+  if (T > 1 && T <= CT && B <= READOUT_DSPLIT_MAX_B) bytes += dsplit_xch_bytes(B, h) + dsplit_flag_bytes(B, h);
   return bytes;
 }
 
@@ -2099,7 +2105,8 @@ extern "C" int uttt_fast_readout(int B, int T, int d, int h, const void* x, int 
   // 2-CTA clusters when that saves waves and the workspace holds the exchange area
   int KS = 1;
   const size_t fbytes = dsplit_flag_bytes(B, h);
-  if (T > 1 && T <= CT && B <= DSPLIT_MAX_B && (d / 128) % 2 == 0 && dsplit_factor((long long)grid.y * B) == 2) {
+  if (T > 1 && T <= CT && B <= READOUT_DSPLIT_MAX_B && (d / 128) % 2 == 0 &&
+      dsplit_factor((long long)grid.y * B) == 2) {
     const size_t xb = dsplit_xch_bytes(B, h);
     if (ws.used + xb + fbytes <= ws.cap) {
       p.xch = ws.take<float>(xb / sizeof(float));
