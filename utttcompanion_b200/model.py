@@ -87,6 +87,15 @@ def rope_tables(head_dim: int, n_pos: int, theta: float):
     return emb.cos(), emb.sin()
 
 
+
+def _host_list(values, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A small host-side list as a device tensor without stalling the host: staged in pinned
+    memory and copied asynchronously on the current stream (a plain ``torch.tensor(...,
+    device=...)`` copies from pageable memory and waits for the stream to drain)."""
+    if torch.device(device).type != "cuda":
+        return torch.tensor(values, dtype=dtype, device=device)
+    return torch.tensor(values, dtype=dtype).pin_memory().to(device, non_blocking=True)
+
 def _seg(start, length, op, out, out_ld, aux=None, aux_ld=0, scale=0.0, out_f32=False, aux2=None):
     return _lib.Segment(start, length, op, int(out_f32), out.data_ptr(), out_ld,
                         None if aux is None else aux.data_ptr(), aux_ld, scale,
@@ -276,8 +285,8 @@ class UtttB200:
             raise ValueError("prompt longer than the RoPE table")
         dev = self.device
         h = self._embed(ids)
-        slot_t = torch.tensor([slot], dtype=torch.int32, device=dev)
-        sidx = torch.tensor([state_index], dtype=torch.int32, device=dev)
+        slot_t = _host_list([slot], torch.int32, dev)
+        sidx = _host_list([state_index], torch.int32, dev)
         qkv = torch.empty(T, self.qkv_dim, dtype=torch.bfloat16, device=dev)
         qs = torch.empty(T, nh * hd, dtype=torch.bfloat16, device=dev)
         kb = torch.empty(1, nkv, T, hd, dtype=torch.bfloat16, device=dev)
@@ -330,9 +339,10 @@ class UtttB200:
             tile_state += [int(si)] * (sp // 64)
         if int(ids.min()) < 0 or int(ids.max()) >= self.emb.shape[0]:
             raise ValueError("token id outside the vocabulary")
-        h = self._embed(ids)
-        tiles = torch.tensor(tile_state, dtype=torch.int32, device=dev)
-        slot_t = [torch.tensor([int(s_)], dtype=torch.int32, device=dev) for s_ in slots]
+        h = self._embed(ids.pin_memory().to(dev, non_blocking=True))
+        tiles = _host_list(tile_state, torch.int32, dev)
+        slot_all = _host_list([int(s_) for s_ in slots], torch.int32, dev)
+        slot_t = [slot_all[j:j + 1] for j in range(len(slots))]
         qkv = torch.empty(R, self.qkv_dim, dtype=torch.bfloat16, device=dev)
         qs = torch.empty(R, nh * hd, dtype=torch.bfloat16, device=dev)
         kv_off = [0]
@@ -361,7 +371,7 @@ class UtttB200:
             q = self._q_proj(lay, x2)
             r = self._readout(q.reshape(R // 64, 64, d), read_packed, read_down, tiles)
             x = self._resid_linear(h, r.reshape(R, d), lay.w_o, self.layers[i + 1].attn_norm if i + 1 < L else self.norm)
-        last = torch.tensor([o + T - 1 for o, T in zip(offs, lens)], dtype=torch.long, device=dev)
+        last = _host_list([o + T - 1 for o, T in zip(offs, lens)], torch.long, dev)
         return self._lm_head(x.index_select(0, last).contiguous())
 
     # ------------------------------------------------------------------ KV rings <-> chronological caches
@@ -497,7 +507,8 @@ class UtttB200:
         A row whose turn is gated off is simply not committed, so the pull can always run."""
         cfg = self.cfg
         dev = self.device
-        ids = interaction_ids.to(device=dev)
+        ids = interaction_ids if interaction_ids.is_cuda else interaction_ids.pin_memory()
+        ids = ids.to(device=dev, non_blocking=True)
         B, T = ids.shape
         C, W = cfg.chunk_size, cfg.sliding_window_size
         d, hd, nh, nkv = cfg.d_model, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
@@ -515,7 +526,7 @@ class UtttB200:
             m_host = attention_mask.reshape(B, T).to(dtype=torch.float32).cpu()
             pos_idx = torch.arange(T).expand(B, T)
             last = torch.where(m_host != 0, pos_idx, torch.full_like(pos_idx, -1)).max(dim=1).values.tolist()
-            mask_all = m_host.to(device=dev).contiguous()
+            mask_all = m_host.contiguous().pin_memory().to(device=dev, non_blocking=True)
         h_all = self._embed(ids).reshape(B, T, d)
         hist_k: List[Optional[torch.Tensor]] = [None] * L
         hist_v: List[Optional[torch.Tensor]] = [None] * L
@@ -531,13 +542,13 @@ class UtttB200:
                 cur.step += L                      # the reference still steps through padded chunks
                 continue
             if len(keep_rows) < len(alive):        # compact: rows with nothing left leave the batch
-                sel = torch.tensor([alive.index(r) for r in keep_rows], dtype=torch.long, device=dev)
+                sel = _host_list([alive.index(r) for r in keep_rows], torch.long, dev)
                 for i in range(L):
                     if hist_k[i] is not None:
                         hist_k[i] = hist_k[i].index_select(0, sel)
                         hist_v[i] = hist_v[i].index_select(0, sel)
                 alive = keep_rows
-                rows = torch.tensor(alive, dtype=torch.int32, device=dev)
+                rows = _host_list(alive, torch.int32, dev)
             Bc = len(alive)
             R = Bc * Cc
             rows_l = rows.long()
@@ -601,8 +612,7 @@ class UtttB200:
             g = None
             if guard is not None:
                 # the rows whose last valid token is in this chunk take their final update here
-                fin = torch.tensor([1 if off <= last[r] < off + Cc else 0 for r in alive], dtype=torch.int32,
-                                   device=dev)
+                fin = _host_list([1 if off <= last[r] < off + Cc else 0 for r in alive], torch.int32, dev)
                 sums = torch.zeros(Bc, 4, dtype=torch.float32, device=dev)
                 g = (*guard, fin, sums)
             chunk_write(Kr, Vr, Er, Ar, cur.w_up, cur.w_gate, cur.w_down, cur.s_up, cur.s_gate, cur.s_down,

@@ -35,7 +35,7 @@ import torch
 
 from . import _lib
 from .fastweight import _stream, workspace
-from .model import EOS_ID, PAD_ID, DecodeGraph, DecodeTable, FastState, UtttB200
+from .model import EOS_ID, PAD_ID, DecodeGraph, DecodeTable, FastState, UtttB200, _host_list
 
 
 class PersonaRouter:
@@ -130,7 +130,7 @@ class PersonaArena:
         return s
 
     def state(self, slots: List[int]) -> FastState:
-        idx = torch.as_tensor(slots, device=self.w_up.device)
+        idx = _host_list(list(slots), torch.long, self.w_up.device)
         return FastState(self.w_up[idx], self.w_gate[idx], self.w_down[idx], self.s_up[idx], self.s_gate[idx],
                          self.s_down[idx], self.engine.ln_w, self.engine.ln_b)
 
