@@ -810,6 +810,30 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     t = torch.tensor([e0.elapsed_time(e1) / steps], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dec_ms = float(t.item())
+    # where an (eager) step's time goes: the all-reduces of z against the kernels every rank runs
+    # whole (projections + finish, attention, row-wise, LM head) and the split readout, per step,
+    # CUDA events on the step's stream, max over ranks
+    bsteps = 3
+    hs.timing = []
+    lib.uttt_profile_enable(1)
+    for _ in range(bsteps):
+        tokens = eng.greedy(eng.decode_step(tokens, pos, slots, packed, down, slots))[0]
+        pos += 1
+    torch.cuda.synchronize()
+    pms = np.zeros(16, np.float32)
+    pcnt = np.zeros(16, np.int32)
+    lib.uttt_profile_read(pms.ctypes.data, pcnt.ctypes.data)
+    lib.uttt_profile_enable(0)
+    ar_ms = sum(a.elapsed_time(b) for a, b in hs.timing)
+    n_ar = len(hs.timing)
+    hs.timing = None
+    kinds = {"allreduce_z": ar_ms, "readout_partial": float(pms[4]), "readout_finish": float(pms[5]),
+             "projections": float(pms[6]), "projection_finish": float(pms[7]), "attention": float(pms[8]),
+             "rowwise_argmax": float(pms[9] + pms[10])}
+    kt = torch.tensor([v / bsteps for v in kinds.values()], device=device, dtype=torch.float64)
+    dist.all_reduce(kt, op=dist.ReduceOp.MAX)
+    breakdown = {k: float(v) for k, v in zip(kinds, kt.tolist())}
+    breakdown["allreduces_per_step"] = n_ar / bsteps
     slow_bytes = sum(x.numel() * x.element_size() for lay in eng.layers for x in (lay.wqkv, lay.wo, lay.w_q, lay.w_o))
     slow_bytes += eng.lm_head.numel() * eng.lm_head.element_size()
     per_gpu = P * 3.0 * cfg.d_model * (cfg.d_ff_fast // world) * 2.0 * cfg.n_layers + slow_bytes
@@ -822,6 +846,7 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
         "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,
         "per_gpu_fast_weight_bytes_per_step": per_gpu,
         "per_gpu_hbm_gbs": per_gpu / (dec_ms / 1e3) / 1e9,
+        "eager_step_breakdown_ms": breakdown,
         "parity": parity,
     }
 

@@ -34,6 +34,8 @@ class HiddenSplit:
         self.world = dist.get_world_size(group) if world is None else world
         if not 0 <= self.rank < self.world:
             raise ValueError("rank outside the group")
+        # a list: every all-reduce appends its (start, end) CUDA events on the current stream
+        self.timing = None
 
     def bounds(self, h: int) -> Tuple[int, int]:
         """[lo, hi) of this rank's hidden units (equal slices, each a multiple of 8)."""
@@ -51,7 +53,14 @@ class HiddenSplit:
     def all_reduce(self, z: torch.Tensor) -> None:
         import torch.distributed as dist
         if self.world > 1:
+            if self.timing is None:
+                dist.all_reduce(z, op=dist.ReduceOp.SUM, group=self.group)
+                return
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
             dist.all_reduce(z, op=dist.ReduceOp.SUM, group=self.group)
+            e1.record()
+            self.timing.append((e0, e1))
 
     def readout(self, x: torch.Tensor, packed: torch.Tensor, down: torch.Tensor, state_index: torch.Tensor,
                 ln_weight: torch.Tensor, ln_bias: torch.Tensor, eps: float) -> torch.Tensor:
