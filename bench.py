@@ -877,12 +877,20 @@ def hsplit_parity(device, rank, hs, cfg, full_rows, prompts, first_split, tokens
         first = torch.stack([ref.prefill(prompts[p], p, rp, rd, p) for p in range(len(prompts))]).float()
         slots = torch.arange(len(prompts), dtype=torch.int32, device=device)
         step0 = ref.decode_step(tokens0, pos0, slots, rp, rd, slots).float()
+        # the unsplit engine against itself: the same prefill and step once more (its atomic FP32
+        # accumulation order varies from run to run, and a flipped BF16 rounding of z is amplified
+        # by the LayerNorm and 34 layers), the noise floor of any second implementation
+        first2 = torch.stack([ref.prefill(prompts[p], p, rp, rd, p) for p in range(len(prompts))]).float()
+        step02 = ref.decode_step(tokens0, pos0, slots, rp, rd, slots).float()
+        self_diff = max(float((first2 - first).abs().max()), float((step02 - step0).abs().max()))
         d_pre = float((first - first_split).abs().max())
         d_dec = float((step0 - step0_split).abs().max())
         same = bool(torch.equal(first.argmax(-1), first_split.argmax(-1))
                     and torch.equal(step0.argmax(-1), step0_split.argmax(-1)))
+        bound = max(2e-2, 2.0 * self_diff)
         out.update(max_abs_logit_diff_prefill=d_pre, max_abs_logit_diff_decode=d_dec, greedy_equal=same,
-                   within_2e2=max(d_pre, d_dec) <= 2e-2)
+                   within_2e2=max(d_pre, d_dec) <= 2e-2, unsplit_repeat_diff=self_diff, logit_bound=bound,
+                   within_bound=max(d_pre, d_dec) <= bound)
         del ref, rp, rd
         torch.cuda.empty_cache()
     # one split write of two personas' layer state against the unsplit write

@@ -234,8 +234,10 @@ int uttt_fast_readout(int B, int T, int d, int h, const void* x, int w_dtype, co
  * uttt_fast_readout_partial writes that slice's z = h_slice W_down_slice,
  * FP32 (B, T, d) (z is zeroed first; T == 1 runs the decode GEMV, T > 1 the
  * tensor-core tiles; the workspace only holds the status word).  After the ranks' z are summed (an all-reduce),
- * uttt_readout_finish applies out = x + LayerNorm(bf16(z)) * ln_weight +
- * ln_bias to `rows` rows of (rows, d).  Together they equal uttt_fast_readout
+ * uttt_readout_finish applies out = x + LayerNorm(z) * ln_weight + ln_bias to
+ * `rows` rows of (rows, d), z rounded to BF16 first when z_bf16 != 0 (as the
+ * decode readout, T == 1, does; the tensor-core tiles of T > 1 keep z in
+ * FP32).  Together they equal uttt_fast_readout
  * (swiglu_packed_forward, model/uttt_layer.py:250-257): every hidden unit's
  * u, g and h are computed whole on one rank.
  */
@@ -243,7 +245,7 @@ int uttt_fast_readout_partial(int B, int T, int d, int h, const void* x, const v
                               const int* state_index, float* z, void* workspace, size_t workspace_bytes,
                               void* stream);
 int uttt_readout_finish(int rows, int d, const float* z, const void* x, const float* ln_weight, const float* ln_bias,
-                        float eps, void* out, int out_dtype, void* stream);
+                        float eps, void* out, int out_dtype, int z_bf16, void* stream);
 
 /* ---- slow-weight projections -------------------------------------------- */
 /*

@@ -1973,7 +1973,7 @@ int launch_readout_decode(int B, int d, int h, const __nv_bfloat16* x, const __n
                           const __nv_bfloat16* wd, const int* state_index, const float* ln_w, const float* ln_b,
                           float eps, float* zacc, unsigned* done, void* out, int out_bf16, cudaStream_t st);
 int launch_readout_finish(int B, int d, const float* z, const __nv_bfloat16* x, const float* ln_w, const float* ln_b,
-                          float eps, void* out, int out_bf16, cudaStream_t st);
+                          float eps, void* out, int out_bf16, int z_bf16, cudaStream_t st);
 }
 
 extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void* x, const void* w_packed,
@@ -2019,14 +2019,15 @@ extern "C" int uttt_fast_readout_partial(int B, int T, int d, int h, const void*
 }
 
 extern "C" int uttt_readout_finish(int B, int d, const float* z, const void* x, const float* ln_weight,
-                                   const float* ln_bias, float eps, void* out, int out_dtype, void* stream) {
+                                   const float* ln_bias, float eps, void* out, int out_dtype, int z_bf16,
+                                   void* stream) {
   UTTT_REQUIRE(B > 0 && d > 0 && z && x && ln_weight && ln_bias && out, UTTT_ERR_INVALID);
   UTTT_REQUIRE(out_dtype == UTTT_DTYPE_F32 || out_dtype == UTTT_DTYPE_BF16, UTTT_ERR_INVALID);
   UTTT_REQUIRE(d % 128 == 0 && d <= 4096 && eps > 0.f, UTTT_ERR_UNSUPPORTED);
   cudaStream_t st = (cudaStream_t)stream;
   ProfScope ps(UTTT_PROF_READOUT_LN, st);
   return launch_readout_finish(B, d, z, (const __nv_bfloat16*)x, ln_weight, ln_bias, eps, out,
-                               out_dtype == UTTT_DTYPE_BF16, st);
+                               out_dtype == UTTT_DTYPE_BF16, z_bf16 != 0, st);
 }
 
 extern "C" size_t uttt_fast_readout_workspace(int B, int T, int d, int h) {

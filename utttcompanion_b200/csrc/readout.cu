@@ -233,14 +233,15 @@ __global__ void __launch_bounds__(GTHREADS, MINB) readout_decode_kernel(
   }
 }
 
-// out = x + LN(bf16(z)) * gamma + beta for one row per CTA: the LayerNorm of a
-// readout whose z was summed across ranks (hidden-dimension split).
+// out = x + LN(z) * gamma + beta for one row per CTA: the LayerNorm of a readout whose z was
+// summed across ranks (hidden-dimension split); z_bf16: z rounded to BF16 first, as the decode
+// readout does (the tensor-core readout of T > 1 tokens keeps z in FP32).
 template <int MD>
 __global__ void __launch_bounds__(GTHREADS) readout_finish_kernel(const float* __restrict__ z,
                                                                   const __nv_bfloat16* __restrict__ x, int d,
                                                                   const float* __restrict__ ln_w,
                                                                   const float* __restrict__ ln_b, float eps,
-                                                                  void* out, int out_bf16) {
+                                                                  void* out, int out_bf16, int z_bf16) {
   __shared__ float red[GTHREADS / 32];
   const int b = blockIdx.x, tid = threadIdx.x;
   constexpr int NZ = MD / GTHREADS;
@@ -251,7 +252,8 @@ __global__ void __launch_bounds__(GTHREADS) readout_finish_kernel(const float* _
     const int c = tid + i * GTHREADS;
     zv[i] = 0.f;
     if (c < d) {
-      zv[i] = round_bf16(z[(size_t)b * d + c]);
+      zv[i] = z[(size_t)b * d + c];
+      if (z_bf16) zv[i] = round_bf16(zv[i]);
       sum += zv[i];
     }
   }
@@ -278,12 +280,12 @@ __global__ void __launch_bounds__(GTHREADS) readout_finish_kernel(const float* _
 }  // namespace
 
 int launch_readout_finish(int B, int d, const float* z, const __nv_bfloat16* x, const float* ln_w, const float* ln_b,
-                          float eps, void* out, int out_bf16, cudaStream_t st) {
+                          float eps, void* out, int out_bf16, int z_bf16, cudaStream_t st) {
   if (d % 128 != 0 || d > MAXD) return UTTT_ERR_UNSUPPORTED;
   if (d <= 1024)
-    readout_finish_kernel<1024><<<B, GTHREADS, 0, st>>>(z, x, d, ln_w, ln_b, eps, out, out_bf16);
+    readout_finish_kernel<1024><<<B, GTHREADS, 0, st>>>(z, x, d, ln_w, ln_b, eps, out, out_bf16, z_bf16);
   else
-    readout_finish_kernel<MAXD><<<B, GTHREADS, 0, st>>>(z, x, d, ln_w, ln_b, eps, out, out_bf16);
+    readout_finish_kernel<MAXD><<<B, GTHREADS, 0, st>>>(z, x, d, ln_w, ln_b, eps, out, out_bf16, z_bf16);
   return launch_status();
 }
 

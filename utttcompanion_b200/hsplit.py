@@ -82,7 +82,9 @@ class HiddenSplit:
                                                  _ptr(sidx), z.data_ptr(), ws.data_ptr(), ws.numel(), stream),
                    "uttt_fast_readout_partial")
         self.all_reduce(z)
+        # z rounded to BF16 before the LayerNorm exactly where the unsplit readout rounds it (decode)
         _lib.check(lib.uttt_readout_finish(B * T, d, z.data_ptr(), x.data_ptr(), ln_weight.data_ptr(),
-                                           ln_bias.data_ptr(), float(eps), out.data_ptr(), _lib.DTYPE_BF16, stream),
+                                           ln_bias.data_ptr(), float(eps), out.data_ptr(), _lib.DTYPE_BF16,
+                                           1 if T == 1 else 0, stream),
                    "uttt_readout_finish")
         return out
