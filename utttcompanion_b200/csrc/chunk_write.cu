@@ -850,9 +850,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
                                                                 const __grid_constant__ WMaps wm,
                                                                 const ChunkParams p, int update) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3, empty3, dh_done, ops_ready, gfull, gfree, wfullA[3], wfullB[4];
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], full3, empty3, dh_done, ops_ready, gfull, gfree, wfullA[3], wfullB[6];
   __shared__ uint64_t a_ready, kfull, ug_free, h_ready, fullz[2], emptyz[2], zfull[2], zfree[2];
-  __shared__ uint64_t ffull[NF], fempty[NF], qdoneA[3], qdoneB[4];
+  __shared__ uint64_t ffull[NF], fempty[NF], qdoneA[3], qdoneB[6];
   __shared__ uint32_t tmem_slot;
   __shared__ ChunkStats st_sh;
   uint8_t* slots = align1024(smem_raw);             // 96 KB: phase-1 ring | W staging | Z' ring
@@ -911,7 +911,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       mbar_init(&wfullA[i], 1);
       mbar_init(&qdoneA[i], NPROD);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 6; ++i) {
       mbar_init(&wfullB[i], 1);
       mbar_init(&qdoneB[i], NPROD);
     }
@@ -944,7 +944,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   // feeds the next chunk's U', G'), loop B updates W_down and turns each
   // updated quarter straight into the next chunk's Z' operand, so W'_down is
   // never read back.  The threads only touch TMEM and shared memory; the copy
-  // engine keeps HBM busy with up to 3 (A) / 4 (B) quarters in flight.
+  // engine keeps HBM busy with up to 3 (A) / 6 (B) quarters in flight.
   float scale = 1.f;
   if (update && p.clip > 0.f) scale = fminf(1.f, p.clip * rsqrtf(p.norm2[b] + 1e-8f));
   if (update && p.clip_out && t == 0 && tid == 0) p.clip_out[(size_t)b * p.n_chunks + p.chunk_index] = scale;
@@ -953,11 +953,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
   // With beta == 0 the momentum of this chunk is never read again unless this
   // is the last chunk of the call that changes this state.
   const bool write_s = kMomentum || !st.later_active;
-  // Staging holds W only (3 quarters of W_up + W_gate, 4 of W_down in flight);
+  // Staging holds W only (3 quarters of W_up + W_gate, 6 of W_down in flight: loop B's stream is
+  // bounded by its depth, so the next chunk's Z' operand has one A tile, not two);
   // each producer moves its own momentum values between registers and HBM
   // (lanes are consecutive hidden rows, so S_up / S_gate accesses coalesce).
   constexpr int bytesA = 2 * WTILE, nbufA = 3;
-  constexpr int bytesB = WTILE, nbufB = 4;
+  constexpr int bytesB = WTILE, nbufB = 6;
   const int nq = kSplit ? 4 * nch : p.d / QW;   // this rank's 32-wide quarters (local counter)
   const bool fuse = kFuse && update;
   // the next chunk's forward reads the (possibly unchanged) tiles as well
@@ -1388,10 +1389,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
           g_down += dx * dx + dy * dy + dz * dz + dw * dw;
         }
       }
-      uint8_t* zA = (j & 1) ? sAU : slots + 4 * WTILE;  // Z' A tiles [128 d][128 hidden], MN-major
+      uint8_t* zA = sAU;                                // Z' A tile [128 d][128 hidden], MN-major
       if (fuse) {
         // this thread's 16 W'_down values of its hidden row -> BF16 A tile of d tile j
-        if (qq == 0) mbar_wait(&emptyz[j & 1], ((j >> 1) & 1) ^ 1, p.status);
+        if (qq == 0) mbar_wait(&emptyz[0], (j & 1) ^ 1, p.status);   // one A tile: Z' of tile j-1 done
         const int dd = qq * QW + cq;                    // d within the 128-wide tile
         uint4 p0, p1;
         p0.x = pack_bf16x2(w4[0].x, w4[0].y); p0.y = pack_bf16x2(w4[0].z, w4[0].w);
@@ -1403,7 +1404,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
         *reinterpret_cast<uint4*>(blk + sw128_offset(row, (dd & 63) * 2 + 16)) = p1;
       }
       fence_proxy_async_smem();
-      if (fuse && qq == 3) mbar_arrive(&fullz[j & 1]);
+      if (fuse && qq == 3) mbar_arrive(&fullz[0]);
       mbar_arrive(&qdoneB[buf]);
       if (fuse && qq == 3 && j > 0) drain_z(j - 1);
     }
@@ -1590,16 +1591,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) chunk_bwd_kernel(const __grid_
       const uint32_t id_z = idesc_bf16(128, 64, true, true);
       const uint32_t hb = smem_u32(sH);
       auto next_z = [&](int mt) {
-        const int zb = mt & 1;
-        mbar_wait(&fullz[zb], (mt >> 1) & 1, p.status);
+        const int zb = mt & 1;                     // TMEM accumulator (double); A tile single
+        mbar_wait(&fullz[0], mt & 1, p.status);
         mbar_wait(&zfree[zb], ((mt >> 1) & 1) ^ 1, p.status);
         tc_fence_after();
-        const uint32_t a = smem_u32(zb ? sAU : slots + 4 * WTILE);
+        const uint32_t a = smem_u32(sAU);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           mma_bf16(tZN + zb * 64, sdesc_sw128(a + ks * 2048, 16384, 1024), sdesc_sw128(hb + ks * 2048, 8192, 1024),
                    id_z, ks > 0 ? 1u : 0u);
-        mma_commit(&emptyz[zb]);
+        mma_commit(&emptyz[0]);
         mma_commit(&zfull[zb]);
       };
       if (fuse) {
