@@ -1658,6 +1658,13 @@ namespace {
 // one-tile forward); at the 1.58B shape (54 hidden tiles) that saves waves for 1, 3, 4, 6, 9, 11,
 // 12, 14 and 15 rows.  The workspace sizes include the exchange area up to this batch.
 constexpr int DSPLIT_MAX_B = 16;
+// ... and, once the unsplit grid fills the SMs, only when each CTA of the pair still streams at
+// least 8 of the 128-wide d chunks: at d = 1024 and 8 states (176 CTAs) the split fused launch took
+// 0.245 ms against 0.197 ms unsplit, the two exchanges outweighing the halved stream (a memory-bound
+// partial last wave is cheap), while at d = 2560 it gains (6 rows: 1.29 -> 1.20 ms, 9 rows: 1.77 ->
+// 1.72 ms).  Below one wave it always gains (d = 1024, 2 rows: 0.086 -> 0.073 ms; d = 768, 4 rows:
+// 0.120 -> 0.093 ms).
+constexpr int DSPLIT_MIN_D = 2048;
 // the same for the tensor-core readout of one token tile (uttt_fast_readout)
 constexpr int READOUT_DSPLIT_MAX_B = 4;
 size_t dsplit_xch_bytes(int B, int h) {
@@ -1849,7 +1856,7 @@ int chunk_write_impl(int B, int T, int C, int d, int h, int chunk_begin, int n_c
   // fewer waves.  Used when it saves waves and the caller's workspace holds the exchange area.
   const int ntiles = (h + HT - 1) / HT;
   int KS = 1;
-  if (B <= DSPLIT_MAX_B && (d / 128) % 2 == 0) {
+  if (B <= DSPLIT_MAX_B && (d >= DSPLIT_MIN_D || (long long)ntiles * B < num_sms()) && (d / 128) % 2 == 0) {
     const size_t xb = dsplit_xch_bytes(B, h), fb = dsplit_flag_bytes(B, h);
     if (dsplit_factor((long long)ntiles * B) == 2 && ws.used + xb + fb <= ws.cap) {
       p.xch = ws.take<float>(xb / sizeof(float));
