@@ -750,6 +750,9 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     sd = wl.random_state_dict(cfg, seed=0, device=device)          # identical on every rank
     eng = UtttB200(sd, cfg, device=device, max_personas=P, max_positions=spec["prompt_max"] + steps + 64,
                    hsplit=hs)
+    # the decode readouts' z sums through NVLink peer memory (one kernel per layer, no NCCL call);
+    # NCCL stays for the prefill and the write
+    peer = hs.enable_peer_exchange(max_rows=P, d=cfg.d_model, device=device)
     w0 = (sd["fast_weight_pool.w_up_init"], sd["fast_weight_pool.w_gate_init"], sd["fast_weight_pool.w_down_init"])
     del sd
     full = wl.perturbed_persona_states(*w0, P, spec["perturb_std"], seed=100, device=device)
@@ -807,6 +810,7 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     torch.cuda.synchronize()
     del graph                            # a graph holding NCCL calls goes before the process group
     torch.cuda.synchronize()
+    hs.check_peer_exchange()             # raises if a flag wait of the exchange expired
     t = torch.tensor([e0.elapsed_time(e1) / steps], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dec_ms = float(t.item())
@@ -834,13 +838,18 @@ def hsplit_decode_workload(device, rank, world, lib, spec, steps=48):
     dist.all_reduce(kt, op=dist.ReduceOp.MAX)
     breakdown = {k: float(v) for k, v in zip(kinds, kt.tolist())}
     breakdown["allreduces_per_step"] = n_ar / bsteps
+    breakdown["z_sum"] = ("NVLink peer exchange fused with the finish (uttt_split_exchange_finish; its time is "
+                          "readout_finish)" if peer else "NCCL all-reduce + readout finish")
+    hs.check_peer_exchange()
+    hs.close_peer_exchange()
     slow_bytes = sum(x.numel() * x.element_size() for lay in eng.layers for x in (lay.wqkv, lay.wo, lay.w_q, lay.w_o))
     slow_bytes += eng.lm_head.numel() * eng.lm_head.element_size()
     per_gpu = P * 3.0 * cfg.d_model * (cfg.d_ff_fast // world) * 2.0 * cfg.n_layers + slow_bytes
     del packed, down, eng
     return {
         "workload": f"1.58B packed greedy decode, every persona's fast-weight hidden units split over {world} GPUs "
-                    f"(NCCL all-reduce of the readout z per layer), {mode} steps",
+                    f"(readout z summed per layer {'through NVLink peer memory' if peer else 'by NCCL all-reduce'}), "
+                    f"{mode} steps",
         "personas": P, "prompts": spec["prompt_desc"],
         "prompt_tokens": {"min": min(lens), "max": max(lens), "mean": float(np.mean(lens))},
         "decode_tok_s": P / (dec_ms / 1e3), "decode_ms_per_step": dec_ms, "decode_steps_timed": steps,

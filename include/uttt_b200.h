@@ -247,6 +247,35 @@ int uttt_fast_readout_partial(int B, int T, int d, int h, const void* x, const v
 int uttt_readout_finish(int rows, int d, const float* z, const void* x, const float* ln_weight, const float* ln_bias,
                         float eps, void* out, int out_dtype, int z_bf16, void* stream);
 
+/*
+ * The same sum-and-finish without NCCL, over NVLink peer memory: each rank
+ * owns an exchange area of uttt_split_exchange_bytes(world, max_rows, d)
+ * bytes, allocated by uttt_ipc_alloc (zeroed; `handle` receives its 64-byte
+ * CUDA IPC handle) and mapped by every other rank with uttt_ipc_open.
+ * uttt_split_exchange_finish is one kernel per call: every row's CTA stores
+ * this rank's partial z row into each peer's area, raises a flag there,
+ * waits for every peer's flag (at most max_polls polls each; an expired wait
+ * records UTTT_ERR_TIMEOUT in the workspace status word), sums the partials
+ * in rank order and writes out = x + LayerNorm(z) * ln_weight + ln_bias (z
+ * rounded to BF16 first when z_bf16 != 0), as uttt_readout_finish does after
+ * an all-reduce.  `areas` is a host array of the world ranks' area addresses
+ * as mapped in this process (this rank's own at index rank); rows <=
+ * max_rows, 2 <= world <= 8.  Every rank must make the same sequence of
+ * calls: a per-area epoch, bumped after each call, keys the flags and
+ * alternates two receive buffers.  Plain P2P stores only (no multicast).
+ * uttt_ipc_close unmaps a peer's area, uttt_ipc_free releases this rank's.
+ * No counterpart in the reference (which runs one GPU).
+ */
+size_t uttt_split_exchange_bytes(int world, int max_rows, int d);
+int uttt_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int uttt_ipc_open(const void* handle, void** ptr);
+int uttt_ipc_close(void* ptr);
+int uttt_ipc_free(void* ptr);
+int uttt_split_exchange_finish(int rows, int d, const float* z_partial, const void* x, const float* ln_weight,
+                               const float* ln_bias, float eps, void* out, int out_dtype, int z_bf16, int rank,
+                               int world, int max_rows, void* const* areas, unsigned max_polls, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* ---- slow-weight projections -------------------------------------------- */
 /*
  * y = x W^T for BF16 x (M, K) and an nn.Linear weight W (N, K), FP32

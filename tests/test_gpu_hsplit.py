@@ -7,8 +7,10 @@ across the ranks: the logits must match an unsplit engine on the same inputs
 ranks.  The batched chunk-TTT write (momentum + clipping, ragged masks) sums
 every chunk's partial Z and the clip norms across the ranks: each rank's
 updated slices must equal the same slices of the unsplit write (state rel-L2
-<= 1e-3, update rel-L2 <= 1e-2) with the same per-layer surprise.  Skipped
-with fewer than two visible GPUs."""
+<= 1e-3, update rel-L2 <= 1e-2) with the same per-layer surprise.  The decode
+steps are run a second time with the NVLink peer exchange
+(uttt_split_exchange_finish) in place of the NCCL all-reduce, within the same
+bound.  Skipped with fewer than two visible GPUs."""
 
 import datetime
 import os
@@ -64,6 +66,12 @@ def _rank_main(rank, world, port, out_dir):
     local = [w.to(dev) for w in hs.shard(*full)]
     packed, down = eng.read_copies(*local)
     split = _run(eng, packed, down, prompts, forced)
+    # prefill and decode again with the NVLink peer exchange summing the decode readouts in place of
+    # the NCCL all-reduce (the prefill's readouts of more rows keep NCCL)
+    peer_on = hs.enable_peer_exchange(max_rows=P, d=cfg.d_model, device=dev)
+    peer = _run(eng, packed, down, prompts, forced)
+    hs.check_peer_exchange()                 # no flag wait expired
+    hs.close_peer_exchange()
     # batched write on prompt + forced tokens, ragged (right-padded) with masks
     turns = [prompts[p].tolist() + [int(f[p]) for f in forced] for p in range(P)]
     Tpad = ((max(len(t) for t in turns) + 63) // 64) * 64
@@ -80,10 +88,10 @@ def _rank_main(rank, world, port, out_dir):
     ref_eng = UtttB200(sd, cfg, device=dev, max_personas=P)
     rp, rd = ref_eng.read_copies(*(w.to(dev) for w in full))
     ref = _run(ref_eng, rp, rd, prompts, forced)
-    worst = 0.0
-    for a, b in zip(split, ref):
-        excess = (torch.abs(a - b) - (LOGIT_TOL + torch.abs(b) / 128)).max().item()
-        worst = max(worst, excess)
+    worst, worst_peer = 0.0, 0.0
+    for a, c, b in zip(split, peer, ref):
+        worst = max(worst, (torch.abs(a - b) - (LOGIT_TOL + torch.abs(b) / 128)).max().item())
+        worst_peer = max(worst_peer, (torch.abs(c - b) - (LOGIT_TOL + torch.abs(b) / 128)).max().item())
     fullw = [w.to(dev) for w in full]
     st_ref = FastState(*fullw, *(torch.zeros_like(w) for w in fullw), ref_eng.ln_w.clone(), ref_eng.ln_b.clone())
     new_ref, _, pl_ref = ref_eng.test_time_update_batch(inter, st_ref, mask)
@@ -94,7 +102,8 @@ def _rank_main(rank, world, port, out_dir):
         state_err = max(state_err, float(torch.linalg.norm(got - want) / torch.linalg.norm(want)))
         delta_err = max(delta_err, float(torch.linalg.norm((got - w0) - (want - w0)) / torch.linalg.norm(want - w0)))
     surprise_err = float(np.max(np.abs(np.array(pl_split) - np.array(pl_ref)) / np.abs(np.array(pl_ref))))
-    np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array([worst, state_err, delta_err, surprise_err]))
+    np.save(os.path.join(out_dir, f"rank{rank}.npy"),
+            np.array([worst, state_err, delta_err, surprise_err, float(peer_on), worst_peer]))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
@@ -107,7 +116,9 @@ def test_two_rank_hidden_split_decode_and_write_match_unsplit(tmp_path):
         p.join(timeout=300)
         assert p.exitcode == 0
     for r in range(2):
-        worst, state_err, delta_err, surprise_err = np.load(os.path.join(str(tmp_path), f"rank{r}.npy"))
+        worst, state_err, delta_err, surprise_err, peer_on, worst_peer = np.load(
+            os.path.join(str(tmp_path), f"rank{r}.npy"))
         assert worst <= 0.0, (r, worst)
+        assert peer_on == 1.0 and worst_peer <= 0.0, (r, peer_on, worst_peer)
         assert state_err <= 1e-3 and delta_err <= 1e-2, (r, state_err, delta_err)
         assert surprise_err <= 1e-3, (r, surprise_err)

@@ -61,6 +61,13 @@ SIGNATURES: Dict[str, tuple] = {
     "uttt_fast_readout": (i32, [i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, f32, vp, i32, vp, sz, vp]),
     "uttt_fast_readout_partial": (i32, [i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]),
     "uttt_readout_finish": (i32, [i32, i32, vp, vp, vp, vp, f32, vp, i32, i32, vp]),
+    "uttt_split_exchange_bytes": (sz, [i32, i32, i32]),
+    "uttt_ipc_alloc": (i32, [sz, vp, vp]),
+    "uttt_ipc_open": (i32, [vp, vp]),
+    "uttt_ipc_close": (i32, [vp]),
+    "uttt_ipc_free": (i32, [vp]),
+    "uttt_split_exchange_finish": (i32, [i32, i32, vp, vp, vp, vp, f32, vp, i32, i32, i32, i32, i32, vp, C.c_uint,
+                                         vp, sz, vp]),
     "uttt_linear_workspace": (sz, [i32, i32]),
     "uttt_linear": (i32, [i32, i32, i32, vp, vp, i32, vp, f32, vp, sz, vp]),
     "uttt_attn_decode": (i32, [i32, i32, i32, i32, i32, vp, i32, vp, vp, vp, vp, vp, vp, vp, i32, vp]),
