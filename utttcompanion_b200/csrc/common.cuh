@@ -5,7 +5,7 @@
 //     the caller-provided status word and fall through, so a lost arrival can
 //     never hang the GPU (the host then reports UTTT_ERR_TIMEOUT).
 //   * TMA (cp.async.bulk.tensor) tiles land in 128-byte-swizzled shared memory;
-//     no load anywhere uses .multicast::cluster.
+//     no load anywhere is multicast to the CTAs of a cluster.
 //   * tcgen05.mma (kind::f16, BF16 x BF16 -> FP32) is issued by one thread,
 //     accumulates in tensor memory and is drained with tcgen05.ld.
 #pragma once
