@@ -101,7 +101,9 @@ class HiddenSplit:
             check_status(self._peer["ws"], "uttt_split_exchange_finish")
 
     def close_peer_exchange(self) -> None:
-        """Unmap the peers' areas and free this rank's (after every exchange has completed)."""
+        """Unmap the peers' areas and free this rank's.  Every rank calls it after its exchanges have
+        completed and after every CUDA graph that captured an exchange has been released (a replay
+        would store into the freed areas)."""
         if self._peer is None:
             return
         lib = _lib.load()
