@@ -58,9 +58,10 @@ class HiddenSplit:
         import torch.distributed as dist
         if self.world < 2 or self.world > 8 or self._peer is not None:
             return self._peer is not None
+        import contextlib
         lib = _lib.load()
         dev = torch.device(device)
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev) if dev.type == "cuda" else contextlib.nullcontext():
             nbytes = int(lib.uttt_split_exchange_bytes(self.world, max_rows, d))
             own = ctypes.c_void_p()
             handle = (ctypes.c_char * 64)()
@@ -91,7 +92,7 @@ class HiddenSplit:
             self._peer = {"areas_arr": arr, "areas": ctypes.cast(arr, ctypes.c_void_p), "own": own.value,
                           "opened": opened,
                           "max_rows": int(max_rows), "d": int(d), "device": dev,
-                          "ws": workspace(256, dev, slot=4)}
+                          "ws": workspace(256, dev, slot=4) if dev.type == "cuda" else None}
         return True
 
     def check_peer_exchange(self) -> None:
